@@ -1,0 +1,104 @@
+/*
+ * vesper_b200.h -- the C ABI of libvesper_b200.so, the B200 (sm_100a) kernels of the
+ * mstampfli/vesper-preview column hot path.
+ *
+ * Conventions (every entry point):
+ *   - plain device pointers and sizes; `stream` is a cudaStream_t passed as void* (NULL = the
+ *     legacy default stream); work is enqueued on it and the call returns without synchronizing,
+ *     so every entry point can be captured in a CUDA graph;
+ *   - no allocation: outputs and workspaces are the caller's (size queries are provided);
+ *   - the return value is VB_OK or an error code; vb_last_error() gives the message of the last
+ *     failure on the calling host thread;
+ *   - tensors are dense and row-major in the layouts named below; `dtype` codes are VB_F32,
+ *     VB_BF16 and VB_F16;
+ *   - deterministic: no floating-point atomics; reductions run in a fixed order.
+ *
+ * Each declaration cites the reference interface (file:line inside mstampfli/vesper-preview) whose
+ * work it performs.
+ */
+#ifndef VESPER_B200_H
+#define VESPER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VB_API __attribute__((visibility("default")))
+#else
+#define VB_API
+#endif
+
+enum { VB_OK = 0, VB_ERR_INVALID = 1, VB_ERR_CUDA = 2, VB_ERR_TIMEOUT = 3 };
+enum { VB_F32 = 0, VB_BF16 = 1, VB_F16 = 2 };
+
+/* The message of the last failed call on this host thread ("" if none). */
+VB_API const char *vb_last_error(void);
+/* ABI version of this library. */
+VB_API int vb_abi_version(void);
+
+/* ---- RMSNorm --------------------------------------------------------------------------------
+ * y = x / sqrt(mean(x^2) + eps) * weight per row, computed scale-safely (each row divided by
+ * max(max|x|, floor) first), statistics in float32, y in x's dtype; inv[r] = 1/sqrt(mean(x^2)+eps).
+ * Replaces vesper/kernels/norm_triton.py:85-93 (rms_forward), reached from
+ * vesper/kernels/norm.py:24-52 (fused_rms_norm) and vesper/column.py:178-180 (RMSNorm.forward).
+ * x, y: [rows, width] of `dtype`; weight: [width] float32; inv: [rows] float32. */
+VB_API int vb_rms_norm_fwd(const void *x, const float *weight, void *y, float *inv, int64_t rows,
+                    int width, float floor_, float eps, int dtype, void *stream);
+
+/* Bytes of workspace vb_rms_norm_bwd needs (the gain gradient's fixed-order partial sums). */
+VB_API size_t vb_rms_norm_bwd_workspace(int64_t rows, int width);
+
+/* dx = inv * (dy*g - xhat * mean(dy*g*xhat)), xhat = x*inv; dweight = sum over rows of dy*xhat
+ * (float32, fixed-order). Replaces vesper/kernels/norm_triton.py:96-109 (rms_backward). */
+VB_API int vb_rms_norm_bwd(const void *x, const float *weight, const void *dy, const float *inv,
+                    void *dx, float *dweight, void *workspace, int64_t rows, int width,
+                    int dtype, void *stream);
+
+/* ---- causal key filter + key normalisation ---------------------------------------------------
+ * u[b,t,j] = sum_r taps[r,j] * full[b, t+K-1-r, j] with full = cat(hist, z) along t, then
+ * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's
+ * dtype. z, keys: [B,T,W] (keys viewed [B,T,heads,W/heads]); hist: [B,K-1,W] float32;
+ * taps: [K,W] float32. Replaces vesper/kernels/keys_triton.py:148-156 (keys_forward) reached from
+ * vesper/kernels/keys.py:28-46 (fused_keys) and vesper/column.py:255-289 (RecurrentSublayer.keys). */
+VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void *keys, int B, int T,
+                int width, int heads, int taps_count, float floor_, int dtype, void *stream);
+
+VB_API size_t vb_keys_bwd_workspace(int B, int T, int width, int heads, int taps_count);
+
+/* Gradients of sum(keys * grad_keys): grad_z [B,T,W] in z's dtype, grad_taps [K,W] float32
+ * (fixed-order), grad_hist [B,K-1,W] float32 (skipped when NULL). Replaces
+ * vesper/kernels/keys_triton.py:159-177 (keys_backward) and vesper/kernels/keys.py:67-78
+ * (_history_gradient). */
+VB_API int vb_keys_bwd(const void *z, const float *hist, const float *taps, const void *grad_keys,
+                void *grad_z, float *grad_taps, float *grad_hist, void *workspace, int B, int T,
+                int width, int heads, int taps_count, float floor_, int dtype, void *stream);
+
+/* ---- delta-rule scan, float32 (token-serial) --------------------------------------------------
+ * H_t = H_{t-1} + beta_t k_t (v_t - H_{t-1}^T k_t)^T, o_t = H_t^T q_t, H read as [key, value].
+ * q, k, v, o: [B,T,H,D] float32; beta: [B,T,H]; state0, state_n: [B,H,D,D]; resid: [B,T,H,D]
+ * float32 (v_t - H_{t-1}^T k_t, saved for the backward; may be NULL). D <= 256.
+ * Replaces vesper/kernels/delta_scan.py:156-187 (delta_scan_fused_fp32, which ran fla-core's
+ * fused_recurrent_delta_rule) with the semantics of vesper/recurrence.py:143-217. */
+VB_API int vb_delta_scan_f32_fwd(const float *q, const float *k, const float *v, const float *beta,
+                          const float *state0, float *o, float *state_n, float *resid, int B,
+                          int T, int H, int D, void *stream);
+
+VB_API size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D);
+
+/* Gradients of sum(o*dout) + sum(state_n*dstate_n) (dstate_n may be NULL = zero) for all five
+ * inputs; `resid` from the forward. */
+VB_API int vb_delta_scan_f32_bwd(const float *q, const float *k, const float *v, const float *beta,
+                          const float *state0, const float *resid, const float *dout,
+                          const float *dstate_n, float *dq, float *dk, float *dv, float *dbeta,
+                          float *dstate0, void *workspace, int B, int T, int H, int D,
+                          void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VESPER_B200_H */

@@ -1,0 +1,338 @@
+// The causal key filter with its key normalisation, forward and backward
+// (vesper/column.py:255-289 RecurrentSublayer.keys; vesper/recurrence.py:91-115 normalize_keys).
+//
+// Layout: one warp walks a run of consecutive tokens of one (batch row, head); each lane holds
+// EPL = head_dim/32 adjacent channels. The last K rows of the filter input stay in registers, so
+// every element of z is read from HBM once (plus K-1 rows of overlap per run), and the key is
+// written once. The backward walks its run in reverse with the next K-1 input gradients in
+// registers, recomputing the filter output, and fuses dz, the taps' gradient (per-warp partial
+// sums, reduced in a fixed order) and the history's gradient into the same pass.
+#include "common.cuh"
+
+namespace vb {
+int column_sum(const float* partial, float* out, int parts, int width, cudaStream_t st);
+
+namespace {
+
+constexpr int RUN = 64;        // tokens per warp
+constexpr int WARPS = 4;       // warps per CTA
+
+template <int EPL>
+struct Vec {
+  float v[EPL];
+};
+
+// loads EPL channels [c, c+EPL) of row `t` of the filter input (z for t >= 0, else history)
+template <typename T, int EPL>
+__device__ __forceinline__ void load_in(const T* __restrict__ z, const float* __restrict__ hist,
+                                        int b, int t, int T_, int W, int K, int c, bool live,
+                                        float (&out)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) out[e] = 0.f;
+  if (!live) return;
+  if (t >= 0) {
+    const T* p = z + ((int64_t)b * T_ + t) * W + c;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) out[e] = to_f32<T>(p[e]);
+  } else if (t >= -(K - 1)) {
+    const float* p = hist + ((int64_t)b * (K - 1) + (K - 1 + t)) * W + c;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) out[e] = p[e];
+  }
+}
+
+// normalize_keys of one head vector spread over the warp: returns scale, den, sq
+template <int EPL>
+__device__ __forceinline__ void norm_stats(const float (&u)[EPL], float floor_, float& scale,
+                                           float& den, float& sq) {
+  float amax = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) amax = fmaxf(amax, fabsf(u[e]));
+  scale = fmaxf(warp_max(amax), floor_);
+  float s2 = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float s = u[e] / scale;
+    s2 += s * s;
+  }
+  sq = warp_sum(s2);
+  den = sqrtf(fmaxf(sq, 1.0f));
+}
+
+template <typename T, int EPL, int K>
+__global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restrict__ z,
+                                                              const float* __restrict__ hist,
+                                                              const float* __restrict__ taps,
+                                                              T* __restrict__ out, int B, int T_,
+                                                              int W, int heads, int runs,
+                                                              float floor_) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (gw >= B * heads * runs) return;
+  const int run = gw % runs, head = (gw / runs) % heads, b = gw / (runs * heads);
+  const int hd = W / heads;
+  const bool live = lane * EPL < hd;  // head widths below 32 leave lanes idle
+  const int c = head * hd + lane * EPL;
+  float tp[K][EPL];
+#pragma unroll
+  for (int r = 0; r < K; ++r)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) tp[r][e] = live ? __ldg(taps + (int64_t)r * W + c + e) : 0.f;
+  const int t0 = run * RUN, t1 = min(T_, t0 + RUN);
+  float win[K][EPL];  // win[r] = input row t - r
+#pragma unroll
+  for (int r = 1; r < K; ++r) load_in<T, EPL>(z, hist, b, t0 - r, T_, W, K, c, live, win[r]);
+  for (int t = t0; t < t1; ++t) {
+    load_in<T, EPL>(z, hist, b, t, T_, W, K, c, live, win[0]);
+    float u[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      float a = 0.f;
+#pragma unroll
+      for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[r][e], a);
+      u[e] = a;
+    }
+    float scale, den, sq;
+    norm_stats<EPL>(u, floor_, scale, den, sq);
+    if (live) {
+      T* p = out + ((int64_t)b * T_ + t) * W + c;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) p[e] = from_f32<T>((u[e] / scale) / den);
+    }
+#pragma unroll
+    for (int r = K - 1; r > 0; --r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) win[r][e] = win[r - 1][e];
+  }
+}
+
+// Backward over one run in reverse. partial: [B * runs, K, W] taps-gradient partial sums.
+template <typename T, int EPL, int K>
+__global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
+    const T* __restrict__ z, const float* __restrict__ hist, const float* __restrict__ taps,
+    const T* __restrict__ gk, T* __restrict__ dz, float* __restrict__ dhist,
+    float* __restrict__ partial, int B, int T_, int W, int heads, int runs, float floor_) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (gw >= B * heads * runs) return;
+  const int run = gw % runs, head = (gw / runs) % heads, b = gw / (runs * heads);
+  const int hd = W / heads;
+  const bool live = lane * EPL < hd;
+  const int c = head * hd + lane * EPL;
+  float tp[K][EPL];
+#pragma unroll
+  for (int r = 0; r < K; ++r)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) tp[r][e] = live ? __ldg(taps + (int64_t)r * W + c + e) : 0.f;
+  const int t0 = run * RUN, t1 = min(T_, t0 + RUN);
+  const int thi = min(T_ - 1, t1 + K - 2);  // the next run's first K-1 gradients are recomputed
+  float win[K][EPL];   // win[r] = input row t - r
+  float dring[K][EPL]; // dring[r] = du at t + r
+  float dt[K][EPL];    // taps gradient over this run
+#pragma unroll
+  for (int r = 0; r < K; ++r)
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) { dring[r][e] = 0.f; dt[r][e] = 0.f; }
+  // before the step for token t the window holds the rows of step t + 1: win[r] = row t + 1 - r
+#pragma unroll
+  for (int r = 0; r < K; ++r) load_in<T, EPL>(z, hist, b, thi + 1 - r, T_, W, K, c, live && r > 0, win[r]);
+  for (int t = thi; t >= t0; --t) {
+    // slide one row older: win[r] = row t - r; only the oldest row is new
+#pragma unroll
+    for (int r = 0; r < K - 1; ++r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) win[r][e] = win[r + 1][e];
+    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, win[K - 1]);
+    float u[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      float a = 0.f;
+#pragma unroll
+      for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[r][e], a);
+      u[e] = a;
+    }
+    float scale, den, sq;
+    norm_stats<EPL>(u, floor_, scale, den, sq);
+    float g[EPL];
+    if (live) {
+      const T* p = gk + ((int64_t)b * T_ + t) * W + c;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) g[e] = to_f32<T>(p[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) g[e] = 0.f;
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dot += g[e] * (u[e] / scale);
+    dot = warp_sum(dot);
+    // shift the gradient ring: dring[r] <- du at t + r
+#pragma unroll
+    for (int r = K - 1; r > 0; --r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) dring[r][e] = dring[r - 1][e];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const float s = u[e] / scale;
+      const float through = sq >= 1.0f ? s * (dot / (den * den * den)) : 0.f;
+      dring[0][e] = (g[e] / den - through) / scale;
+    }
+    if (t < t1) {
+#pragma unroll
+      for (int r = 0; r < K; ++r)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dt[r][e] = fmaf(dring[0][e], win[r][e], dt[r][e]);
+      float o[EPL];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        float a = 0.f;
+#pragma unroll
+        for (int r = 0; r < K; ++r)
+          if (t + r < T_) a = fmaf(tp[r][e], dring[r][e], a);
+        o[e] = a;
+      }
+      if (live) {
+        T* p = dz + ((int64_t)b * T_ + t) * W + c;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) p[e] = from_f32<T>(o[e]);
+      }
+    }
+  }
+  if (live) {
+    float* p = partial + (((int64_t)b * runs + run) * K) * W + c;
+#pragma unroll
+    for (int r = 0; r < K; ++r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) p[(int64_t)r * W + e] = dt[r][e];
+  }
+  // history rows p = 0..K-2 feed u[t] for t = p - (K-1) + r >= 0; dring[r] = du at t0 + r = r
+  if (dhist != nullptr && run == 0 && live) {
+#pragma unroll
+    for (int p = 0; p < K - 1; ++p) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) {
+        float a = 0.f;
+#pragma unroll
+        for (int r = 0; r < K; ++r) {
+          const int t = p - (K - 1) + r;
+          if (t >= 0 && t < T_) a = fmaf(tp[r][e], dring[t][e], a);
+        }
+        dhist[((int64_t)b * (K - 1) + p) * W + c + e] = a;
+      }
+    }
+  }
+}
+
+template <typename T, int EPL>
+int launch_fwd(const void* z, const float* hist, const float* taps, void* out, int B, int T_, int W,
+               int heads, int K, float floor_, cudaStream_t st) {
+  const int runs = (T_ + RUN - 1) / RUN;
+  const int warps = B * heads * runs;
+  const int ctas = (warps + WARPS - 1) / WARPS;
+#define VB_KEYS_FWD(KK)                                                                          \
+  case KK:                                                                                       \
+    keys_fwd_kernel<T, EPL, KK><<<ctas, WARPS * 32, 0, st>>>((const T*)z, hist, taps, (T*)out, B, \
+                                                             T_, W, heads, runs, floor_);        \
+    break;
+  switch (K) {
+    VB_KEYS_FWD(1) VB_KEYS_FWD(2) VB_KEYS_FWD(3) VB_KEYS_FWD(4)
+    VB_KEYS_FWD(5) VB_KEYS_FWD(6) VB_KEYS_FWD(7) VB_KEYS_FWD(8)
+    default: set_error("keys: filter width %d not in [1, 8]", K); return VB_ERR_INVALID;
+  }
+#undef VB_KEYS_FWD
+  VB_LAUNCH_CHECK("keys_fwd");
+  return VB_OK;
+}
+
+template <typename T, int EPL>
+int launch_bwd(const void* z, const float* hist, const float* taps, const void* gk, void* dz,
+               float* dtaps, float* dhist, float* partial, int B, int T_, int W, int heads, int K,
+               float floor_, cudaStream_t st) {
+  const int runs = (T_ + RUN - 1) / RUN;
+  const int warps = B * heads * runs;
+  const int ctas = (warps + WARPS - 1) / WARPS;
+#define VB_KEYS_BWD(KK)                                                                           \
+  case KK:                                                                                        \
+    keys_bwd_kernel<T, EPL, KK><<<ctas, WARPS * 32, 0, st>>>((const T*)z, hist, taps, (const T*)gk, \
+                                                             (T*)dz, dhist, partial, B, T_, W,    \
+                                                             heads, runs, floor_);                \
+    break;
+  switch (K) {
+    VB_KEYS_BWD(1) VB_KEYS_BWD(2) VB_KEYS_BWD(3) VB_KEYS_BWD(4)
+    VB_KEYS_BWD(5) VB_KEYS_BWD(6) VB_KEYS_BWD(7) VB_KEYS_BWD(8)
+    default: set_error("keys: filter width %d not in [1, 8]", K); return VB_ERR_INVALID;
+  }
+#undef VB_KEYS_BWD
+  VB_LAUNCH_CHECK("keys_bwd");
+  return column_sum(partial, dtaps, B * runs, K * W, st);
+}
+
+int check_shape(int B, int T_, int W, int heads, int K) {
+  VB_REQUIRE(B >= 0 && T_ >= 0 && W > 0 && heads > 0 && W % heads == 0,
+             "keys: bad shape B=%d T=%d W=%d heads=%d", B, T_, W, heads);
+  const int hd = W / heads;
+  VB_REQUIRE((hd & (hd - 1)) == 0 && hd >= 1 && hd <= 256,
+             "keys: head width %d must be a power of two up to 256", hd);
+  VB_REQUIRE(K >= 1 && K <= 8, "keys: filter width %d not in [1, 8]", K);
+  return VB_OK;
+}
+
+}  // namespace
+}  // namespace vb
+
+using namespace vb;
+
+#define VB_KEYS_EPL_DISPATCH(hd, EPL, ...)       \
+  [&]() -> int {                                 \
+    if (hd <= 32) { constexpr int EPL = 1; return __VA_ARGS__(); } \
+    if (hd == 64) { constexpr int EPL = 2; return __VA_ARGS__(); } \
+    if (hd == 128) { constexpr int EPL = 4; return __VA_ARGS__(); } \
+    { constexpr int EPL = 8; return __VA_ARGS__(); }               \
+  }()
+
+extern "C" int vb_keys_fwd(const void* z, const float* hist, const float* taps, void* keys, int B,
+                           int T, int width, int heads, int taps_count, float floor_, int dtype,
+                           void* stream) {
+  int rc = check_shape(B, T, width, heads, taps_count);
+  if (rc) return rc;
+  if (B == 0 || T == 0) return VB_OK;
+  VB_REQUIRE(z && taps && keys && (hist || taps_count == 1), "keys_fwd: null pointer");
+  const int hd = width / heads;
+  cudaStream_t st = (cudaStream_t)stream;
+  return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
+    return VB_KEYS_EPL_DISPATCH(hd, EPL, [&]() -> int {
+      return launch_fwd<Tt, EPL>(z, hist, taps, keys, B, T, width, heads, taps_count, floor_, st);
+    });
+  });
+}
+
+extern "C" size_t vb_keys_bwd_workspace(int B, int T, int width, int heads, int taps_count) {
+  const int runs = (T + RUN - 1) / RUN;
+  const size_t parts = (size_t)(B > 0 ? B : 1) * (size_t)(runs > 0 ? runs : 1);
+  return parts * (size_t)(taps_count > 0 ? taps_count : 1) * (size_t)(width > 0 ? width : 1) * sizeof(float);
+}
+
+extern "C" int vb_keys_bwd(const void* z, const float* hist, const float* taps, const void* grad_keys,
+                           void* grad_z, float* grad_taps, float* grad_hist, void* workspace, int B,
+                           int T, int width, int heads, int taps_count, float floor_, int dtype,
+                           void* stream) {
+  int rc = check_shape(B, T, width, heads, taps_count);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (B == 0 || T == 0) {
+    VB_CUDA_CHECK(cudaMemsetAsync(grad_taps, 0, sizeof(float) * taps_count * width, st), "keys_bwd");
+    if (grad_hist && B > 0)
+      VB_CUDA_CHECK(cudaMemsetAsync(grad_hist, 0, sizeof(float) * B * (taps_count - 1) * width, st),
+                    "keys_bwd");
+    return VB_OK;
+  }
+  VB_REQUIRE(z && taps && grad_keys && grad_z && grad_taps && workspace && (hist || taps_count == 1),
+             "keys_bwd: null pointer");
+  const int hd = width / heads;
+  return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
+    return VB_KEYS_EPL_DISPATCH(hd, EPL, [&]() -> int {
+      return launch_bwd<Tt, EPL>(z, hist, taps, grad_keys, grad_z, grad_taps, grad_hist,
+                                 (float*)workspace, B, T, width, heads, taps_count, floor_, st);
+    });
+  });
+}

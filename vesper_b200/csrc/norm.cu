@@ -1,0 +1,205 @@
+// Scale-safe RMSNorm, forward and backward (the reference's column.RMSNorm, vesper/column.py:159-188,
+// and its gradient vesper/kernels/norm_triton.py:47-82).
+//
+// Forward: one warp per row, the row held in registers (16-byte vector loads when the width
+// allows), one read and one write of the row. Backward: one warp per row for dx; the gain
+// gradient is summed per warp in shared memory, per CTA in warp order, then across CTAs in CTA
+// order by a second kernel: no atomics, the same bits on every run.
+#include "common.cuh"
+
+namespace vb {
+namespace {
+
+constexpr int WARPS = 8;          // rows in flight per CTA (forward) / warps per CTA (backward)
+constexpr int MAXV = 8;           // 16-byte vectors per lane in the vector path
+constexpr int BWD_ROWS_PER_WARP = 8;
+
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict__ x,
+                                                             const float* __restrict__ w,
+                                                             T* __restrict__ y, float* __restrict__ inv,
+                                                             int64_t rows, int width, float floor_,
+                                                             float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * width;
+  T* yr = y + row * width;
+  if constexpr (VEC) {
+    constexpr int E = 16 / sizeof(T);
+    const int nv = width / E;
+    float v[MAXV][E];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        load_vec<T, E>(xr + vi * E, v[i]);
+#pragma unroll
+        for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
+      }
+    }
+    const float scale = fmaxf(warp_max(amax), floor_);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (lane + 32 * i < nv) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float z = v[i][e] / scale;
+          ss += z * z;
+        }
+      }
+    }
+    const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float g[E], o[E];
+        const float4* gp = reinterpret_cast<const float4*>(w + vi * E);
+#pragma unroll
+        for (int q = 0; q < E / 4; ++q) {
+          float4 g4 = __ldg(gp + q);
+          g[4 * q] = g4.x; g[4 * q + 1] = g4.y; g[4 * q + 2] = g4.z; g[4 * q + 3] = g4.w;
+        }
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = v[i][e] / scale / rms * g[e];
+        store_vec<T, E>(yr + vi * E, o);
+      }
+    }
+    if (lane == 0) inv[row] = 1.0f / (scale * rms);
+  } else {
+    float amax = 0.f;
+    for (int j = lane; j < width; j += 32) amax = fmaxf(amax, fabsf(to_f32<T>(xr[j])));
+    const float scale = fmaxf(warp_max(amax), floor_);
+    float ss = 0.f;
+    for (int j = lane; j < width; j += 32) {
+      const float z = to_f32<T>(xr[j]) / scale;
+      ss += z * z;
+    }
+    const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
+    for (int j = lane; j < width; j += 32)
+      yr[j] = from_f32<T>(to_f32<T>(xr[j]) / scale / rms * __ldg(w + j));
+    if (lane == 0) inv[row] = 1.0f / (scale * rms);
+  }
+}
+
+// dx per row; the gain's gradient per CTA into partial[blockIdx.x][width].
+template <typename T>
+__global__ void __launch_bounds__(WARPS * 32) rms_bwd_kernel(const T* __restrict__ x,
+                                                             const float* __restrict__ w,
+                                                             const T* __restrict__ dy,
+                                                             const float* __restrict__ inv,
+                                                             T* __restrict__ dx,
+                                                             float* __restrict__ partial,
+                                                             int64_t rows, int width) {
+  extern __shared__ float acc[];  // [WARPS][width]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* mine = acc + (size_t)warp * width;
+  for (int j = lane; j < width; j += 32) mine[j] = 0.f;
+  const int64_t row0 = (int64_t)blockIdx.x * WARPS * BWD_ROWS_PER_WARP;
+  for (int k = 0; k < BWD_ROWS_PER_WARP; ++k) {
+    const int64_t row = row0 + (int64_t)k * WARPS + warp;
+    if (row >= rows) break;
+    const T* xr = x + row * width;
+    const T* dr = dy + row * width;
+    const float iv = __ldg(inv + row);
+    float s = 0.f;
+    for (int j = lane; j < width; j += 32) {
+      const float xh = to_f32<T>(xr[j]) * iv;
+      s += to_f32<T>(dr[j]) * __ldg(w + j) * xh;
+    }
+    const float mean = warp_sum(s) / (float)width;
+    T* out = dx + row * width;
+    for (int j = lane; j < width; j += 32) {
+      const float xh = to_f32<T>(xr[j]) * iv;
+      const float d = to_f32<T>(dr[j]);
+      out[j] = from_f32<T>(iv * (d * __ldg(w + j) - xh * mean));
+      mine[j] += d * xh;
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < width; j += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < WARPS; ++q) t += acc[(size_t)q * width + j];
+    partial[(size_t)blockIdx.x * width + j] = t;
+  }
+}
+
+__global__ void column_sum_kernel(const float* __restrict__ partial, float* __restrict__ out,
+                                  int parts, int width) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= width) return;
+  float t = 0.f;
+  for (int p = 0; p < parts; ++p) t += partial[(size_t)p * width + j];
+  out[j] = t;
+}
+
+int bwd_ctas(int64_t rows) {
+  const int64_t per = (int64_t)WARPS * BWD_ROWS_PER_WARP;
+  return (int)((rows + per - 1) / per);
+}
+
+}  // namespace
+
+// Sums `parts` rows of `partial [parts, width]` in row order into out[width].
+int column_sum(const float* partial, float* out, int parts, int width, cudaStream_t st) {
+  column_sum_kernel<<<(width + 255) / 256, 256, 0, st>>>(partial, out, parts, width);
+  VB_LAUNCH_CHECK("column_sum");
+  return VB_OK;
+}
+
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" int vb_rms_norm_fwd(const void* x, const float* weight, void* y, float* inv, int64_t rows,
+                               int width, float floor_, float eps, int dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_fwd: bad shape rows=%lld width=%d", (long long)rows, width);
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(x && weight && y && inv, "rms_norm_fwd: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int ctas = (int)((rows + WARPS - 1) / WARPS);
+  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
+    constexpr int E = 16 / sizeof(T);
+    const bool vec = width % E == 0 && width <= 32 * MAXV * E && aligned16(x) && aligned16(y) &&
+                     aligned16(weight);
+    if (vec)
+      rms_fwd_kernel<T, true><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
+                                                           width, floor_, eps);
+    else
+      rms_fwd_kernel<T, false><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
+                                                            width, floor_, eps);
+    VB_LAUNCH_CHECK("rms_norm_fwd");
+    return VB_OK;
+  });
+}
+
+extern "C" size_t vb_rms_norm_bwd_workspace(int64_t rows, int width) {
+  return (size_t)(rows > 0 ? bwd_ctas(rows) : 1) * (size_t)width * sizeof(float);
+}
+
+extern "C" int vb_rms_norm_bwd(const void* x, const float* weight, const void* dy, const float* inv,
+                               void* dx, float* dweight, void* workspace, int64_t rows, int width,
+                               int dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_bwd: bad shape rows=%lld width=%d", (long long)rows, width);
+  VB_REQUIRE(width <= 4096, "rms_norm_bwd: width %d exceeds the kernel's 4096", width);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows == 0) {
+    VB_CUDA_CHECK(cudaMemsetAsync(dweight, 0, sizeof(float) * width, st), "rms_norm_bwd");
+    return VB_OK;
+  }
+  VB_REQUIRE(x && weight && dy && inv && dx && dweight && workspace, "rms_norm_bwd: null pointer");
+  const int ctas = bwd_ctas(rows);
+  const size_t smem = sizeof(float) * WARPS * width;
+  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    rms_bwd_kernel<T><<<ctas, WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
+                                                      (T*)dx, (float*)workspace, rows, width);
+    VB_LAUNCH_CHECK("rms_norm_bwd");
+    return column_sum((const float*)workspace, dweight, ctas, width, st);
+  });
+}

@@ -1,0 +1,369 @@
+// The delta-rule scan in float32, token by token (the contract of vesper/kernels/delta_scan.py:156-187,
+// delta_scan_fused_fp32; semantics vesper/recurrence.py:118-163).
+//
+// Per (batch, head) the state H [key i, value j] is spread over a CTA: lane l of every warp holds
+// key rows i = l, l+32, ... and warp w holds value columns j = 32*jb + 4w .. 4w+3 of the CTA's
+// column block jb. Per token the two reads of the state (H^T k before the write, H^T q after)
+// are warp reductions over i. The backward runs the gradient recurrence in reverse
+// (G = dL/dH_t: G += q do^T, dr = beta G^T k, G -= k dr^T) and then the state recurrence forward
+// again for the terms that need H (dq = H_t do, dk's H_{t-1} dr); the reductions over value columns
+// that span CTAs go through fixed-order partial sums (deterministic).
+#include "common.cuh"
+
+namespace vb {
+namespace {
+
+constexpr int NWARP = 8;          // warps per CTA
+constexpr int CPW = 4;            // value columns per warp
+constexpr int BV = NWARP * CPW;   // value columns per CTA
+
+template <int NI>
+__global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ beta, const float* __restrict__ s0, float* __restrict__ o,
+    float* __restrict__ sn, float* __restrict__ resid, int T, int H, int D) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int jb = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int j0 = jb * BV + warp * CPW;
+  float S[NI][CPW];
+  const float* s0p = s0 + (int64_t)bh * D * D;
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      S[m][c] = (i < D && j < D) ? s0p[(int64_t)i * D + j] : 0.f;
+    }
+  }
+  for (int t = 0; t < T; ++t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    const float* kp = k + row * D;
+    const float* qp = q + row * D;
+    float kk[NI], qq[NI], vv[CPW];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const int i = lane + 32 * m;
+      kk[m] = i < D ? __ldg(kp + i) : 0.f;
+      qq[m] = i < D ? __ldg(qp + i) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? __ldg(v + row * D + j0 + c) : 0.f;
+    const float bt = __ldg(beta + row);
+    float red[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      float a = 0.f;
+#pragma unroll
+      for (int m = 0; m < NI; ++m) a = fmaf(S[m][c], kk[m], a);
+      red[c] = a;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) red[c] += __shfl_xor_sync(0xffffffffu, red[c], off);
+    float r[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) r[c] = vv[c] - red[c];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const float bk = bt * kk[m];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) S[m][c] = fmaf(bk, r[c], S[m][c]);
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      float a = 0.f;
+#pragma unroll
+      for (int m = 0; m < NI; ++m) a = fmaf(S[m][c], qq[m], a);
+      red[c] = a;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) red[c] += __shfl_xor_sync(0xffffffffu, red[c], off);
+    if (lane < CPW) {
+      float ov = red[0], rv = r[0];
+#pragma unroll
+      for (int c = 1; c < CPW; ++c)
+        if (lane == c) { ov = red[c]; rv = r[c]; }
+      const int j = j0 + lane;
+      if (j < D) {
+        o[row * D + j] = ov;
+        if (resid) resid[row * D + j] = rv;
+      }
+    }
+  }
+  float* snp = sn + (int64_t)bh * D * D;
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      if (i < D && j < D) snp[(int64_t)i * D + j] = S[m][c];
+    }
+  }
+}
+
+// Sums one [D] vector over the CTA's warps (warp order) into out[D]; red: smem [NWARP][D].
+template <int NI>
+__device__ __forceinline__ void cta_sum_store(float (&part)[NI], float* red, float* out, int D) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+    if (i < D) red[warp * D + i] = part[m];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) a += red[w * D + i];
+    out[i] = a;
+  }
+  __syncthreads();
+}
+
+// Phase A (reverse): G, dv, the partial of G r over this CTA's columns, dstate0.
+// Phase B (forward): the partials of H_{t-1} dr and H_t do over this CTA's columns.
+// part: [3][NJB][B*T*H][D] = (G r, H_{t-1} dr, H_t do).
+template <int NI>
+__global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ beta,
+    const float* __restrict__ s0, const float* __restrict__ resid, const float* __restrict__ dout,
+    const float* __restrict__ dsn, float* __restrict__ dv, float* __restrict__ ds0,
+    float* __restrict__ part, int B, int T, int H, int D) {
+  extern __shared__ float red[];  // [NWARP][D]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int jb = blockIdx.x, NJB = gridDim.x, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int j0 = jb * BV + warp * CPW;
+  const int64_t rows = (int64_t)B * T * H;
+  float* part_gr = part + ((int64_t)0 * NJB + jb) * rows * D;
+  float* part_hd = part + ((int64_t)1 * NJB + jb) * rows * D;
+  float* part_dq = part + ((int64_t)2 * NJB + jb) * rows * D;
+  float G[NI][CPW];
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      G[m][c] = (dsn && i < D && j < D) ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
+    }
+  }
+  for (int t = T - 1; t >= 0; --t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    float kk[NI], qq[NI], gg[CPW], rr[CPW];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const int i = lane + 32 * m;
+      kk[m] = i < D ? __ldg(k + row * D + i) : 0.f;
+      qq[m] = i < D ? __ldg(q + row * D + i) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const bool ok = j0 + c < D;
+      gg[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
+      rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
+    }
+    const float bt = __ldg(beta + row);
+#pragma unroll
+    for (int m = 0; m < NI; ++m)
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) G[m][c] = fmaf(qq[m], gg[c], G[m][c]);
+    float red_c[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      float a = 0.f;
+#pragma unroll
+      for (int m = 0; m < NI; ++m) a = fmaf(G[m][c], kk[m], a);
+      red_c[c] = a;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) red_c[c] += __shfl_xor_sync(0xffffffffu, red_c[c], off);
+    float dr[CPW];
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) dr[c] = bt * red_c[c];
+    if (lane < CPW) {
+      float x = dr[0];
+#pragma unroll
+      for (int c = 1; c < CPW; ++c)
+        if (lane == c) x = dr[c];
+      if (j0 + lane < D) dv[row * D + j0 + lane] = x;
+    }
+    float gr[NI];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      float a = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) a = fmaf(G[m][c], rr[c], a);
+      gr[m] = a;
+    }
+    cta_sum_store<NI>(gr, red, part_gr + row * D, D);
+#pragma unroll
+    for (int m = 0; m < NI; ++m)
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) G[m][c] = fmaf(-kk[m], dr[c], G[m][c]);
+  }
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      if (i < D && j < D) ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = G[m][c];
+    }
+  }
+  __syncthreads();  // dv of this CTA's columns is complete before phase B reads it back
+  float S[NI][CPW];
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      S[m][c] = (i < D && j < D) ? s0[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
+    }
+  }
+  for (int t = 0; t < T; ++t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    float kk[NI], gg[CPW], rr[CPW], dr[CPW];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const int i = lane + 32 * m;
+      kk[m] = i < D ? __ldg(k + row * D + i) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const bool ok = j0 + c < D;
+      gg[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
+      rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
+      dr[c] = ok ? dv[row * D + j0 + c] : 0.f;
+    }
+    const float bt = __ldg(beta + row);
+    float hd[NI];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      float a = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) a = fmaf(S[m][c], dr[c], a);
+      hd[m] = a;
+    }
+    cta_sum_store<NI>(hd, red, part_hd + row * D, D);
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const float bk = bt * kk[m];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) S[m][c] = fmaf(bk, rr[c], S[m][c]);
+    }
+    float dq[NI];
+#pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      float a = 0.f;
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) a = fmaf(S[m][c], gg[c], a);
+      dq[m] = a;
+    }
+    cta_sum_store<NI>(dq, red, part_dq + row * D, D);
+  }
+}
+
+// Per (b, t, h): sums the column-block partials in order; dk = beta * Gr - H dr, dbeta = k . Gr.
+__global__ void scan_f32_finish_kernel(const float* __restrict__ k, const float* __restrict__ beta,
+                                       const float* __restrict__ part, float* __restrict__ dq,
+                                       float* __restrict__ dk, float* __restrict__ dbeta,
+                                       int64_t rows, int D, int NJB) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float bt = beta[row];
+  float dotk = 0.f;
+  for (int i = lane; i < D; i += 32) {
+    float gr = 0.f, hd = 0.f, qd = 0.f;
+    for (int jb = 0; jb < NJB; ++jb) {
+      gr += part[((int64_t)0 * NJB + jb) * rows * D + row * D + i];
+      hd += part[((int64_t)1 * NJB + jb) * rows * D + row * D + i];
+      qd += part[((int64_t)2 * NJB + jb) * rows * D + row * D + i];
+    }
+    dq[row * D + i] = qd;
+    dk[row * D + i] = bt * gr - hd;
+    dotk = fmaf(k[row * D + i], gr, dotk);
+  }
+  dotk = warp_sum(dotk);
+  if (lane == 0) dbeta[row] = dotk;
+}
+
+int njb(int D) { return (D + BV - 1) / BV; }
+
+int check(int B, int T, int H, int D) {
+  VB_REQUIRE(B >= 0 && T >= 0 && H >= 0 && D > 0, "delta_scan_f32: bad shape B=%d T=%d H=%d D=%d", B, T, H, D);
+  VB_REQUIRE(D <= 256, "delta_scan_f32: head dimension %d exceeds the kernel's 256", D);
+  VB_REQUIRE((int64_t)B * H <= 65535, "delta_scan_f32: B*H = %lld exceeds 65535", (long long)B * H);
+  return VB_OK;
+}
+
+#define VB_NI_DISPATCH(D, NI, ...)                                    \
+  [&]() -> int {                                                      \
+    if ((D) <= 32) { constexpr int NI = 1; return __VA_ARGS__(); }    \
+    if ((D) <= 64) { constexpr int NI = 2; return __VA_ARGS__(); }    \
+    if ((D) <= 128) { constexpr int NI = 4; return __VA_ARGS__(); }   \
+    { constexpr int NI = 8; return __VA_ARGS__(); }                   \
+  }()
+
+}  // namespace
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" int vb_delta_scan_f32_fwd(const float* q, const float* k, const float* v, const float* beta,
+                                     const float* state0, float* o, float* state_n, float* resid,
+                                     int B, int T, int H, int D, void* stream) {
+  int rc = check(B, T, H, D);
+  if (rc) return rc;
+  if (B == 0 || H == 0) return VB_OK;
+  VB_REQUIRE(q && k && v && beta && state0 && o && state_n, "delta_scan_f32_fwd: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid(njb(D), B * H);
+  return VB_NI_DISPATCH(D, NI, [&]() -> int {
+    scan_f32_fwd_kernel<NI><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, state0, o, state_n, resid, T, H, D);
+    VB_LAUNCH_CHECK("delta_scan_f32_fwd");
+    return VB_OK;
+  });
+}
+
+extern "C" size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D) {
+  const size_t rows = (size_t)(B > 0 ? B : 0) * (size_t)(T > 0 ? T : 0) * (size_t)(H > 0 ? H : 0);
+  return 3 * (size_t)njb(D > 0 ? D : 1) * (rows > 0 ? rows : 1) * (size_t)(D > 0 ? D : 1) * sizeof(float);
+}
+
+extern "C" int vb_delta_scan_f32_bwd(const float* q, const float* k, const float* v, const float* beta,
+                                     const float* state0, const float* resid, const float* dout,
+                                     const float* dstate_n, float* dq, float* dk, float* dv,
+                                     float* dbeta, float* dstate0, void* workspace, int B, int T,
+                                     int H, int D, void* stream) {
+  (void)v;
+  int rc = check(B, T, H, D);
+  if (rc) return rc;
+  if (B == 0 || H == 0) return VB_OK;
+  VB_REQUIRE(q && k && beta && state0 && resid && dout && dq && dk && dv && dbeta && dstate0 && workspace,
+             "delta_scan_f32_bwd: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid(njb(D), B * H);
+  const size_t smem = sizeof(float) * NWARP * D;
+  float* part = (float*)workspace;
+  return VB_NI_DISPATCH(D, NI, [&]() -> int {
+    scan_f32_bwd_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, beta, state0, resid, dout, dstate_n,
+                                                            dv, dstate0, part, B, T, H, D);
+    VB_LAUNCH_CHECK("delta_scan_f32_bwd");
+    const int64_t rows = (int64_t)B * T * H;
+    if (rows > 0) {
+      scan_f32_finish_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(k, beta, part, dq, dk, dbeta, rows,
+                                                                    D, njb(D));
+      VB_LAUNCH_CHECK("delta_scan_f32_finish");
+    }
+    return VB_OK;
+  });
+}

@@ -1,0 +1,138 @@
+"""The delta-rule scan on a B200: hand-written sm_100a kernels behind the reference's contract.
+
+PRIMITIVE fused delta scan, the drop-in for ``vesper/kernels/delta_scan.py`` of
+mstampfli/vesper-preview. ``delta_scan_fused`` and ``delta_scan_fused_fp32`` compute what
+``vesper.recurrence.delta_scan_chunked`` computes: per head the state ``H [dk, dk]`` read as
+``H^T q`` after the token's own write,
+
+    H_t = H_{t-1} + beta_t k_t (v_t - H_{t-1}^T k_t)^T        o_t = H_t^T q_t,
+
+forward and backward, the gradient reaching the initial state too (also when the state does not
+require one: no fresh-leaf workaround is needed). Interface: ``q, k, v [b, n, h, dk]``,
+``beta [b, n, h]``, ``state [b, h, dk, dk]`` float32.
+
+``delta_scan_fused``: bfloat16 inputs, float32 state; the chunked WY form (64-token chunks) with
+the intra-chunk transform and the chunk-state products on tcgen05 tensor cores, the per-chunk
+states checkpointed in the forward and reused by the backward.
+
+``delta_scan_fused_fp32``: float32 throughout, token by token (``vb_delta_scan_f32_*``).
+
+Zero tokens return ``(q, state)`` with the same state object, as the reference does.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from vesper_b200 import _lib
+from vesper_b200.contracts import ContractError, Dims, check_shape
+
+MAX_HEAD_DIM = 256
+INPUT_DTYPE = torch.bfloat16  # delta_scan_fused's q, k, v, beta
+FP32_INPUT_DTYPE = torch.float32  # delta_scan_fused_fp32's q, k, v, beta
+STATE_DTYPE = torch.float32
+
+
+def fused_scan_available() -> bool:
+    """Whether the fused scans can run here: a CUDA device and the built library."""
+    if not torch.cuda.is_available():
+        return False
+    try:
+        _lib.load()
+    except OSError:
+        return False
+    return True
+
+
+def _checked_length(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, input_dtype: torch.dtype
+) -> int:
+    """The one contract check of both scans (``vesper/kernels/delta_scan.py:93-119``)."""
+    dims: Dims = {}
+    check_shape("q", q, ("b", "n", "h", "dk"), dims, input_dtype)
+    check_shape("k", k, ("b", "n", "h", "dk"), dims, input_dtype)
+    check_shape("v", v, ("b", "n", "h", "dk"), dims, input_dtype)
+    check_shape("beta", beta, ("b", "n", "h"), dims, input_dtype)
+    check_shape("state", state, ("b", "h", "dk", "dk"), dims, STATE_DTYPE)
+    if q.device.type != "cuda":
+        msg = f"the fused scan runs on CUDA only, got q on {q.device}"
+        raise ContractError(msg)
+    for name, tensor in (("k", k), ("v", v), ("beta", beta), ("state", state)):
+        if tensor.device != q.device:
+            msg = f"{name} is on {tensor.device}, q on {q.device}"
+            raise ContractError(msg)
+    if dims["dk"] > MAX_HEAD_DIM:
+        msg = f"head dimension {dims['dk']} exceeds the kernel's {MAX_HEAD_DIM}"
+        raise ContractError(msg)
+    return dims["n"]
+
+
+# --- float32, token-serial ----------------------------------------------------------------------
+
+
+def scan_f32_forward(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, keep_resid: bool
+) -> tuple[Tensor, Tensor, Tensor | None]:
+    b, n, h, d = q.shape
+    o = torch.empty_like(q)
+    sn = torch.empty_like(state)
+    resid = torch.empty_like(v) if keep_resid else None
+    _lib.call(
+        "vb_delta_scan_f32_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+        state.data_ptr(), o.data_ptr(), sn.data_ptr(), _lib.ptr(resid), b, n, h, d,
+        _lib.stream(q.device),
+    )  # fmt: skip
+    return o, sn, resid
+
+
+def scan_f32_backward(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, resid: Tensor,
+    d_o: Tensor, d_sn: Tensor | None,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
+    b, n, h, d = q.shape
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dbeta, ds0 = torch.empty_like(beta), torch.empty_like(state)
+    ws = _lib.workspace(_lib.query("vb_delta_scan_f32_bwd_workspace", b, n, h, d), q.device)
+    _lib.call(
+        "vb_delta_scan_f32_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+        state.data_ptr(), resid.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(),
+        dk.data_ptr(), dv.data_ptr(), dbeta.data_ptr(), ds0.data_ptr(), ws.data_ptr(), b, n, h, d,
+        _lib.stream(q.device),
+    )  # fmt: skip
+    return dq, dk, dv, dbeta, ds0
+
+
+class _ScanF32(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor):  # type: ignore[override]
+        q, k, v, beta, state = (t.contiguous() for t in (q, k, v, beta, state))
+        keep = any(ctx.needs_input_grad)
+        o, sn, resid = scan_f32_forward(q, k, v, beta, state, keep)
+        if keep:
+            ctx.save_for_backward(q, k, v, beta, state, resid)
+        return o, sn
+
+    @staticmethod
+    def backward(ctx, d_o: Tensor | None, d_sn: Tensor | None):  # type: ignore[override]
+        q, k, v, beta, state, resid = ctx.saved_tensors
+        d_o = torch.zeros_like(q) if d_o is None else d_o.contiguous().to(torch.float32)
+        d_sn = None if d_sn is None else d_sn.contiguous().to(torch.float32)
+        grads = scan_f32_backward(q, k, v, beta, state, resid, d_o, d_sn)
+        return grads
+
+
+def delta_scan_fused_fp32(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
+) -> tuple[Tensor, Tensor]:
+    """Apply ``n`` tokens to the state in float32 (the reference's precision).
+
+    Returns ``(o [b, n, h, dk], state_n)`` in float32; with no tokens, ``(q, state)``.
+
+    Raises:
+        ContractError: on a shape, dtype or device mismatch, or a head dimension above 256.
+    """
+    if _checked_length(q, k, v, beta, state, FP32_INPUT_DTYPE) == 0:
+        return q, state
+    o, sn = _ScanF32.apply(q, k, v, beta, state)
+    return o, sn

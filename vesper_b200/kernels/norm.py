@@ -1,0 +1,79 @@
+"""``RMSNorm`` on a B200: one hand-written kernel per direction.
+
+PRIMITIVE ``fused_rms_norm(x, weight, floor, eps)``: the drop-in for
+``vesper/kernels/norm.py:24-52`` of mstampfli/vesper-preview (same signature, same result dtype,
+the gain's gradient in the weight's dtype). Each row is divided by its largest magnitude (floored
+at ``floor``) before squaring, the statistics and the gain are applied in float32 and the result
+returns in ``x``'s dtype (``vesper/column.py:159-188``). The forward keeps ``inv = 1/sqrt(mean(x^2)
++ eps)`` per row; the backward is the analytic gradient with the scale held constant, the gain's
+summed in a fixed order (deterministic). Kernels: ``vb_rms_norm_fwd`` / ``vb_rms_norm_bwd``.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from vesper_b200 import _lib
+from vesper_b200.contracts import ContractError
+
+SUPPORTED = (torch.float32, torch.bfloat16, torch.float16)
+
+
+def fused_rms_norm(x: Tensor, weight: Tensor, floor: float, eps: float) -> Tensor:
+    """``[..., d] -> [..., d]`` in ``x``'s dtype; ``x`` on CUDA, ``weight [d]``."""
+    if x.device.type != "cuda":
+        msg = f"the fused RMSNorm runs on CUDA only, got x on {x.device}"
+        raise ContractError(msg)
+    if x.dtype not in SUPPORTED:
+        msg = f"x: dtype must be one of {SUPPORTED}, got {x.dtype}"
+        raise ContractError(msg)
+    if weight.shape != (x.shape[-1],):
+        msg = f"weight: expected shape ({x.shape[-1]},), got {tuple(weight.shape)}"
+        raise ContractError(msg)
+    rows = x.reshape(-1, x.shape[-1])
+    out: Tensor = _FusedRMSNorm.apply(rows, weight, floor, eps)
+    return out.view(x.shape)
+
+
+def rms_forward(x: Tensor, weight: Tensor, floor: float, eps: float) -> tuple[Tensor, Tensor]:
+    """``(y, inv)`` of row-contiguous ``x [N, d]``: ``y`` in ``x``'s dtype, ``inv`` float32."""
+    n, width = x.shape
+    y = torch.empty_like(x)
+    inv = torch.empty(n, dtype=torch.float32, device=x.device)
+    w32 = weight.to(torch.float32).contiguous()
+    _lib.call(
+        "vb_rms_norm_fwd", x.data_ptr(), w32.data_ptr(), y.data_ptr(), inv.data_ptr(), n, width,
+        floor, eps, _lib.DTYPE_CODE[x.dtype], _lib.stream(x.device),
+    )  # fmt: skip
+    return y, inv
+
+
+def rms_backward(x: Tensor, weight: Tensor, dy: Tensor, inv: Tensor) -> tuple[Tensor, Tensor]:
+    """``(dx, dg)``: the input's gradient in ``x``'s dtype and the gain's in float32."""
+    n, width = x.shape
+    dx = torch.empty_like(x)
+    dg = torch.empty(width, dtype=torch.float32, device=x.device)
+    w32 = weight.to(torch.float32).contiguous()
+    ws = _lib.workspace(_lib.query("vb_rms_norm_bwd_workspace", n, width), x.device)
+    _lib.call(
+        "vb_rms_norm_bwd", x.data_ptr(), w32.data_ptr(), dy.data_ptr(), inv.data_ptr(),
+        dx.data_ptr(), dg.data_ptr(), ws.data_ptr(), n, width, _lib.DTYPE_CODE[x.dtype],
+        _lib.stream(x.device),
+    )  # fmt: skip
+    return dx, dg
+
+
+class _FusedRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, weight: Tensor, floor: float, eps: float) -> Tensor:  # type: ignore[override]
+        rows = x.contiguous()
+        y, inv = rms_forward(rows, weight, floor, eps)
+        ctx.save_for_backward(rows, weight, inv)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy: Tensor):  # type: ignore[override]
+        rows, weight, inv = ctx.saved_tensors
+        dx, dg = rms_backward(rows, weight, dy.contiguous().to(rows.dtype), inv)
+        return dx, dg.to(weight.dtype), None, None
