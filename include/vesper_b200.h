@@ -97,6 +97,31 @@ VB_API int vb_delta_scan_f32_bwd(const float *q, const float *k, const float *v,
                           float *dstate0, void *workspace, int B, int T, int H, int D,
                           void *stream);
 
+/* ---- delta-rule scan, bfloat16 (chunked WY form on tcgen05) -----------------------------------
+ * The same recurrence as above with bf16 q, k, v, beta, o [B,T,H,D] / [B,T,H] and float32
+ * state0, state_n [B,H,D,D]; 64-token chunks, D <= 128 and a multiple of 8, 16-byte aligned
+ * tensors. `saved` (vb_delta_scan_bf16_saved_bytes) receives what the backward reuses: the
+ * per-chunk (I + strictly_lower(diag(beta) K K^T))^-1 tiles and the per-chunk state checkpoints.
+ * `status` is one device int32: a kernel that gave up waiting on the tensor core ORs in a bit
+ * (the caller checks it after synchronising; it is never reset here).
+ * Replaces vesper/kernels/delta_scan.py:132-153 (delta_scan_fused, which ran fla-core's
+ * chunk_delta_rule) with the semantics of vesper/recurrence.py:166-217. */
+VB_API size_t vb_delta_scan_bf16_saved_bytes(int B, int T, int H, int D);
+
+VB_API int vb_delta_scan_bf16_fwd(const void *q, const void *k, const void *v, const void *beta,
+                                  const float *state0, void *o, float *state_n, void *saved,
+                                  int *status, int B, int T, int H, int D, void *stream);
+
+VB_API size_t vb_delta_scan_bf16_bwd_workspace(int B, int T, int H, int D);
+
+/* Gradients of sum(o*dout) + sum(state_n*dstate_n) (dstate_n may be NULL = zero): dq, dk, dv,
+ * dbeta in bf16, dstate0 in float32; `saved` from the forward on the same inputs. */
+VB_API int vb_delta_scan_bf16_bwd(const void *q, const void *k, const void *v, const void *beta,
+                                  const void *saved, const void *dout, const float *dstate_n,
+                                  void *dq, void *dk, void *dv, void *dbeta, float *dstate0,
+                                  void *workspace, int *status, int B, int T, int H, int D,
+                                  void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -38,6 +38,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_delta_scan_f32_fwd": (_I, [_P] * 8 + [_I, _I, _I, _I, _P]),
     "vb_delta_scan_f32_bwd_workspace": (_SZ, [_I, _I, _I, _I]),
     "vb_delta_scan_f32_bwd": (_I, [_P] * 14 + [_I, _I, _I, _I, _P]),
+    "vb_delta_scan_bf16_saved_bytes": (_SZ, [_I, _I, _I, _I]),
+    "vb_delta_scan_bf16_fwd": (_I, [_P] * 9 + [_I, _I, _I, _I, _P]),
+    "vb_delta_scan_bf16_bwd_workspace": (_SZ, [_I, _I, _I, _I]),
+    "vb_delta_scan_bf16_bwd": (_I, [_P] * 14 + [_I, _I, _I, _I, _P]),
 }
 
 

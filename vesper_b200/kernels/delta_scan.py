@@ -29,6 +29,7 @@ from vesper_b200 import _lib
 from vesper_b200.contracts import ContractError, Dims, check_shape
 
 MAX_HEAD_DIM = 256
+BF16_MAX_HEAD_DIM = 128  # the chunked kernel pads the head dimension to one 128-wide tile
 INPUT_DTYPE = torch.bfloat16  # delta_scan_fused's q, k, v, beta
 FP32_INPUT_DTYPE = torch.float32  # delta_scan_fused_fp32's q, k, v, beta
 STATE_DTYPE = torch.float32
@@ -66,6 +67,114 @@ def _checked_length(
         msg = f"head dimension {dims['dk']} exceeds the kernel's {MAX_HEAD_DIM}"
         raise ContractError(msg)
     return dims["n"]
+
+
+# --- device status word ----------------------------------------------------------------------------
+
+_STATUS: dict[torch.device, Tensor] = {}
+
+
+def status_word(device: torch.device) -> Tensor:
+    """The int32 the bf16 scan's kernels OR an error bit into (a bounded wait that gave up)."""
+    word = _STATUS.get(device)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[device] = word
+    return word
+
+
+def check_status(device: torch.device) -> None:
+    """Synchronise and raise if a kernel on ``device`` reported a timeout (never under capture)."""
+    word = _STATUS.get(device)
+    if word is not None and int(word.item()) != 0:
+        value = int(word.item())
+        word.zero_()
+        msg = f"a delta-scan kernel gave up waiting on the tensor core (status {value})"
+        raise _lib.KernelError(msg)
+
+
+# --- bfloat16, chunked on tcgen05 -------------------------------------------------------------------
+
+
+def scan_bf16_forward(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
+) -> tuple[Tensor, Tensor, Tensor]:
+    b, n, h, d = q.shape
+    o = torch.empty_like(q)
+    sn = torch.empty_like(state)
+    saved = _lib.workspace(_lib.query("vb_delta_scan_bf16_saved_bytes", b, n, h, d), q.device)
+    _lib.call(
+        "vb_delta_scan_bf16_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+        state.data_ptr(), o.data_ptr(), sn.data_ptr(), saved.data_ptr(),
+        status_word(q.device).data_ptr(), b, n, h, d, _lib.stream(q.device),
+    )  # fmt: skip
+    return o, sn, saved
+
+
+def scan_bf16_backward(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, saved: Tensor, d_o: Tensor, d_sn: Tensor | None
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    b, n, h, d = q.shape
+    dq, dk, dv, dbeta = (torch.empty_like(t) for t in (q, k, v, beta))
+    ds0 = torch.empty(b, h, d, d, dtype=torch.float32, device=q.device)
+    ws = _lib.workspace(_lib.query("vb_delta_scan_bf16_bwd_workspace", b, n, h, d), q.device)
+    _lib.call(
+        "vb_delta_scan_bf16_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+        saved.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(), dk.data_ptr(),
+        dv.data_ptr(), dbeta.data_ptr(), ds0.data_ptr(), ws.data_ptr(),
+        status_word(q.device).data_ptr(), b, n, h, d, _lib.stream(q.device),
+    )  # fmt: skip
+    return dq, dk, dv, dbeta, ds0
+
+
+class _ScanBF16(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor):  # type: ignore[override]
+        q, k, v, beta, state = (t.contiguous() for t in (q, k, v, beta, state))
+        o, sn, saved = scan_bf16_forward(q, k, v, beta, state)
+        if any(ctx.needs_input_grad):
+            ctx.save_for_backward(q, k, v, beta, saved)
+        return o, sn
+
+    @staticmethod
+    def backward(ctx, d_o: Tensor | None, d_sn: Tensor | None):  # type: ignore[override]
+        q, k, v, beta, saved = ctx.saved_tensors
+        d_o = torch.zeros_like(q) if d_o is None else d_o.contiguous().to(torch.bfloat16)
+        d_sn = None if d_sn is None else d_sn.contiguous().to(torch.float32)
+        return scan_bf16_backward(q, k, v, beta, saved, d_o, d_sn)
+
+
+def delta_scan_fused(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
+) -> tuple[Tensor, Tensor]:
+    """Apply ``n`` tokens to the state with the chunked bfloat16 kernels (the reference's form).
+
+    Args:
+        q: ``[b, n, h, dk]`` queries, bfloat16, on a CUDA device.
+        k: ``[b, n, h, dk]`` keys, bfloat16, L2 norm at most one.
+        v: ``[b, n, h, dk]`` values, bfloat16.
+        beta: ``[b, n, h]`` write strengths in [0, 1], bfloat16.
+        state: ``[b, h, dk, dk]`` the state before the first token, float32.
+
+    Returns:
+        ``(o, state_n)``: ``o [b, n, h, dk]`` in bfloat16 and the state after the last token in
+        float32. With no tokens, the empty query tensor and the unchanged state.
+
+    Raises:
+        ContractError: on a shape, dtype or device mismatch, or a head dimension above the
+            kernel's bound (128 for this chunked kernel; ``delta_scan_fused_fp32`` takes 256).
+    """
+    if _checked_length(q, k, v, beta, state, INPUT_DTYPE) == 0:
+        return q, state
+    if q.shape[-1] > BF16_MAX_HEAD_DIM or q.shape[-1] % 8 != 0:
+        msg = (
+            f"head dimension {q.shape[-1]} exceeds the chunked kernel's {BF16_MAX_HEAD_DIM}"
+            if q.shape[-1] > BF16_MAX_HEAD_DIM
+            else f"head dimension {q.shape[-1]} must be a multiple of 8"
+        )
+        raise ContractError(msg)
+    o, sn = _ScanBF16.apply(q, k, v, beta, state)
+    return o, sn
 
 
 # --- float32, token-serial ----------------------------------------------------------------------
