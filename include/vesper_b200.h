@@ -39,6 +39,8 @@ enum { VB_F32 = 0, VB_BF16 = 1, VB_F16 = 2 };
 VB_API const char *vb_last_error(void);
 /* ABI version of this library. */
 VB_API int vb_abi_version(void);
+/* Kernels this library has launched in this process (every entry point counts its own). */
+VB_API unsigned long long vb_launch_count(void);
 
 /* ---- RMSNorm --------------------------------------------------------------------------------
  * y = x / sqrt(mean(x^2) + eps) * weight per row, computed scale-safely (each row divided by

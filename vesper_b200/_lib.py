@@ -29,6 +29,7 @@ _SZ = ctypes.c_size_t
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_last_error": (ctypes.c_char_p, []),
     "vb_abi_version": (_I, []),
+    "vb_launch_count": (ctypes.c_ulonglong, []),
     "vb_rms_norm_fwd": (_I, [_P, _P, _P, _P, _I64, _I, _F, _F, _I, _P]),
     "vb_rms_norm_bwd_workspace": (_SZ, [_I64, _I]),
     "vb_rms_norm_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I, _I, _P]),
@@ -80,6 +81,11 @@ def call(name: str, *args: object) -> None:
 def query(name: str, *args: object) -> int:
     """Call a size query entry point."""
     return int(getattr(load(), name)(*args))
+
+
+def launch_count() -> int:
+    """Kernels the library has launched so far in this process."""
+    return int(load().vb_launch_count())
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

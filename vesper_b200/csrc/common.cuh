@@ -17,6 +17,8 @@ namespace vb {
 // Records the message returned by vb_last_error() for the calling host thread.
 void set_error(const char* fmt, ...);
 void clear_error();
+// Counts kernel launches made by this library (read with vb_launch_count()).
+void count_launch();
 
 #define VB_REQUIRE(cond, ...)                \
   do {                                       \
@@ -33,6 +35,7 @@ void clear_error();
       ::vb::set_error("%s: launch failed: %s", what, cudaGetErrorString(e_));        \
       return VB_ERR_CUDA;                                                            \
     }                                                                                \
+    ::vb::count_launch();                                                            \
   } while (0)
 
 #define VB_CUDA_CHECK(call, what)                                                    \
