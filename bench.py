@@ -411,8 +411,7 @@ def main() -> None:
     p.add_argument("--steps-ref", type=int, default=0, help="reference samples (default: min(steps, 10))")
     p.add_argument("--warmup-ref", type=int, default=0)
     args = p.parse_args()
-    global B
-    B = args.batch
+    globals()["B"] = args.batch
     if args.impl == "reference":
         if not args.steps_ref:
             args.steps_ref = min(args.steps, 10)
