@@ -60,6 +60,21 @@ VB_API int vb_rms_norm_bwd(const void *x, const float *weight, const void *dy, c
                     void *dx, float *dweight, void *workspace, int64_t rows, int width,
                     int dtype, void *stream);
 
+/* The same backward as vb_rms_norm_bwd for callers that cannot allocate device memory (a plugin
+ * host with a pre-planned memory budget, a loop that must not allocate, a capture or memory plan
+ * an allocation would break): no workspace argument, and no cudaMalloc, cudaFree or allocating
+ * library call inside. The gain gradient's partial sums live in a file-scope device array of
+ * 2^20 floats (4 MiB, held by every GPU that loads the library until exit), which bounds
+ * ceil(rows / 64) * width <= 2^20 (e.g. 65536 rows at width 1024); larger calls return
+ * VB_ERR_INVALID with the limit in vb_last_error(). The array's address is looked up once per
+ * device by the first call made with that device current, so make that first call before any
+ * stream capture. All calls share the array: calls that overlap on the GPU (other streams, other
+ * host threads) race and must be serialised by the caller. Nothing needs clearing between calls:
+ * each call writes every partial sum it reads. Has no counterpart in the reference. */
+VB_API int vb_rms_norm_bwd_noalloc(const void *x, const float *weight, const void *dy,
+                                   const float *inv, void *dx, float *dweight, int64_t rows,
+                                   int width, int dtype, void *stream);
+
 /* ---- causal key filter + key normalisation ---------------------------------------------------
  * u[b,t,j] = sum_r taps[r,j] * full[b, t+K-1-r, j] with full = cat(hist, z) along t, then
  * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's

@@ -5,6 +5,8 @@
 // allows), one read and one write of the row. Backward: one warp per row for dx; the gain
 // gradient is summed per warp in shared memory, per CTA in warp order, then across CTAs in CTA
 // order by a second kernel: no atomics, the same bits on every run.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace vb {
@@ -201,5 +203,70 @@ extern "C" int vb_rms_norm_bwd(const void* x, const float* weight, const void* d
                                                       (T*)dx, (float*)workspace, rows, width);
     VB_LAUNCH_CHECK("rms_norm_bwd");
     return column_sum((const float*)workspace, dweight, ctas, width, st);
+  });
+}
+
+// ---- RMSNorm backward without allocation ------------------------------------------------------
+// For callers that cannot call cudaMalloc or take memory from an allocator (a plugin host whose
+// device memory is planned up front, a real-time loop that must not allocate, code that runs
+// where an allocation would break a graph capture or a fixed memory plan): the gain gradient's
+// per-CTA partial sums live in this file-scope array instead of a caller-provided workspace.
+// Every GPU that loads the library holds the 4 MiB until the process exits.
+namespace vb {
+namespace {
+constexpr size_t NOALLOC_PARTIAL_FLOATS = size_t(1) << 20;  // 4 MiB of float partial sums
+static __device__ __align__(256) float g_rms_bwd_scratch[NOALLOC_PARTIAL_FLOATS];
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_scratch_mutex;
+float* g_scratch_device[NOALLOC_MAX_DEVICES] = {};
+
+// The array's device address on the current device, looked up once per device: in host code
+// the array's name is only a stand-in, not a device address.
+int scratch_on_current_device(float** out) {
+  int dev = -1;
+  VB_CUDA_CHECK(cudaGetDevice(&dev), "rms_norm_bwd_noalloc: cudaGetDevice");
+  VB_REQUIRE(dev >= 0 && dev < NOALLOC_MAX_DEVICES, "rms_norm_bwd_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_device[dev] == nullptr) {
+    void* p = nullptr;
+    VB_CUDA_CHECK(cudaGetSymbolAddress(&p, g_rms_bwd_scratch), "rms_norm_bwd_noalloc: cudaGetSymbolAddress");
+    g_scratch_device[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_device[dev];
+  return VB_OK;
+}
+}  // namespace
+}  // namespace vb
+
+extern "C" int vb_rms_norm_bwd_noalloc(const void* x, const float* weight, const void* dy,
+                                       const float* inv, void* dx, float* dweight, int64_t rows,
+                                       int width, int dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_bwd_noalloc: bad shape rows=%lld width=%d", (long long)rows, width);
+  VB_REQUIRE(width <= 4096, "rms_norm_bwd_noalloc: width %d exceeds the kernel's 4096", width);
+  const int ctas = rows > 0 ? bwd_ctas(rows) : 0;
+  VB_REQUIRE((size_t)ctas * (size_t)width <= NOALLOC_PARTIAL_FLOATS,
+             "rms_norm_bwd_noalloc: %lld rows of width %d need %zu partial sums, above the fixed "
+             "scratch of %zu floats (at this width at most %lld rows); use vb_rms_norm_bwd with a "
+             "workspace",
+             (long long)rows, width, (size_t)ctas * (size_t)width, NOALLOC_PARTIAL_FLOATS,
+             (long long)(NOALLOC_PARTIAL_FLOATS / (size_t)width) * WARPS * BWD_ROWS_PER_WARP);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows == 0) {
+    VB_CUDA_CHECK(cudaMemsetAsync(dweight, 0, sizeof(float) * width, st), "rms_norm_bwd_noalloc");
+    return VB_OK;
+  }
+  VB_REQUIRE(x && weight && dy && inv && dx && dweight, "rms_norm_bwd_noalloc: null pointer");
+  float* partial = nullptr;
+  int rc = scratch_on_current_device(&partial);
+  if (rc) return rc;
+  // every partial row this call reads is written by this call first: nothing needs clearing
+  const size_t smem = sizeof(float) * WARPS * width;
+  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    rms_bwd_kernel<T><<<ctas, WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
+                                                      (T*)dx, partial, rows, width);
+    VB_LAUNCH_CHECK("rms_norm_bwd_noalloc");
+    return column_sum(partial, dweight, ctas, width, st);
   });
 }
