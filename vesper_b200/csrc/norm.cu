@@ -130,13 +130,24 @@ __global__ void __launch_bounds__(WARPS * 32) rms_bwd_kernel(const T* __restrict
   }
 }
 
-__global__ void column_sum_kernel(const float* __restrict__ partial, float* __restrict__ out,
-                                  int parts, int width) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= width) return;
+// out[j] = sum over p of partial[p][j]: lane <-> column, warp w sums parts w, w+8, ... in order,
+// then the 8 warp sums are added in warp order (a fixed tree: the same bits on every run)
+__global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict__ partial,
+                                                         float* __restrict__ out, int parts, int width) {
+  __shared__ float acc[8][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
   float t = 0.f;
-  for (int p = 0; p < parts; ++p) t += partial[(size_t)p * width + j];
-  out[j] = t;
+  if (j < width)
+    for (int p = warp; p < parts; p += 8) t += __ldg(partial + (size_t)p * width + j);
+  acc[warp][lane] = t;
+  __syncthreads();
+  if (warp == 0 && j < width) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += acc[w][lane];
+    out[j] = s;
+  }
 }
 
 int bwd_ctas(int64_t rows) {
@@ -148,7 +159,7 @@ int bwd_ctas(int64_t rows) {
 
 // Sums `parts` rows of `partial [parts, width]` in row order into out[width].
 int column_sum(const float* partial, float* out, int parts, int width, cudaStream_t st) {
-  column_sum_kernel<<<(width + 255) / 256, 256, 0, st>>>(partial, out, parts, width);
+  column_sum_kernel<<<(width + 31) / 32, 256, 0, st>>>(partial, out, parts, width);
   VB_LAUNCH_CHECK("column_sum");
   return VB_OK;
 }

@@ -22,7 +22,10 @@
 //            (H_c, dH_{c+1}) in one pass: dq, dk, dv, dbeta.
 // Waits on the tensor core are bounded (2 s): a timeout sets bit 1 of *status and the kernel
 // leaves after releasing its tensor memory.
+#include <cstring>
+
 #include "common.cuh"
+#include "tmap.cuh"
 #include "umma.cuh"
 
 namespace vb {
@@ -42,34 +45,17 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return (uint8_t*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
 }
 
-// cp.async of a [64 token][d] slice (rows t < valid, channels < D, zero elsewhere) into a tile
-__device__ __forceinline__ void load_tokens(uint8_t* tile, const bf16* __restrict__ src,
-                                            int64_t row0, int64_t row_stride, int valid, int D) {
-  const uint32_t base = smem_u32(tile);
-  for (int q = threadIdx.x; q < C * (DP / 8); q += NT) {
-    const int r = q >> 4, j = q & 15;
-    const bool ok = r < valid && 8 * j < D;
-    const bf16* p = ok ? src + (row0 + r) * row_stride + 8 * j : src;
-    cp_async16(base + sw_chunk(64, r, j), p, ok ? 16u : 0u);
-  }
+// beta of this thread's token (threads < 64) as a raw load whose latency overlaps later work;
+// the value is stored to shared memory only where it is first needed
+__device__ __forceinline__ bf16 fetch_beta(const bf16* __restrict__ beta, int64_t row0, int H, int valid) {
+  const int t = threadIdx.x;
+  return (t < C && t < valid) ? beta[(row0 + t) * H] : __float2bfloat16_rn(0.f);
 }
 
-__device__ __forceinline__ void load_linear(uint8_t* dst, const uint8_t* __restrict__ src, uint32_t bytes) {
-  const uint32_t base = smem_u32(dst);
-  for (uint32_t q = threadIdx.x; q < bytes / 16; q += NT) cp_async16(base + 16 * q, src + 16 * q, 16u);
-}
-
-__device__ __forceinline__ void store_linear(uint8_t* __restrict__ dst, const uint8_t* src, uint32_t bytes) {
-  for (uint32_t q = threadIdx.x; q < bytes / 16; q += NT)
-    reinterpret_cast<uint4*>(dst)[q] = reinterpret_cast<const uint4*>(src)[q];
-}
-
-__device__ __forceinline__ void load_beta(float* bsm, const bf16* __restrict__ beta, int64_t row0,
-                                          int H, int valid) {
-  if (threadIdx.x < C) {
-    const int t = threadIdx.x;
-    bsm[t] = t < valid ? __bfloat162float(beta[(row0 + t) * H]) : 0.f;
-  }
+// TMA loads of one [64 token][128 d] tile (two 64-channel boxes) of chunk t0 of (b, h)
+__device__ __forceinline__ void tma_tile(uint8_t* tile, const CUtensorMap* map, uint64_t* bar, int h, int t0, int b) {
+  tma_load_4d(tile, map, bar, 0, h, t0, b);
+  tma_load_4d(tile + TILE_TD / 2, map, bar, 64, h, t0, b);
 }
 
 // T'[t][s] = X[t][s] * beta_s (bf16 tile images, one 8-element chunk per step)
@@ -92,6 +78,114 @@ __device__ __forceinline__ void ld64(uint32_t tm, int col, float (&v)[64]) {
   tmem_wait_ld();
 }
 
+// A 128-column fp32 tensor-memory row (this thread's lane) -> bf16 row r of a [rows][128] tile.
+__device__ __forceinline__ void tmem_row_to_tile(uint32_t lane_tm, int col, uint8_t* tile, int rows, int r) {
+#pragma unroll
+  for (int c0 = 0; c0 < DP; c0 += 32) {
+    float v[32];
+    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
+    tmem_wait_ld();
+    st_row32_bf16(tile, rows, r, c0, v);
+  }
+}
+
+// A 64-column fp32 tensor-memory row -> bf16 row r of a [rows][64] tile; with `mask_after` >= 0
+// the columns above it are zeroed (the causal mask of P)
+__device__ __forceinline__ void tmem_row64_to_tile(uint32_t lane_tm, int col, uint8_t* tile, int rows,
+                                                   int r, bool write, int mask_after = -1) {
+#pragma unroll
+  for (int c0 = 0; c0 < 64; c0 += 32) {
+    float v[32];
+    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
+    tmem_wait_ld();
+    if (mask_after >= 0) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = c0 + e <= mask_after ? v[e] : 0.f;
+    }
+    if (write) st_row32_bf16(tile, rows, r, c0, v);
+  }
+}
+
+// (a - b) of two 64-column tensor-memory rows -> bf16 row r of a [rows][64] tile
+__device__ __forceinline__ void tmem_diff64_to_tile(uint32_t lane_tm, int col_a, int col_b, uint8_t* tile,
+                                                    int rows, int r) {
+#pragma unroll
+  for (int c0 = 0; c0 < 64; c0 += 32) {
+    float x[32], y[32];
+    tmem_ld32(lane_tm + (uint32_t)(col_a + c0), x);
+    tmem_ld32(lane_tm + (uint32_t)(col_b + c0), y);
+    tmem_wait_ld();
+#pragma unroll
+    for (int e = 0; e < 32; ++e) x[e] -= y[e];
+    st_row32_bf16(tile, rows, r, c0, x);
+  }
+}
+
+// A 128-column fp32 tensor-memory row -> bf16 global row dst[0, D) (when `store` holds)
+__device__ __forceinline__ void tmem_row_to_global(uint32_t lane_tm, int col, bf16* dst, int D, bool store) {
+#pragma unroll
+  for (int c0 = 0; c0 < DP; c0 += 32) {
+    float v[32];
+    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
+    tmem_wait_ld();
+    if (store) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = c0 + 8 * j;
+        if (i < D) {
+          uint4 w;
+          w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+          w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+          w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+          w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+          *reinterpret_cast<uint4*>(dst + i) = w;
+        }
+      }
+    }
+  }
+}
+
+// A 128-column fp32 tensor-memory row j -> column j of a float32 [D][D] matrix (rows i < D)
+__device__ __forceinline__ void tmem_row_to_column(uint32_t lane_tm, int col, float* mat, int D, int j) {
+#pragma unroll
+  for (int c0 = 0; c0 < DP; c0 += 32) {
+    float v[32];
+    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
+    tmem_wait_ld();
+    if (j < D) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (c0 + e < D) mat[(int64_t)(c0 + e) * D + j] = v[e];
+    }
+  }
+}
+
+// Column j of a float32 [D][D] matrix (zero-padded to 128) -> tensor-memory row and bf16 tile row
+__device__ __forceinline__ void column_to_tmem_and_tile(const float* mat, int D, int j, uint32_t lane_tm,
+                                                        int col, uint8_t* tile) {
+#pragma unroll
+  for (int c0 = 0; c0 < DP; c0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = (mat != nullptr && c0 + e < D && j < D) ? mat[(int64_t)(c0 + e) * D + j] : 0.f;
+    tmem_st32(lane_tm + (uint32_t)(col + c0), v);
+    st_row32_bf16(tile, 128, j, c0, v);
+  }
+  tmem_wait_st();
+}
+
+// One MMA of K = 16 * steps: D (+)= A x B over k-steps; `a_mn` / `b_mn` select the MN-major
+// descriptor form (tile rows = K index) over the K-major one (tile rows = M or N index).
+// Not inlined: its descriptor arithmetic must not be hoisted into the calling kernel's loop.
+__device__ __noinline__ void mma_seq(uint32_t d, uint32_t a, int a_rows, int a_mn, uint32_t b, int b_rows,
+                                     int b_mn, uint32_t idesc, int steps, uint32_t accumulate_first) {
+  for (int s = 0; s < steps; ++s) {
+    const uint64_t ad = a_mn ? desc_mn(a, a_rows, s) : desc_k(a, a_rows, s);
+    const uint64_t bd = b_mn ? desc_mn(b, b_rows, s) : desc_k(b, b_rows, s);
+    umma_bf16(d, ad, bd, idesc, (s > 0 || accumulate_first) ? 1u : 0u);
+  }
+}
+
 // all threads: bounded wait on the MMA barrier; flips the phase
 __device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t& phase, int* status) {
   const bool ok = mbar_wait(bar, phase);
@@ -112,7 +206,7 @@ __device__ __forceinline__ void publish() {
 // ------------------------------------------------------------------------------------------
 // prep: X = (I + strictly_lower(diag(beta) K K^T))^-1 per chunk, bf16 tile image [64 t][64 s]
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT) scan_prep_kernel(const bf16* __restrict__ k,
+__global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ CUtensorMap kmap,
                                                        const bf16* __restrict__ beta,
                                                        uint8_t* __restrict__ xt, int T, int H,
                                                        int D, int NC, int* status) {
@@ -122,18 +216,22 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const bf16* __restrict__ 
   uint8_t* Xs = sm + TILE_TD;                         // 8 KB
   float* A = reinterpret_cast<float*>(sm + TILE_TD + TILE_TT);  // [64][65]
   __shared__ float bsm[C];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
   const int t0 = c * C, valid = min(C, T - t0);
   const int64_t row0 = (int64_t)b * T + t0;
-  load_tokens(Kt, k + (int64_t)h * D, row0, (int64_t)H * D, valid, D);
-  cp_async_commit();
-  load_beta(bsm, beta + h, row0, H, valid);
-  if (tid == 0) { mbar_init(&bar, 1); mbar_fence_init(); }
+  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&lbar, TILE_TD);
+    tma_tile(Kt, &kmap, &lbar, h, t0, b);
+  }
+  const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 64); tmem_relinquish(); }
-  cp_async_wait_all();
+  if (tid < C) bsm[tid] = __bfloat162float(bv);
+  if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
   publish();
   const uint32_t tm = tbase;
   if (tid == 0) {
@@ -168,154 +266,168 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const bf16* __restrict__ 
 #pragma unroll
     for (int t = 0; t < 64; ++t) *reinterpret_cast<bf16*>(Xs + sw_offset(64, t, j)) = __float2bfloat16_rn(x[t]);
   }
+  fence_async_smem();
   __syncthreads();
-  store_linear(xt + (size_t)blockIdx.x * TILE_TT, Xs, TILE_TT);
+  if (tid == 0) {
+    bulk_store(xt + (size_t)blockIdx.x * TILE_TT, Xs, TILE_TT);
+    bulk_commit();
+    bulk_wait_all();
+  }
 }
 
 // ------------------------------------------------------------------------------------------
-// forward: one CTA per (b, h); thread j <-> tensor-memory lane j <-> value index j
+// forward: one CTA per (b, h); thread j <-> tensor-memory lane j <-> value index j.
+// Software pipeline over chunks: the next chunk's tiles are prefetched into the other buffer
+// set, and its state-independent products (U^T, W^T, Q K^T) are issued with this chunk's state
+// update, so each chunk costs two tensor-core round trips:
+//   B_c: X = H^T W_c^T, O = Q_c H              -> delta_c = U_c - X
+//   C_c: H^T += delta_c^T K_c, O += P_c delta_c, and U, W, Q K^T of chunk c+1
 // ------------------------------------------------------------------------------------------
 struct FwdSmem {
-  static constexpr uint32_t Kt = 0, Qt = Kt + TILE_TD, Vt = Qt + TILE_TD, Xt = Vt + TILE_TD,
-                            Tt = Xt + TILE_TT, Pt = Tt + TILE_TT, Wr = Pt + TILE_TT,
+  // two buffer sets of the per-chunk input tiles
+  static constexpr uint32_t SET = 3 * TILE_TD + TILE_TT;  // K, Q, V, X
+  static constexpr uint32_t Kt = 0, Qt = TILE_TD, Vt = 2 * TILE_TD, Xt = 3 * TILE_TD;
+  static constexpr uint32_t Tt = 2 * SET, Pt = Tt + TILE_TT, Wr = Pt + TILE_TT,
                             Ha = Wr + TILE_JT, Da = Ha + TILE_JI, END = Da + TILE_JT;
 };
 // tensor-memory columns
 constexpr int F_H = 0, F_U = 128, F_W = 192, F_X = 256, F_QK = 320, F_O = 384;
 
+struct ChunkAt {
+  int t0, valid;
+  int64_t row0;
+};
+__device__ __forceinline__ ChunkAt chunk_at(int b, int c, int T) {
+  ChunkAt a;
+  a.t0 = c * C;
+  a.valid = min(C, T - a.t0);
+  a.row0 = (int64_t)b * T + a.t0;
+  return a;
+}
+
 __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+    const __grid_constant__ CUtensorMap vmap,
     const bf16* __restrict__ beta, const float* __restrict__ s0, const uint8_t* __restrict__ xt,
     bf16* __restrict__ o, float* __restrict__ sn, uint8_t* __restrict__ hck, int T, int H, int D,
     int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Kt = sm + FwdSmem::Kt, *Qt = sm + FwdSmem::Qt, *Vt = sm + FwdSmem::Vt;
-  uint8_t *Xt = sm + FwdSmem::Xt, *Tt = sm + FwdSmem::Tt, *Pt = sm + FwdSmem::Pt;
-  uint8_t *Wr = sm + FwdSmem::Wr, *Ha = sm + FwdSmem::Ha, *Da = sm + FwdSmem::Da;
-  __shared__ float bsm[C];
-  __shared__ uint64_t bar;
+  uint8_t *Tt = sm + FwdSmem::Tt, *Pt = sm + FwdSmem::Pt, *Wr = sm + FwdSmem::Wr;
+  uint8_t *Ha = sm + FwdSmem::Ha, *Da = sm + FwdSmem::Da;
+  __shared__ float bsm[2][C];
+  __shared__ uint64_t bar, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int64_t ld = (int64_t)H * D;  // elements between consecutive tokens of one head
-  if (tid == 0) { mbar_init(&bar, 1); mbar_fence_init(); }
+  bf16 bpre = __float2bfloat16_rn(0.f);  // the prefetched beta of the chunk being loaded
+  uint32_t lphase[2] = {0u, 0u};
+  auto set = [&](int c) { return sm + (uint32_t)(c & 1) * FwdSmem::SET; };
+  auto load_chunk = [&](int c) {  // one thread issues TMA for the chunk's tiles
+    const ChunkAt a = chunk_at(b, c, T);
+    uint8_t* s = set(c);
+    if (tid == 0) {
+      uint64_t* lb = &lbar[c & 1];
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + TILE_TT);
+      tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
+      tma_tile(s + FwdSmem::Qt, &qmap, lb, h, a.t0, b);
+      tma_tile(s + FwdSmem::Vt, &vmap, lb, h, a.t0, b);
+      bulk_load(s + FwdSmem::Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT, lb);
+    }
+    bpre = fetch_beta(beta + h, a.row0, H, a.valid);
+  };
+  auto wait_chunk = [&](int c) -> bool {
+    const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
+    lphase[c & 1] ^= 1u;
+    if (!r && tid == 0) atomicOr(status, 4);
+    return r;
+  };
+  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_fence_init(); }
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
+  __syncthreads();
+  if (NC > 0) load_chunk(0);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
   const uint32_t lane_tm = taddr(tm, warp * 32, 0);  // this warp's lane quarter
-  // H^T row j = column j of the initial state
-  {
-    const int j = tid;
-    float row[DP];
-#pragma unroll
-    for (int i = 0; i < DP; ++i) row[i] = (i < D && j < D) ? s0[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) tmem_st32(lane_tm + F_H + 32 * q4, *reinterpret_cast<float(*)[32]>(row + 32 * q4));
-    tmem_wait_st();
-    st_row64_bf16(Ha, 128, j, 0, row);
-    st_row64_bf16(Ha, 128, j, 1, row + 64);
-  }
-  publish();
+  column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, tid, lane_tm, F_H, Ha);
+  const uint32_t sT = smem_u32(Tt), sP = smem_u32(Pt), sW = smem_u32(Wr), sH = smem_u32(Ha), sD = smem_u32(Da);
+  const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);   // U^T, W^T: A MN-major, B K-major
+  const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);    // Q K^T
+  auto issue_state_free = [&](int c) {                // U^T, W^T, Q K^T of chunk c (thread 0)
+    const uint32_t sK = smem_u32(set(c) + FwdSmem::Kt), sQ = smem_u32(set(c) + FwdSmem::Qt);
+    const uint32_t sV = smem_u32(set(c) + FwdSmem::Vt);
+    mma_seq(tm + F_U, sV, 64, 1, sT, 64, 0, id_tn, 4, 0u);
+    mma_seq(tm + F_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
+    mma_seq(tm + F_QK, sQ, 64, 0, sK, 64, 0, id_qk, 8, 0u);
+  };
+  auto readout_state_free = [&]() {  // W^T rows -> Wr, P rows -> Pt (all threads)
+    tmem_row64_to_tile(lane_tm, F_W, Wr, 128, tid, true);
+    const int t = warp * 16 + (lane & 15);
+    tmem_row64_to_tile(lane_tm, F_QK, Pt, 64, t, lane < 16, t);
+  };
   uint32_t phase = 0;
   bool ok = true;
-  const uint32_t sK = smem_u32(Kt), sQ = smem_u32(Qt), sV = smem_u32(Vt), sT = smem_u32(Tt);
-  const uint32_t sP = smem_u32(Pt), sW = smem_u32(Wr), sH = smem_u32(Ha), sD = smem_u32(Da);
-  for (int c = 0; c < NC && ok; ++c) {
-    const int t0 = c * C, valid = min(C, T - t0);
-    const int64_t row0 = (int64_t)b * T + t0;
-    load_tokens(Kt, k + (int64_t)h * D, row0, ld, valid, D);
-    load_tokens(Qt, q + (int64_t)h * D, row0, ld, valid, D);
-    load_tokens(Vt, v + (int64_t)h * D, row0, ld, valid, D);
-    load_linear(Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT);
-    cp_async_commit();
-    load_beta(bsm, beta + h, row0, H, valid);
-    // checkpoint H_c (the bf16 copy the chunk's products read) while the loads land
-    store_linear(hck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
-    cp_async_wait_all();
+  if (NC > 0) {
+    if (tid < C) bsm[0][tid] = __bfloat162float(bpre);
+    ok = wait_chunk(0);
     __syncthreads();
-    scale_columns(Tt, Xt, bsm);
+    scale_columns(Tt, set(0) + FwdSmem::Xt, bsm[0]);
     publish();
     if (tid == 0) {
-      const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);  // A MN-major, B K-major
-      for (int s = 0; s < 4; ++s) {
-        umma_bf16(tm + F_U, desc_mn(sV, 64, s), desc_k(sT, 64, s), id_tn, s > 0);
-        umma_bf16(tm + F_W, desc_mn(sK, 64, s), desc_k(sT, 64, s), id_tn, s > 0);
-      }
-      const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);
-      for (int s = 0; s < 8; ++s) umma_bf16(tm + F_QK, desc_k(sQ, 64, s), desc_k(sK, 64, s), id_qk, s > 0);
+      issue_state_free(0);
       umma_commit(&bar);
     }
     ok = mma_wait(&bar, phase, status);
-    {
-      float w[64];
-      ld64(lane_tm, F_W, w);
-      st_row64_bf16(Wr, 128, tid, 0, w);  // W^T row i: MN-major B operand [i][t]
-      float p[64];
-      ld64(lane_tm, F_QK, p);
-      const int t = warp * 16 + (lane & 15);
-      if (lane < 16) {
-#pragma unroll
-        for (int s = 0; s < 64; ++s) p[s] = s <= t ? p[s] : 0.f;
-        st_row64_bf16(Pt, 64, t, 0, p);
-      }
-    }
+    readout_state_free();
     publish();
+  }
+  for (int c = 0; c < NC && ok; ++c) {
+    const ChunkAt a = chunk_at(b, c, T);
+    const bool more = c + 1 < NC;
+    if (more) load_chunk(c + 1);
+    // checkpoint H_c (the bf16 copy the chunk's products read) while the loads land
+    if (tid == 0) {
+      bulk_store(hck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
+      bulk_commit();
+    }
+    const uint32_t sQ = smem_u32(set(c) + FwdSmem::Qt), sK = smem_u32(set(c) + FwdSmem::Kt);
     if (tid == 0) {
       const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);  // A K-major (H^T), B MN-major (W^T rows)
-      for (int s = 0; s < 8; ++s) umma_bf16(tm + F_X, desc_k(sH, 128, s), desc_mn(sW, 128, s), id_hw, s > 0);
+      mma_seq(tm + F_X, sH, 128, 0, sW, 128, 1, id_hw, 8, 0u);
       const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);  // O = Q H: both K-major
-      for (int s = 0; s < 8; ++s) umma_bf16(tm + F_O, desc_k(sQ, 64, s), desc_k(sH, 128, s), id_qh, s > 0);
+      mma_seq(tm + F_O, sQ, 64, 0, sH, 128, 0, id_qh, 8, 0u);
       umma_commit(&bar);
     }
-    ok = ok && mma_wait(&bar, phase, status);
-    {
-      float u[64], x[64];
-      ld64(lane_tm, F_U, u);
-      ld64(lane_tm, F_X, x);
-#pragma unroll
-      for (int s = 0; s < 64; ++s) u[s] -= x[s];
-      st_row64_bf16(Da, 128, tid, 0, u);  // delta^T row j: [j][t]
+    ok = mma_wait(&bar, phase, status);
+    tmem_diff64_to_tile(lane_tm, F_U, F_X, Da, 128, tid);  // delta^T row j: [j][t]
+    if (more) {
+      if (tid < C) bsm[(c + 1) & 1][tid] = __bfloat162float(bpre);
+      ok = wait_chunk(c + 1) && ok;
+      __syncthreads();
+      scale_columns(Tt, set(c + 1) + FwdSmem::Xt, bsm[(c + 1) & 1]);
     }
+    if (tid == 0) bulk_wait_read();  // the checkpoint has left Ha before the readout rewrites it
     publish();
-    if (tid == 0) {
+    if (tid == 0 && ok) {
       const uint32_t id_dk = idesc_bf16(128, 128, 0, 1);  // H^T += delta^T K (B MN-major)
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + F_H, desc_k(sD, 128, s), desc_mn(sK, 64, s), id_dk, 1u);
+      mma_seq(tm + F_H, sD, 128, 0, sK, 64, 1, id_dk, 4, 1u);
       const uint32_t id_pd = idesc_bf16(64, 128, 0, 0);  // O += P delta
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + F_O, desc_k(sP, 64, s), desc_k(sD, 128, s), id_pd, 1u);
+      mma_seq(tm + F_O, sP, 64, 0, sD, 128, 0, id_pd, 4, 1u);
+      if (more) issue_state_free(c + 1);
       umma_commit(&bar);
     }
     ok = ok && mma_wait(&bar, phase, status);
     {
       // O rows: lanes 0-15 of each warp hold tokens t = 16 w + l
       const int t = warp * 16 + (lane & 15);
-      float orow[DP];
-      ld64(lane_tm, F_O, *reinterpret_cast<float(*)[64]>(orow));
-      ld64(lane_tm, F_O + 64, *reinterpret_cast<float(*)[64]>(orow + 64));
-      if (lane < 16 && t < valid) {
-        bf16* dst = o + (row0 + t) * ld + (int64_t)h * D;
-        for (int i = 0; i < D; i += 8) {
-          uint4 w;
-          w.x = pack_bf16(orow[i], orow[i + 1]);
-          w.y = pack_bf16(orow[i + 2], orow[i + 3]);
-          w.z = pack_bf16(orow[i + 4], orow[i + 5]);
-          w.w = pack_bf16(orow[i + 6], orow[i + 7]);
-          *reinterpret_cast<uint4*>(dst + i) = w;
-        }
-      }
-      float hrow[DP];
-      ld64(lane_tm, F_H, *reinterpret_cast<float(*)[64]>(hrow));
-      ld64(lane_tm, F_H + 64, *reinterpret_cast<float(*)[64]>(hrow + 64));
-      st_row64_bf16(Ha, 128, tid, 0, hrow);
-      st_row64_bf16(Ha, 128, tid, 1, hrow + 64);
-      if (c == NC - 1) {
-        const int j = tid;
-        if (j < D)
-          for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = hrow[i];
-      }
+      tmem_row_to_global(lane_tm, F_O, o + (a.row0 + t) * ld + (int64_t)h * D, D, lane < 16 && t < a.valid);
+      tmem_row_to_tile(lane_tm, F_H, Ha, 128, tid);
+      if (!more) tmem_row_to_column(lane_tm, F_H, sn + (int64_t)bh * D * D, D, tid);
     }
+    if (more) readout_state_free();
     publish();
   }
   if (NC == 0) {
@@ -323,132 +435,139 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
     if (j < D)
       for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = s0[(int64_t)bh * D * D + (int64_t)i * D + j];
   }
+  if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tm, 512);
 }
 
 // ------------------------------------------------------------------------------------------
-// backward, sequential: dH^T chain in tensor memory; checkpoints dH_{c+1} per chunk
+// backward, sequential: dH^T chain in tensor memory; checkpoints dH_{c+1} per chunk. Pipelined
+// like the forward, in reverse chunk order:
+//   B_c: ddelta_c^T = dH^T K_c^T + dO_c^T P_c, dH^T += dO_c^T Q_c      -> ddelta_c
+//   C_c: dH^T -= ddelta_c^T W_c, and W^T, Q K^T of chunk c-1
 // ------------------------------------------------------------------------------------------
 struct DhSmem {
-  static constexpr uint32_t Kt = 0, Qt = Kt + TILE_TD, Gt = Qt + TILE_TD, Xt = Gt + TILE_TD,
-                            Tt = Xt + TILE_TT, Pt = Tt + TILE_TT, Wk = Pt + TILE_TT,
+  static constexpr uint32_t SET = 3 * TILE_TD + TILE_TT;  // K, Q, dO, X
+  static constexpr uint32_t Kt = 0, Qt = TILE_TD, Gt = 2 * TILE_TD, Xt = 3 * TILE_TD;
+  static constexpr uint32_t Tt = 2 * SET, Pt = Tt + TILE_TT, Wk = Pt + TILE_TT,
                             Ha = Wk + TILE_JT, Da = Ha + TILE_JI, END = Da + TILE_JT;
 };
 constexpr int G_H = 0, G_W = 128, G_D = 192, G_QK = 256;
 
 __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ beta,
-    const uint8_t* __restrict__ xt, const bf16* __restrict__ dout, const float* __restrict__ dsn,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+    const __grid_constant__ CUtensorMap gmap, const bf16* __restrict__ beta,
+    const uint8_t* __restrict__ xt, const float* __restrict__ dsn,
     float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Kt = sm + DhSmem::Kt, *Qt = sm + DhSmem::Qt, *Gt = sm + DhSmem::Gt;
-  uint8_t *Xt = sm + DhSmem::Xt, *Tt = sm + DhSmem::Tt, *Pt = sm + DhSmem::Pt;
-  uint8_t *Wk = sm + DhSmem::Wk, *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
-  __shared__ float bsm[C];
-  __shared__ uint64_t bar;
+  uint8_t *Tt = sm + DhSmem::Tt, *Pt = sm + DhSmem::Pt, *Wk = sm + DhSmem::Wk;
+  uint8_t *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
+  __shared__ float bsm[2][C];
+  __shared__ uint64_t bar, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int64_t ld = (int64_t)H * D;
-  if (tid == 0) { mbar_init(&bar, 1); mbar_fence_init(); }
+  bf16 bpre = __float2bfloat16_rn(0.f);
+  uint32_t lphase[2] = {0u, 0u};
+  auto set = [&](int c) { return sm + (uint32_t)(c & 1) * DhSmem::SET; };
+  auto load_chunk = [&](int c) {
+    const ChunkAt a = chunk_at(b, c, T);
+    uint8_t* s = set(c);
+    if (tid == 0) {
+      uint64_t* lb = &lbar[c & 1];
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + TILE_TT);
+      tma_tile(s + DhSmem::Kt, &kmap, lb, h, a.t0, b);
+      tma_tile(s + DhSmem::Qt, &qmap, lb, h, a.t0, b);
+      tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
+      bulk_load(s + DhSmem::Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT, lb);
+    }
+    bpre = fetch_beta(beta + h, a.row0, H, a.valid);
+  };
+  auto wait_chunk = [&](int c) -> bool {
+    const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
+    lphase[c & 1] ^= 1u;
+    if (!r && tid == 0) atomicOr(status, 4);
+    return r;
+  };
+  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_fence_init(); }
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
+  __syncthreads();
+  if (NC > 0) load_chunk(NC - 1);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
   const uint32_t lane_tm = taddr(tm, warp * 32, 0);
-  {
-    const int j = tid;
-    float row[DP];
-#pragma unroll
-    for (int i = 0; i < DP; ++i)
-      row[i] = (dsn != nullptr && i < D && j < D) ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) tmem_st32(lane_tm + G_H + 32 * q4, *reinterpret_cast<float(*)[32]>(row + 32 * q4));
-    tmem_wait_st();
-    st_row64_bf16(Ha, 128, j, 0, row);
-    st_row64_bf16(Ha, 128, j, 1, row + 64);
-  }
-  publish();
+  column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, tid, lane_tm, G_H, Ha);
+  const uint32_t sT = smem_u32(Tt), sP = smem_u32(Pt), sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
+  const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
+  const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);
+  auto issue_state_free = [&](int c) {  // W^T, Q K^T of chunk c (thread 0)
+    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sQ = smem_u32(set(c) + DhSmem::Qt);
+    mma_seq(tm + G_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
+    mma_seq(tm + G_QK, sQ, 64, 0, sK, 64, 0, id_qk, 8, 0u);
+  };
+  auto readout_state_free = [&]() {
+    tmem_row64_to_tile(lane_tm, G_W, Wk, 128, tid, true);  // W^T row i: K-major B [i][t]
+    const int t = warp * 16 + (lane & 15);
+    tmem_row64_to_tile(lane_tm, G_QK, Pt, 64, t, lane < 16, t);
+  };
   uint32_t phase = 0;
   bool ok = true;
-  const uint32_t sK = smem_u32(Kt), sQ = smem_u32(Qt), sG = smem_u32(Gt), sT = smem_u32(Tt);
-  const uint32_t sP = smem_u32(Pt), sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
-  for (int c = NC - 1; c >= 0 && ok; --c) {
-    const int t0 = c * C, valid = min(C, T - t0);
-    const int64_t row0 = (int64_t)b * T + t0;
-    load_tokens(Kt, k + (int64_t)h * D, row0, ld, valid, D);
-    load_tokens(Qt, q + (int64_t)h * D, row0, ld, valid, D);
-    load_tokens(Gt, dout + (int64_t)h * D, row0, ld, valid, D);
-    load_linear(Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT);
-    cp_async_commit();
-    load_beta(bsm, beta + h, row0, H, valid);
-    store_linear(dhck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);  // dH_{c+1}
-    cp_async_wait_all();
+  if (NC > 0) {
+    if (tid < C) bsm[(NC - 1) & 1][tid] = __bfloat162float(bpre);
+    ok = wait_chunk(NC - 1);
     __syncthreads();
-    scale_columns(Tt, Xt, bsm);
+    scale_columns(Tt, set(NC - 1) + DhSmem::Xt, bsm[(NC - 1) & 1]);
     publish();
     if (tid == 0) {
-      const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + G_W, desc_mn(sK, 64, s), desc_k(sT, 64, s), id_tn, s > 0);
-      const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);
-      for (int s = 0; s < 8; ++s) umma_bf16(tm + G_QK, desc_k(sQ, 64, s), desc_k(sK, 64, s), id_qk, s > 0);
-      // ddelta^T = dH^T K^T (+ dO^T P below)
-      const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);
-      for (int s = 0; s < 8; ++s) umma_bf16(tm + G_D, desc_k(sH, 128, s), desc_k(sK, 64, s), id_hk, s > 0);
-      // dH^T += dO^T Q
-      const uint32_t id_oq = idesc_bf16(128, 128, 1, 1);
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + G_H, desc_mn(sG, 64, s), desc_mn(sQ, 64, s), id_oq, 1u);
+      issue_state_free(NC - 1);
       umma_commit(&bar);
     }
     ok = mma_wait(&bar, phase, status);
-    {
-      float w[64];
-      ld64(lane_tm, G_W, w);
-      st_row64_bf16(Wk, 128, tid, 0, w);  // W^T row i: K-major B [i][t]
-      float p[64];
-      ld64(lane_tm, G_QK, p);
-      const int t = warp * 16 + (lane & 15);
-      if (lane < 16) {
-#pragma unroll
-        for (int s = 0; s < 64; ++s) p[s] = s <= t ? p[s] : 0.f;
-        st_row64_bf16(Pt, 64, t, 0, p);
-      }
-    }
+    readout_state_free();
     publish();
+  }
+  for (int c = NC - 1; c >= 0 && ok; --c) {
+    const bool more = c > 0;
+    if (more) load_chunk(c - 1);
+    if (tid == 0) {  // checkpoint dH_{c+1}
+      bulk_store(dhck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
+      bulk_commit();
+    }
+    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sQ = smem_u32(set(c) + DhSmem::Qt);
+    const uint32_t sG = smem_u32(set(c) + DhSmem::Gt);
     if (tid == 0) {
-      const uint32_t id_op = idesc_bf16(128, 64, 1, 1);  // dO^T (MN) x P (MN)
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + G_D, desc_mn(sG, 64, s), desc_mn(sP, 64, s), id_op, 1u);
+      const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);  // ddelta^T = dH^T K^T
+      mma_seq(tm + G_D, sH, 128, 0, sK, 64, 0, id_hk, 8, 0u);
+      const uint32_t id_op = idesc_bf16(128, 64, 1, 1);  // += dO^T (MN) x P (MN)
+      mma_seq(tm + G_D, sG, 64, 1, sP, 64, 1, id_op, 4, 1u);
+      const uint32_t id_oq = idesc_bf16(128, 128, 1, 1);  // dH^T += dO^T Q
+      mma_seq(tm + G_H, sG, 64, 1, sQ, 64, 1, id_oq, 4, 1u);
       umma_commit(&bar);
     }
-    ok = ok && mma_wait(&bar, phase, status);
-    {
-      float d[64];
-      ld64(lane_tm, G_D, d);
-      st_row64_bf16(Da, 128, tid, 0, d);  // ddelta^T row j
+    ok = mma_wait(&bar, phase, status);
+    tmem_row64_to_tile(lane_tm, G_D, Da, 128, tid, true);  // ddelta^T row j
+    if (more) {
+      if (tid < C) bsm[(c - 1) & 1][tid] = __bfloat162float(bpre);
+      ok = wait_chunk(c - 1) && ok;
+      __syncthreads();
+      scale_columns(Tt, set(c - 1) + DhSmem::Xt, bsm[(c - 1) & 1]);
     }
+    if (tid == 0) bulk_wait_read();
     publish();
-    if (tid == 0) {
+    if (tid == 0 && ok) {
       const uint32_t id_dw = idesc_bf16(128, 128, 0, 0, 1);  // dH^T -= ddelta^T W
-      for (int s = 0; s < 4; ++s) umma_bf16(tm + G_H, desc_k(sD, 128, s), desc_k(sW, 128, s), id_dw, 1u);
+      mma_seq(tm + G_H, sD, 128, 0, sW, 128, 0, id_dw, 4, 1u);
+      if (more) issue_state_free(c - 1);
       umma_commit(&bar);
     }
     ok = ok && mma_wait(&bar, phase, status);
-    {
-      float hrow[DP];
-      ld64(lane_tm, G_H, *reinterpret_cast<float(*)[64]>(hrow));
-      ld64(lane_tm, G_H + 64, *reinterpret_cast<float(*)[64]>(hrow + 64));
-      st_row64_bf16(Ha, 128, tid, 0, hrow);
-      st_row64_bf16(Ha, 128, tid, 1, hrow + 64);
-      if (c == 0) {
-        const int j = tid;
-        if (j < D)
-          for (int i = 0; i < D; ++i) ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = hrow[i];
-      }
-    }
+    tmem_row_to_tile(lane_tm, G_H, Ha, 128, tid);
+    if (c == 0) tmem_row_to_column(lane_tm, G_H, ds0 + (int64_t)bh * D * D, D, tid);
+    if (more) readout_state_free();
     publish();
   }
   if (NC == 0) {
@@ -457,6 +576,7 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
       for (int i = 0; i < D; ++i)
         ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = dsn ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
   }
+  if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tm, 512);
@@ -480,9 +600,10 @@ constexpr int R_DP = 64, R_DW = 128, R_DV = 256, R_DT = 384;                    
 constexpr int R_DQ = 128, R_Y = 256, R_Z = 320, R_DK = 128;                       // batches 4-7
 
 __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
-    const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v,
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap gmap,
     const bf16* __restrict__ beta, const uint8_t* __restrict__ xt, const uint8_t* __restrict__ hck,
-    const uint8_t* __restrict__ dhck, const bf16* __restrict__ dout, bf16* __restrict__ dq,
+    const uint8_t* __restrict__ dhck, bf16* __restrict__ dq,
     bf16* __restrict__ dk, bf16* __restrict__ dv, bf16* __restrict__ dbeta, int T, int H, int D,
     int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
@@ -497,7 +618,7 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   uint8_t* dGt = Pt;   // [64][64]
   float* scr = reinterpret_cast<float*>(Ht);  // [64][65] floats
   __shared__ float bsm[C], db1[C];
-  __shared__ uint64_t bar;
+  __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
@@ -506,19 +627,23 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   const int64_t row0 = (int64_t)b * T + t0;
   const int trow = warp * 16 + (lane & 15);  // token row of an M=64 accumulator (lane < 16)
   const bool rowlane = lane < 16;
-  load_tokens(Qt, q + (int64_t)h * D, row0, ld, valid, D);
-  load_tokens(Kt, k + (int64_t)h * D, row0, ld, valid, D);
-  load_tokens(Vt, v + (int64_t)h * D, row0, ld, valid, D);
-  load_tokens(Gt, dout + (int64_t)h * D, row0, ld, valid, D);
   const size_t chunk = (size_t)bh * NC + c;
-  load_linear(Ht, hck + chunk * TILE_JI, TILE_JI);
-  load_linear(dHt, dhck + chunk * TILE_JI, TILE_JI);
-  load_linear(Xt, xt + chunk * TILE_TT, TILE_TT);
-  cp_async_commit();
-  load_beta(bsm, beta + h, row0, H, valid);
-  if (tid == 0) { mbar_init(&bar, 1); mbar_fence_init(); }
+  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
+  __syncthreads();
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + TILE_TT);
+    tma_tile(Qt, &qmap, &lbar, h, t0, b);
+    tma_tile(Kt, &kmap, &lbar, h, t0, b);
+    tma_tile(Vt, &vmap, &lbar, h, t0, b);
+    tma_tile(Gt, &gmap, &lbar, h, t0, b);
+    bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar);
+    bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar);
+    bulk_load(Xt, xt + chunk * TILE_TT, TILE_TT, &lbar);
+  }
+  const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
-  cp_async_wait_all();
+  if (tid < C) bsm[tid] = __bfloat162float(bv);
+  if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
   __syncthreads();
   scale_columns(Tt, Xt, bsm);
   publish();
@@ -534,17 +659,13 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 1: K K^T, Q K^T, W^T, U^T, ddelta^T = dH'^T K^T
   if (tid == 0) {
     const uint32_t id64 = idesc_bf16(64, 64, 0, 0);
-    for (int s = 0; s < 8; ++s) {
-      umma_bf16(tm + R_KK, desc_k(sK, 64, s), desc_k(sK, 64, s), id64, s > 0);
-      umma_bf16(tm + R_QK, desc_k(sQ, 64, s), desc_k(sK, 64, s), id64, s > 0);
-    }
+    mma_seq(tm + R_KK, sK, 64, 0, sK, 64, 0, id64, 8, 0u);
+    mma_seq(tm + R_QK, sQ, 64, 0, sK, 64, 0, id64, 8, 0u);
     const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
-    for (int s = 0; s < 4; ++s) {
-      umma_bf16(tm + R_W, desc_mn(sK, 64, s), desc_k(sT, 64, s), id_tn, s > 0);
-      umma_bf16(tm + R_U, desc_mn(sV, 64, s), desc_k(sT, 64, s), id_tn, s > 0);
-    }
+    mma_seq(tm + R_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
+    mma_seq(tm + R_U, sV, 64, 1, sT, 64, 0, id_tn, 4, 0u);
     const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DD, desc_k(sdH, 128, s), desc_k(sK, 64, s), id_hk, s > 0);
+    mma_seq(tm + R_DD, sdH, 128, 0, sK, 64, 0, id_hk, 8, 0u);
     umma_commit(&bar);
   }
   ok = mma_wait(&bar, phase, status);
@@ -564,9 +685,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 2: X = H^T W^T; ddelta^T += dO^T P
   if (tid == 0 && ok) {
     const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_X, desc_k(sH, 128, s), desc_mn(sW, 128, s), id_hw, s > 0);
+    mma_seq(tm + R_X, sH, 128, 0, sW, 128, 1, id_hw, 8, 0u);
     const uint32_t id_op = idesc_bf16(128, 64, 1, 1);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DD, desc_mn(sG, 64, s), desc_mn(sP, 64, s), id_op, 1u);
+    mma_seq(tm + R_DD, sG, 64, 1, sP, 64, 1, id_op, 4, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -585,13 +706,13 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 3: dP = dO delta^T; dW = -ddelta H^T; dV = T'^T ddelta; dT' = ddelta V^T
   if (tid == 0 && ok) {
     const uint32_t id_dp = idesc_bf16(64, 64, 0, 1);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DP, desc_k(sG, 64, s), desc_mn(sD, 128, s), id_dp, s > 0);
+    mma_seq(tm + R_DP, sG, 64, 0, sD, 128, 1, id_dp, 8, 0u);
     const uint32_t id_dw = idesc_bf16(64, 128, 1, 1, 1);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DW, desc_mn(sdD, 128, s), desc_mn(sH, 128, s), id_dw, s > 0);
+    mma_seq(tm + R_DW, sdD, 128, 1, sH, 128, 1, id_dw, 8, 0u);
     const uint32_t id_dv = idesc_bf16(64, 128, 1, 0);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DV, desc_mn(sT, 64, s), desc_k(sdD, 128, s), id_dv, s > 0);
+    mma_seq(tm + R_DV, sT, 64, 1, sdD, 128, 0, id_dv, 4, 0u);
     const uint32_t id_dt = idesc_bf16(64, 64, 1, 0);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DT, desc_mn(sdD, 128, s), desc_k(sV, 64, s), id_dt, s > 0);
+    mma_seq(tm + R_DT, sdD, 128, 1, sV, 64, 0, id_dt, 8, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -614,7 +735,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
     ld64(lane_tm, R_DV + 64, *reinterpret_cast<float(*)[64]>(r + 64));
     if (rowlane && trow < valid) {
       bf16* dst = dv + (row0 + trow) * ld + (int64_t)h * D;
-      for (int i = 0; i < D; i += 8) {
+      #pragma unroll
+        for (int i = 0; i < DP; i += 8) {
+          if (i >= D) break;
         uint4 w4;
         w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
         w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
@@ -626,11 +749,11 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 4: dQ = dO H^T + dP K; dT' += dW K^T
   if (tid == 0 && ok) {
     const uint32_t id_oh = idesc_bf16(64, 128, 0, 1);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DQ, desc_k(sG, 64, s), desc_mn(sH, 128, s), id_oh, s > 0);
+    mma_seq(tm + R_DQ, sG, 64, 0, sH, 128, 1, id_oh, 8, 0u);
     const uint32_t id_pk = idesc_bf16(64, 128, 0, 1);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DQ, desc_k(sdP, 64, s), desc_mn(sK, 64, s), id_pk, 1u);
+    mma_seq(tm + R_DQ, sdP, 64, 0, sK, 64, 1, id_pk, 4, 1u);
     const uint32_t id_wk = idesc_bf16(64, 64, 0, 0);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DT, desc_k(sdW, 64, s), desc_k(sK, 64, s), id_wk, 1u);
+    mma_seq(tm + R_DT, sdW, 64, 0, sK, 64, 0, id_wk, 8, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -640,7 +763,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
     ld64(lane_tm, R_DQ + 64, *reinterpret_cast<float(*)[64]>(r + 64));
     if (rowlane && trow < valid) {
       bf16* dst = dq + (row0 + trow) * ld + (int64_t)h * D;
-      for (int i = 0; i < D; i += 8) {
+      #pragma unroll
+        for (int i = 0; i < DP; i += 8) {
+          if (i >= D) break;
         uint4 w4;
         w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
         w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
@@ -670,7 +795,7 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 5: Y = dX X^T
   if (tid == 0 && ok) {
     const uint32_t id = idesc_bf16(64, 64, 0, 0);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_Y, desc_k(sdX, 64, s), desc_k(sX, 64, s), id, s > 0);
+    mma_seq(tm + R_Y, sdX, 64, 0, sX, 64, 0, id, 4, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -683,7 +808,7 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 6: Z = X^T Y; dA = -Z (strictly lower)
   if (tid == 0 && ok) {
     const uint32_t id = idesc_bf16(64, 64, 1, 1);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_Z, desc_mn(sX, 64, s), desc_mn(sY, 64, s), id, s > 0);
+    mma_seq(tm + R_Z, sX, 64, 1, sY, 64, 1, id, 4, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -714,11 +839,11 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 7: dK = dP^T Q + delta dH'^T + T'^T dW + (dG + dG^T) K
   if (tid == 0 && ok) {
     const uint32_t id_mn = idesc_bf16(64, 128, 1, 1);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DK, desc_mn(sdP, 64, s), desc_mn(sQ, 64, s), id_mn, s > 0);
-    for (int s = 0; s < 8; ++s) umma_bf16(tm + R_DK, desc_mn(sD, 128, s), desc_mn(sdH, 128, s), id_mn, 1u);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DK, desc_mn(sT, 64, s), desc_mn(sdW, 64, s), id_mn, 1u);
+    mma_seq(tm + R_DK, sdP, 64, 1, sQ, 64, 1, id_mn, 4, 0u);
+    mma_seq(tm + R_DK, sD, 128, 1, sdH, 128, 1, id_mn, 8, 1u);
+    mma_seq(tm + R_DK, sT, 64, 1, sdW, 64, 1, id_mn, 4, 1u);
     const uint32_t id_gk = idesc_bf16(64, 128, 0, 1);
-    for (int s = 0; s < 4; ++s) umma_bf16(tm + R_DK, desc_k(sdG, 64, s), desc_mn(sK, 64, s), id_gk, 1u);
+    mma_seq(tm + R_DK, sdG, 64, 0, sK, 64, 1, id_gk, 4, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -728,7 +853,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
     ld64(lane_tm, R_DK + 64, *reinterpret_cast<float(*)[64]>(r + 64));
     if (rowlane && trow < valid) {
       bf16* dst = dk + (row0 + trow) * ld + (int64_t)h * D;
-      for (int i = 0; i < D; i += 8) {
+      #pragma unroll
+        for (int i = 0; i < DP; i += 8) {
+          if (i >= D) break;
         uint4 w4;
         w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
         w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
@@ -786,15 +913,21 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
   const int NC = nchunks(T);
   uint8_t* xt = (uint8_t*)saved;
   uint8_t* hck = xt + (size_t)B * H * NC * TILE_TT;
+  CUtensorMap qm, km, vm;
   if (NC > 0) {
+    if ((rc = make_token_map(&qm, q, B, T, H, D)) || (rc = make_token_map(&km, k, B, T, H, D)) ||
+        (rc = make_token_map(&vm, v, B, T, H, D)))
+      return rc;
     const size_t sp = smem_bytes(TILE_TD + TILE_TT + 64 * 65 * 4);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp), "prep attr");
-    scan_prep_kernel<<<B * H * NC, NT, sp, st>>>((const bf16*)k, (const bf16*)beta, xt, T, H, D, NC, status);
+    scan_prep_kernel<<<B * H * NC, NT, sp, st>>>(km, (const bf16*)beta, xt, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 prep");
+  } else {
+    memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm));
   }
   const size_t sf = smem_bytes(FwdSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sf), "fwd attr");
-  scan_fwd_kernel<<<B * H, NT, sf, st>>>((const bf16*)q, (const bf16*)k, (const bf16*)v, (const bf16*)beta,
+  scan_fwd_kernel<<<B * H, NT, sf, st>>>(qm, km, vm, (const bf16*)beta,
                                          state0, xt, (bf16*)o, state_n, hck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 fwd");
   return VB_OK;
@@ -816,16 +949,24 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   const uint8_t* xt = (const uint8_t*)saved;
   const uint8_t* hck = xt + (size_t)B * H * NC * TILE_TT;
   uint8_t* dhck = (uint8_t*)workspace;
+  CUtensorMap qm, km, vm, gm;
+  if (NC > 0) {
+    if ((rc = make_token_map(&qm, q, B, T, H, D)) || (rc = make_token_map(&km, k, B, T, H, D)) ||
+        (rc = make_token_map(&vm, v, B, T, H, D)) || (rc = make_token_map(&gm, dout, B, T, H, D)))
+      return rc;
+  } else {
+    memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm)); memset(&gm, 0, sizeof(gm));
+  }
   const size_t sd = smem_bytes(DhSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd), "dh attr");
-  scan_dh_kernel<<<B * H, NT, sd, st>>>((const bf16*)q, (const bf16*)k, (const bf16*)beta, xt, (const bf16*)dout,
+  scan_dh_kernel<<<B * H, NT, sd, st>>>(qm, km, gm, (const bf16*)beta, xt,
                                         dstate_n, dstate0, dhck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 dh");
   if (NC > 0) {
     const size_t sg = smem_bytes(GrSmem::END);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sg), "grad attr");
-    scan_grad_kernel<<<B * H * NC, NT, sg, st>>>((const bf16*)q, (const bf16*)k, (const bf16*)v, (const bf16*)beta,
-                                                 xt, hck, dhck, (const bf16*)dout, (bf16*)dq, (bf16*)dk, (bf16*)dv,
+    scan_grad_kernel<<<B * H * NC, NT, sg, st>>>(qm, km, vm, gm, (const bf16*)beta,
+                                                 xt, hck, dhck, (bf16*)dq, (bf16*)dk, (bf16*)dv,
                                                  (bf16*)dbeta, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 grad");
   }

@@ -173,6 +173,42 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// ---- TMA / bulk copies (no cluster multicast anywhere) ---------------------------------------
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+// tiled 4-D tensor load into shared memory, completing `bytes` on `bar`
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* map, uint64_t* bar, int x, int y,
+                                            int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+// untiled bulk copy global -> shared (16-byte aligned, size a multiple of 16)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// untiled bulk copy shared -> global, tracked by the issuing thread's bulk async-group
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(smem_u32(src)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the issuing thread's bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... and their writes are complete
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_tmap(const void* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
 // packs two floats into a bf16x2 word (lo in the low half)
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -190,6 +226,19 @@ __device__ __forceinline__ void st_row64_bf16(uint8_t* tile, int rows, int r, in
     w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
     w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
     *reinterpret_cast<uint4*>(tile + sw_chunk(rows, r, a * 8 + j)) = w;
+  }
+}
+
+// Writes 32 floats as bf16 into row r, columns [c0, c0 + 32) of a swizzled tile (c0 % 32 == 0).
+__device__ __forceinline__ void st_row32_bf16(uint8_t* tile, int rows, int r, int c0, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(tile + sw_chunk(rows, r, c0 / 8 + j)) = w;
   }
 }
 
