@@ -174,15 +174,20 @@ __device__ __forceinline__ void column_to_tmem_and_tile(const float* mat, int D,
   tmem_wait_st();
 }
 
-// One MMA of K = 16 * steps: D (+)= A x B over k-steps; `a_mn` / `b_mn` select the MN-major
-// descriptor form (tile rows = K index) over the K-major one (tile rows = M or N index).
-// Not inlined: its descriptor arithmetic must not be hoisted into the calling kernel's loop.
-__device__ __noinline__ void mma_seq(uint32_t d, uint32_t a, int a_rows, int a_mn, uint32_t b, int b_rows,
-                                     int b_mn, uint32_t idesc, int steps, uint32_t accumulate_first) {
-  for (int s = 0; s < steps; ++s) {
-    const uint64_t ad = a_mn ? desc_mn(a, a_rows, s) : desc_k(a, a_rows, s);
-    const uint64_t bd = b_mn ? desc_mn(b, b_rows, s) : desc_k(b, b_rows, s);
-    umma_bf16(d, ad, bd, idesc, (s > 0 || accumulate_first) ? 1u : 0u);
+// One MMA of K = 16 * STEPS, D (+)= A x B: the k-step descriptors are the step-0 descriptor plus a
+// compile-time offset (the start-address field counts 16-byte units), so each step costs one
+// add and the issue. A_MN / B_MN select the MN-major form (tile rows = K index) over the K-major
+// one (tile rows = the M or N index, `A_ROWS` / `B_ROWS` rows per 64-element atom).
+template <int STEPS, int A_MN, int A_ROWS, int B_MN, int B_ROWS>
+__device__ __forceinline__ void mma_seq(uint32_t d, uint32_t a, uint32_t b, uint32_t idesc,
+                                        uint32_t accumulate_first) {
+  const uint64_t a0 = A_MN ? desc_mn(a, A_ROWS, 0) : desc_k(a, A_ROWS, 0);
+  const uint64_t b0 = B_MN ? desc_mn(b, B_ROWS, 0) : desc_k(b, B_ROWS, 0);
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const uint64_t ao = A_MN ? (uint64_t)(s * 128) : (uint64_t)(((s >> 2) * A_ROWS * 128 + (s & 3) * 32) >> 4);
+    const uint64_t bo = B_MN ? (uint64_t)(s * 128) : (uint64_t)(((s >> 2) * B_ROWS * 128 + (s & 3) * 32) >> 4);
+    umma_bf16(d, a0 + ao, b0 + bo, idesc, (s > 0 || accumulate_first) ? 1u : 0u);
   }
 }
 
@@ -236,8 +241,7 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   const uint32_t tm = tbase;
   if (tid == 0) {
     const uint32_t id = idesc_bf16(64, 64, 0, 0);
-    for (int s = 0; s < DP / 16; ++s)
-      umma_bf16(tm, desc_k(smem_u32(Kt), 64, s), desc_k(smem_u32(Kt), 64, s), id, s > 0 ? 1u : 0u);
+    mma_seq<DP / 16, 0, 64, 0, 64>(tm, smem_u32(Kt), smem_u32(Kt), id, 0u);
     umma_commit(&bar);
   }
   uint32_t phase = 0;
@@ -359,9 +363,9 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
   auto issue_state_free = [&](int c) {                // U^T, W^T, Q K^T of chunk c (thread 0)
     const uint32_t sK = smem_u32(set(c) + FwdSmem::Kt), sQ = smem_u32(set(c) + FwdSmem::Qt);
     const uint32_t sV = smem_u32(set(c) + FwdSmem::Vt);
-    mma_seq(tm + F_U, sV, 64, 1, sT, 64, 0, id_tn, 4, 0u);
-    mma_seq(tm + F_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
-    mma_seq(tm + F_QK, sQ, 64, 0, sK, 64, 0, id_qk, 8, 0u);
+    mma_seq<4, 1, 64, 0, 64>(tm + F_U, sV, sT, id_tn, 0u);
+    mma_seq<4, 1, 64, 0, 64>(tm + F_W, sK, sT, id_tn, 0u);
+    mma_seq<8, 0, 64, 0, 64>(tm + F_QK, sQ, sK, id_qk, 0u);
   };
   auto readout_state_free = [&]() {  // W^T rows -> Wr, P rows -> Pt (all threads)
     tmem_row64_to_tile(lane_tm, F_W, Wr, 128, tid, true);
@@ -396,9 +400,9 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
     const uint32_t sQ = smem_u32(set(c) + FwdSmem::Qt), sK = smem_u32(set(c) + FwdSmem::Kt);
     if (tid == 0) {
       const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);  // A K-major (H^T), B MN-major (W^T rows)
-      mma_seq(tm + F_X, sH, 128, 0, sW, 128, 1, id_hw, 8, 0u);
+      mma_seq<8, 0, 128, 1, 128>(tm + F_X, sH, sW, id_hw, 0u);
       const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);  // O = Q H: both K-major
-      mma_seq(tm + F_O, sQ, 64, 0, sH, 128, 0, id_qh, 8, 0u);
+      mma_seq<8, 0, 64, 0, 128>(tm + F_O, sQ, sH, id_qh, 0u);
       umma_commit(&bar);
     }
     ok = mma_wait(&bar, phase, status);
@@ -413,9 +417,9 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
     publish();
     if (tid == 0 && ok) {
       const uint32_t id_dk = idesc_bf16(128, 128, 0, 1);  // H^T += delta^T K (B MN-major)
-      mma_seq(tm + F_H, sD, 128, 0, sK, 64, 1, id_dk, 4, 1u);
+      mma_seq<4, 0, 128, 1, 64>(tm + F_H, sD, sK, id_dk, 1u);
       const uint32_t id_pd = idesc_bf16(64, 128, 0, 0);  // O += P delta
-      mma_seq(tm + F_O, sP, 64, 0, sD, 128, 0, id_pd, 4, 1u);
+      mma_seq<4, 0, 64, 0, 128>(tm + F_O, sP, sD, id_pd, 1u);
       if (more) issue_state_free(c + 1);
       umma_commit(&bar);
     }
@@ -506,8 +510,8 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
   const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);
   auto issue_state_free = [&](int c) {  // W^T, Q K^T of chunk c (thread 0)
     const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sQ = smem_u32(set(c) + DhSmem::Qt);
-    mma_seq(tm + G_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
-    mma_seq(tm + G_QK, sQ, 64, 0, sK, 64, 0, id_qk, 8, 0u);
+    mma_seq<4, 1, 64, 0, 64>(tm + G_W, sK, sT, id_tn, 0u);
+    mma_seq<8, 0, 64, 0, 64>(tm + G_QK, sQ, sK, id_qk, 0u);
   };
   auto readout_state_free = [&]() {
     tmem_row64_to_tile(lane_tm, G_W, Wk, 128, tid, true);  // W^T row i: K-major B [i][t]
@@ -541,11 +545,11 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     const uint32_t sG = smem_u32(set(c) + DhSmem::Gt);
     if (tid == 0) {
       const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);  // ddelta^T = dH^T K^T
-      mma_seq(tm + G_D, sH, 128, 0, sK, 64, 0, id_hk, 8, 0u);
+      mma_seq<8, 0, 128, 0, 64>(tm + G_D, sH, sK, id_hk, 0u);
       const uint32_t id_op = idesc_bf16(128, 64, 1, 1);  // += dO^T (MN) x P (MN)
-      mma_seq(tm + G_D, sG, 64, 1, sP, 64, 1, id_op, 4, 1u);
+      mma_seq<4, 1, 64, 1, 64>(tm + G_D, sG, sP, id_op, 1u);
       const uint32_t id_oq = idesc_bf16(128, 128, 1, 1);  // dH^T += dO^T Q
-      mma_seq(tm + G_H, sG, 64, 1, sQ, 64, 1, id_oq, 4, 1u);
+      mma_seq<4, 1, 64, 1, 64>(tm + G_H, sG, sQ, id_oq, 1u);
       umma_commit(&bar);
     }
     ok = mma_wait(&bar, phase, status);
@@ -560,7 +564,7 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     publish();
     if (tid == 0 && ok) {
       const uint32_t id_dw = idesc_bf16(128, 128, 0, 0, 1);  // dH^T -= ddelta^T W
-      mma_seq(tm + G_H, sD, 128, 0, sW, 128, 0, id_dw, 4, 1u);
+      mma_seq<4, 0, 128, 0, 128>(tm + G_H, sD, sW, id_dw, 1u);
       if (more) issue_state_free(c - 1);
       umma_commit(&bar);
     }
@@ -659,13 +663,13 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 1: K K^T, Q K^T, W^T, U^T, ddelta^T = dH'^T K^T
   if (tid == 0) {
     const uint32_t id64 = idesc_bf16(64, 64, 0, 0);
-    mma_seq(tm + R_KK, sK, 64, 0, sK, 64, 0, id64, 8, 0u);
-    mma_seq(tm + R_QK, sQ, 64, 0, sK, 64, 0, id64, 8, 0u);
+    mma_seq<8, 0, 64, 0, 64>(tm + R_KK, sK, sK, id64, 0u);
+    mma_seq<8, 0, 64, 0, 64>(tm + R_QK, sQ, sK, id64, 0u);
     const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
-    mma_seq(tm + R_W, sK, 64, 1, sT, 64, 0, id_tn, 4, 0u);
-    mma_seq(tm + R_U, sV, 64, 1, sT, 64, 0, id_tn, 4, 0u);
+    mma_seq<4, 1, 64, 0, 64>(tm + R_W, sK, sT, id_tn, 0u);
+    mma_seq<4, 1, 64, 0, 64>(tm + R_U, sV, sT, id_tn, 0u);
     const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);
-    mma_seq(tm + R_DD, sdH, 128, 0, sK, 64, 0, id_hk, 8, 0u);
+    mma_seq<8, 0, 128, 0, 64>(tm + R_DD, sdH, sK, id_hk, 0u);
     umma_commit(&bar);
   }
   ok = mma_wait(&bar, phase, status);
@@ -685,9 +689,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 2: X = H^T W^T; ddelta^T += dO^T P
   if (tid == 0 && ok) {
     const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);
-    mma_seq(tm + R_X, sH, 128, 0, sW, 128, 1, id_hw, 8, 0u);
+    mma_seq<8, 0, 128, 1, 128>(tm + R_X, sH, sW, id_hw, 0u);
     const uint32_t id_op = idesc_bf16(128, 64, 1, 1);
-    mma_seq(tm + R_DD, sG, 64, 1, sP, 64, 1, id_op, 4, 1u);
+    mma_seq<4, 1, 64, 1, 64>(tm + R_DD, sG, sP, id_op, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -706,13 +710,13 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 3: dP = dO delta^T; dW = -ddelta H^T; dV = T'^T ddelta; dT' = ddelta V^T
   if (tid == 0 && ok) {
     const uint32_t id_dp = idesc_bf16(64, 64, 0, 1);
-    mma_seq(tm + R_DP, sG, 64, 0, sD, 128, 1, id_dp, 8, 0u);
+    mma_seq<8, 0, 64, 1, 128>(tm + R_DP, sG, sD, id_dp, 0u);
     const uint32_t id_dw = idesc_bf16(64, 128, 1, 1, 1);
-    mma_seq(tm + R_DW, sdD, 128, 1, sH, 128, 1, id_dw, 8, 0u);
+    mma_seq<8, 1, 128, 1, 128>(tm + R_DW, sdD, sH, id_dw, 0u);
     const uint32_t id_dv = idesc_bf16(64, 128, 1, 0);
-    mma_seq(tm + R_DV, sT, 64, 1, sdD, 128, 0, id_dv, 4, 0u);
+    mma_seq<4, 1, 64, 0, 128>(tm + R_DV, sT, sdD, id_dv, 0u);
     const uint32_t id_dt = idesc_bf16(64, 64, 1, 0);
-    mma_seq(tm + R_DT, sdD, 128, 1, sV, 64, 0, id_dt, 8, 0u);
+    mma_seq<8, 1, 128, 0, 64>(tm + R_DT, sdD, sV, id_dt, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -749,11 +753,11 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 4: dQ = dO H^T + dP K; dT' += dW K^T
   if (tid == 0 && ok) {
     const uint32_t id_oh = idesc_bf16(64, 128, 0, 1);
-    mma_seq(tm + R_DQ, sG, 64, 0, sH, 128, 1, id_oh, 8, 0u);
+    mma_seq<8, 0, 64, 1, 128>(tm + R_DQ, sG, sH, id_oh, 0u);
     const uint32_t id_pk = idesc_bf16(64, 128, 0, 1);
-    mma_seq(tm + R_DQ, sdP, 64, 0, sK, 64, 1, id_pk, 4, 1u);
+    mma_seq<4, 0, 64, 1, 64>(tm + R_DQ, sdP, sK, id_pk, 1u);
     const uint32_t id_wk = idesc_bf16(64, 64, 0, 0);
-    mma_seq(tm + R_DT, sdW, 64, 0, sK, 64, 0, id_wk, 8, 1u);
+    mma_seq<8, 0, 64, 0, 64>(tm + R_DT, sdW, sK, id_wk, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -795,7 +799,7 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 5: Y = dX X^T
   if (tid == 0 && ok) {
     const uint32_t id = idesc_bf16(64, 64, 0, 0);
-    mma_seq(tm + R_Y, sdX, 64, 0, sX, 64, 0, id, 4, 0u);
+    mma_seq<4, 0, 64, 0, 64>(tm + R_Y, sdX, sX, id, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -808,7 +812,7 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 6: Z = X^T Y; dA = -Z (strictly lower)
   if (tid == 0 && ok) {
     const uint32_t id = idesc_bf16(64, 64, 1, 1);
-    mma_seq(tm + R_Z, sX, 64, 1, sY, 64, 1, id, 4, 0u);
+    mma_seq<4, 1, 64, 1, 64>(tm + R_Z, sX, sY, id, 0u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
@@ -839,11 +843,11 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   // batch 7: dK = dP^T Q + delta dH'^T + T'^T dW + (dG + dG^T) K
   if (tid == 0 && ok) {
     const uint32_t id_mn = idesc_bf16(64, 128, 1, 1);
-    mma_seq(tm + R_DK, sdP, 64, 1, sQ, 64, 1, id_mn, 4, 0u);
-    mma_seq(tm + R_DK, sD, 128, 1, sdH, 128, 1, id_mn, 8, 1u);
-    mma_seq(tm + R_DK, sT, 64, 1, sdW, 64, 1, id_mn, 4, 1u);
+    mma_seq<4, 1, 64, 1, 64>(tm + R_DK, sdP, sQ, id_mn, 0u);
+    mma_seq<8, 1, 128, 1, 128>(tm + R_DK, sD, sdH, id_mn, 1u);
+    mma_seq<4, 1, 64, 1, 64>(tm + R_DK, sT, sdW, id_mn, 1u);
     const uint32_t id_gk = idesc_bf16(64, 128, 0, 1);
-    mma_seq(tm + R_DK, sdG, 64, 0, sK, 64, 1, id_gk, 4, 1u);
+    mma_seq<4, 0, 64, 1, 64>(tm + R_DK, sdG, sK, id_gk, 1u);
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
