@@ -60,7 +60,7 @@ __device__ __forceinline__ void tma_tile(uint8_t* tile, const CUtensorMap* map, 
 
 // T'[t][s] = X[t][s] * beta_s (bf16 tile images, one 8-element chunk per step)
 __device__ __forceinline__ void scale_columns(uint8_t* Tt, const uint8_t* Xt, const float* bsm) {
-  for (int q = threadIdx.x; q < 64 * 8; q += NT) {
+  for (int q = threadIdx.x; q < 64 * 8; q += blockDim.x) {
     const int r = q >> 3, j = q & 7;
     const uint32_t off = sw_chunk(64, r, j);
     uint4 w = *reinterpret_cast<const uint4*>(Xt + off);
@@ -76,88 +76,6 @@ __device__ __forceinline__ void ld64(uint32_t tm, int col, float (&v)[64]) {
   tmem_ld32(tm + (uint32_t)col, *reinterpret_cast<float(*)[32]>(a));
   tmem_ld32(tm + (uint32_t)col + 32, *reinterpret_cast<float(*)[32]>(a + 32));
   tmem_wait_ld();
-}
-
-// A 128-column fp32 tensor-memory row (this thread's lane) -> bf16 row r of a [rows][128] tile.
-__device__ __forceinline__ void tmem_row_to_tile(uint32_t lane_tm, int col, uint8_t* tile, int rows, int r) {
-#pragma unroll
-  for (int c0 = 0; c0 < DP; c0 += 32) {
-    float v[32];
-    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
-    tmem_wait_ld();
-    st_row32_bf16(tile, rows, r, c0, v);
-  }
-}
-
-// A 64-column fp32 tensor-memory row -> bf16 row r of a [rows][64] tile; with `mask_after` >= 0
-// the columns above it are zeroed (the causal mask of P)
-__device__ __forceinline__ void tmem_row64_to_tile(uint32_t lane_tm, int col, uint8_t* tile, int rows,
-                                                   int r, bool write, int mask_after = -1) {
-#pragma unroll
-  for (int c0 = 0; c0 < 64; c0 += 32) {
-    float v[32];
-    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
-    tmem_wait_ld();
-    if (mask_after >= 0) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] = c0 + e <= mask_after ? v[e] : 0.f;
-    }
-    if (write) st_row32_bf16(tile, rows, r, c0, v);
-  }
-}
-
-// (a - b) of two 64-column tensor-memory rows -> bf16 row r of a [rows][64] tile
-__device__ __forceinline__ void tmem_diff64_to_tile(uint32_t lane_tm, int col_a, int col_b, uint8_t* tile,
-                                                    int rows, int r) {
-#pragma unroll
-  for (int c0 = 0; c0 < 64; c0 += 32) {
-    float x[32], y[32];
-    tmem_ld32(lane_tm + (uint32_t)(col_a + c0), x);
-    tmem_ld32(lane_tm + (uint32_t)(col_b + c0), y);
-    tmem_wait_ld();
-#pragma unroll
-    for (int e = 0; e < 32; ++e) x[e] -= y[e];
-    st_row32_bf16(tile, rows, r, c0, x);
-  }
-}
-
-// A 128-column fp32 tensor-memory row -> bf16 global row dst[0, D) (when `store` holds)
-__device__ __forceinline__ void tmem_row_to_global(uint32_t lane_tm, int col, bf16* dst, int D, bool store) {
-#pragma unroll
-  for (int c0 = 0; c0 < DP; c0 += 32) {
-    float v[32];
-    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
-    tmem_wait_ld();
-    if (store) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int i = c0 + 8 * j;
-        if (i < D) {
-          uint4 w;
-          w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
-          w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
-          w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
-          w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
-          *reinterpret_cast<uint4*>(dst + i) = w;
-        }
-      }
-    }
-  }
-}
-
-// A 128-column fp32 tensor-memory row j -> column j of a float32 [D][D] matrix (rows i < D)
-__device__ __forceinline__ void tmem_row_to_column(uint32_t lane_tm, int col, float* mat, int D, int j) {
-#pragma unroll
-  for (int c0 = 0; c0 < DP; c0 += 32) {
-    float v[32];
-    tmem_ld32(lane_tm + (uint32_t)(col + c0), v);
-    tmem_wait_ld();
-    if (j < D) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (c0 + e < D) mat[(int64_t)(c0 + e) * D + j] = v[e];
-    }
-  }
 }
 
 // Column j of a float32 [D][D] matrix (zero-padded to 128) -> tensor-memory row and bf16 tile row
@@ -209,17 +127,24 @@ __device__ __forceinline__ void publish() {
 }
 
 // ------------------------------------------------------------------------------------------
-// prep: X = (I + strictly_lower(diag(beta) K K^T))^-1 per chunk, bf16 tile image [64 t][64 s]
+// prep, chunk-parallel: one stacked product [K; Q] K^T (M=128) gives K K^T (rows 0-63) and Q K^T
+// (rows 64-127). From K K^T: X = (I + strictly_lower(diag(beta) K K^T))^-1 by float32 forward
+// substitution (one thread per column); from Q K^T: P = lower_inclusive(Q K^T). Per chunk the
+// scratch holds the bf16 tile images [X 8 KB][P 8 KB].
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ CUtensorMap kmap,
+constexpr uint32_t PREP_BYTES = 2 * TILE_TT;  // per chunk: X then P
+
+__global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                       const __grid_constant__ CUtensorMap kmap,
                                                        const bf16* __restrict__ beta,
                                                        uint8_t* __restrict__ xt, int T, int H,
                                                        int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* Kt = sm;                                   // 16 KB
-  uint8_t* Xs = sm + TILE_TD;                         // 8 KB
-  float* A = reinterpret_cast<float*>(sm + TILE_TD + TILE_TT);  // [64][65]
+  uint8_t* KQ = sm;                                   // [128 rows][128 d]: K rows 0-63, Q rows 64-127
+  uint8_t* Xs = sm + TILE_JI;                         // [X 8 KB][P 8 KB]
+  uint8_t* Ps = Xs + TILE_TT;
+  float* A = reinterpret_cast<float*>(sm + TILE_JI + 2 * TILE_TT);  // [64][65]
   __shared__ float bsm[C];
   __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
@@ -230,8 +155,11 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
   __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(&lbar, TILE_TD);
-    tma_tile(Kt, &kmap, &lbar, h, t0, b);
+    mbar_arrive_expect_tx(&lbar, 2 * TILE_TD);
+    tma_load_4d(KQ, &kmap, &lbar, 0, h, t0, b);
+    tma_load_4d(KQ + TILE_JI / 2, &kmap, &lbar, 64, h, t0, b);
+    tma_load_4d(KQ + TILE_TD / 2, &qmap, &lbar, 0, h, t0, b);
+    tma_load_4d(KQ + TILE_JI / 2 + TILE_TD / 2, &qmap, &lbar, 64, h, t0, b);
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 64); tmem_relinquish(); }
@@ -240,18 +168,28 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   publish();
   const uint32_t tm = tbase;
   if (tid == 0) {
-    const uint32_t id = idesc_bf16(64, 64, 0, 0);
-    mma_seq<DP / 16, 0, 64, 0, 64>(tm, smem_u32(Kt), smem_u32(Kt), id, 0u);
+    mma_seq<DP / 16, 0, 128, 0, 128>(tm, smem_u32(KQ), smem_u32(KQ), idesc_bf16(128, 64, 0, 0), 0u);
     umma_commit(&bar);
   }
   uint32_t phase = 0;
   const bool ok = mma_wait(&bar, phase, status);
-  const int row = warp * 16 + (lane & 15);
-  float v[64];
-  ld64(taddr(tm, warp * 32, 0), 0, v);
-  if (lane < 16) {
+  {
+    const int row = tid;  // M=128 layout: thread <-> lane <-> row
 #pragma unroll
-    for (int s = 0; s < 64; ++s) A[row * 65 + s] = s < row ? bsm[row] * v[s] : 0.f;
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      float v[32];
+      tmem_ld32(taddr(tm, warp * 32, c0), v);
+      tmem_wait_ld();
+      if (row < C) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) A[row * 65 + c0 + e] = c0 + e < row ? bsm[row] * v[e] : 0.f;
+      } else {
+        const int t = row - C;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = c0 + e <= t ? v[e] : 0.f;
+        st_row32_bf16(Ps, 64, t, c0, v);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -273,29 +211,34 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   fence_async_smem();
   __syncthreads();
   if (tid == 0) {
-    bulk_store(xt + (size_t)blockIdx.x * TILE_TT, Xs, TILE_TT);
+    bulk_store(xt + (size_t)blockIdx.x * PREP_BYTES, Xs, PREP_BYTES);
     bulk_commit();
     bulk_wait_all();
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// forward: one CTA per (b, h); thread j <-> tensor-memory lane j <-> value index j.
-// Software pipeline over chunks: the next chunk's tiles are prefetched into the other buffer
-// set, and its state-independent products (U^T, W^T, Q K^T) are issued with this chunk's state
-// update, so each chunk costs two tensor-core round trips:
-//   B_c: X = H^T W_c^T, O = Q_c H              -> delta_c = U_c - X
-//   C_c: H^T += delta_c^T K_c, O += P_c delta_c, and U, W, Q K^T of chunk c+1
+// forward: one CTA (256 threads) per (b, h). H^T lives in tensor memory (lane j = value index,
+// column i = key index); the chunk's products run in the "rows t" form with the token rows
+// duplicated over both halves of the 128 lanes, so all eight warps share every readout:
+//   [U | W] = [T'; T'] [V | K]         (N = 256, issued during the previous chunk)
+//   X = [W; W] H,  O = Q H              (batch B)  -> delta = U - X        (rows t)
+//   H^T += delta^T K                    (batch C1) -> bf16 copy of H for the next chunk
+//   O += P delta, [U | W] of chunk c+1  (batch C2) -> O stored, W of chunk c+1 staged
+// Warp w reads lane quarter w % 4; the two warps of a quarter split the columns (w / 4).
 // ------------------------------------------------------------------------------------------
+constexpr int NT2 = 256;
 struct FwdSmem {
-  // two buffer sets of the per-chunk input tiles
-  static constexpr uint32_t SET = 3 * TILE_TD + TILE_TT;  // K, Q, V, X
-  static constexpr uint32_t Kt = 0, Qt = TILE_TD, Vt = 2 * TILE_TD, Xt = 3 * TILE_TD;
-  static constexpr uint32_t Tt = 2 * SET, Pt = Tt + TILE_TT, Wr = Pt + TILE_TT,
-                            Ha = Wr + TILE_JT, Da = Ha + TILE_JI, END = Da + TILE_JT;
+  // per-chunk input set: [V | K] adjacent (the MN-major B operand [V | K]), then Q, X, P
+  static constexpr uint32_t Vt = 0, Kt = TILE_TD, Qt = 2 * TILE_TD, Xt = 3 * TILE_TD, Pt = Xt + TILE_TT;
+  static constexpr uint32_t SET = Pt + TILE_TT;  // 64 KB
+  static constexpr uint32_t TT = 2 * SET,            // [T'; T'] 128 rows x 64
+      WW = TT + TILE_JT,                             // [W; W] 128 rows x 128
+      Ha = WW + TILE_JI,                             // H^T bf16 [j][i]
+      Dr = Ha + TILE_JI,                             // delta rows [t][j]
+      END = Dr + TILE_TD;
 };
-// tensor-memory columns
-constexpr int F_H = 0, F_U = 128, F_W = 192, F_X = 256, F_QK = 320, F_O = 384;
+constexpr int F_H = 0, F_U = 128, F_W = 256, F_X = 256, F_O = 384;
 
 struct ChunkAt {
   int t0, valid;
@@ -309,35 +252,48 @@ __device__ __forceinline__ ChunkAt chunk_at(int b, int c, int T) {
   return a;
 }
 
-__global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
+// T' = X diag(beta) written twice: rows 0-63 and rows 64-127 of a 128-row tile
+__device__ __forceinline__ void scale_columns_twice(uint8_t* TT, const uint8_t* Xt, const float* bsm) {
+  for (int q = threadIdx.x; q < 64 * 8; q += blockDim.x) {
+    const int r = q >> 3, j = q & 7;
+    uint4 w = *reinterpret_cast<const uint4*>(Xt + sw_chunk(64, r, j));
+    bf16* e = reinterpret_cast<bf16*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16_rn(__bfloat162float(e[i]) * bsm[8 * j + i]);
+    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r, j)) = w;
+    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r + 64, j)) = w;
+  }
+}
+
+__global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    const __grid_constant__ CUtensorMap vmap,
+    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
     const bf16* __restrict__ beta, const float* __restrict__ s0, const uint8_t* __restrict__ xt,
-    bf16* __restrict__ o, float* __restrict__ sn, uint8_t* __restrict__ hck, int T, int H, int D,
+    float* __restrict__ sn, uint8_t* __restrict__ hck, int T, int H, int D,
     int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Tt = sm + FwdSmem::Tt, *Pt = sm + FwdSmem::Pt, *Wr = sm + FwdSmem::Wr;
-  uint8_t *Ha = sm + FwdSmem::Ha, *Da = sm + FwdSmem::Da;
+  uint8_t *TT = sm + FwdSmem::TT, *WW = sm + FwdSmem::WW, *Ha = sm + FwdSmem::Ha, *Dr = sm + FwdSmem::Dr;
   __shared__ float bsm[2][C];
-  __shared__ uint64_t bar, lbar[2];
+  __shared__ uint64_t barB, barH, barC, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int lane128 = quarter * 32 + lane;   // this thread's tensor-memory lane
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  const int64_t ld = (int64_t)H * D;  // elements between consecutive tokens of one head
-  bf16 bpre = __float2bfloat16_rn(0.f);  // the prefetched beta of the chunk being loaded
+  bf16 bpre = __float2bfloat16_rn(0.f);
   uint32_t lphase[2] = {0u, 0u};
   auto set = [&](int c) { return sm + (uint32_t)(c & 1) * FwdSmem::SET; };
-  auto load_chunk = [&](int c) {  // one thread issues TMA for the chunk's tiles
+  auto load_chunk = [&](int c) {
     const ChunkAt a = chunk_at(b, c, T);
     uint8_t* s = set(c);
     if (tid == 0) {
       uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + TILE_TT);
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES);
+      tma_tile(s + FwdSmem::Vt, &vmap, lb, h, a.t0, b);
       tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
       tma_tile(s + FwdSmem::Qt, &qmap, lb, h, a.t0, b);
-      tma_tile(s + FwdSmem::Vt, &vmap, lb, h, a.t0, b);
-      bulk_load(s + FwdSmem::Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT, lb);
+      bulk_load(s + FwdSmem::Xt, xt + ((size_t)bh * NC + c) * PREP_BYTES, PREP_BYTES, lb);
     }
     bpre = fetch_beta(beta + h, a.row0, H, a.valid);
   };
@@ -347,95 +303,142 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
     if (!r && tid == 0) atomicOr(status, 4);
     return r;
   };
-  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_fence_init(); }
+  if (tid == 0) {
+    mbar_init(&barB, 1); mbar_init(&barH, 1); mbar_init(&barC, 1);
+    mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
+    mbar_fence_init();
+  }
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
   __syncthreads();
   if (NC > 0) load_chunk(0);
-  tc_fence_before();
-  __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);  // this warp's lane quarter
-  column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, tid, lane_tm, F_H, Ha);
-  const uint32_t sT = smem_u32(Tt), sP = smem_u32(Pt), sW = smem_u32(Wr), sH = smem_u32(Ha), sD = smem_u32(Da);
-  const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);   // U^T, W^T: A MN-major, B K-major
-  const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);    // Q K^T
-  auto issue_state_free = [&](int c) {                // U^T, W^T, Q K^T of chunk c (thread 0)
-    const uint32_t sK = smem_u32(set(c) + FwdSmem::Kt), sQ = smem_u32(set(c) + FwdSmem::Qt);
-    const uint32_t sV = smem_u32(set(c) + FwdSmem::Vt);
-    mma_seq<4, 1, 64, 0, 64>(tm + F_U, sV, sT, id_tn, 0u);
-    mma_seq<4, 1, 64, 0, 64>(tm + F_W, sK, sT, id_tn, 0u);
-    mma_seq<8, 0, 64, 0, 64>(tm + F_QK, sQ, sK, id_qk, 0u);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
+  // H^T row j = column j of the initial state (warps 0-3; warps 4-7 idle here)
+  if (half == 0) column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, lane128, lane_tm, F_H, Ha);
+  const uint32_t sTT = smem_u32(TT), sWW = smem_u32(WW), sH = smem_u32(Ha), sD = smem_u32(Dr);
+  const uint32_t id_uw = idesc_bf16(128, 256, 0, 1);  // [T';T'] (K) x [V|K] (MN)
+  const uint32_t id_xo = idesc_bf16(128, 128, 0, 0);  // X = [W;W] H: both K-major
+  const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);   // O = Q H
+  const uint32_t id_hk = idesc_bf16(128, 128, 1, 1);  // H^T += delta^T K: both MN-major
+  const uint32_t id_pd = idesc_bf16(64, 128, 0, 1);   // O += P delta
+  // token row of this thread in the duplicated "rows t" layout, and its 32-column slice
+  const int trow = lane128 & 63;
+  const int upper = lane128 >> 6;  // 0: lanes 0-63, 1: lanes 64-127
+  auto readout_w = [&]() {         // W rows (duplicated lanes) -> [W; W]
+    const int c0 = half * 64;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float v[32];
+      tmem_ld32(lane_tm + (uint32_t)(F_W + c0 + 32 * k), v);
+      tmem_wait_ld();
+      st_row32_bf16(WW, 128, upper * 64 + trow, c0 + 32 * k, v);
+    }
   };
-  auto readout_state_free = [&]() {  // W^T rows -> Wr, P rows -> Pt (all threads)
-    tmem_row64_to_tile(lane_tm, F_W, Wr, 128, tid, true);
-    const int t = warp * 16 + (lane & 15);
-    tmem_row64_to_tile(lane_tm, F_QK, Pt, 64, t, lane < 16, t);
-  };
-  uint32_t phase = 0;
+  uint32_t pB = 0, pH = 0, pC = 0;
   bool ok = true;
   if (NC > 0) {
     if (tid < C) bsm[0][tid] = __bfloat162float(bpre);
     ok = wait_chunk(0);
     __syncthreads();
-    scale_columns(Tt, set(0) + FwdSmem::Xt, bsm[0]);
+    scale_columns_twice(TT, set(0) + FwdSmem::Xt, bsm[0]);
     publish();
     if (tid == 0) {
-      issue_state_free(0);
-      umma_commit(&bar);
+      mma_seq<4, 0, 128, 1, 64>(tm + F_U, sTT, smem_u32(set(0) + FwdSmem::Vt), id_uw, 0u);
+      umma_commit(&barC);
     }
-    ok = mma_wait(&bar, phase, status);
-    readout_state_free();
+    ok = mma_wait(&barC, pC, status) && ok;
+    if (NC > 1) load_chunk(1);
+    readout_w();
     publish();
   }
   for (int c = 0; c < NC && ok; ++c) {
     const ChunkAt a = chunk_at(b, c, T);
     const bool more = c + 1 < NC;
-    if (more) load_chunk(c + 1);
-    // checkpoint H_c (the bf16 copy the chunk's products read) while the loads land
-    if (tid == 0) {
+    if (tid == 0) {  // checkpoint H_c (the bf16 copy the chunk's products read)
       bulk_store(hck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
       bulk_commit();
     }
     const uint32_t sQ = smem_u32(set(c) + FwdSmem::Qt), sK = smem_u32(set(c) + FwdSmem::Kt);
+    const uint32_t sP = smem_u32(set(c) + FwdSmem::Pt);
     if (tid == 0) {
-      const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);  // A K-major (H^T), B MN-major (W^T rows)
-      mma_seq<8, 0, 128, 1, 128>(tm + F_X, sH, sW, id_hw, 0u);
-      const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);  // O = Q H: both K-major
-      mma_seq<8, 0, 64, 0, 128>(tm + F_O, sQ, sH, id_qh, 0u);
-      umma_commit(&bar);
+      mma_seq<8, 0, 128, 0, 128>(tm + F_X, sWW, sH, id_xo, 0u);  // X = [W;W] H
+      umma_commit(&barB);
+      mma_seq<8, 0, 64, 0, 128>(tm + F_O, sQ, sH, id_qh, 0u);    // O = Q H (waited on with C2)
     }
-    ok = mma_wait(&bar, phase, status);
-    tmem_diff64_to_tile(lane_tm, F_U, F_X, Da, 128, tid);  // delta^T row j: [j][t]
+    ok = mma_wait(&barB, pB, status) && ok;
+    {
+      // delta = U - X, rows t (Dr was released by the previous chunk's O store before the
+      // barrier that ended that chunk); lanes 0-63 take columns 0-63, lanes 64-127 columns 64-127
+      const int c0 = upper * 64 + half * 32;
+      float u[32], x[32];
+      tmem_ld32(lane_tm + (uint32_t)(F_U + c0), u);
+      tmem_ld32(lane_tm + (uint32_t)(F_X + c0), x);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) u[e] -= x[e];
+      st_row32_bf16(Dr, 64, trow, c0, u);
+    }
     if (more) {
       if (tid < C) bsm[(c + 1) & 1][tid] = __bfloat162float(bpre);
       ok = wait_chunk(c + 1) && ok;
       __syncthreads();
-      scale_columns(Tt, set(c + 1) + FwdSmem::Xt, bsm[(c + 1) & 1]);
+      scale_columns_twice(TT, set(c + 1) + FwdSmem::Xt, bsm[(c + 1) & 1]);
     }
-    if (tid == 0) bulk_wait_read();  // the checkpoint has left Ha before the readout rewrites it
+    if (tid == 0) bulk_wait_read();  // the checkpoint has left Ha before it is rewritten
     publish();
     if (tid == 0 && ok) {
-      const uint32_t id_dk = idesc_bf16(128, 128, 0, 1);  // H^T += delta^T K (B MN-major)
-      mma_seq<4, 0, 128, 1, 64>(tm + F_H, sD, sK, id_dk, 1u);
-      const uint32_t id_pd = idesc_bf16(64, 128, 0, 0);  // O += P delta
-      mma_seq<4, 0, 64, 0, 128>(tm + F_O, sP, sD, id_pd, 1u);
-      if (more) issue_state_free(c + 1);
-      umma_commit(&bar);
+      mma_seq<4, 1, 64, 1, 64>(tm + F_H, sD, sK, id_hk, 1u);     // H^T += delta^T K
+      umma_commit(&barH);
+      mma_seq<4, 0, 64, 1, 64>(tm + F_O, sP, sD, id_pd, 1u);     // O += P delta
+      if (more) mma_seq<4, 0, 128, 1, 64>(tm + F_U, sTT, smem_u32(set(c + 1) + FwdSmem::Vt), id_uw, 0u);
+      umma_commit(&barC);
     }
-    ok = ok && mma_wait(&bar, phase, status);
+    ok = ok && mma_wait(&barH, pH, status);
     {
-      // O rows: lanes 0-15 of each warp hold tokens t = 16 w + l
-      const int t = warp * 16 + (lane & 15);
-      tmem_row_to_global(lane_tm, F_O, o + (a.row0 + t) * ld + (int64_t)h * D, D, lane < 16 && t < a.valid);
-      tmem_row_to_tile(lane_tm, F_H, Ha, 128, tid);
-      if (!more) tmem_row_to_column(lane_tm, F_H, sn + (int64_t)bh * D * D, D, tid);
+      // H^T row j -> bf16 Ha (and the final state)
+      const int c0 = half * 64;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v[32];
+        tmem_ld32(lane_tm + (uint32_t)(F_H + c0 + 32 * k), v);
+        tmem_wait_ld();
+        st_row32_bf16(Ha, 128, lane128, c0 + 32 * k, v);
+        if (!more && lane128 < D) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c0 + 32 * k + e < D) sn[(int64_t)bh * D * D + (int64_t)(c0 + 32 * k + e) * D + lane128] = v[e];
+        }
+      }
     }
-    if (more) readout_state_free();
+    ok = ok && mma_wait(&barC, pC, status);
+    if (c + 2 < NC) load_chunk(c + 2);  // set (c & 1) is free: every product of chunk c is done
+    {
+      // O rows (M=64 layout: lanes 0-15 of each quarter hold t = 16 quarter + lane) staged in
+      // Dr (free once the state update has completed) for one TMA store
+      const int t = quarter * 16 + (lane & 15);
+      const int c0 = half * 64;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v[32];
+        tmem_ld32(lane_tm + (uint32_t)(F_O + c0 + 32 * k), v);
+        tmem_wait_ld();
+        if (lane < 16) st_row32_bf16(Dr, 64, t, c0 + 32 * k, v);
+      }
+    }
+    if (more) readout_w();
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tma_store_4d(&omap, Dr, 0, h, a.t0, b);
+      if (D > 64) tma_store_4d(&omap, Dr + TILE_TD / 2, 64, h, a.t0, b);
+      bulk_commit();
+      bulk_wait_read();  // Dr is rewritten by the next chunk's delta readout
+    }
     publish();
   }
-  if (NC == 0) {
-    const int j = tid;
+  if (NC == 0 && half == 0) {
+    const int j = lane128;
     if (j < D)
       for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = s0[(int64_t)bh * D * D + (int64_t)i * D + j];
   }
@@ -446,32 +449,35 @@ __global__ void __launch_bounds__(NT, 1) scan_fwd_kernel(
 }
 
 // ------------------------------------------------------------------------------------------
-// backward, sequential: dH^T chain in tensor memory; checkpoints dH_{c+1} per chunk. Pipelined
-// like the forward, in reverse chunk order:
-//   B_c: ddelta_c^T = dH^T K_c^T + dO_c^T P_c, dH^T += dO_c^T Q_c      -> ddelta_c
-//   C_c: dH^T -= ddelta_c^T W_c, and W^T, Q K^T of chunk c-1
+// backward, sequential (256 threads): the dH^T chain in tensor memory, in reverse chunk order,
+// checkpointing the bf16 dH_{c+1} per chunk:
+//   B:  ddelta^T = dH^T K^T;  [ddelta^T | dH^T] += dO^T [P | Q]    (N = 192)
+//   C1: dH^T -= ddelta^T W                                          -> bf16 copy of dH
+//   C2: W of chunk c-1 = T' K                                       -> staged for the next C1
 // ------------------------------------------------------------------------------------------
 struct DhSmem {
-  static constexpr uint32_t SET = 3 * TILE_TD + TILE_TT;  // K, Q, dO, X
-  static constexpr uint32_t Kt = 0, Qt = TILE_TD, Gt = 2 * TILE_TD, Xt = 3 * TILE_TD;
-  static constexpr uint32_t Tt = 2 * SET, Pt = Tt + TILE_TT, Wk = Pt + TILE_TT,
-                            Ha = Wk + TILE_JT, Da = Ha + TILE_JI, END = Da + TILE_JT;
+  // per-chunk input set: X, then P immediately before Q (the MN-major B operand [P | Q]), K, dO
+  static constexpr uint32_t Xt = 0, Pt = TILE_TT, Qt = 2 * TILE_TT, Kt = Qt + TILE_TD, Gt = Kt + TILE_TD;
+  static constexpr uint32_t SET = Gt + TILE_TD;  // 64 KB
+  static constexpr uint32_t Tt = 2 * SET, Wk = Tt + TILE_TT, Ha = Wk + TILE_TD, Da = Ha + TILE_JI,
+                            END = Da + TILE_JT;
 };
-constexpr int G_H = 0, G_W = 128, G_D = 192, G_QK = 256;
+constexpr int G_D = 0, G_H = 64, G_W = 192;
 
-__global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
+__global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap gmap, const bf16* __restrict__ beta,
     const uint8_t* __restrict__ xt, const float* __restrict__ dsn,
     float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Tt = sm + DhSmem::Tt, *Pt = sm + DhSmem::Pt, *Wk = sm + DhSmem::Wk;
-  uint8_t *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
+  uint8_t *Tt = sm + DhSmem::Tt, *Wk = sm + DhSmem::Wk, *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
   __shared__ float bsm[2][C];
-  __shared__ uint64_t bar, lbar[2];
+  __shared__ uint64_t barB, barH, barC, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int lane128 = quarter * 32 + lane;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   bf16 bpre = __float2bfloat16_rn(0.f);
   uint32_t lphase[2] = {0u, 0u};
@@ -481,11 +487,11 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     uint8_t* s = set(c);
     if (tid == 0) {
       uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + TILE_TT);
-      tma_tile(s + DhSmem::Kt, &kmap, lb, h, a.t0, b);
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES);
+      bulk_load(s + DhSmem::Xt, xt + ((size_t)bh * NC + c) * PREP_BYTES, PREP_BYTES, lb);
       tma_tile(s + DhSmem::Qt, &qmap, lb, h, a.t0, b);
+      tma_tile(s + DhSmem::Kt, &kmap, lb, h, a.t0, b);
       tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
-      bulk_load(s + DhSmem::Xt, xt + ((size_t)bh * NC + c) * TILE_TT, TILE_TT, lb);
     }
     bpre = fetch_beta(beta + h, a.row0, H, a.valid);
   };
@@ -495,30 +501,36 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     if (!r && tid == 0) atomicOr(status, 4);
     return r;
   };
-  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_fence_init(); }
+  if (tid == 0) {
+    mbar_init(&barB, 1); mbar_init(&barH, 1); mbar_init(&barC, 1);
+    mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
+    mbar_fence_init();
+  }
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
   __syncthreads();
   if (NC > 0) load_chunk(NC - 1);
-  tc_fence_before();
-  __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);
-  column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, tid, lane_tm, G_H, Ha);
-  const uint32_t sT = smem_u32(Tt), sP = smem_u32(Pt), sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
-  const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
-  const uint32_t id_qk = idesc_bf16(64, 64, 0, 0);
-  auto issue_state_free = [&](int c) {  // W^T, Q K^T of chunk c (thread 0)
-    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sQ = smem_u32(set(c) + DhSmem::Qt);
-    mma_seq<4, 1, 64, 0, 64>(tm + G_W, sK, sT, id_tn, 0u);
-    mma_seq<8, 0, 64, 0, 64>(tm + G_QK, sQ, sK, id_qk, 0u);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
+  if (half == 0)
+    column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, lane128, lane_tm, G_H, Ha);
+  const uint32_t sT = smem_u32(Tt), sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
+  const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);       // ddelta^T = dH^T K^T
+  const uint32_t id_opq = idesc_bf16(128, 192, 1, 1);     // [ddelta^T | dH^T] += dO^T [P | Q]
+  const uint32_t id_dw = idesc_bf16(128, 128, 0, 1, 1);   // dH^T -= ddelta^T W
+  const uint32_t id_tk = idesc_bf16(64, 128, 0, 1);       // W = T' K
+  auto readout_w = [&]() {  // W rows (M=64 layout) -> Wk [t][i]
+    const int t = quarter * 16 + (lane & 15);
+    const int c0 = half * 64;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float v[32];
+      tmem_ld32(lane_tm + (uint32_t)(G_W + c0 + 32 * k), v);
+      tmem_wait_ld();
+      if (lane < 16) st_row32_bf16(Wk, 64, t, c0 + 32 * k, v);
+    }
   };
-  auto readout_state_free = [&]() {
-    tmem_row64_to_tile(lane_tm, G_W, Wk, 128, tid, true);  // W^T row i: K-major B [i][t]
-    const int t = warp * 16 + (lane & 15);
-    tmem_row64_to_tile(lane_tm, G_QK, Pt, 64, t, lane < 16, t);
-  };
-  uint32_t phase = 0;
+  uint32_t pB = 0, pH = 0, pC = 0;
   bool ok = true;
   if (NC > 0) {
     if (tid < C) bsm[(NC - 1) & 1][tid] = __bfloat162float(bpre);
@@ -527,33 +539,35 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     scale_columns(Tt, set(NC - 1) + DhSmem::Xt, bsm[(NC - 1) & 1]);
     publish();
     if (tid == 0) {
-      issue_state_free(NC - 1);
-      umma_commit(&bar);
+      mma_seq<4, 0, 64, 1, 64>(tm + G_W, sT, smem_u32(set(NC - 1) + DhSmem::Kt), id_tk, 0u);
+      umma_commit(&barC);
     }
-    ok = mma_wait(&bar, phase, status);
-    readout_state_free();
+    ok = mma_wait(&barC, pC, status) && ok;
+    if (NC > 1) load_chunk(NC - 2);
+    readout_w();
     publish();
   }
   for (int c = NC - 1; c >= 0 && ok; --c) {
     const bool more = c > 0;
-    if (more) load_chunk(c - 1);
     if (tid == 0) {  // checkpoint dH_{c+1}
       bulk_store(dhck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
       bulk_commit();
     }
-    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sQ = smem_u32(set(c) + DhSmem::Qt);
+    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sP = smem_u32(set(c) + DhSmem::Pt);
     const uint32_t sG = smem_u32(set(c) + DhSmem::Gt);
     if (tid == 0) {
-      const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);  // ddelta^T = dH^T K^T
-      mma_seq<8, 0, 128, 0, 64>(tm + G_D, sH, sK, id_hk, 0u);
-      const uint32_t id_op = idesc_bf16(128, 64, 1, 1);  // += dO^T (MN) x P (MN)
-      mma_seq<4, 1, 64, 1, 64>(tm + G_D, sG, sP, id_op, 1u);
-      const uint32_t id_oq = idesc_bf16(128, 128, 1, 1);  // dH^T += dO^T Q
-      mma_seq<4, 1, 64, 1, 64>(tm + G_H, sG, sQ, id_oq, 1u);
-      umma_commit(&bar);
+      mma_seq<8, 0, 128, 0, 64>(tm + G_D, sH, sK, id_hk, 0u);   // ddelta^T = dH^T K^T
+      mma_seq<4, 1, 64, 1, 64>(tm + G_D, sG, sP, id_opq, 1u);   // [ddelta^T | dH^T] += dO^T [P | Q]
+      umma_commit(&barB);
     }
-    ok = mma_wait(&bar, phase, status);
-    tmem_row64_to_tile(lane_tm, G_D, Da, 128, tid, true);  // ddelta^T row j
+    ok = mma_wait(&barB, pB, status) && ok;
+    {
+      const int c0 = half * 32;
+      float v[32];
+      tmem_ld32(lane_tm + (uint32_t)(G_D + c0), v);
+      tmem_wait_ld();
+      st_row32_bf16(Da, 128, lane128, c0, v);  // ddelta^T row j
+    }
     if (more) {
       if (tid < C) bsm[(c - 1) & 1][tid] = __bfloat162float(bpre);
       ok = wait_chunk(c - 1) && ok;
@@ -563,19 +577,34 @@ __global__ void __launch_bounds__(NT, 1) scan_dh_kernel(
     if (tid == 0) bulk_wait_read();
     publish();
     if (tid == 0 && ok) {
-      const uint32_t id_dw = idesc_bf16(128, 128, 0, 0, 1);  // dH^T -= ddelta^T W
-      mma_seq<4, 0, 128, 0, 128>(tm + G_H, sD, sW, id_dw, 1u);
-      if (more) issue_state_free(c - 1);
-      umma_commit(&bar);
+      mma_seq<4, 0, 128, 1, 64>(tm + G_H, sD, sW, id_dw, 1u);   // dH^T -= ddelta^T W
+      umma_commit(&barH);
+      if (more) mma_seq<4, 0, 64, 1, 64>(tm + G_W, sT, smem_u32(set(c - 1) + DhSmem::Kt), id_tk, 0u);
+      umma_commit(&barC);
     }
-    ok = ok && mma_wait(&bar, phase, status);
-    tmem_row_to_tile(lane_tm, G_H, Ha, 128, tid);
-    if (c == 0) tmem_row_to_column(lane_tm, G_H, ds0 + (int64_t)bh * D * D, D, tid);
-    if (more) readout_state_free();
+    ok = ok && mma_wait(&barH, pH, status);
+    {
+      const int c0 = half * 64;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v[32];
+        tmem_ld32(lane_tm + (uint32_t)(G_H + c0 + 32 * k), v);
+        tmem_wait_ld();
+        st_row32_bf16(Ha, 128, lane128, c0 + 32 * k, v);
+        if (c == 0 && lane128 < D) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c0 + 32 * k + e < D) ds0[(int64_t)bh * D * D + (int64_t)(c0 + 32 * k + e) * D + lane128] = v[e];
+        }
+      }
+    }
+    ok = ok && mma_wait(&barC, pC, status);
+    if (c >= 2) load_chunk(c - 2);  // set (c & 1) is free: every product of chunk c is done
+    if (more) readout_w();
     publish();
   }
-  if (NC == 0) {
-    const int j = tid;
+  if (NC == 0 && half == 0) {
+    const int j = lane128;
     if (j < D)
       for (int i = 0; i < D; ++i)
         ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = dsn ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
@@ -599,7 +628,7 @@ struct GrSmem {
   // Y over Vt (dead after dT'), dGs over Pt (dead after ddelta), float scratch over Ht (dead
   // after dQ and dW)
 };
-constexpr int R_KK = 0, R_QK = 64, R_W = 128, R_U = 192, R_DD = 256, R_X = 320;   // batches 1-2
+constexpr int R_KK = 0, R_W = 128, R_U = 192, R_DD = 256, R_X = 320;   // batches 1-2
 constexpr int R_DP = 64, R_DW = 128, R_DV = 256, R_DT = 384;                      // batch 3
 constexpr int R_DQ = 128, R_Y = 256, R_Z = 320, R_DK = 128;                       // batches 4-7
 
@@ -635,14 +664,15 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
   __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + TILE_TT);
+    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + 2 * TILE_TT);
     tma_tile(Qt, &qmap, &lbar, h, t0, b);
     tma_tile(Kt, &kmap, &lbar, h, t0, b);
     tma_tile(Vt, &vmap, &lbar, h, t0, b);
     tma_tile(Gt, &gmap, &lbar, h, t0, b);
     bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar);
     bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar);
-    bulk_load(Xt, xt + chunk * TILE_TT, TILE_TT, &lbar);
+    bulk_load(Xt, xt + chunk * PREP_BYTES, TILE_TT, &lbar);
+    bulk_load(Pt, xt + chunk * PREP_BYTES + TILE_TT, TILE_TT, &lbar);
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
@@ -664,7 +694,6 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   if (tid == 0) {
     const uint32_t id64 = idesc_bf16(64, 64, 0, 0);
     mma_seq<8, 0, 64, 0, 64>(tm + R_KK, sK, sK, id64, 0u);
-    mma_seq<8, 0, 64, 0, 64>(tm + R_QK, sQ, sK, id64, 0u);
     const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
     mma_seq<4, 1, 64, 0, 64>(tm + R_W, sK, sT, id_tn, 0u);
     mma_seq<4, 1, 64, 0, 64>(tm + R_U, sV, sT, id_tn, 0u);
@@ -677,13 +706,6 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
     float w[64];
     ld64(lane_tm, R_W, w);
     st_row64_bf16(Wr, 128, tid, 0, w);
-    float p[64];
-    ld64(lane_tm, R_QK, p);
-    if (rowlane) {
-#pragma unroll
-      for (int s = 0; s < 64; ++s) p[s] = s <= trow ? p[s] : 0.f;
-      st_row64_bf16(Pt, 64, trow, 0, p);
-    }
   }
   publish();
   // batch 2: X = H^T W^T; ddelta^T += dO^T P
@@ -894,7 +916,7 @@ extern "C" size_t vb_delta_scan_bf16_saved_bytes(int B, int T, int H, int D) {
   (void)D;
   const size_t seqs = (size_t)(B > 0 ? B : 0) * (size_t)(H > 0 ? H : 0);
   const size_t nc = (size_t)nchunks(T > 0 ? T : 0);
-  const size_t n = seqs * nc * (TILE_TT + TILE_JI);
+  const size_t n = seqs * nc * (PREP_BYTES + TILE_JI);
   return n > 0 ? n : 16;
 }
 
@@ -916,23 +938,24 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
   cudaStream_t st = (cudaStream_t)stream;
   const int NC = nchunks(T);
   uint8_t* xt = (uint8_t*)saved;
-  uint8_t* hck = xt + (size_t)B * H * NC * TILE_TT;
-  CUtensorMap qm, km, vm;
+  uint8_t* hck = xt + (size_t)B * H * NC * PREP_BYTES;
+  CUtensorMap qm, km, vm, om;
+  memset(&om, 0, sizeof(om));
   if (NC > 0) {
     if ((rc = make_token_map(&qm, q, B, T, H, D)) || (rc = make_token_map(&km, k, B, T, H, D)) ||
-        (rc = make_token_map(&vm, v, B, T, H, D)))
+        (rc = make_token_map(&vm, v, B, T, H, D)) || (rc = make_token_map(&om, o, B, T, H, D)))
       return rc;
-    const size_t sp = smem_bytes(TILE_TD + TILE_TT + 64 * 65 * 4);
+    const size_t sp = smem_bytes(TILE_JI + 2 * TILE_TT + 64 * 65 * 4);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp), "prep attr");
-    scan_prep_kernel<<<B * H * NC, NT, sp, st>>>(km, (const bf16*)beta, xt, T, H, D, NC, status);
+    scan_prep_kernel<<<B * H * NC, NT, sp, st>>>(qm, km, (const bf16*)beta, xt, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 prep");
   } else {
     memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm));
   }
   const size_t sf = smem_bytes(FwdSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sf), "fwd attr");
-  scan_fwd_kernel<<<B * H, NT, sf, st>>>(qm, km, vm, (const bf16*)beta,
-                                         state0, xt, (bf16*)o, state_n, hck, T, H, D, NC, status);
+  scan_fwd_kernel<<<B * H, NT2, sf, st>>>(qm, km, vm, om, (const bf16*)beta,
+                                         state0, xt, state_n, hck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 fwd");
   return VB_OK;
 }
@@ -951,7 +974,7 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   cudaStream_t st = (cudaStream_t)stream;
   const int NC = nchunks(T);
   const uint8_t* xt = (const uint8_t*)saved;
-  const uint8_t* hck = xt + (size_t)B * H * NC * TILE_TT;
+  const uint8_t* hck = xt + (size_t)B * H * NC * PREP_BYTES;
   uint8_t* dhck = (uint8_t*)workspace;
   CUtensorMap qm, km, vm, gm;
   if (NC > 0) {
@@ -963,7 +986,7 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   }
   const size_t sd = smem_bytes(DhSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd), "dh attr");
-  scan_dh_kernel<<<B * H, NT, sd, st>>>(qm, km, gm, (const bf16*)beta, xt,
+  scan_dh_kernel<<<B * H, NT2, sd, st>>>(qm, km, gm, (const bf16*)beta, xt,
                                         dstate_n, dstate0, dhck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 dh");
   if (NC > 0) {

@@ -200,6 +200,13 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                "r"(bytes)
                : "memory");
 }
+// tiled 4-D tensor store from shared memory (bulk async-group); rows outside the tensor are skipped
+__device__ __forceinline__ void tma_store_4d(const void* map, const void* src, int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(map),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // the issuing thread's bulk stores have finished reading shared memory
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
