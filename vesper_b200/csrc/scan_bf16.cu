@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   __shared__ float bsm[C];
   __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
   const int t0 = c * C, valid = min(C, T - t0);
   const int64_t row0 = (int64_t)b * T + t0;
