@@ -12,50 +12,62 @@
 namespace vb {
 namespace {
 
-constexpr int WARPS = 8;          // rows in flight per CTA (forward) / warps per CTA (backward)
-constexpr int MAXV = 8;           // 16-byte vectors per lane in the vector path
-constexpr int BWD_ROWS_PER_WARP = 8;
+constexpr int WARPS = 8;          // warps per CTA (forward rows in flight; backward warps)
+constexpr int FWD_ROWS_PER_WARP = 2;   // rows each forward warp loads before computing
+constexpr int BWD_WARPS = 4;
+constexpr int BWD_ROWS_PER_WARP = 16;
+constexpr int BWD_ROWS_PER_CTA = BWD_WARPS * BWD_ROWS_PER_WARP;
 
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict__ x,
-                                                             const float* __restrict__ w,
-                                                             T* __restrict__ y, float* __restrict__ inv,
-                                                             int64_t rows, int width, float floor_,
-                                                             float eps) {
+// 16-byte vector loads of E = 16/sizeof(T) elements; VPL vectors per lane cover 32*E*VPL channels
+template <typename T, int VPL>
+__device__ __forceinline__ void load_row(const T* __restrict__ row, int nv, int lane, float (&v)[VPL][16 / sizeof(T)]) {
+  constexpr int E = 16 / sizeof(T);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nv) load_vec<T, E>(row + vi * E, v[i]);
+    else {
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[i][e] = 0.f;
+    }
+  }
+}
+
+template <typename T, int VPL>
+__global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const T* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 T* __restrict__ y, float* __restrict__ inv,
+                                                                 int64_t rows, int width, float floor_,
+                                                                 float eps) {
+  constexpr int E = 16 / sizeof(T);
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const T* xr = x + row * width;
-  T* yr = y + row * width;
-  if constexpr (VEC) {
-    constexpr int E = 16 / sizeof(T);
-    const int nv = width / E;
-    float v[MAXV][E];
+  const int64_t row0 = ((int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5)) * FWD_ROWS_PER_WARP;
+  const int nv = width / E;
+  float v[FWD_ROWS_PER_WARP][VPL][E];
+#pragma unroll
+  for (int r = 0; r < FWD_ROWS_PER_WARP; ++r)
+    if (row0 + r < rows) load_row<T, VPL>(x + (row0 + r) * width, nv, lane, v[r]);
+#pragma unroll
+  for (int r = 0; r < FWD_ROWS_PER_WARP; ++r) {
+    const int64_t row = row0 + r;
+    if (row >= rows) break;
     float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = lane + 32 * i;
-      if (vi < nv) {
-        load_vec<T, E>(xr + vi * E, v[i]);
+    for (int i = 0; i < VPL; ++i)
 #pragma unroll
-        for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
-      }
-    }
+      for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(v[r][i][e]));
     const float scale = fmaxf(warp_max(amax), floor_);
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      if (lane + 32 * i < nv) {
+    for (int i = 0; i < VPL; ++i)
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const float z = v[i][e] / scale;
-          ss += z * z;
-        }
+      for (int e = 0; e < E; ++e) {
+        const float z = v[r][i][e] / scale;
+        ss += z * z;
       }
-    }
     const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
+    for (int i = 0; i < VPL; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
         float g[E], o[E];
@@ -66,43 +78,135 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict
           g[4 * q] = g4.x; g[4 * q + 1] = g4.y; g[4 * q + 2] = g4.z; g[4 * q + 3] = g4.w;
         }
 #pragma unroll
-        for (int e = 0; e < E; ++e) o[e] = v[i][e] / scale / rms * g[e];
-        store_vec<T, E>(yr + vi * E, o);
+        for (int e = 0; e < E; ++e) o[e] = v[r][i][e] / scale / rms * g[e];
+        store_vec<T, E>(y + row * width + vi * E, o);
       }
     }
-    if (lane == 0) inv[row] = 1.0f / (scale * rms);
-  } else {
-    float amax = 0.f;
-    for (int j = lane; j < width; j += 32) amax = fmaxf(amax, fabsf(to_f32<T>(xr[j])));
-    const float scale = fmaxf(warp_max(amax), floor_);
-    float ss = 0.f;
-    for (int j = lane; j < width; j += 32) {
-      const float z = to_f32<T>(xr[j]) / scale;
-      ss += z * z;
-    }
-    const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
-    for (int j = lane; j < width; j += 32)
-      yr[j] = from_f32<T>(to_f32<T>(xr[j]) / scale / rms * __ldg(w + j));
     if (lane == 0) inv[row] = 1.0f / (scale * rms);
   }
 }
 
-// dx per row; the gain's gradient per CTA into partial[blockIdx.x][width].
 template <typename T>
-__global__ void __launch_bounds__(WARPS * 32) rms_bwd_kernel(const T* __restrict__ x,
+__global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict__ x,
                                                              const float* __restrict__ w,
-                                                             const T* __restrict__ dy,
-                                                             const float* __restrict__ inv,
-                                                             T* __restrict__ dx,
-                                                             float* __restrict__ partial,
-                                                             int64_t rows, int width) {
-  extern __shared__ float acc[];  // [WARPS][width]
+                                                             T* __restrict__ y, float* __restrict__ inv,
+                                                             int64_t rows, int width, float floor_,
+                                                             float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + row * width;
+  T* yr = y + row * width;
+  float amax = 0.f;
+  for (int j = lane; j < width; j += 32) amax = fmaxf(amax, fabsf(to_f32<T>(xr[j])));
+  const float scale = fmaxf(warp_max(amax), floor_);
+  float ss = 0.f;
+  for (int j = lane; j < width; j += 32) {
+    const float z = to_f32<T>(xr[j]) / scale;
+    ss += z * z;
+  }
+  const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
+  for (int j = lane; j < width; j += 32) yr[j] = from_f32<T>(to_f32<T>(xr[j]) / scale / rms * __ldg(w + j));
+  if (lane == 0) inv[row] = 1.0f / (scale * rms);
+}
+
+// Vector backward: each warp walks BWD_ROWS_PER_WARP rows with the next row's x and dy loaded
+// while the current one is computed; the gain gradient stays in registers per lane, then is
+// summed over the CTA's warps in warp order into partial[blockIdx.x][width].
+template <typename T, int VPL>
+__global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __restrict__ x,
+                                                                     const float* __restrict__ w,
+                                                                     const T* __restrict__ dy,
+                                                                     const float* __restrict__ inv,
+                                                                     T* __restrict__ dx,
+                                                                     float* __restrict__ partial,
+                                                                     int64_t rows, int width) {
+  constexpr int E = 16 / sizeof(T);
+  extern __shared__ float acc_s[];  // [BWD_WARPS][width]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = width / E;
+  float acc[VPL][E];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[i][e] = 0.f;
+  const int64_t row0 = (int64_t)blockIdx.x * BWD_ROWS_PER_CTA;
+  float xv[2][VPL][E], dv[2][VPL][E];
+  int64_t row = row0 + warp;
+  if (row < rows) {
+    load_row<T, VPL>(x + row * width, nv, lane, xv[0]);
+    load_row<T, VPL>(dy + row * width, nv, lane, dv[0]);
+  }
+#pragma unroll 2
+  for (int k = 0; k < BWD_ROWS_PER_WARP; ++k) {
+    const int cur = k & 1;
+    row = row0 + (int64_t)k * BWD_WARPS + warp;
+    if (row >= rows) break;
+    const int64_t nrow = row + BWD_WARPS;
+    if (k + 1 < BWD_ROWS_PER_WARP && nrow < rows) {
+      load_row<T, VPL>(x + nrow * width, nv, lane, xv[cur ^ 1]);
+      load_row<T, VPL>(dy + nrow * width, nv, lane, dv[cur ^ 1]);
+    }
+    const float iv = __ldg(inv + row);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) s += dv[cur][i][e] * __ldg(w + vi * E + e) * (xv[cur][i][e] * iv);
+      }
+    }
+    const float mean = warp_sum(s) / (float)width;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float o[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float xh = xv[cur][i][e] * iv;
+          const float d = dv[cur][i][e];
+          o[e] = iv * (d * __ldg(w + vi * E + e) - xh * mean);
+          acc[i][e] += d * xh;
+        }
+        store_vec<T, E>(dx + row * width + vi * E, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nv) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc_s[(size_t)warp * width + vi * E + e] = acc[i][e];
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < width; j += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < BWD_WARPS; ++q) t += acc_s[(size_t)q * width + j];
+    partial[(size_t)blockIdx.x * width + j] = t;
+  }
+}
+
+// Scalar backward for widths without a 16-byte vector path.
+template <typename T>
+__global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_kernel(const T* __restrict__ x,
+                                                                 const float* __restrict__ w,
+                                                                 const T* __restrict__ dy,
+                                                                 const float* __restrict__ inv,
+                                                                 T* __restrict__ dx,
+                                                                 float* __restrict__ partial,
+                                                                 int64_t rows, int width) {
+  extern __shared__ float acc[];  // [BWD_WARPS][width]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float* mine = acc + (size_t)warp * width;
   for (int j = lane; j < width; j += 32) mine[j] = 0.f;
-  const int64_t row0 = (int64_t)blockIdx.x * WARPS * BWD_ROWS_PER_WARP;
+  const int64_t row0 = (int64_t)blockIdx.x * BWD_ROWS_PER_CTA;
   for (int k = 0; k < BWD_ROWS_PER_WARP; ++k) {
-    const int64_t row = row0 + (int64_t)k * WARPS + warp;
+    const int64_t row = row0 + (int64_t)k * BWD_WARPS + warp;
     if (row >= rows) break;
     const T* xr = x + row * width;
     const T* dr = dy + row * width;
@@ -125,7 +229,7 @@ __global__ void __launch_bounds__(WARPS * 32) rms_bwd_kernel(const T* __restrict
   for (int j = threadIdx.x; j < width; j += blockDim.x) {
     float t = 0.f;
 #pragma unroll
-    for (int q = 0; q < WARPS; ++q) t += acc[(size_t)q * width + j];
+    for (int q = 0; q < BWD_WARPS; ++q) t += acc[(size_t)q * width + j];
     partial[(size_t)blockIdx.x * width + j] = t;
   }
 }
@@ -150,10 +254,28 @@ __global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict
   }
 }
 
-int bwd_ctas(int64_t rows) {
-  const int64_t per = (int64_t)WARPS * BWD_ROWS_PER_WARP;
-  return (int)((rows + per - 1) / per);
+int bwd_ctas(int64_t rows) { return (int)((rows + BWD_ROWS_PER_CTA - 1) / BWD_ROWS_PER_CTA); }
+
+// vectors per lane of the vector paths: 16-byte vectors of E elements, 32 lanes
+template <typename T>
+int vpl_for(int width) {
+  constexpr int E = 16 / sizeof(T);
+  if (width % E) return 0;
+  const int nv = width / E;
+  for (int v : {1, 2, 4, 8})
+    if (nv <= 32 * v) return v;
+  return 0;
 }
+
+#define VB_VPL_DISPATCH(vpl, VPL, ...)                               \
+  [&]() -> int {                                                     \
+    switch (vpl) {                                                   \
+      case 1: { constexpr int VPL = 1; return __VA_ARGS__(); }       \
+      case 2: { constexpr int VPL = 2; return __VA_ARGS__(); }       \
+      case 4: { constexpr int VPL = 4; return __VA_ARGS__(); }       \
+      default: { constexpr int VPL = 8; return __VA_ARGS__(); }      \
+    }                                                                \
+  }()
 
 }  // namespace
 
@@ -162,6 +284,32 @@ int column_sum(const float* partial, float* out, int parts, int width, cudaStrea
   column_sum_kernel<<<(width + 31) / 32, 256, 0, st>>>(partial, out, parts, width);
   VB_LAUNCH_CHECK("column_sum");
   return VB_OK;
+}
+
+// dx and the per-CTA gain partials (vector path when the width allows), then the fixed-order sum
+int launch_bwd(const void* x, const float* weight, const void* dy, const float* inv, void* dx, float* dweight,
+               float* partial, int64_t rows, int width, int dtype, cudaStream_t st) {
+  const int ctas = bwd_ctas(rows);
+  const size_t smem = sizeof(float) * BWD_WARPS * width;
+  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
+    const int vpl = vpl_for<T>(width);
+    if (vpl && aligned16(x) && aligned16(dy) && aligned16(dx)) {
+      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
+        if (smem > 48 * 1024)
+          cudaFuncSetAttribute(rms_bwd_vec_kernel<T, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        rms_bwd_vec_kernel<T, VPL><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
+                                                                       (T*)dx, partial, rows, width);
+        return 0;
+      });
+    } else {
+      if (smem > 48 * 1024)
+        cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      rms_bwd_kernel<T><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv, (T*)dx,
+                                                            partial, rows, width);
+    }
+    VB_LAUNCH_CHECK("rms_norm_bwd");
+    return column_sum(partial, dweight, ctas, width, st);
+  });
 }
 
 }  // namespace vb
@@ -174,17 +322,21 @@ extern "C" int vb_rms_norm_fwd(const void* x, const float* weight, void* y, floa
   if (rows == 0) return VB_OK;
   VB_REQUIRE(x && weight && y && inv, "rms_norm_fwd: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  const int ctas = (int)((rows + WARPS - 1) / WARPS);
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    constexpr int E = 16 / sizeof(T);
-    const bool vec = width % E == 0 && width <= 32 * MAXV * E && aligned16(x) && aligned16(y) &&
-                     aligned16(weight);
-    if (vec)
-      rms_fwd_kernel<T, true><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
-                                                           width, floor_, eps);
-    else
-      rms_fwd_kernel<T, false><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
-                                                            width, floor_, eps);
+    const int vpl = vpl_for<T>(width);
+    if (vpl && aligned16(x) && aligned16(y) && aligned16(weight)) {
+      const int64_t per = (int64_t)WARPS * FWD_ROWS_PER_WARP;
+      const int ctas = (int)((rows + per - 1) / per);
+      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
+        rms_fwd_vec_kernel<T, VPL><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
+                                                                width, floor_, eps);
+        return 0;
+      });
+    } else {
+      const int ctas = (int)((rows + WARPS - 1) / WARPS);
+      rms_fwd_kernel<T><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows, width,
+                                                     floor_, eps);
+    }
     VB_LAUNCH_CHECK("rms_norm_fwd");
     return VB_OK;
   });
@@ -206,15 +358,7 @@ extern "C" int vb_rms_norm_bwd(const void* x, const float* weight, const void* d
   }
   VB_REQUIRE(x && weight && dy && inv && dx && dweight && workspace, "rms_norm_bwd: null pointer");
   const int ctas = bwd_ctas(rows);
-  const size_t smem = sizeof(float) * WARPS * width;
-  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    rms_bwd_kernel<T><<<ctas, WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
-                                                      (T*)dx, (float*)workspace, rows, width);
-    VB_LAUNCH_CHECK("rms_norm_bwd");
-    return column_sum((const float*)workspace, dweight, ctas, width, st);
-  });
+  return launch_bwd(x, weight, dy, inv, dx, dweight, (float*)workspace, rows, width, dtype, st);
 }
 
 // ---- RMSNorm backward without allocation ------------------------------------------------------
@@ -260,7 +404,7 @@ extern "C" int vb_rms_norm_bwd_noalloc(const void* x, const float* weight, const
              "scratch of %zu floats (at this width at most %lld rows); use vb_rms_norm_bwd with a "
              "workspace",
              (long long)rows, width, (size_t)ctas * (size_t)width, NOALLOC_PARTIAL_FLOATS,
-             (long long)(NOALLOC_PARTIAL_FLOATS / (size_t)width) * WARPS * BWD_ROWS_PER_WARP);
+             (long long)(NOALLOC_PARTIAL_FLOATS / (size_t)width) * BWD_ROWS_PER_CTA);
   cudaStream_t st = (cudaStream_t)stream;
   if (rows == 0) {
     VB_CUDA_CHECK(cudaMemsetAsync(dweight, 0, sizeof(float) * width, st), "rms_norm_bwd_noalloc");
@@ -271,13 +415,5 @@ extern "C" int vb_rms_norm_bwd_noalloc(const void* x, const float* weight, const
   int rc = scratch_on_current_device(&partial);
   if (rc) return rc;
   // every partial row this call reads is written by this call first: nothing needs clearing
-  const size_t smem = sizeof(float) * WARPS * width;
-  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    rms_bwd_kernel<T><<<ctas, WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
-                                                      (T*)dx, partial, rows, width);
-    VB_LAUNCH_CHECK("rms_norm_bwd_noalloc");
-    return column_sum(partial, dweight, ctas, width, st);
-  });
+  return launch_bwd(x, weight, dy, inv, dx, dweight, partial, rows, width, dtype, st);
 }
