@@ -139,6 +139,32 @@ VB_API int vb_delta_scan_bf16_bwd(const void *q, const void *k, const void *v, c
                                   void *workspace, int *status, int B, int T, int H, int D,
                                   void *stream);
 
+/* ---- windowed attention ------------------------------------------------------------------
+ * Softmax attention of q [B,NQ,H,DK] over keys, values [B,L,HKV,DK] (bf16 or f16 by `dtype`,
+ * DK a multiple of 16 in [16, 128], H a multiple of HKV, 16-byte aligned tensors): query row r
+ * at key index p attends the keys j with p - window < j <= p, scale 1/sqrt(DK), query head h
+ * reading key head h / (H / HKV). `qpos` NULL: p = L - NQ + r (the cache's L - NQ rows come
+ * first, then the chunk; the reference's zero-query padding of the cache rows is not needed).
+ * `qpos` [B,NQ] int32: the positions of compacted query rows, ascending along each batch row;
+ * `counts` [B] int32 (or NULL = NQ) says how many rows of each batch are live, the rest get zero
+ * output and no gradient. `lse` [B,H,NQ] float32 is saved for the backward (base-2 log-sum-exp
+ * of the scaled scores). `status`: as for the scan.
+ * Replaces vesper/kernels/window_attn.py:27-39 (window_attention, which ran fla-core's
+ * parallel_attn) with the semantics of vesper/attention.py:340-407 (WindowedAttention.attend). */
+VB_API int vb_window_attn_fwd(const void *q, const int *qpos, const int *counts, const void *keys,
+                              const void *values, void *o, float *lse, int *status, int B, int NQ,
+                              int L, int H, int HKV, int DK, int window, int dtype, void *stream);
+
+VB_API size_t vb_window_attn_bwd_workspace(int B, int NQ, int H);
+
+/* Gradients of sum(o*dout): dq [B,NQ,H,DK], dkeys, dvalues [B,L,HKV,DK] in the input type, from
+ * the forward's o and lse; deterministic (no atomics). */
+VB_API int vb_window_attn_bwd(const void *q, const int *qpos, const int *counts, const void *keys,
+                              const void *values, const void *o, const float *lse,
+                              const void *dout, void *dq, void *dkeys, void *dvalues,
+                              void *workspace, int *status, int B, int NQ, int L, int H, int HKV,
+                              int DK, int window, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

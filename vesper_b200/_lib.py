@@ -44,6 +44,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_delta_scan_bf16_fwd": (_I, [_P] * 9 + [_I, _I, _I, _I, _P]),
     "vb_delta_scan_bf16_bwd_workspace": (_SZ, [_I, _I, _I, _I]),
     "vb_delta_scan_bf16_bwd": (_I, [_P] * 14 + [_I, _I, _I, _I, _P]),
+    "vb_window_attn_fwd": (_I, [_P] * 8 + [_I] * 8 + [_P]),
+    "vb_window_attn_bwd_workspace": (_SZ, [_I, _I, _I]),
+    "vb_window_attn_bwd": (_I, [_P] * 13 + [_I] * 8 + [_P]),
 }
 
 
@@ -102,3 +105,27 @@ def stream(device: torch.device) -> int:
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     """Scratch memory from torch's caching allocator (graph-capturable, never cudaMalloc here)."""
     return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+
+
+# --- device status word ----------------------------------------------------------------------------
+
+_STATUS: dict[torch.device, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """The int32 the tensor-core kernels OR an error bit into (a bounded wait that gave up)."""
+    word = _STATUS.get(device)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[device] = word
+    return word
+
+
+def check_status(device: torch.device) -> None:
+    """Synchronise and raise if a kernel on ``device`` reported a timeout (never under capture)."""
+    word = _STATUS.get(device)
+    if word is not None and int(word.item()) != 0:
+        value = int(word.item())
+        word.zero_()
+        msg = f"a kernel gave up waiting on the tensor core or a copy (status {value})"
+        raise KernelError(msg)

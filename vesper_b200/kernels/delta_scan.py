@@ -69,28 +69,9 @@ def _checked_length(
     return dims["n"]
 
 
-# --- device status word ----------------------------------------------------------------------------
-
-_STATUS: dict[torch.device, Tensor] = {}
-
-
-def status_word(device: torch.device) -> Tensor:
-    """The int32 the bf16 scan's kernels OR an error bit into (a bounded wait that gave up)."""
-    word = _STATUS.get(device)
-    if word is None:
-        word = torch.zeros(1, dtype=torch.int32, device=device)
-        _STATUS[device] = word
-    return word
-
-
-def check_status(device: torch.device) -> None:
-    """Synchronise and raise if a kernel on ``device`` reported a timeout (never under capture)."""
-    word = _STATUS.get(device)
-    if word is not None and int(word.item()) != 0:
-        value = int(word.item())
-        word.zero_()
-        msg = f"a delta-scan kernel gave up waiting on the tensor core (status {value})"
-        raise _lib.KernelError(msg)
+# the device status word the bf16 scan's kernels report a timeout through (shared by the library)
+status_word = _lib.status_word
+check_status = _lib.check_status
 
 
 # --- bfloat16, chunked on tcgen05 -------------------------------------------------------------------
