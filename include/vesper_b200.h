@@ -165,6 +165,37 @@ VB_API int vb_window_attn_bwd(const void *q, const int *qpos, const int *counts,
                               void *workspace, int *status, int B, int NQ, int L, int H, int HKV,
                               int DK, int window, int dtype, void *stream);
 
+/* ---- the loop's active-token bookkeeping --------------------------------------------------
+ * Per batch row of `active` [B,N] (one byte per token, nonzero = active): idx[b][r] = the r-th
+ * active token (ascending), -1 beyond the count; rank[b][t] = its compact row, -1 for a halted
+ * token; counts[b] = the active count; qpos (optional, may be NULL) = idx + qpos_offset, the
+ * attention's key index of each compact row. Device arrays, no host synchronisation.
+ * Replaces the dense compute of halted tokens in vesper/loop.py:349-465 (Loop.forward), which
+ * computes every position and discards the halted ones (vesper/loop.py:24-26). */
+VB_API int vb_compact_index(const unsigned char *active, int *idx, int *rank, int *counts,
+                            int *qpos, int B, int N, int qpos_offset, void *stream);
+
+/* Row copies over up to 12 tensors in one launch; tensor i is a byte array of rows of
+ * row_bytes[i]; a NULL source pointer (or array) reads as zero bytes.
+ * select: out_i[t] = (mask[t] != 0) != invert ? a_i[t] : b_i[t] over `tokens` rows: the
+ * copy-forward merges of vesper/column.py:140-143 (_carry) and vesper/loop.py:523-537 (_merge),
+ * and the zeroing of inactive rows (vesper/loop.py:427-428), as one launch each. */
+VB_API int vb_select_rows(const unsigned char *mask, int invert, int ntensors,
+                          const void *const *a, const void *const *b, void *const *out,
+                          const long long *row_bytes, long long tokens, void *stream);
+
+/* gather: dst_i[b][r] = src_i[b][idx[b][r]] for r < counts[b] (counts NULL = all NC rows) and an
+ * index inside [0, N); zero otherwise. src_i is [B,N,row], dst_i [B,NC,row]. */
+VB_API int vb_gather_rows(const int *idx, const int *counts, int B, int N, int NC, int ntensors,
+                          const void *const *src, void *const *dst, const long long *row_bytes,
+                          void *stream);
+
+/* expand: dst_i[b][t] = src_i[b][rank[b][t]] where 0 <= rank < NC, else fallback_i[b][t] (NULL =
+ * zero). src_i is [B,NC,row], fallback_i and dst_i [B,N,row]. The inverse of gather. */
+VB_API int vb_expand_rows(const int *rank, int B, int N, int NC, int ntensors,
+                          const void *const *src, const void *const *fallback, void *const *dst,
+                          const long long *row_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_window_attn_fwd": (_I, [_P] * 8 + [_I] * 8 + [_P]),
     "vb_window_attn_bwd_workspace": (_SZ, [_I, _I, _I]),
     "vb_window_attn_bwd": (_I, [_P] * 13 + [_I] * 8 + [_P]),
+    "vb_compact_index": (_I, [_P] * 5 + [_I, _I, _I, _P]),
+    "vb_select_rows": (_I, [_P, _I, _I, _P, _P, _P, _P, ctypes.c_longlong, _P]),
+    "vb_gather_rows": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "vb_expand_rows": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
 }
 
 

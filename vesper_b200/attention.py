@@ -1,0 +1,204 @@
+"""Windowed attention sublayer on a B200 (the contract of ``vesper/attention.py`` of
+mstampfli/vesper-preview): rotary GQA projections, exact softmax over the last ``window`` keys.
+
+Same parameters (``w_q, w_k, w_v, w_o``), layouts and cache semantics as the reference's
+``WindowedAttention`` (``vesper/attention.py:219-407``), ``KVCache`` / ``kv_cache_push``
+(``:30-175``) and ``rotary`` (``:178-217``). In bfloat16 or float16 the softmax runs in the
+tcgen05 kernel (``vesper_b200.kernels.window_attn``) over the cache rows and the chunk directly;
+given the loop's compaction of the active tokens, it computes only their queries. float32 keeps
+the reference's blocked, masked attention (as the reference does), run by torch on the device.
+The decode ring (``RingKVCache``) is not part of this build.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F  # noqa: N812
+from torch import Tensor, nn
+
+from vesper_b200.contracts import ContractError, Dims, check_shape, require
+from vesper_b200.kernels.compact import Compaction, expand_rows, gather_rows
+from vesper_b200.kernels.window_attn import window_attention, window_attention_active
+
+WINDOW_KERNEL_DTYPES = (torch.bfloat16, torch.float16)  # float32 keeps the blocked path
+
+
+@dataclass(frozen=True, slots=True)
+class KVCache:
+    """The last ``m <= window`` entries of one window, oldest first: ``k, v [b, m, hkv, dk]``
+    (keys rotated) and ``pos [b, m]`` int64."""
+
+    k: Tensor
+    v: Tensor
+    pos: Tensor
+    window: int
+
+
+def kv_cache_empty(b: int, hkv: int, dk: int, window: int, dtype: torch.dtype, device: torch.device) -> KVCache:
+    """An empty cache (``m = 0``) for ``window`` entries (``vesper/attention.py:43-63``)."""
+    if window < 1:
+        msg = f"window must be at least 1, got {window}"
+        raise ValueError(msg)
+    return KVCache(
+        k=torch.zeros(b, 0, hkv, dk, dtype=dtype, device=device),
+        v=torch.zeros(b, 0, hkv, dk, dtype=dtype, device=device),
+        pos=torch.zeros(b, 0, dtype=torch.long, device=device),
+        window=window,
+    )
+
+
+def kv_cache_push(cache: KVCache, k: Tensor, v: Tensor, pos: Tensor) -> KVCache:
+    """The newest ``min(m + n, window)`` entries of the cache followed by the chunk
+    (``vesper/attention.py:142-175``); with no new entries, the cache itself."""
+    dims: Dims = {}
+    check_shape("cache.k", cache.k, ("b", "m", "hkv", "dk"), dims)
+    check_shape("cache.v", cache.v, ("b", "m", "hkv", "dk"), dims)
+    check_shape("cache.pos", cache.pos, ("b", "m"), dims, dtype=torch.long)
+    check_shape("k", k, ("b", "n", "hkv", "dk"), dims)
+    check_shape("v", v, ("b", "n", "hkv", "dk"), dims)
+    check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
+    w, m, n = cache.window, dims["m"], dims["n"]
+    if n == 0:
+        return cache
+    keep_new = min(n, w)
+    keep_old = min(m, w - keep_new)
+    return KVCache(
+        k=torch.cat([cache.k[:, m - keep_old :], k[:, n - keep_new :]], dim=1),
+        v=torch.cat([cache.v[:, m - keep_old :], v[:, n - keep_new :]], dim=1),
+        pos=torch.cat([cache.pos[:, m - keep_old :], pos[:, n - keep_new :]], dim=1),
+        window=w,
+    )
+
+
+def rotary(x: Tensor, pos: Tensor, base: float) -> Tensor:
+    """Rotate pairs ``(x[2j], x[2j+1])`` by ``pos * base^(-2j/dk)``, phases in float64
+    (``vesper/attention.py:178-217``)."""
+    dims: Dims = {}
+    check_shape("x", x, ("b", "n", "heads", "dk"), dims)
+    check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
+    dk = dims["dk"]
+    if dk % 2 != 0:
+        msg = f"dk must be even for rotary pairs, got {dk}"
+        raise ValueError(msg)
+    if not 1.0 < base < float("inf"):
+        msg = f"rotary base must be finite and above 1, got {base}"
+        raise ValueError(msg)
+    half = dk // 2
+    inv_freq = base ** (-(torch.arange(0, half, dtype=torch.float64, device=x.device) * (2.0 / dk)))
+    angle = pos.to(torch.float64)[:, :, None] * inv_freq
+    cos = angle.cos().to(x.dtype)[:, :, None, :]
+    sin = angle.sin().to(x.dtype)[:, :, None, :]
+    x1, x2 = x[..., 0::2], x[..., 1::2]
+    return torch.stack([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1).flatten(-2)
+
+
+class WindowedAttention(nn.Module):
+    """Projections, rotary, windowed softmax over cache and chunk, output projection."""
+
+    def __init__(self, d: int, heads: int, kv_groups: int, head_dim: int, window: int, rotary_base: float,
+                 generator: torch.Generator | None = None) -> None:  # fmt: skip
+        """The reference's initialization, draw for draw (``vesper/attention.py:226-267``)."""
+        super().__init__()
+        if heads % kv_groups != 0:
+            msg = f"heads ({heads}) must be divisible by kv_groups ({kv_groups})"
+            raise ValueError(msg)
+        if window < 1:
+            msg = f"window must be at least 1, got {window}"
+            raise ValueError(msg)
+        if not 1.0 < rotary_base < float("inf"):
+            msg = f"rotary base must be finite and above 1, got {rotary_base}"
+            raise ValueError(msg)
+        self.heads, self.kv_heads, self.head_dim = heads, heads // kv_groups, head_dim
+        self.window, self.rotary_base = window, rotary_base
+        std = 1.0 / math.sqrt(d)
+        kv = self.kv_heads * head_dim
+        self.w_q = nn.Parameter(torch.randn(heads * head_dim, d, generator=generator) * std)
+        self.w_k = nn.Parameter(torch.randn(kv, d, generator=generator) * std)
+        self.w_v = nn.Parameter(torch.randn(kv, d, generator=generator) * std)
+        self.w_o = nn.Parameter(torch.randn(d, heads * head_dim, generator=generator) * std)
+
+    def project(self, x: Tensor, pos: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        """Rotated ``q [b,n,h,dk]``, rotated ``k [b,n,hkv,dk]`` and ``v``."""
+        dims: Dims = {}
+        check_shape("x", x, ("b", "n", "d"), dims)
+        check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
+        if pos.shape[1] > 1:
+            require((pos[:, 1:] - pos[:, :-1] == 1).all(), "pos: positions must be consecutive within a chunk")
+        b, n = x.shape[0], x.shape[1]
+        q = F.linear(x, self.w_q).view(b, n, self.heads, self.head_dim)
+        k = F.linear(x, self.w_k).view(b, n, self.kv_heads, self.head_dim)
+        v = F.linear(x, self.w_v).view(b, n, self.kv_heads, self.head_dim)
+        return rotary(q, pos, self.rotary_base), rotary(k, pos, self.rotary_base), v
+
+    def output(self, o: Tensor) -> Tensor:
+        """``[b, n, h, dk] -> [b, n, d]``."""
+        return F.linear(o.flatten(2), self.w_o)
+
+    def attend(self, q: Tensor, k: Tensor, v: Tensor, pos: Tensor, cache: KVCache,
+               compaction: Compaction | None = None) -> tuple[Tensor, KVCache]:  # fmt: skip
+        """Windowed softmax over the cache and the chunk; the new cache.
+
+        ``compaction`` (the loop's active set, its ``qpos`` offset by the cache length): only the
+        active queries are computed, the halted ones' outputs are zero (the loop discards them).
+        """
+        dims: Dims = {"hkv": self.kv_heads, "dk": self.head_dim, "h": self.heads}
+        check_shape("q", q, ("b", "n", "h", "dk"), dims)
+        check_shape("k", k, ("b", "n", "hkv", "dk"), dims)
+        check_shape("v", v, ("b", "n", "hkv", "dk"), dims)
+        check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
+        check_shape("cache.k", cache.k, ("b", "m", "hkv", "dk"), dims)
+        check_shape("cache.v", cache.v, ("b", "m", "hkv", "dk"), dims)
+        check_shape("cache.pos", cache.pos, ("b", "m"), dims, dtype=torch.long)
+        if cache.window != self.window:
+            msg = f"cache window {cache.window} does not match the layer's {self.window}"
+            raise ContractError(msg)
+        n, w = dims["n"], self.window
+        if n == 0:
+            return q.new_zeros(dims["b"], 0, self.w_o.shape[0]), cache
+        if q.device.type != "cuda":
+            msg = f"the windowed attention runs on CUDA only, got {q.device}"
+            raise ContractError(msg)
+        if q.dtype in WINDOW_KERNEL_DTYPES:
+            kpos = torch.cat([cache.pos, pos], dim=1)
+            require((kpos[:, 1:] - kpos[:, :-1] == 1).all(), "attend: cache and chunk positions must be consecutive")
+            keys = torch.cat([cache.k.to(q.dtype), k.to(q.dtype)], dim=1)
+            vals = torch.cat([cache.v.to(q.dtype), v.to(q.dtype)], dim=1)
+            if compaction is None:
+                o = window_attention(q, keys, vals, w)
+            else:
+                (qc,) = gather_rows(compaction, [q])
+                oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
+                (o,) = expand_rows(compaction, [oc])
+            return self.output(o), kv_cache_push(cache, k, v, pos)
+        return self.output(self._blocked(q, k, v, pos, cache)), kv_cache_push(cache, k, v, pos)
+
+    def _blocked(self, q: Tensor, k: Tensor, v: Tensor, pos: Tensor, cache: KVCache) -> Tensor:
+        """The reference's float32 path (``vesper/attention.py:384-407``): query blocks of
+        ``window`` tokens, each over at most three windows of keys, under the position mask."""
+        n, w = q.shape[1], self.window
+        outs: list[Tensor] = []
+        for s in range(0, n, w):
+            e = min(s + w, n)
+            first = max(0, s - w + 1)
+            if s < w:
+                keys = torch.cat([cache.k, k[:, first:e]], dim=1)
+                vals = torch.cat([cache.v, v[:, first:e]], dim=1)
+                kpos = torch.cat([cache.pos, pos[:, first:e]], dim=1)
+            else:
+                keys, vals, kpos = k[:, first:e], v[:, first:e], pos[:, first:e]
+            qpos = pos[:, s:e]
+            allowed = (kpos[:, None, :] <= qpos[:, :, None]) & (kpos[:, None, :] > qpos[:, :, None] - w)
+            block = F.scaled_dot_product_attention(
+                q[:, s:e].transpose(1, 2), keys.transpose(1, 2), vals.transpose(1, 2),
+                attn_mask=allowed[:, None, :, :], enable_gqa=True,
+            )  # fmt: skip
+            outs.append(block.transpose(1, 2))
+        return torch.cat(outs, dim=1)
+
+    def forward(self, x: Tensor, pos: Tensor, cache: KVCache) -> tuple[Tensor, KVCache]:
+        """``project`` then ``attend``."""
+        q, k, v = self.project(x, pos)
+        return self.attend(q, k, v, pos, cache)

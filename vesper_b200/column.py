@@ -1,0 +1,335 @@
+"""One column on a B200 (the contract of ``vesper/column.py`` of mstampfli/vesper-preview).
+
+Pre-RMSNorm residual sublayers in the reference's order: the recurrent core (projections, causal
+key filter, delta-rule scan), windowed attention, the feed-forward ``W_2 relu(W_1 x)^2``. The
+classes keep the reference's parameter names, shapes and initialization draws, so a reference
+``state_dict`` loads unchanged, and its per-pass state (``ColumnState``), its copy-forward
+(``Carry`` / ``Projections``) and its ``step`` contract. What runs differs: RMSNorm, the key filter,
+the scan and the attention are this package's sm_100a kernels (no reference scan: the reference's
+``delta_scan_chunked`` is the oracle the tests compare with), the copy-forward merges are one
+multi-tensor select per merge point, and with a carry the attention computes the active queries
+only (the halted ones' outputs are discarded by the loop anyway). Projections stay cuBLAS GEMMs.
+"""
+
+from __future__ import annotations
+
+import math
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
+from typing import Literal
+
+import torch
+import torch.nn.functional as F  # noqa: N812
+from torch import Tensor, nn
+
+from vesper_b200.attention import KVCache, WindowedAttention, kv_cache_empty
+from vesper_b200.contracts import ContractError, Dims, check_shape
+from vesper_b200.kernels.compact import compact_index, select_rows
+from vesper_b200.kernels.delta_scan import delta_scan_fused, delta_scan_fused_fp32, fused_scan_available
+from vesper_b200.kernels.keys import fused_keys
+from vesper_b200.kernels.norm import fused_rms_norm
+
+ScanImpl = Literal["fused", "fused-fp32"]
+SCAN_IMPLS: tuple[ScanImpl, ...] = ("fused", "fused-fp32")
+FUSED_INPUT_DTYPES: dict[ScanImpl, torch.dtype] = {"fused": torch.bfloat16, "fused-fp32": torch.float32}
+STATE_DTYPE = torch.float32
+RMS_EPS = 1e-6  # inside the root (vesper/column.py:59)
+RMS_SCALE_FLOOR = 1e-3  # the row scale's floor (vesper/column.py:60)
+
+
+@dataclass(frozen=True)
+class ColumnShape:
+    """The column's geometry (``vesper/column.py:64-90``)."""
+
+    d: int
+    heads: int
+    kv_groups: int
+    head_dim: int
+    window: int
+    rotary_base: float
+    ffn_mult: int
+    block: int
+    key_conv: int
+
+    @property
+    def key_history(self) -> int:
+        return max(self.key_conv - 1, 0)
+
+    @property
+    def kv_heads(self) -> int:
+        return self.heads // self.kv_groups
+
+
+@dataclass(frozen=True)
+class Projections:
+    """What a chunk writes into a pass's states per position (``vesper/column.py:122-137``)."""
+
+    rec_z: Tensor
+    rec_k: Tensor
+    rec_v: Tensor
+    rec_beta: Tensor
+    attn_k: Tensor
+    attn_v: Tensor
+
+
+@dataclass(frozen=True)
+class Carry:
+    """Which tokens are active (``bool[b, n]``) and what the halted ones write instead."""
+
+    active: Tensor
+    projections: Projections
+
+
+@dataclass(frozen=True)
+class ColumnState:
+    """Per-pass recurrent states ``h[t] [b,h,dk,dk]``, windows ``kv[t]``, key histories
+    ``key_history[t] [b,K-1,d]`` (``vesper/column.py:429-441``)."""
+
+    h: tuple[Tensor, ...]
+    kv: tuple[KVCache, ...]
+    key_history: tuple[Tensor, ...]
+
+
+def init_column_state(shape: ColumnShape, b: int, t_max: int, dtype: torch.dtype, device: torch.device) -> ColumnState:
+    """Cold state (``vesper/column.py:444-480``): zero states and histories in
+    ``promote_types(dtype, float32)``, empty windows in ``dtype``."""
+    if t_max < 1:
+        msg = f"t_max must be at least 1, got {t_max}"
+        raise ValueError(msg)
+    dk = shape.head_dim
+    sdt = torch.promote_types(dtype, torch.float32)
+    return ColumnState(
+        h=tuple(torch.zeros(b, shape.heads, dk, dk, dtype=sdt, device=device) for _ in range(t_max)),
+        kv=tuple(kv_cache_empty(b, shape.kv_heads, dk, shape.window, dtype, device) for _ in range(t_max)),
+        key_history=tuple(torch.zeros(b, shape.key_history, shape.d, dtype=sdt, device=device) for _ in range(t_max)),
+    )
+
+
+def map_state(state: ColumnState, f: Callable[[Tensor], Tensor]) -> ColumnState:
+    """Every tensor of ``state`` through ``f`` in a fixed order (``vesper/column.py:483-502``)."""
+    return ColumnState(
+        h=tuple(f(h) for h in state.h),
+        kv=tuple(KVCache(k=f(c.k), v=f(c.v), pos=f(c.pos), window=c.window) for c in state.kv),
+        key_history=tuple(f(z) for z in state.key_history),
+    )
+
+
+def state_tensors(states: Sequence[ColumnState]) -> list[Tensor]:
+    """Every tensor of ``states`` as a flat list in ``map_state``'s order (for captured graphs)."""
+    out: list[Tensor] = []
+    for state in states:
+        map_state(state, lambda t: out.append(t) or t)
+    return out
+
+
+def with_state_tensors(templates: Sequence[ColumnState], tensors: Sequence[Tensor]) -> list[ColumnState]:
+    """The inverse of ``state_tensors``."""
+    if len(state_tensors(templates)) != len(tensors):
+        msg = f"{len(tensors)} state tensors for a structure of {len(state_tensors(templates))}"
+        raise ValueError(msg)
+    feed = iter(tensors)
+    return [map_state(s, lambda _: next(feed)) for s in templates]
+
+
+def _require_cuda(x: Tensor, what: str) -> None:
+    if x.device.type != "cuda":
+        msg = f"the {what} runs on CUDA only, got {x.device}"
+        raise ContractError(msg)
+
+
+class RMSNorm(nn.Module):
+    """``x / sqrt(mean(x^2) + 1e-6) * g``, scale-safe, one kernel each way (``fused_rms_norm``)."""
+
+    def __init__(self, d: int) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(d))
+
+    def forward(self, x: Tensor) -> Tensor:
+        d = self.weight.shape[0]
+        if x.shape[-1] != d:
+            msg = f"RMSNorm: last axis must be {d}, got {x.shape[-1]} (shape {tuple(x.shape)})"
+            raise ContractError(msg)
+        return fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS)
+
+
+class RecurrentSublayer(nn.Module):
+    """``q, k, v``, the write strength, the causal key filter, the delta-rule scan, ``W_o``."""
+
+    def __init__(self, shape: ColumnShape, generator: torch.Generator | None = None) -> None:
+        """The reference's parameters and draws (``vesper/column.py:198-234``)."""
+        super().__init__()
+        d, heads, head_dim = shape.d, shape.heads, shape.head_dim
+        if heads * head_dim != d:
+            msg = f"heads ({heads}) * head_dim ({head_dim}) must equal d ({d})"
+            raise ValueError(msg)
+        if shape.block < 1:
+            msg = f"block must be at least 1, got {shape.block}"
+            raise ValueError(msg)
+        self.heads, self.head_dim, self.block = heads, head_dim, shape.block
+        self.scan_impl: ScanImpl = "fused"
+        std = 1.0 / math.sqrt(d)
+        self.w_q = nn.Parameter(torch.randn(d, d, generator=generator) * std)
+        self.w_k = nn.Parameter(torch.randn(d, d, generator=generator) * std)
+        self.w_v = nn.Parameter(torch.randn(d, d, generator=generator) * std)
+        self.w_o = nn.Parameter(torch.randn(d, d, generator=generator) * std)
+        self.w_beta = nn.Parameter(torch.randn(heads, d, generator=generator) * std)
+        self.key_conv = shape.key_conv
+        self.conv_k: nn.Parameter | None = None
+        if shape.key_conv:
+            bound = 1.0 / math.sqrt(shape.key_conv)
+            self.conv_k = nn.Parameter(torch.rand(shape.key_conv, d, generator=generator) * (2 * bound) - bound)
+
+    def project(self, x: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        """``q, v [b,n,h,dk]``, the key input ``z = W_k x [b,n,d]`` and ``beta = sigmoid(W_beta x)``."""
+        dims: Dims = {}
+        check_shape("x", x, ("b", "n", "d"), dims)
+        b, n = dims["b"], dims["n"]
+        q = F.linear(x, self.w_q).view(b, n, self.heads, self.head_dim)
+        z = F.linear(x, self.w_k)
+        v = F.linear(x, self.w_v).view(b, n, self.heads, self.head_dim)
+        return q, z, v, torch.sigmoid(F.linear(x, self.w_beta))
+
+    def keys(self, z: Tensor, history: Tensor) -> tuple[Tensor, Tensor]:
+        """Normalized keys from the filter over ``(history, z)`` and the next history
+        (``vesper/column.py:255-289``): the newest ``K-1`` inputs, an owned float32 copy."""
+        b, n, d = z.shape
+        if n == 0:
+            return z.view(b, 0, self.heads, self.head_dim), history
+        if self.conv_k is None:  # no filter: the key is normalize_keys(z), a one-tap filter of one
+            taps = torch.ones(1, d, dtype=torch.float32, device=z.device)
+            return fused_keys(z, history, taps, self.heads), history
+        width = self.key_conv
+        k = fused_keys(z, history, self.conv_k, self.heads)
+        compute = torch.promote_types(z.dtype, torch.float32)
+        tail = z[:, max(0, n - (width - 1)) :].to(compute)
+        return k, torch.cat([history.to(compute)[:, n:], tail], dim=1)
+
+    def scan(self, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor) -> tuple[Tensor, Tensor]:
+        """The scan (``scan_impl``) with autocast off, then ``W_o`` in the activation dtype."""
+        kernel = delta_scan_fused if self.scan_impl == "fused" else delta_scan_fused_fp32
+        dtype = FUSED_INPUT_DTYPES[self.scan_impl]
+        with torch.autocast(device_type=q.device.type, enabled=False):
+            o, new_state = kernel(q.to(dtype), k.to(dtype), v.to(dtype), beta.to(dtype), state.to(STATE_DTYPE))
+        return F.linear(o.to(q.dtype).flatten(2), self.w_o), new_state
+
+    def forward(self, x: Tensor, state: Tensor, history: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+        q, z, v, beta = self.project(x)
+        k, history_next = self.keys(z, history)
+        y, state_next = self.scan(q, k, v, beta, state)
+        return y, state_next, history_next
+
+
+class FFN(nn.Module):
+    """``W_2 relu(W_1 x)^2`` (``vesper/ffn.py:20-60``), the square as a product in the
+    activation dtype, as the reference computes it."""
+
+    def __init__(self, d: int, ffn_mult: int, generator: torch.Generator | None = None) -> None:
+        super().__init__()
+        if ffn_mult < 1:
+            msg = f"ffn_mult must be at least 1, got {ffn_mult}"
+            raise ValueError(msg)
+        hidden = ffn_mult * d
+        self.w1 = nn.Parameter(torch.randn(hidden, d, generator=generator) / math.sqrt(d))
+        self.w2 = nn.Parameter(torch.randn(d, hidden, generator=generator) / math.sqrt(hidden))
+
+    def forward(self, x: Tensor) -> Tensor:
+        h = F.relu(F.linear(x, self.w1))
+        return F.linear(h * h, self.w2)
+
+
+def set_scan(model: nn.Module, impl: str) -> int:
+    """Choose the scan of every ``RecurrentSublayer`` (``vesper/column.py:353-384``); the
+    reference scan is not part of this build (it is the tests' oracle)."""
+    if impl not in SCAN_IMPLS:
+        msg = f"scan must be one of {SCAN_IMPLS}, got {impl!r}"
+        raise ValueError(msg)
+    sublayers = [m for m in model.modules() if isinstance(m, RecurrentSublayer)]
+    if not sublayers:
+        msg = "the model has no recurrent sublayer to set"
+        raise ValueError(msg)
+    if any(p.device.type != "cuda" for p in model.parameters()):
+        msg = "the fused scan needs the model on CUDA"
+        raise ValueError(msg)
+    if not fused_scan_available():
+        msg = "the fused scan needs a CUDA device and the built library"
+        raise ValueError(msg)
+    for s in sublayers:
+        s.scan_impl = impl  # type: ignore[assignment]
+    return len(sublayers)
+
+
+class Column(nn.Module):
+    """Recurrent core, windowed attention and FFN, each pre-RMSNorm with a residual."""
+
+    def __init__(self, shape: ColumnShape, generator: torch.Generator | None = None) -> None:
+        super().__init__()
+        self.norm_rec = RMSNorm(shape.d)
+        self.rec = RecurrentSublayer(shape, generator)
+        self.norm_attn = RMSNorm(shape.d)
+        self.attn = WindowedAttention(shape.d, shape.heads, shape.kv_groups, shape.head_dim, shape.window,
+                                      shape.rotary_base, generator)  # fmt: skip
+        self.norm_ffn = RMSNorm(shape.d)
+        self.ffn = FFN(shape.d, shape.ffn_mult, generator)
+
+    def step(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int, *,
+             carry: Carry | None = None) -> tuple[Tensor, ColumnState, Projections]:  # fmt: skip
+        """One pass over a chunk through the state of pass ``pass_index`` (``vesper/column.py:709-812``).
+
+        With a carry, halted tokens write their carried projections: the key input is merged
+        before the filter and ``k, v, beta`` after it (one select launch), the attention keys and
+        values after their projection (one launch), and the attention runs the active queries
+        only. The output at halted positions is not meaningful; the loop discards it.
+        """
+        if not len(state.h) == len(state.kv) == len(state.key_history):
+            msg = f"state has {len(state.h)} recurrent states, {len(state.kv)} windows and {len(state.key_history)} key histories"
+            raise ValueError(msg)
+        if not 0 <= pass_index < len(state.h):
+            msg = f"pass_index must lie in [0, {len(state.h)}), got {pass_index}"
+            raise ValueError(msg)
+        _require_cuda(x, "column")
+        history = state.key_history[pass_index]
+        check_shape("state.key_history", history, ("b", "w", "d"),
+                    {"b": x.shape[0], "w": max(self.rec.key_conv - 1, 0), "d": x.shape[2]})  # fmt: skip
+        if carry is not None:
+            dims: Dims = {"b": x.shape[0], "n": x.shape[1], "d": x.shape[2], "h": self.rec.heads,
+                          "hkv": self.attn.kv_heads, "dk": self.rec.head_dim}  # fmt: skip
+            p = carry.projections
+            check_shape("carry.active", carry.active, ("b", "n"), dims, dtype=torch.bool)
+            check_shape("carry.rec_z", p.rec_z, ("b", "n", "d"), dims)
+            check_shape("carry.rec_k", p.rec_k, ("b", "n", "h", "dk"), dims)
+            check_shape("carry.rec_v", p.rec_v, ("b", "n", "h", "dk"), dims)
+            check_shape("carry.rec_beta", p.rec_beta, ("b", "n", "h"), dims)
+            check_shape("carry.attn_k", p.attn_k, ("b", "n", "hkv", "dk"), dims)
+            check_shape("carry.attn_v", p.attn_v, ("b", "n", "hkv", "dk"), dims)
+
+        q, z, v, beta = self.rec.project(self.norm_rec.forward(x))
+        if carry is not None:
+            (z,) = select_rows(carry.active, [z], [carry.projections.rec_z.to(z.dtype)])
+        k, history_next = self.rec.keys(z, history)
+        if carry is not None:
+            p = carry.projections
+            k, v, beta = select_rows(carry.active, [k, v, beta],
+                                     [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
+        r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index])
+        x = x + r
+
+        aq, ak, av = self.attn.project(self.norm_attn.forward(x), pos)
+        window = state.kv[pass_index]
+        compaction = None
+        if carry is not None:
+            ak, av = select_rows(carry.active, [ak, av],
+                                 [carry.projections.attn_k.to(ak.dtype), carry.projections.attn_v.to(av.dtype)])  # fmt: skip
+            compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
+        a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
+        x = x + a
+
+        x = x + self.ffn.forward(self.norm_ffn.forward(x))
+        h = tuple(h_new if i == pass_index else s for i, s in enumerate(state.h))
+        kv = tuple(kv_new if i == pass_index else c for i, c in enumerate(state.kv))
+        hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))
+        written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
+        return x, ColumnState(h=h, kv=kv, key_history=hist), written
+
+    def forward(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int) -> tuple[Tensor, ColumnState]:
+        y, new_state, _ = self.step(x, pos, state, pass_index)
+        return y, new_state

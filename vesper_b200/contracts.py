@@ -55,3 +55,37 @@ def require_cuda(what: str, first: torch.Tensor, **others: torch.Tensor | None) 
         if tensor is not None and tensor.device != first.device:
             msg = f"{name} is on {tensor.device}, the first input on {first.device}"
             raise ContractError(msg)
+
+
+def require(condition: torch.Tensor, message: str) -> None:
+    """A value contract computed on the device (``vesper/contracts.py:104-131``'s ``require``).
+
+    Eagerly the one-element bool is read back and a false one raises ``ContractError(message)``.
+    While a CUDA graph is being captured a read-back would end the capture, so the violation is
+    recorded instead: bit 4 is ORed into the device status word (``_lib.status_word``), which
+    ``_lib.check_status`` reads after the replay and raises on. Unlike the reference, no device
+    assert is ever recorded: a violated contract never faults the GPU.
+    """
+    if condition.dtype != torch.bool or condition.numel() != 1:
+        msg = f"require: the condition must be one bool, got {condition.dtype} {tuple(condition.shape)}"
+        raise ContractError(msg)
+    if condition.is_cuda and torch.cuda.is_current_stream_capturing():
+        from vesper_b200 import _lib  # noqa: PLC0415  # the library loads only for device work
+
+        word = _lib.status_word(condition.device)
+        word.bitwise_or_(condition.logical_not().reshape(1).to(torch.int32) * 4)
+        return
+    if not bool(condition.item()):
+        raise ContractError(message)
+
+
+def check_ids(name: str, tensor: torch.Tensor, spec: DimSpec, dims: Dims, vocab: int) -> torch.Tensor:
+    """Ids of ``int32`` or ``int64`` within ``[0, vocab)``, returned as ``int64``
+    (``vesper/contracts.py:75-101``)."""
+    check_shape(name, tensor, spec, dims)
+    if tensor.dtype not in (torch.int32, torch.int64):
+        msg = f"{name}: dtype must be int32 or int64, got {tensor.dtype}"
+        raise ContractError(msg)
+    if tensor.numel() > 0:
+        require(((tensor >= 0) & (tensor < vocab)).all(), f"{name}: every id must lie in [0, vocab={vocab})")
+    return tensor.long()
