@@ -6,6 +6,11 @@ with q, v, beta and the upstream gradient as further inputs, then the backward t
 (gradients of x, the gain, the taps, q, v and beta). Synthetic inputs with the config's
 distributions. Inputs are far larger than L2 (about 1 GB per step), so no flush is needed.
 
+A second leg times config 4, the looped d512 model's training step (13 columns x 8 passes with ACT
+halting and copy-forward, B=32 x T=2048 per GPU, activation recomputation, clip, AdamW), captured
+as one CUDA graph, data-parallel with one NCCL all-reduce of the gradient bucket per step; it is
+reported under ``train_step`` in the same line (``--no-train`` skips it).
+
 Usage: ``python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]``; for N > 1
 it is launched by torchrun, one rank per GPU, each rank running the same per-GPU workload on its own
 (batch x head) units with no collective on the data path (weak scaling); the time is the maximum
@@ -298,6 +303,11 @@ def run_ours(args) -> None:
         "host_wall_ms_per_step": round(wall_ms, 3),
     }  # fmt: skip
 
+    # --- the looped model's training step (config 4), data-parallel over the ranks ------------
+    del inp, leaves, host, outs_host, results, o, grads, saved
+    torch.cuda.empty_cache()
+    train = None if args.no_train else train_leg(args, device, world, rank, local)
+
     # --- CPU baseline: the oracle (float64 C port of the reference path) on rank 0 at N=1 ------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -314,7 +324,7 @@ def run_ours(args) -> None:
                 "taps": TAPS, "tokens_per_gpu_step": B * T, "l2": "inputs larger than L2 (~1 GB per step), no flush",
                 "sharding": "each rank its own (batch x head) units, no collective", "graph": "CUDA graph replay",
             },
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "train_step": train,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks.summary(),
@@ -323,6 +333,68 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+TRAIN_B, TRAIN_T = 32, 2048  # config 4: rows of 2048 tokens per GPU
+
+
+def train_leg(args, device, world: int, rank: int, local: int) -> dict:
+    """Config 4: the looped d512 model's captured training step, B=32 x T=2048 per GPU, DP over NCCL.
+
+    Forward (13 columns x 8 passes, ACT halting, copy-forward, recomputation), objective, backward,
+    the all-reduce of the gradient bucket (N > 1), clip and AdamW: one CUDA graph replay per step.
+    Tokens/s = N x B x T / the maximum over ranks of the mean replay time (CUDA events).
+    """
+    import torch
+    import torch.distributed as dist
+
+    from vesper_b200 import _lib
+    from vesper_b200.model import Vesper, count_parameters
+    from vesper_b200.train import VESPER_S, TrainStep
+
+    cfg = VESPER_S
+    model = Vesper(cfg.shape, cfg.vocab, cfg.columns, cfg.t_max, cfg.halt_epsilon,
+                   torch.Generator().manual_seed(0)).to(device)  # fmt: skip
+    trainer = TrainStep(model, cfg, b=TRAIN_B, n=TRAIN_T, distributed=world > 1, warm=3)
+    g = torch.Generator(device=device).manual_seed(99 + rank)
+    batches = [torch.randint(0, cfg.vocab, (TRAIN_B, TRAIN_T + 1), device=device, generator=g) for _ in range(2)]
+    for i in range(5):  # three eager steps, the capture and two replays
+        trainer.load(batches[i % 2][:, :-1], batches[i % 2][:, 1:])
+        out = trainer.run()
+    torch.cuda.synchronize(device)
+    _lib.check_status(device)
+    steps = max(1, args.train_steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0.record()
+    for i in range(steps):
+        trainer.load(batches[i % 2][:, :-1], batches[i % 2][:, 1:])
+        out = trainer.run()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    _lib.check_status(device)
+    iters = torch.bincount(out[4].flatten(), minlength=cfg.t_max + 1).tolist()
+    loss = float(out[0])
+    trainer.release()
+    torch.cuda.synchronize(device)
+    return {
+        "metric": "vesper-s train tokens/s", "value": round(world * TRAIN_B * TRAIN_T / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "ms_per_step": round(ms, 2), "steps": steps, "warmup": 5,
+        "scaling": "weak", "dtype": "bf16 autocast (float32 master weights, AdamW)",
+        "config": {"workload": "config 4: looped model training step", "params": count_parameters(model),
+                   "d_model": cfg.shape.d, "columns": cfg.columns, "t_max": cfg.t_max, "vocab": cfg.vocab,
+                   "global_batch": world * TRAIN_B, "seq_len": TRAIN_T, "parallelism": f"dp{world}",
+                   "halting": "ACT, random-init head, halt_epsilon 0.01", "recompute": cfg.recompute,
+                   "exchange": "one NCCL all-reduce of the float32 gradient bucket, inside the step graph"},
+        "pass_counts": iters, "loss": round(loss, 4),
+    }  # fmt: skip
 
 
 def cpu_sample(rows: int = 1) -> dict:
@@ -406,6 +478,8 @@ def main() -> None:
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    p.add_argument("--no-train", action="store_true", help="skip the config-4 training-step leg")
+    p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")
     p.add_argument("--steps-ref", type=int, default=0, help="reference samples (default: min(steps, 10))")
