@@ -58,19 +58,6 @@ __device__ __forceinline__ void tma_tile(uint8_t* tile, const CUtensorMap* map, 
   tma_load_4d(tile + TILE_TD / 2, map, bar, 64, h, t0, b);
 }
 
-// T'[t][s] = X[t][s] * beta_s (bf16 tile images, one 8-element chunk per step)
-__device__ __forceinline__ void scale_columns(uint8_t* Tt, const uint8_t* Xt, const float* bsm) {
-  for (int q = threadIdx.x; q < 64 * 8; q += blockDim.x) {
-    const int r = q >> 3, j = q & 7;
-    const uint32_t off = sw_chunk(64, r, j);
-    uint4 w = *reinterpret_cast<const uint4*>(Xt + off);
-    bf16* e = reinterpret_cast<bf16*>(&w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16_rn(__bfloat162float(e[i]) * bsm[8 * j + i]);
-    *reinterpret_cast<uint4*>(Tt + off) = w;
-  }
-}
-
 __device__ __forceinline__ void ld64(uint32_t tm, int col, float (&v)[64]) {
   float* a = v;
   tmem_ld32(tm + (uint32_t)col, *reinterpret_cast<float(*)[32]>(a));
@@ -126,13 +113,28 @@ __device__ __forceinline__ void publish() {
   tc_fence_after();
 }
 
+// T' = X diag(beta) written twice: rows 0-63 and rows 64-127 of a 128-row tile; thread t of n
+__device__ __forceinline__ void scale_columns_twice(uint8_t* TT, const uint8_t* Xt, const float* bsm, int t, int n) {
+  for (int q = t; q < 64 * 8; q += n) {
+    const int r = q >> 3, j = q & 7;
+    uint4 w = *reinterpret_cast<const uint4*>(Xt + sw_chunk(64, r, j));
+    bf16* e = reinterpret_cast<bf16*>(&w);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16_rn(__bfloat162float(e[i]) * bsm[8 * j + i]);
+    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r, j)) = w;
+    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r + 64, j)) = w;
+  }
+}
+
 // ------------------------------------------------------------------------------------------
 // prep, chunk-parallel: one stacked product [K; Q] K^T (M=128) gives K K^T (rows 0-63) and Q K^T
 // (rows 64-127). From K K^T: X = (I + strictly_lower(diag(beta) K K^T))^-1 by float32 forward
 // substitution (one thread per column); from Q K^T: P = lower_inclusive(Q K^T). Per chunk the
-// scratch holds the bf16 tile images [X 8 KB][P 8 KB].
+// scratch holds the bf16 tile images [X 8 KB][P 8 KB][T'; T' 16 KB], T' = bf16(bf16(X) beta).
 // ------------------------------------------------------------------------------------------
-constexpr uint32_t PREP_BYTES = 2 * TILE_TT;  // per chunk: X then P
+// per chunk: X [64][64], P [64][64], then T' = X diag(beta) written twice ([T'; T'], 128 rows): the
+// forward's stacked [T';T'] operand, whose first 8 KB is the plain T' tile the backward reads
+constexpr uint32_t PREP_X = 0, PREP_P = TILE_TT, PREP_T = 2 * TILE_TT, PREP_BYTES = 4 * TILE_TT;
 
 __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ CUtensorMap qmap,
                                                        const __grid_constant__ CUtensorMap kmap,
@@ -141,10 +143,11 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
                                                        int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* KQ = sm;                                   // [128 rows][128 d]: K rows 0-63, Q rows 64-127
-  uint8_t* Xs = sm + TILE_JI;                         // [X 8 KB][P 8 KB]
-  uint8_t* Ps = Xs + TILE_TT;
-  float* A = reinterpret_cast<float*>(sm + TILE_JI + 2 * TILE_TT);  // [64][65]
+  uint8_t* KQ = sm;  // [128 rows][128 d]: K rows 0-63, Q rows 64-127; dead once the product is read
+  uint8_t* Xs = sm;  // then the output image over it: [X 8 KB][P 8 KB][T'; T' 16 KB]
+  uint8_t* Ps = Xs + PREP_P;
+  uint8_t* TTs = Xs + PREP_T;
+  float* A = reinterpret_cast<float*>(sm + PREP_BYTES);  // [64][65]
   __shared__ float bsm[C];
   __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
@@ -163,8 +166,8 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 64); tmem_relinquish(); }
-  if (tid < C) bsm[tid] = __bfloat162float(bv);
   if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
+  if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
   publish();
   const uint32_t tm = tbase;
   if (tid == 0) {
@@ -208,6 +211,8 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
 #pragma unroll
     for (int t = 0; t < 64; ++t) *reinterpret_cast<bf16*>(Xs + sw_offset(64, t, j)) = __float2bfloat16_rn(x[t]);
   }
+  __syncthreads();
+  scale_columns_twice(TTs, Xs, bsm, tid, NT);
   fence_async_smem();
   __syncthreads();
   if (tid == 0) {
@@ -229,11 +234,11 @@ __global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ C
 // ------------------------------------------------------------------------------------------
 constexpr int NT2 = 256;
 struct FwdSmem {
-  // per-chunk input set: [V | K] adjacent (the MN-major B operand [V | K]), then Q, X, P
-  static constexpr uint32_t Vt = 0, Kt = TILE_TD, Qt = 2 * TILE_TD, Xt = 3 * TILE_TD, Pt = Xt + TILE_TT;
-  static constexpr uint32_t SET = Pt + TILE_TT;  // 64 KB
-  static constexpr uint32_t TT = 2 * SET,            // [T'; T'] 128 rows x 64
-      WW = TT + TILE_JT,                             // [W; W] 128 rows x 128
+  // per-chunk input set: [V | K] adjacent (the MN-major B operand [V | K]), Q, then P and
+  // [T'; T'] (128 rows x 64) as the prep wrote them
+  static constexpr uint32_t Vt = 0, Kt = TILE_TD, Qt = 2 * TILE_TD, Pt = 3 * TILE_TD, TT = Pt + TILE_TT;
+  static constexpr uint32_t SET = TT + TILE_JT;  // 72 KB
+  static constexpr uint32_t WW = 2 * SET,            // [W; W] 128 rows x 128
       Ha = WW + TILE_JI,                             // H^T bf16 [j][i]
       Dr = Ha + TILE_JI,                             // delta rows [t][j]
       END = Dr + TILE_TD;
@@ -252,19 +257,6 @@ __device__ __forceinline__ ChunkAt chunk_at(int b, int c, int T) {
   return a;
 }
 
-// T' = X diag(beta) written twice: rows 0-63 and rows 64-127 of a 128-row tile
-__device__ __forceinline__ void scale_columns_twice(uint8_t* TT, const uint8_t* Xt, const float* bsm) {
-  for (int q = threadIdx.x; q < 64 * 8; q += blockDim.x) {
-    const int r = q >> 3, j = q & 7;
-    uint4 w = *reinterpret_cast<const uint4*>(Xt + sw_chunk(64, r, j));
-    bf16* e = reinterpret_cast<bf16*>(&w);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16_rn(__bfloat162float(e[i]) * bsm[8 * j + i]);
-    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r, j)) = w;
-    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r + 64, j)) = w;
-  }
-}
-
 __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
@@ -273,15 +265,13 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
     int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *TT = sm + FwdSmem::TT, *WW = sm + FwdSmem::WW, *Ha = sm + FwdSmem::Ha, *Dr = sm + FwdSmem::Dr;
-  __shared__ float bsm[2][C];
+  uint8_t *WW = sm + FwdSmem::WW, *Ha = sm + FwdSmem::Ha, *Dr = sm + FwdSmem::Dr;
   __shared__ uint64_t barB, barH, barC, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, half = warp >> 2;
   const int lane128 = quarter * 32 + lane;   // this thread's tensor-memory lane
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  bf16 bpre = __float2bfloat16_rn(0.f);
   uint32_t lphase[2] = {0u, 0u};
   auto set = [&](int c) { return sm + (uint32_t)(c & 1) * FwdSmem::SET; };
   auto load_chunk = [&](int c) {
@@ -289,13 +279,12 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
     uint8_t* s = set(c);
     if (tid == 0) {
       uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES);
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES - PREP_P);
       tma_tile(s + FwdSmem::Vt, &vmap, lb, h, a.t0, b);
       tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
       tma_tile(s + FwdSmem::Qt, &qmap, lb, h, a.t0, b);
-      bulk_load(s + FwdSmem::Xt, xt + ((size_t)bh * NC + c) * PREP_BYTES, PREP_BYTES, lb);
+      bulk_load(s + FwdSmem::Pt, xt + ((size_t)bh * NC + c) * PREP_BYTES + PREP_P, PREP_BYTES - PREP_P, lb);
     }
-    bpre = fetch_beta(beta + h, a.row0, H, a.valid);
   };
   auto wait_chunk = [&](int c) -> bool {
     const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
@@ -316,7 +305,7 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
   const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   // H^T row j = column j of the initial state (warps 0-3; warps 4-7 idle here)
   if (half == 0) column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, lane128, lane_tm, F_H, Ha);
-  const uint32_t sTT = smem_u32(TT), sWW = smem_u32(WW), sH = smem_u32(Ha), sD = smem_u32(Dr);
+  const uint32_t sWW = smem_u32(WW), sH = smem_u32(Ha), sD = smem_u32(Dr);
   const uint32_t id_uw = idesc_bf16(128, 256, 0, 1);  // [T';T'] (K) x [V|K] (MN)
   const uint32_t id_xo = idesc_bf16(128, 128, 0, 0);  // X = [W;W] H: both K-major
   const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);   // O = Q H
@@ -338,13 +327,10 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
   uint32_t pB = 0, pH = 0, pC = 0;
   bool ok = true;
   if (NC > 0) {
-    if (tid < C) bsm[0][tid] = __bfloat162float(bpre);
     ok = wait_chunk(0);
-    __syncthreads();
-    scale_columns_twice(TT, set(0) + FwdSmem::Xt, bsm[0]);
     publish();
     if (tid == 0) {
-      mma_seq<4, 0, 128, 1, 64>(tm + F_U, sTT, smem_u32(set(0) + FwdSmem::Vt), id_uw, 0u);
+      mma_seq<4, 0, 128, 1, 64>(tm + F_U, smem_u32(set(0) + FwdSmem::TT), smem_u32(set(0) + FwdSmem::Vt), id_uw, 0u);
       umma_commit(&barC);
     }
     ok = mma_wait(&barC, pC, status) && ok;
@@ -379,19 +365,15 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
       for (int e = 0; e < 32; ++e) u[e] -= x[e];
       st_row32_bf16(Dr, 64, trow, c0, u);
     }
-    if (more) {
-      if (tid < C) bsm[(c + 1) & 1][tid] = __bfloat162float(bpre);
-      ok = wait_chunk(c + 1) && ok;
-      __syncthreads();
-      scale_columns_twice(TT, set(c + 1) + FwdSmem::Xt, bsm[(c + 1) & 1]);
-    }
+    if (more) ok = wait_chunk(c + 1) && ok;
     if (tid == 0) bulk_wait_read();  // the checkpoint has left Ha before it is rewritten
     publish();
     if (tid == 0 && ok) {
       mma_seq<4, 1, 64, 1, 64>(tm + F_H, sD, sK, id_hk, 1u);     // H^T += delta^T K
       umma_commit(&barH);
       mma_seq<4, 0, 64, 1, 64>(tm + F_O, sP, sD, id_pd, 1u);     // O += P delta
-      if (more) mma_seq<4, 0, 128, 1, 64>(tm + F_U, sTT, smem_u32(set(c + 1) + FwdSmem::Vt), id_uw, 0u);
+      if (more)
+        mma_seq<4, 0, 128, 1, 64>(tm + F_U, smem_u32(set(c + 1) + FwdSmem::TT), smem_u32(set(c + 1) + FwdSmem::Vt), id_uw, 0u);
       umma_commit(&barC);
     }
     ok = ok && mma_wait(&barH, pH, status);
@@ -456,11 +438,10 @@ __global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
 //   C2: W of chunk c-1 = T' K                                       -> staged for the next C1
 // ------------------------------------------------------------------------------------------
 struct DhSmem {
-  // per-chunk input set: X, then P immediately before Q (the MN-major B operand [P | Q]), K, dO
-  static constexpr uint32_t Xt = 0, Pt = TILE_TT, Qt = 2 * TILE_TT, Kt = Qt + TILE_TD, Gt = Kt + TILE_TD;
+  // per-chunk input set: T', then P immediately before Q (the MN-major B operand [P | Q]), K, dO
+  static constexpr uint32_t Tt = 0, Pt = TILE_TT, Qt = 2 * TILE_TT, Kt = Qt + TILE_TD, Gt = Kt + TILE_TD;
   static constexpr uint32_t SET = Gt + TILE_TD;  // 64 KB
-  static constexpr uint32_t Tt = 2 * SET, Wk = Tt + TILE_TT, Ha = Wk + TILE_TD, Da = Ha + TILE_JI,
-                            END = Da + TILE_JT;
+  static constexpr uint32_t Wk = 2 * SET, Ha = Wk + TILE_TD, Da = Ha + TILE_JI, END = Da + TILE_JT;
 };
 constexpr int G_D = 0, G_H = 64, G_W = 192;
 
@@ -471,15 +452,13 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Tt = sm + DhSmem::Tt, *Wk = sm + DhSmem::Wk, *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
-  __shared__ float bsm[2][C];
+  uint8_t *Wk = sm + DhSmem::Wk, *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
   __shared__ uint64_t barB, barH, barC, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, half = warp >> 2;
   const int lane128 = quarter * 32 + lane;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  bf16 bpre = __float2bfloat16_rn(0.f);
   uint32_t lphase[2] = {0u, 0u};
   auto set = [&](int c) { return sm + (uint32_t)(c & 1) * DhSmem::SET; };
   auto load_chunk = [&](int c) {
@@ -487,13 +466,14 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     uint8_t* s = set(c);
     if (tid == 0) {
       uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES);
-      bulk_load(s + DhSmem::Xt, xt + ((size_t)bh * NC + c) * PREP_BYTES, PREP_BYTES, lb);
+      mbar_arrive_expect_tx(lb, 3 * TILE_TD + 2 * TILE_TT);
+      const uint8_t* pre = xt + ((size_t)bh * NC + c) * PREP_BYTES;
+      bulk_load(s + DhSmem::Tt, pre + PREP_T, TILE_TT, lb);
+      bulk_load(s + DhSmem::Pt, pre + PREP_P, TILE_TT, lb);
       tma_tile(s + DhSmem::Qt, &qmap, lb, h, a.t0, b);
       tma_tile(s + DhSmem::Kt, &kmap, lb, h, a.t0, b);
       tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
     }
-    bpre = fetch_beta(beta + h, a.row0, H, a.valid);
   };
   auto wait_chunk = [&](int c) -> bool {
     const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
@@ -514,7 +494,7 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
   const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   if (half == 0)
     column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, lane128, lane_tm, G_H, Ha);
-  const uint32_t sT = smem_u32(Tt), sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
+  const uint32_t sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
   const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);       // ddelta^T = dH^T K^T
   const uint32_t id_opq = idesc_bf16(128, 192, 1, 1);     // [ddelta^T | dH^T] += dO^T [P | Q]
   const uint32_t id_dw = idesc_bf16(128, 128, 0, 1, 1);   // dH^T -= ddelta^T W
@@ -533,13 +513,11 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
   uint32_t pB = 0, pH = 0, pC = 0;
   bool ok = true;
   if (NC > 0) {
-    if (tid < C) bsm[(NC - 1) & 1][tid] = __bfloat162float(bpre);
     ok = wait_chunk(NC - 1);
-    __syncthreads();
-    scale_columns(Tt, set(NC - 1) + DhSmem::Xt, bsm[(NC - 1) & 1]);
     publish();
     if (tid == 0) {
-      mma_seq<4, 0, 64, 1, 64>(tm + G_W, sT, smem_u32(set(NC - 1) + DhSmem::Kt), id_tk, 0u);
+      mma_seq<4, 0, 64, 1, 64>(tm + G_W, smem_u32(set(NC - 1) + DhSmem::Tt), smem_u32(set(NC - 1) + DhSmem::Kt),
+                               id_tk, 0u);
       umma_commit(&barC);
     }
     ok = mma_wait(&barC, pC, status) && ok;
@@ -568,18 +546,15 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
       tmem_wait_ld();
       st_row32_bf16(Da, 128, lane128, c0, v);  // ddelta^T row j
     }
-    if (more) {
-      if (tid < C) bsm[(c - 1) & 1][tid] = __bfloat162float(bpre);
-      ok = wait_chunk(c - 1) && ok;
-      __syncthreads();
-      scale_columns(Tt, set(c - 1) + DhSmem::Xt, bsm[(c - 1) & 1]);
-    }
+    if (more) ok = wait_chunk(c - 1) && ok;
     if (tid == 0) bulk_wait_read();
     publish();
     if (tid == 0 && ok) {
       mma_seq<4, 0, 128, 1, 64>(tm + G_H, sD, sW, id_dw, 1u);   // dH^T -= ddelta^T W
       umma_commit(&barH);
-      if (more) mma_seq<4, 0, 64, 1, 64>(tm + G_W, sT, smem_u32(set(c - 1) + DhSmem::Kt), id_tk, 0u);
+      if (more)
+        mma_seq<4, 0, 64, 1, 64>(tm + G_W, smem_u32(set(c - 1) + DhSmem::Tt), smem_u32(set(c - 1) + DhSmem::Kt),
+                                 id_tk, 0u);
       umma_commit(&barC);
     }
     ok = ok && mma_wait(&barH, pH, status);
@@ -632,7 +607,25 @@ constexpr int R_KK = 0, R_W = 128, R_U = 192, R_DD = 256, R_X = 320;   // batche
 constexpr int R_DP = 64, R_DW = 128, R_DV = 256, R_DT = 384;                      // batch 3
 constexpr int R_DQ = 128, R_Y = 256, R_Z = 320, R_DK = 128;                       // batches 4-7
 
-__global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
+constexpr int NG = 256;  // threads of the local-gradient kernel: two warps per lane quadrant
+__device__ __forceinline__ void ld32w(uint32_t tm, int col, float (&v)[32]) {
+  tmem_ld32(tm + (uint32_t)col, v);
+  tmem_wait_ld();
+}
+// row `r` of a float32 accumulator (64 of its columns from `c0`) as bf16 at columns c0.. of a
+// [64 t][128] global row (dq, dk, dv); columns at or past D are skipped
+__device__ __forceinline__ void store_row64(bf16* dst, const float* r, int c0, int D) {
+#pragma unroll
+  for (int i = 0; i < 64; i += 8) {
+    if (c0 + i >= D) break;
+    uint4 w4;
+    w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
+    w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
+    *reinterpret_cast<uint4*>(dst + c0 + i) = w4;
+  }
+}
+
+__global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap gmap,
     const bf16* __restrict__ beta, const uint8_t* __restrict__ xt, const uint8_t* __restrict__ hck,
@@ -650,39 +643,41 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   uint8_t* Yt = Vt;    // [64][64]
   uint8_t* dGt = Pt;   // [64][64]
   float* scr = reinterpret_cast<float*>(Ht);  // [64][65] floats
-  __shared__ float bsm[C], db1[C];
+  __shared__ float bsm[C], db1[C], db2s[2][C];
   __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warps w and w + 4 share tensor-memory lane quadrant w % 4 and split the columns (half)
+  const int quarter = warp & 3, half = warp >> 2;
+  const int lane128 = quarter * 32 + lane;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
   const int t0 = c * C, valid = min(C, T - t0);
   const int64_t ld = (int64_t)H * D;
   const int64_t row0 = (int64_t)b * T + t0;
-  const int trow = warp * 16 + (lane & 15);  // token row of an M=64 accumulator (lane < 16)
+  const int trow = quarter * 16 + (lane & 15);  // token row of an M=64 accumulator (lane < 16)
   const bool rowlane = lane < 16;
   const size_t chunk = (size_t)bh * NC + c;
   if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
   __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + 2 * TILE_TT);
+    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + 3 * TILE_TT);
     tma_tile(Qt, &qmap, &lbar, h, t0, b);
     tma_tile(Kt, &kmap, &lbar, h, t0, b);
     tma_tile(Vt, &vmap, &lbar, h, t0, b);
     tma_tile(Gt, &gmap, &lbar, h, t0, b);
     bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar);
     bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar);
-    bulk_load(Xt, xt + chunk * PREP_BYTES, TILE_TT, &lbar);
-    bulk_load(Pt, xt + chunk * PREP_BYTES + TILE_TT, TILE_TT, &lbar);
+    bulk_load(Xt, xt + chunk * PREP_BYTES + PREP_X, TILE_TT, &lbar);
+    bulk_load(Pt, xt + chunk * PREP_BYTES + PREP_P, TILE_TT, &lbar);
+    bulk_load(Tt, xt + chunk * PREP_BYTES + PREP_T, TILE_TT, &lbar);
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
-  if (tid < C) bsm[tid] = __bfloat162float(bv);
   if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
-  __syncthreads();
-  scale_columns(Tt, Xt, bsm);
+  if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
   publish();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   const uint32_t sQ = smem_u32(Qt), sK = smem_u32(Kt), sV = smem_u32(Vt), sG = smem_u32(Gt);
   const uint32_t sH = smem_u32(Ht), sdH = smem_u32(dHt), sX = smem_u32(Xt), sT = smem_u32(Tt);
   const uint32_t sP = smem_u32(Pt), sD = smem_u32(Dt), sdD = smem_u32(dDt), sW = smem_u32(Wr);
@@ -703,9 +698,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = mma_wait(&bar, phase, status);
   {
-    float w[64];
-    ld64(lane_tm, R_W, w);
-    st_row64_bf16(Wr, 128, tid, 0, w);
+    float w[32];
+    ld32w(lane_tm, R_W + half * 32, w);
+    st_row32_bf16(Wr, 128, lane128, half * 32, w);
   }
   publish();
   // batch 2: X = H^T W^T; ddelta^T += dO^T P
@@ -718,15 +713,15 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
-    float u[64], x[64];
-    ld64(lane_tm, R_U, u);
-    ld64(lane_tm, R_X, x);
+    float u[32], x[32];
+    tmem_ld32(lane_tm + (uint32_t)(R_U + half * 32), u);
+    tmem_ld32(lane_tm + (uint32_t)(R_X + half * 32), x);
+    tmem_wait_ld();
 #pragma unroll
-    for (int s = 0; s < 64; ++s) u[s] -= x[s];
-    st_row64_bf16(Dt, 128, tid, 0, u);  // delta^T [j][t]
-    float d[64];
-    ld64(lane_tm, R_DD, d);
-    st_row64_bf16(dDt, 128, tid, 0, d);  // ddelta^T [j][t]
+    for (int s = 0; s < 32; ++s) u[s] -= x[s];
+    st_row32_bf16(Dt, 128, lane128, half * 32, u);  // delta^T [j][t]
+    ld32w(lane_tm, R_DD + half * 32, x);
+    st_row32_bf16(dDt, 128, lane128, half * 32, x);  // ddelta^T [j][t]
   }
   publish();
   // batch 3: dP = dO delta^T; dW = -ddelta H^T; dV = T'^T ddelta; dT' = ddelta V^T
@@ -743,33 +738,18 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
-    float a[64];
-    ld64(lane_tm, R_DP, a);
+    float a[32];
+    ld32w(lane_tm, R_DP + half * 32, a);
     if (rowlane) {
 #pragma unroll
-      for (int s = 0; s < 64; ++s) a[s] = s <= trow ? a[s] : 0.f;
-      st_row64_bf16(dPt, 64, trow, 0, a);
+      for (int e = 0; e < 32; ++e) a[e] = half * 32 + e <= trow ? a[e] : 0.f;
+      st_row32_bf16(dPt, 64, trow, half * 32, a);
     }
-    float r[DP];
-    ld64(lane_tm, R_DW, *reinterpret_cast<float(*)[64]>(r));
-    ld64(lane_tm, R_DW + 64, *reinterpret_cast<float(*)[64]>(r + 64));
-    if (rowlane) {
-      st_row64_bf16(dWt, 64, trow, 0, r);
-      st_row64_bf16(dWt, 64, trow, 1, r + 64);
-    }
-    ld64(lane_tm, R_DV, *reinterpret_cast<float(*)[64]>(r));
-    ld64(lane_tm, R_DV + 64, *reinterpret_cast<float(*)[64]>(r + 64));
-    if (rowlane && trow < valid) {
-      bf16* dst = dv + (row0 + trow) * ld + (int64_t)h * D;
-      #pragma unroll
-        for (int i = 0; i < DP; i += 8) {
-          if (i >= D) break;
-        uint4 w4;
-        w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
-        w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
-        *reinterpret_cast<uint4*>(dst + i) = w4;
-      }
-    }
+    float r[64];
+    ld64(lane_tm, R_DW + half * 64, r);
+    if (rowlane) st_row64_bf16(dWt, 64, trow, half, r);
+    ld64(lane_tm, R_DV + half * 64, r);
+    if (rowlane && trow < valid) store_row64(dv + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
   }
   publish();
   // batch 4: dQ = dO H^T + dP K; dT' += dW K^T
@@ -784,32 +764,22 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
-    float r[DP];
-    ld64(lane_tm, R_DQ, *reinterpret_cast<float(*)[64]>(r));
-    ld64(lane_tm, R_DQ + 64, *reinterpret_cast<float(*)[64]>(r + 64));
-    if (rowlane && trow < valid) {
-      bf16* dst = dq + (row0 + trow) * ld + (int64_t)h * D;
-      #pragma unroll
-        for (int i = 0; i < DP; i += 8) {
-          if (i >= D) break;
-        uint4 w4;
-        w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
-        w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
-        *reinterpret_cast<uint4*>(dst + i) = w4;
-      }
-    }
+    float r[64];
+    ld64(lane_tm, R_DQ + half * 64, r);
+    if (rowlane && trow < valid) store_row64(dq + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
     // dT' row t: dX = dT' diag(beta) (bf16 operand), dT' * X products for dbeta's first part
-    float dt[64];
-    ld64(lane_tm, R_DT, dt);
+    float dt[32];
+    ld32w(lane_tm, R_DT + half * 32, dt);
     if (rowlane) {
-      float xr[64], dx[64];
+      float dx[32];
 #pragma unroll
-      for (int s = 0; s < 64; ++s) {
-        xr[s] = __bfloat162float(*reinterpret_cast<const bf16*>(Xt + sw_offset(64, trow, s)));
-        dx[s] = dt[s] * bsm[s];
-        scr[trow * 65 + s] = dt[s] * xr[s];
+      for (int e = 0; e < 32; ++e) {
+        const int s2 = half * 32 + e;
+        const float xr = __bfloat162float(*reinterpret_cast<const bf16*>(Xt + sw_offset(64, trow, s2)));
+        dx[e] = dt[e] * bsm[s2];
+        scr[trow * 65 + s2] = dt[e] * xr;
       }
-      st_row64_bf16(dXt, 64, trow, 0, dx);
+      st_row32_bf16(dXt, 64, trow, half * 32, dx);
     }
   }
   publish();
@@ -826,9 +796,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
-    float y[64];
-    ld64(lane_tm, R_Y, y);
-    if (rowlane) st_row64_bf16(Yt, 64, trow, 0, y);
+    float y[32];
+    ld32w(lane_tm, R_Y + half * 32, y);
+    if (rowlane) st_row32_bf16(Yt, 64, trow, half * 32, y);
   }
   publish();
   // batch 6: Z = X^T Y; dA = -Z (strictly lower)
@@ -838,28 +808,35 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
     umma_commit(&bar);
   }
   ok = ok && mma_wait(&bar, phase, status);
-  float db2 = 0.f;
   {
-    float z[64], kk[64];
-    ld64(lane_tm, R_Z, z);
-    ld64(lane_tm, R_KK, kk);
+    float z[32], kk[32];
+    tmem_ld32(lane_tm + (uint32_t)(R_Z + half * 32), z);
+    tmem_ld32(lane_tm + (uint32_t)(R_KK + half * 32), kk);
+    tmem_wait_ld();
     if (rowlane) {
       const float bt = bsm[trow];
+      float db2 = 0.f;
 #pragma unroll
-      for (int s = 0; s < 64; ++s) {
-        const float da = s < trow ? -z[s] : 0.f;
-        db2 = fmaf(da, kk[s], db2);
-        scr[trow * 65 + s] = bt * da;  // dG
+      for (int e = 0; e < 32; ++e) {
+        const int s2 = half * 32 + e;
+        const float da = s2 < trow ? -z[e] : 0.f;
+        db2 = fmaf(da, kk[e], db2);
+        scr[trow * 65 + s2] = bt * da;  // dG
       }
+      db2s[half][trow] = db2;
     }
   }
   __syncthreads();
   if (rowlane) {
-    float g[64];
+    float g[32];
 #pragma unroll
-    for (int s = 0; s < 64; ++s) g[s] = scr[trow * 65 + s] + scr[s * 65 + trow];
-    st_row64_bf16(dGt, 64, trow, 0, g);
-    if (trow < valid) dbeta[(row0 + trow) * H + h] = __float2bfloat16_rn(db1[trow] + db2);
+    for (int e = 0; e < 32; ++e) {
+      const int s2 = half * 32 + e;
+      g[e] = scr[trow * 65 + s2] + scr[s2 * 65 + trow];
+    }
+    st_row32_bf16(dGt, 64, trow, half * 32, g);
+    if (half == 0 && trow < valid)
+      dbeta[(row0 + trow) * H + h] = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
   }
   publish();
   // batch 7: dK = dP^T Q + delta dH'^T + T'^T dW + (dG + dG^T) K
@@ -874,20 +851,9 @@ __global__ void __launch_bounds__(NT, 1) scan_grad_kernel(
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
-    float r[DP];
-    ld64(lane_tm, R_DK, *reinterpret_cast<float(*)[64]>(r));
-    ld64(lane_tm, R_DK + 64, *reinterpret_cast<float(*)[64]>(r + 64));
-    if (rowlane && trow < valid) {
-      bf16* dst = dk + (row0 + trow) * ld + (int64_t)h * D;
-      #pragma unroll
-        for (int i = 0; i < DP; i += 8) {
-          if (i >= D) break;
-        uint4 w4;
-        w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
-        w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
-        *reinterpret_cast<uint4*>(dst + i) = w4;
-      }
-    }
+    float r[64];
+    ld64(lane_tm, R_DK + half * 64, r);
+    if (rowlane && trow < valid) store_row64(dk + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
   }
   tc_fence_before();
   __syncthreads();
@@ -945,7 +911,7 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
     if ((rc = make_token_map(&qm, q, B, T, H, D)) || (rc = make_token_map(&km, k, B, T, H, D)) ||
         (rc = make_token_map(&vm, v, B, T, H, D)) || (rc = make_token_map(&om, o, B, T, H, D)))
       return rc;
-    const size_t sp = smem_bytes(TILE_JI + 2 * TILE_TT + 64 * 65 * 4);
+    const size_t sp = smem_bytes(PREP_BYTES + 64 * 65 * 4);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp), "prep attr");
     scan_prep_kernel<<<B * H * NC, NT, sp, st>>>(qm, km, (const bf16*)beta, xt, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 prep");
@@ -992,7 +958,7 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   if (NC > 0) {
     const size_t sg = smem_bytes(GrSmem::END);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sg), "grad attr");
-    scan_grad_kernel<<<B * H * NC, NT, sg, st>>>(qm, km, vm, gm, (const bf16*)beta,
+    scan_grad_kernel<<<B * H * NC, NG, sg, st>>>(qm, km, vm, gm, (const bf16*)beta,
                                                  xt, hck, dhck, (bf16*)dq, (bf16*)dk, (bf16*)dv,
                                                  (bf16*)dbeta, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 grad");
