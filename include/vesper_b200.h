@@ -196,6 +196,21 @@ VB_API int vb_expand_rows(const int *rank, int B, int N, int NC, int ntensors,
                           const void *const *src, const void *const *fallback, void *const *dst,
                           const long long *row_bytes, void *stream);
 
+/* ---- fused elementwise ops of the column (bf16, f16 or f32 by `dtype`, 16-byte aligned) ----
+ * relu_square: y = relu(z)^2 and dz from dy, n elements, bit-identical to the reference's
+ * separate relu and product ops in the same dtype. Replaces vesper/kernels/act.py:21
+ * (relu_square) with the semantics of vesper/ffn.py:44-56. */
+VB_API int vb_relu_square_fwd(const void *z, void *y, long long n, int dtype, void *stream);
+VB_API int vb_relu_square_bwd(const void *z, const void *dy, void *dz, long long n, int dtype,
+                              void *stream);
+
+/* rotary: x [tokens, heads, dk] rotated pairwise by pos[token] * inv_freq[j] (inv_freq [dk/2]
+ * float64, pos int64), phases in float64 and each product and sum rounded to the dtype as the
+ * reference's ops round; backward != 0 applies the transposed rotation to an output gradient.
+ * Replaces the op sequence of vesper/attention.py:178-217 (rotary). */
+VB_API int vb_rotary(const void *x, const long long *pos, const double *inv_freq, void *y,
+                     long long tokens, int heads, int dk, int backward, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

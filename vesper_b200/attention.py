@@ -2,9 +2,9 @@
 mstampfli/vesper-preview): rotary GQA projections, exact softmax over the last ``window`` keys.
 
 Same parameters (``w_q, w_k, w_v, w_o``), layouts and cache semantics as the reference's
-``WindowedAttention`` (``vesper/attention.py:219-407``), ``KVCache`` / ``kv_cache_push``
-(``:30-175``) and ``rotary`` (``:178-217``). In bfloat16 or float16 the softmax runs in the
-tcgen05 kernel (``vesper_b200.kernels.window_attn``) over the cache rows and the chunk directly;
+``WindowedAttention`` (``vesper/attention.py:219-407``) and ``KVCache`` / ``kv_cache_push``
+(``:30-175``); ``rotary`` (``:178-217``) is one kernel each way (``vesper_b200.kernels.rotary``).
+In bfloat16 or float16 the softmax runs in the tcgen05 kernel (``vesper_b200.kernels.window_attn``) over the cache rows and the chunk directly;
 given the loop's compaction of the active tokens, it computes only their queries. float32 keeps
 the reference's blocked, masked attention (as the reference does), run by torch on the device.
 The decode ring (``RingKVCache``) is not part of this build.
@@ -21,6 +21,7 @@ from torch import Tensor, nn
 
 from vesper_b200.contracts import ContractError, Dims, check_shape, require
 from vesper_b200.kernels.compact import Compaction, expand_rows, gather_rows
+from vesper_b200.kernels.rotary import rotary
 from vesper_b200.kernels.window_attn import window_attention, window_attention_active
 
 WINDOW_KERNEL_DTYPES = (torch.bfloat16, torch.float16)  # float32 keeps the blocked path
@@ -71,28 +72,6 @@ def kv_cache_push(cache: KVCache, k: Tensor, v: Tensor, pos: Tensor) -> KVCache:
         pos=torch.cat([cache.pos[:, m - keep_old :], pos[:, n - keep_new :]], dim=1),
         window=w,
     )
-
-
-def rotary(x: Tensor, pos: Tensor, base: float) -> Tensor:
-    """Rotate pairs ``(x[2j], x[2j+1])`` by ``pos * base^(-2j/dk)``, phases in float64
-    (``vesper/attention.py:178-217``)."""
-    dims: Dims = {}
-    check_shape("x", x, ("b", "n", "heads", "dk"), dims)
-    check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
-    dk = dims["dk"]
-    if dk % 2 != 0:
-        msg = f"dk must be even for rotary pairs, got {dk}"
-        raise ValueError(msg)
-    if not 1.0 < base < float("inf"):
-        msg = f"rotary base must be finite and above 1, got {base}"
-        raise ValueError(msg)
-    half = dk // 2
-    inv_freq = base ** (-(torch.arange(0, half, dtype=torch.float64, device=x.device) * (2.0 / dk)))
-    angle = pos.to(torch.float64)[:, :, None] * inv_freq
-    cos = angle.cos().to(x.dtype)[:, :, None, :]
-    sin = angle.sin().to(x.dtype)[:, :, None, :]
-    x1, x2 = x[..., 0::2], x[..., 1::2]
-    return torch.stack([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1).flatten(-2)
 
 
 class WindowedAttention(nn.Module):

@@ -24,6 +24,7 @@ from torch import Tensor, nn
 
 from vesper_b200.attention import KVCache, WindowedAttention, kv_cache_empty
 from vesper_b200.contracts import ContractError, Dims, check_shape
+from vesper_b200.kernels.act import relu_square
 from vesper_b200.kernels.compact import compact_index, select_rows
 from vesper_b200.kernels.delta_scan import delta_scan_fused, delta_scan_fused_fp32, fused_scan_available
 from vesper_b200.kernels.keys import fused_keys
@@ -220,8 +221,8 @@ class RecurrentSublayer(nn.Module):
 
 
 class FFN(nn.Module):
-    """``W_2 relu(W_1 x)^2`` (``vesper/ffn.py:20-60``), the square as a product in the
-    activation dtype, as the reference computes it."""
+    """``W_2 relu(W_1 x)^2`` (``vesper/ffn.py:20-60``), the squared ReLU as one kernel each way
+    with the reference's arithmetic (``vesper_b200.kernels.act.relu_square``)."""
 
     def __init__(self, d: int, ffn_mult: int, generator: torch.Generator | None = None) -> None:
         super().__init__()
@@ -233,8 +234,7 @@ class FFN(nn.Module):
         self.w2 = nn.Parameter(torch.randn(d, hidden, generator=generator) / math.sqrt(hidden))
 
     def forward(self, x: Tensor) -> Tensor:
-        h = F.relu(F.linear(x, self.w1))
-        return F.linear(h * h, self.w2)
+        return F.linear(relu_square(F.linear(x, self.w1)), self.w2)
 
 
 def set_scan(model: nn.Module, impl: str) -> int:
