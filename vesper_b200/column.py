@@ -139,7 +139,13 @@ def _require_cuda(x: Tensor, what: str) -> None:
 
 
 class RMSNorm(nn.Module):
-    """``x / sqrt(mean(x^2) + 1e-6) * g``, scale-safe, one kernel each way (``fused_rms_norm``)."""
+    """``x / sqrt(mean(x^2) + 1e-6) * g``, scale-safe, one kernel each way (``fused_rms_norm``).
+
+    Every consumer of a norm's output in the column, the halting head and the output head is a
+    matrix product, which autocast runs in its lower dtype, casting its float32 input each time.
+    Under CUDA autocast the output is therefore cast once here instead: the same cast, so the
+    same values and gradients, made once per norm instead of once per product.
+    """
 
     def __init__(self, d: int) -> None:
         super().__init__()
@@ -150,7 +156,10 @@ class RMSNorm(nn.Module):
         if x.shape[-1] != d:
             msg = f"RMSNorm: last axis must be {d}, got {x.shape[-1]} (shape {tuple(x.shape)})"
             raise ContractError(msg)
-        return fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS)
+        y = fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS)
+        if y.dtype == torch.float32 and y.is_cuda and torch.is_autocast_enabled("cuda"):
+            y = y.to(torch.get_autocast_dtype("cuda"))
+        return y
 
 
 class RecurrentSublayer(nn.Module):
