@@ -30,7 +30,7 @@ namespace {
 
 constexpr int BQ = 128;  // queries per tile (the products' M)
 constexpr int BK = 128;  // keys per tile
-constexpr int NT = 128;  // threads per CTA: one per query (or key) row
+constexpr int NT = 256;  // two threads per query (or key) row, each taking half of the row's columns
 constexpr float LOG2E = 1.4426950408889634f;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -130,6 +130,17 @@ __device__ __forceinline__ void zero_row(E* dst) {
 }
 
 constexpr int cols32(int dk) { return dk < 32 ? 32 : dk; }
+// 32-column chunks of a DK-wide accumulator and the chunks [lo, hi) of one half-row thread
+constexpr int chunks32(int dk) { return (cols32(dk) + 31) / 32; }
+__device__ __forceinline__ int chunk_lo(int n, int half) { return half ? (n + 1) / 2 : 0; }
+__device__ __forceinline__ int chunk_hi(int n, int half) { return half ? n : (n + 1) / 2; }
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz: about 2^-22 relative error; 2^-inf = +0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // ------------------------------------------------------------------------------------------
 // forward
@@ -150,15 +161,18 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   uint8_t* Pt = sm + 5 * TQ;  // P [128 q][128 keys]
   __shared__ uint64_t barS, barO, lbarQ, lbar[2];
   __shared__ uint32_t tbase;
+  __shared__ float xch[2][BQ];  // the two half-row threads' partial maxima, then sums
   const int NQ = qpos.NQ;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;  // warps w and w+4 share lane quadrant w % 4
+  const int r128 = quarter * 32 + lane;             // this thread's row of the tile (its TMEM lane)
   const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int r0 = qtile * BQ, row = r0 + tid;
+  const int r0 = qtile * BQ, row = r0 + r128;
   const int nb = qpos.live(b);
   E* orow = o + (((int64_t)b * NQ + row) * H + h) * DK;
   float* lrow = lse + ((int64_t)b * H + h) * NQ + row;
   if (r0 >= nb) {  // a tile of padding rows only
-    if (row < NQ) { zero_row<DK>(orow); *lrow = 0.f; }
+    if (row < NQ && half == 0) { zero_row<DK>(orow); *lrow = 0.f; }
     return;
   }
   const bool live = row < nb;
@@ -174,8 +188,10 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   constexpr int C_O = BK;  // S in columns [0, 128), O in [128, 128 + DK)
+  constexpr int OCH = chunks32(DK);
+  const int c_lo = chunk_lo(OCH, half), c_hi = chunk_hi(OCH, half);
   const int klo = max(0, qp_first - window + 1), khi = min(L - 1, qp_last);
   const int kt_lo = klo / BK;
   const int ntiles = khi >= klo ? khi / BK - kt_lo + 1 : 0;
@@ -194,7 +210,8 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   bool ok = wait_flag(&lbarQ, pQ, status);
   const uint32_t id_s = idesc_16(BQ, BK, 0, 0, BF);
   const uint32_t id_o = idesc_16(BQ, DK, 0, 1, BF);
-  float m2 = -INFINITY, l = 0.f;  // running max (base-2 units) and denominator
+  float m2 = -INFINITY, l = 0.f;  // running max (base-2 units) and this half's denominator
+  const int kc = half * (BK / 2);  // this thread's 64 keys of each tile
   for (int i = 0; i < ntiles && ok; ++i) {
     ok = wait_flag(&lbar[i & 1], lph[i & 1], status) && ok;
     if (tid == 0) {
@@ -206,40 +223,55 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
     if (i > 0) ok = wait_flag(&barO, pO, status) && ok;
     if (tid == 0 && i + 1 < ntiles) load_kv(i + 1);
     const int k0 = (kt_lo + i) * BK;
-    float sv[BK];
-#pragma unroll
-    for (int c0 = 0; c0 < BK; c0 += 32) tmem_ld32(lane_tm + c0, *reinterpret_cast<float(*)[32]>(sv + c0));
+    // a tile inside every row's window needs no mask (rows ascend in position)
+    const bool interior = k0 + BK - 1 <= qp_first && k0 > qp_last - window && k0 + BK <= L && r0 + BQ <= nb;
+    float sv[BK / 2];
+    tmem_ld32(lane_tm + kc, *reinterpret_cast<float(*)[32]>(sv));
+    tmem_ld32(lane_tm + kc + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
     tmem_wait_ld();
     float mt = -INFINITY;
+    if (interior) {
 #pragma unroll
-    for (int j = 0; j < BK; ++j) {
-      const int kp = k0 + j;
-      const bool in = kp <= qp && kp > qp - window && kp < L;
-      sv[j] = in ? sv[j] * sl2 : -INFINITY;
-      mt = fmaxf(mt, sv[j]);
+      for (int j = 0; j < BK / 2; ++j) {
+        sv[j] *= sl2;
+        mt = fmaxf(mt, sv[j]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < BK / 2; ++j) {
+        const int kp = k0 + kc + j;
+        const bool in = kp <= qp && kp > qp - window && kp < L;
+        sv[j] = in ? sv[j] * sl2 : -INFINITY;
+        mt = fmaxf(mt, sv[j]);
+      }
     }
+    xch[half][r128] = mt;
+    __syncthreads();
+    mt = fmaxf(xch[0][r128], xch[1][r128]);
     const float mnew = fmaxf(m2, mt);
-    const float corr = mnew == -INFINITY ? 1.f : exp2f(m2 - mnew);
-    float ls = 0.f;
+    const float mref = mnew == -INFINITY ? 0.f : mnew;  // all masked so far: every p is 2^-inf = 0
+    const float corr = ex2(m2 - mref);
+    float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
 #pragma unroll
-    for (int j = 0; j < BK; ++j) {
-      const float p = mnew == -INFINITY ? 0.f : exp2f(sv[j] - mnew);
-      sv[j] = p;
-      ls += p;
+    for (int j = 0; j < BK / 2; j += 4) {
+      sv[j] = ex2(sv[j] - mref);
+      sv[j + 1] = ex2(sv[j + 1] - mref);
+      sv[j + 2] = ex2(sv[j + 2] - mref);
+      sv[j + 3] = ex2(sv[j + 3] - mref);
+      ls0 += sv[j]; ls1 += sv[j + 1]; ls2 += sv[j + 2]; ls3 += sv[j + 3];
     }
-    l = l * corr + ls;
+    l = l * corr + ((ls0 + ls1) + (ls2 + ls3));
     m2 = mnew;
-#pragma unroll
-    for (int c0 = 0; c0 < BK; c0 += 32) st_row32<E>(Pt, BQ, tid, c0, sv + c0);
+    st_row32<E>(Pt, BQ, r128, kc, sv);
+    st_row32<E>(Pt, BQ, r128, kc + 32, sv + 32);
     if (i > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
-#pragma unroll
-      for (int c0 = 0; c0 < cols32(DK); c0 += 32) {
+      for (int ch = c_lo; ch < c_hi; ++ch) {
         float ov[32];
-        tmem_ld32(lane_tm + C_O + c0, ov);
+        tmem_ld32(lane_tm + C_O + 32 * ch, ov);
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; ++e) ov[e] *= corr;
-        tmem_st32(lane_tm + C_O + c0, ov);
+        tmem_st32(lane_tm + C_O + 32 * ch, ov);
       }
       tmem_wait_st();
     }
@@ -250,20 +282,24 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
     }
   }
   if (ntiles > 0 && ok) ok = wait_flag(&barO, pO, status);
-  const float inv_l = l > 0.f ? 1.f / l : 0.f;
-#pragma unroll
-  for (int c0 = 0; c0 < cols32(DK); c0 += 32) {
+  xch[half][r128] = l;
+  __syncthreads();
+  const float lt = xch[0][r128] + xch[1][r128];
+  const float inv_l = lt > 0.f ? 1.f / lt : 0.f;
+  for (int ch = c_lo; ch < c_hi; ++ch) {
     float ov[32];
-    tmem_ld32(lane_tm + C_O + c0, ov);
+    tmem_ld32(lane_tm + C_O + 32 * ch, ov);
     tmem_wait_ld();
-    if (live && l > 0.f) store_row<DK, E>(orow, ov, c0, inv_l);
+    if (live && lt > 0.f) store_row<DK, E>(orow, ov, 32 * ch, inv_l);
   }
-  if (live) {
-    if (!(l > 0.f)) zero_row<DK>(orow);
-    *lrow = l > 0.f ? m2 + log2f(l) : 0.f;
-  } else if (row < NQ) {
-    zero_row<DK>(orow);
-    *lrow = 0.f;
+  if (half == 0) {
+    if (live) {
+      if (!(lt > 0.f)) zero_row<DK>(orow);
+      *lrow = lt > 0.f ? m2 + log2f(lt) : 0.f;
+    } else if (row < NQ) {
+      zero_row<DK>(orow);
+      *lrow = 0.f;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -311,13 +347,15 @@ __global__ void __launch_bounds__(NT) attn_dq_kernel(
   __shared__ uint64_t barS, barQ, lbarQ, lbar[2];
   __shared__ uint32_t tbase;
   const int NQ = qpos.NQ;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int r128 = quarter * 32 + lane;
   const int qtile = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int r0 = qtile * BQ, row = r0 + tid;
+  const int r0 = qtile * BQ, row = r0 + r128;
   const int nb = qpos.live(b);
   E* dqrow = dq + (((int64_t)b * NQ + row) * H + h) * DK;
   if (r0 >= nb) {
-    if (row < NQ) zero_row<DK>(dqrow);
+    if (row < NQ && half == 0) zero_row<DK>(dqrow);
     return;
   }
   const bool live = row < nb;
@@ -335,8 +373,10 @@ __global__ void __launch_bounds__(NT) attn_dq_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   constexpr int C_S = 0, C_P = BK, C_Q = 2 * BK;  // S, dP, dQ
+  constexpr int OCH = chunks32(DK);
+  const int c_lo = chunk_lo(OCH, half), c_hi = chunk_hi(OCH, half);
   const int klo = max(0, qp_first - window + 1), khi = min(L - 1, qp_last);
   const int kt_lo = klo / BK;
   const int ntiles = khi >= klo ? khi / BK - kt_lo + 1 : 0;
@@ -367,20 +407,26 @@ __global__ void __launch_bounds__(NT) attn_dq_kernel(
     if (i > 0) ok = wait_flag(&barQ, pQ, status) && ok;
     if (tid == 0 && i + 1 < ntiles) load_kv(i + 1);
     const int k0 = (kt_lo + i) * BK;
+    const bool interior = k0 + BK - 1 <= qp_first && k0 > qp_last - window && k0 + BK <= L && r0 + BQ <= nb;
 #pragma unroll
-    for (int c0 = 0; c0 < BK; c0 += 32) {
+    for (int c0 = half * (BK / 2); c0 < half * (BK / 2) + BK / 2; c0 += 32) {
       float s[32], dp[32];
       tmem_ld32(lane_tm + C_S + c0, s);
       tmem_ld32(lane_tm + C_P + c0, dp);
       tmem_wait_ld();
+      if (interior) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int kp = k0 + c0 + e;
-        const bool in = kp <= qp && kp > qp - window && kp < L;
-        const float p = in ? exp2f(s[e] * sl2 - lse_r) : 0.f;
-        s[e] = p * (dp[e] - dl_r);
+        for (int e = 0; e < 32; ++e) s[e] = ex2(s[e] * sl2 - lse_r) * (dp[e] - dl_r);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int kp = k0 + c0 + e;
+          const bool in = kp <= qp && kp > qp - window && kp < L;
+          const float p = in ? ex2(s[e] * sl2 - lse_r) : 0.f;
+          s[e] = p * (dp[e] - dl_r);
+        }
       }
-      st_row32<E>(dSt, BQ, tid, c0, s);
+      st_row32<E>(dSt, BQ, r128, c0, s);
     }
     ok = publish(ok);
     if (tid == 0 && ok) {
@@ -389,14 +435,13 @@ __global__ void __launch_bounds__(NT) attn_dq_kernel(
     }
   }
   if (ntiles > 0 && ok) ok = wait_flag(&barQ, pQ, status);
-#pragma unroll
-  for (int c0 = 0; c0 < cols32(DK); c0 += 32) {
+  for (int ch = c_lo; ch < c_hi; ++ch) {
     float v[32];
-    tmem_ld32(lane_tm + C_Q + c0, v);
+    tmem_ld32(lane_tm + C_Q + 32 * ch, v);
     tmem_wait_ld();
-    if (live && ntiles > 0) store_row<DK, E>(dqrow, v, c0, scale);
+    if (live && ntiles > 0) store_row<DK, E>(dqrow, v, 32 * ch, scale);
   }
-  if (row < NQ && !(live && ntiles > 0)) zero_row<DK>(dqrow);
+  if (row < NQ && half == 0 && !(live && ntiles > 0)) zero_row<DK>(dqrow);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tm, 512);
@@ -429,12 +474,15 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
   __shared__ uint32_t tbase;
   __shared__ float lse_s[NBUF][BQ], dl_s[NBUF][BQ];
   __shared__ int qp_s[NBUF][BQ];
+  __shared__ int inner_s[NBUF];  // the step's query tile lies inside every key's window: no mask
   const int NQ = qpos.NQ;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int r128 = quarter * 32 + lane;
   const int ktile = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int groups = H / HKV;
   const int k0 = ktile * BK;
-  const int kp = k0 + tid;  // this thread's key
+  const int kp = k0 + r128;  // this thread's key
   const int nb = qpos.live(b);
   // rows whose positions reach this key tile: qpos in [k0, k0 + BK - 1 + window - 1]; positions
   // ascend along a batch row, so the rows form one range, found by bisection
@@ -460,8 +508,10 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, warp * 32, 0);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
   constexpr int C_S = 0, C_P = BK, C_K = 2 * BK, C_V = 2 * BK + cols32(DK);  // S^T, dP^T, dK, dV
+  constexpr int OCH = chunks32(DK);
+  const int c_lo = chunk_lo(OCH, half), c_hi = chunk_hi(OCH, half);
   static_assert(2 * BK + 2 * cols32(DK) <= 512, "tensor memory");
   auto load_q = [&](int s) {
     const int hh = g * groups + s / nqt, qt = qt_lo + s % nqt;
@@ -472,11 +522,17 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
       tma_rows<ATOMS>(Qt(buf), &qmap, lb, hh, qt * BQ, b);
       tma_rows<ATOMS>(Gt(buf), &gmap, lb, hh, qt * BQ, b);
     }
-    const int r = qt * BQ + tid;
-    const bool in = r < nb;
-    qp_s[buf][tid] = in ? qpos.at(b, r) : INT_MAX / 2;
-    lse_s[buf][tid] = in ? lse[((int64_t)b * H + hh) * NQ + r] : 0.f;
-    dl_s[buf][tid] = in ? delta[((int64_t)b * H + hh) * NQ + r] : 0.f;
+    if (tid < BQ) {
+      const int r = qt * BQ + tid;
+      const bool in = r < nb;
+      qp_s[buf][tid] = in ? qpos.at(b, r) : INT_MAX / 2;
+      lse_s[buf][tid] = in ? lse[((int64_t)b * H + hh) * NQ + r] : 0.f;
+      dl_s[buf][tid] = in ? delta[((int64_t)b * H + hh) * NQ + r] : 0.f;
+    }
+    if (tid == 0) {
+      const int q_lo = qpos.at(b, qt * BQ), q_hi = qpos.at(b, min(nb, qt * BQ + BQ) - 1);
+      inner_s[buf] = k0 + BK - 1 <= q_lo && k0 > q_hi - window && k0 + BK <= L && qt * BQ + BQ <= nb;
+    }
   };
   if (tid == 0) {
     mbar_arrive_expect_tx(&lbarK, 2 * TQ);
@@ -502,23 +558,34 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
       if (s > 0) ok = wait_flag(&barA, pA, status) && ok;  // step s-1's products: the other buffer is free
       if (s + 1 < nsteps) load_q(s + 1);
     }
+    const bool inner = inner_s[buf] != 0;
 #pragma unroll
-    for (int c0 = 0; c0 < BQ; c0 += 32) {
+    for (int c0 = half * (BQ / 2); c0 < half * (BQ / 2) + BQ / 2; c0 += 32) {
       float sv[32], dp[32];
       tmem_ld32(lane_tm + C_S + c0, sv);
       tmem_ld32(lane_tm + C_P + c0, dp);
       tmem_wait_ld();
+      if (inner) {
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int q = c0 + e;
-        const int qpv = qp_s[buf][q];
-        const bool in = kp <= qpv && kp > qpv - window && kp < L;
-        const float p = in ? exp2f(sv[e] * sl2 - lse_s[buf][q]) : 0.f;
-        sv[e] = p;
-        dp[e] = p * (dp[e] - dl_s[buf][q]);
+        for (int e = 0; e < 32; ++e) {
+          const int q = c0 + e;
+          const float p = ex2(sv[e] * sl2 - lse_s[buf][q]);
+          sv[e] = p;
+          dp[e] = p * (dp[e] - dl_s[buf][q]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int q = c0 + e;
+          const int qpv = qp_s[buf][q];
+          const bool in = kp <= qpv && kp > qpv - window && kp < L;
+          const float p = in ? ex2(sv[e] * sl2 - lse_s[buf][q]) : 0.f;
+          sv[e] = p;
+          dp[e] = p * (dp[e] - dl_s[buf][q]);
+        }
       }
-      st_row32<E>(Pt, BK, tid, c0, sv);
-      st_row32<E>(dSt, BK, tid, c0, dp);
+      st_row32<E>(Pt, BK, r128, c0, sv);
+      st_row32<E>(dSt, BK, r128, c0, dp);
     }
     ok = publish(ok);
     if (tid == 0 && ok) {
@@ -535,18 +602,17 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
   const bool live = kp < L;
   E* dkr = dk + (((int64_t)b * L + kp) * HKV + g) * DK;
   E* dvr = dv + (((int64_t)b * L + kp) * HKV + g) * DK;
-#pragma unroll
-  for (int c0 = 0; c0 < cols32(DK); c0 += 32) {
+  for (int ch = c_lo; ch < c_hi; ++ch) {
     float kv[32], vv[32];
-    tmem_ld32(lane_tm + C_K + c0, kv);
-    tmem_ld32(lane_tm + C_V + c0, vv);
+    tmem_ld32(lane_tm + C_K + 32 * ch, kv);
+    tmem_ld32(lane_tm + C_V + 32 * ch, vv);
     tmem_wait_ld();
     if (live && nsteps > 0) {
-      store_row<DK, E>(dkr, kv, c0, scale);
-      store_row<DK, E>(dvr, vv, c0, 1.f);
+      store_row<DK, E>(dkr, kv, 32 * ch, scale);
+      store_row<DK, E>(dvr, vv, 32 * ch, 1.f);
     }
   }
-  if (live && nsteps == 0) {
+  if (live && nsteps == 0 && half == 0) {
     zero_row<DK>(dkr);
     zero_row<DK>(dvr);
   }
