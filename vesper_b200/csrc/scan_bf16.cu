@@ -7,19 +7,22 @@
 //   W = T' K,  U = T' V,  delta = U - W H_c,  O = Q H_c + P delta,  H_{c+1} = H_c + K^T delta
 // with P = lower_inclusive(Q K^T) and H [key i, value j] the state at the chunk's start.
 //
+// Substituting delta, the state step and the output are linear in H_c with chunk-local matrices
+//   M = -W^T K (d x d),  Q' = Q - P W:   H_{c+1} = H_c + M^T H_c + K^T U,   O = Q' H_c + P U,
+// and the backward's state step dH_c = dH_{c+1} + Q^T dO - W^T ddelta (ddelta = P^T dO + K dH_{c+1})
+// is dH_c = dH_{c+1} + M dH_{c+1} + Q'^T dO. Only these one-product steps stay on the sequential
+// chains; everything else is chunk-parallel.
+//
 // Kernels (every product is a tcgen05.mma from 128B-swizzled shared-memory tiles into tensor
 // memory; the head dimension is zero-padded to 128 inside the tiles):
-//   prep     chunk-parallel: K K^T (M=64) and the unit-lower-triangular solve for X (float32,
-//            one thread per column), stored as a bf16 tile image per chunk.
+//   prep     chunk-parallel: K K^T and Q K^T, the unit-lower-triangular solve for X (float32,
+//            one thread per column), then U, W, M, Q'; a bf16 tile image per chunk.
 //   forward  one CTA per sequence walks its chunks; H^T lives in tensor memory (fp32, 128 lanes =
-//            value index j, 128 columns = key index i); per chunk: U^T, W^T, Q K^T, then
-//            H^T W^T and Q H, then H^T += delta^T K and O += P delta. The bf16 copy of H_c that
-//            fed the chunk's products is checkpointed (the backward reuses it, no recomputation
-//            of the state chain).
-//   backward one CTA per sequence walks the chunks in reverse for the state gradient
-//            dH_c = dH_{c+1} + Q^T dO - W^T ddelta, ddelta = P^T dO + K dH_{c+1}, checkpointing
-//            the bf16 dH_{c+1}; then a chunk-parallel kernel forms every local gradient from
-//            (H_c, dH_{c+1}) in one pass: dq, dk, dv, dbeta.
+//            value index j, 128 columns = key index i). The bf16 copy of H_c that fed the chunk's
+//            products is checkpointed (the backward reuses it, no recomputation of the chain).
+//   backward one CTA per sequence walks the chunks in reverse for the state gradient,
+//            checkpointing the bf16 dH_{c+1}; then a chunk-parallel kernel forms every local
+//            gradient from (H_c, dH_{c+1}) in one pass: dq, dk, dv, dbeta.
 // Waits on the tensor core are bounded (2 s): a timeout sets bit 1 of *status and the kernel
 // leaves after releasing its tensor memory.
 #include <cstring>
@@ -39,7 +42,6 @@ constexpr uint32_t TILE_TD = 64 * 128 * 2;   // [64 tokens][128 d]
 constexpr uint32_t TILE_JI = 128 * 128 * 2;  // [128][128]
 constexpr uint32_t TILE_TT = 64 * 64 * 2;    // [64][64]
 constexpr uint32_t TILE_JT = 128 * 64 * 2;   // [128 rows][64]
-constexpr int NT = 128;  // threads per CTA
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return (uint8_t*)(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
@@ -113,137 +115,295 @@ __device__ __forceinline__ void publish() {
   tc_fence_after();
 }
 
-// T' = X diag(beta) written twice: rows 0-63 and rows 64-127 of a 128-row tile; thread t of n
-__device__ __forceinline__ void scale_columns_twice(uint8_t* TT, const uint8_t* Xt, const float* bsm, int t, int n) {
-  for (int q = t; q < 64 * 8; q += n) {
-    const int r = q >> 3, j = q & 7;
-    uint4 w = *reinterpret_cast<const uint4*>(Xt + sw_chunk(64, r, j));
-    bf16* e = reinterpret_cast<bf16*>(&w);
+// writes made by threads, as publish(); returns whether every thread's waits succeeded
+__device__ __forceinline__ bool publish_ok(bool ok) {
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  tc_fence_after();
+  return ok;
+}
+
+// every bulk store group of this thread but the newest has finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read_but_newest() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+
+// row r, columns [c0, c0 + 32) of a swizzled bf16 tile: x <- bf16(x - v)
+__device__ __forceinline__ void sub_row32_bf16(uint8_t* tile, int rows, int r, int c0, const float* v) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) e[i] = __float2bfloat16_rn(__bfloat162float(e[i]) * bsm[8 * j + i]);
-    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r, j)) = w;
-    *reinterpret_cast<uint4*>(TT + sw_chunk(128, r + 64, j)) = w;
+  for (int j = 0; j < 4; ++j) {
+    uint4* p = reinterpret_cast<uint4*>(tile + sw_chunk(rows, r, c0 / 8 + j));
+    uint4 w = *p;
+    const bf16* e = reinterpret_cast<const bf16*>(&w);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __bfloat162float(e[i]) - v[8 * j + i];
+    w.x = pack_bf16(o[0], o[1]);
+    w.y = pack_bf16(o[2], o[3]);
+    w.z = pack_bf16(o[4], o[5]);
+    w.w = pack_bf16(o[6], o[7]);
+    *p = w;
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// prep, chunk-parallel: one stacked product [K; Q] K^T (M=128) gives K K^T (rows 0-63) and Q K^T
-// (rows 64-127). From K K^T: X = (I + strictly_lower(diag(beta) K K^T))^-1 by float32 forward
-// substitution (one thread per column); from Q K^T: P = lower_inclusive(Q K^T). Per chunk the
-// scratch holds the bf16 tile images [X 8 KB][P 8 KB][T'; T' 16 KB], T' = bf16(bf16(X) beta).
+// prep, chunk-parallel (two 256-thread CTAs per SM): everything of a chunk that does not depend
+// on the state.
+//   [K; Q] K^T (one M=128 product): A = strictly_lower(diag(beta) K K^T), P = lower_inclusive(Q K^T)
+//   X = (I + A)^-1 by float32 forward substitution (one thread per column), T' = X diag(beta)
+//   U = T' V, W = T' K        (the stacked operand [T'; T'] puts a token row on every lane)
+//   M = -W^T K  (d x d),  Q' = Q - P W
+// Substituting delta = U - W H_c, the chunk's state step and output become
+//   H_{c+1} = H_c + M^T H_c + K^T U,   O = Q' H_c + P U,
+// and the backward's state step dH_c = dH_{c+1} + Q^T dO - W^T ddelta becomes
+//   dH_c = dH_{c+1} + M dH_{c+1} + Q'^T dO:
+// one product per chunk on each chain. Per chunk the image holds the bf16 tiles
+// [X 8K][P 8K][T' 8K][U 16K][Q' 16K][M 32K] (M: 128 rows i, 128 columns i').
 // ------------------------------------------------------------------------------------------
-// per chunk: X [64][64], P [64][64], then T' = X diag(beta) written twice ([T'; T'], 128 rows): the
-// forward's stacked [T';T'] operand, whose first 8 KB is the plain T' tile the backward reads
-constexpr uint32_t PREP_X = 0, PREP_P = TILE_TT, PREP_T = 2 * TILE_TT, PREP_BYTES = 4 * TILE_TT;
+constexpr uint32_t PREP_X = 0, PREP_P = TILE_TT, PREP_T = 2 * TILE_TT, PREP_U = 3 * TILE_TT,
+                   PREP_Q = PREP_U + TILE_TD, PREP_M = PREP_Q + TILE_TD, PREP_BYTES = PREP_M + TILE_JI;
+struct PrepSmem {
+  // KQ [128 rows][128 d]: K in rows 0-63, Q in rows 64-127 of each atom (Q' replaces Q in place);
+  // Vt: V, then U; AF: float32 A [64][65], then atom 0 of M; Ws: the X image, then W, then atom 1
+  // of M; TT: [T'; T'] (128 rows x 64); Ps: P. During the solve Ws and TT hold the float32 X
+  // [64][68] and the block products (3 x [16][20]).
+  static constexpr uint32_t KQ = 0, Vt = TILE_JI, AF = Vt + TILE_TD, Ws = AF + 17 * 1024, TT = Ws + TILE_TD,
+                            Ps = TT + TILE_JT, END = Ps + TILE_TT;
+};
+constexpr int NP = 256;
 
-__global__ void __launch_bounds__(NT) scan_prep_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                       const __grid_constant__ CUtensorMap kmap,
-                                                       const bf16* __restrict__ beta,
-                                                       uint8_t* __restrict__ xt, int T, int H,
-                                                       int D, int NC, int* status) {
+// X = (I + A)^-1 for the strictly lower A (float32 [64][65]) into X (float32 [64][68]), 256
+// threads: the four 16 x 16 diagonal blocks by forward substitution (a thread per column), then
+// the blocks below them one block diagonal at a time, X_ij = -X_ii sum_{j <= k < i} A_ik X_kj,
+// each thread a 1 x 4 strip of an output block. Entries above the diagonal blocks are not written.
+constexpr int XS = 68;  // row stride of X (16-byte aligned rows)
+__device__ __forceinline__ void invert_unit_lower(const float* A, float* X, float* Tm, int tid) {
+  if (tid < C) {
+    const int o = 16 * (tid >> 4), j = tid & 15;
+    float x[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int s = 0; s < r; ++s) {
+        if (s & 1) s1 = fmaf(A[(o + r) * 65 + o + s], x[s], s1);
+        else s0 = fmaf(A[(o + r) * 65 + o + s], x[s], s0);
+      }
+      x[r] = (r == j ? 1.f : 0.f) - (s0 + s1);
+      X[(o + r) * XS + o + j] = x[r];
+    }
+  }
+  __syncthreads();
+  const int jb = tid >> 6, r = (tid >> 2) & 15, q4 = 4 * (tid & 3);
+#pragma unroll
+  for (int d = 1; d < 4; ++d) {
+    const int i = jb + d;
+    const bool act = i < 4;
+    if (act) {  // T = sum_k A_ik X_kj, rows r, columns q4 .. q4 + 3
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = jb; k < i; ++k)
+#pragma unroll
+        for (int s = 0; s < 16; ++s) {
+          const float a = A[(16 * i + r) * 65 + 16 * k + s];
+          const float4 x = *reinterpret_cast<const float4*>(X + (16 * k + s) * XS + 16 * jb + q4);
+          t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
+        }
+      *reinterpret_cast<float4*>(Tm + jb * 320 + r * 20 + q4) = t;
+    }
+    __syncthreads();
+    if (act) {  // X_ij = -X_ii T
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int s = 0; s < 16; ++s) {
+        const float a = X[(16 * i + r) * XS + 16 * i + s];
+        const float4 t = *reinterpret_cast<const float4*>(Tm + jb * 320 + s * 20 + q4);
+        x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
+      }
+      *reinterpret_cast<float4*>(X + (16 * i + r) * XS + 16 * jb + q4) = make_float4(-x.x, -x.y, -x.z, -x.w);
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
+    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+    const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ beta, uint8_t* __restrict__ xt, int T,
+    int H, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* KQ = sm;  // [128 rows][128 d]: K rows 0-63, Q rows 64-127; dead once the product is read
-  uint8_t* Xs = sm;  // then the output image over it: [X 8 KB][P 8 KB][T'; T' 16 KB]
-  uint8_t* Ps = Xs + PREP_P;
-  uint8_t* TTs = Xs + PREP_T;
-  float* A = reinterpret_cast<float*>(sm + PREP_BYTES);  // [64][65]
+  uint8_t *KQ = sm + PrepSmem::KQ, *Vt = sm + PrepSmem::Vt, *Ws = sm + PrepSmem::Ws, *TT = sm + PrepSmem::TT;
+  uint8_t* Ps = sm + PrepSmem::Ps;
+  float* A = reinterpret_cast<float*>(sm + PrepSmem::AF);
+  uint8_t* M0 = sm + PrepSmem::AF;  // M columns 0-63 once A is dead
+  uint8_t* M1 = Ws;                 // M columns 64-127 once W is dead
   __shared__ float bsm[C];
   __shared__ uint64_t bar, lbar;
   __shared__ uint32_t tbase;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quarter = warp & 3, half = warp >> 2;
+  const int lane128 = quarter * 32 + lane;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
   const int t0 = c * C, valid = min(C, T - t0);
   const int64_t row0 = (int64_t)b * T + t0;
+  uint8_t* img = xt + (size_t)blockIdx.x * PREP_BYTES;
   if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
   __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(&lbar, 2 * TILE_TD);
+    mbar_arrive_expect_tx(&lbar, 3 * TILE_TD);
     tma_load_4d(KQ, &kmap, &lbar, 0, h, t0, b);
     tma_load_4d(KQ + TILE_JI / 2, &kmap, &lbar, 64, h, t0, b);
     tma_load_4d(KQ + TILE_TD / 2, &qmap, &lbar, 0, h, t0, b);
     tma_load_4d(KQ + TILE_JI / 2 + TILE_TD / 2, &qmap, &lbar, 64, h, t0, b);
+    tma_tile(Vt, &vmap, &lbar, h, t0, b);
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
-  if (warp == 0) { tmem_alloc(&tbase, 64); tmem_relinquish(); }
-  if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
+  if (warp == 0) { tmem_alloc(&tbase, 256); tmem_relinquish(); }
+  bool ok = mbar_wait(&lbar, 0);
+  if (!ok) atomicOr(status, 4);
   if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
-  publish();
+  ok = publish_ok(ok);
   const uint32_t tm = tbase;
-  if (tid == 0) {
-    mma_seq<DP / 16, 0, 128, 0, 128>(tm, smem_u32(KQ), smem_u32(KQ), idesc_bf16(128, 64, 0, 0), 0u);
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
+  const uint32_t sKQ = smem_u32(KQ), sV = smem_u32(Vt), sW = smem_u32(Ws), sTT = smem_u32(TT), sP = smem_u32(Ps);
+  uint32_t phase = 0;
+  // 1. [K; Q] K^T into columns 0-63
+  if (tid == 0 && ok) {
+    mma_seq<DP / 16, 0, 128, 0, 128>(tm, sKQ, sKQ, idesc_bf16(128, 64, 0, 0), 0u);
     umma_commit(&bar);
   }
-  uint32_t phase = 0;
-  const bool ok = mma_wait(&bar, phase, status);
+  if (ok) ok = mma_wait(&bar, phase, status);
   {
-    const int row = tid;  // M=128 layout: thread <-> lane <-> row
+    float v[32];
+    const int c0 = half * 32;
+    tmem_ld32(lane_tm + (uint32_t)c0, v);
+    tmem_wait_ld();
+    if (lane128 < C) {
+      const int t = lane128;
 #pragma unroll
-    for (int c0 = 0; c0 < 64; c0 += 32) {
+      for (int e = 0; e < 32; ++e) A[t * 65 + c0 + e] = c0 + e < t ? bsm[t] * v[e] : 0.f;
+    } else {
+      const int t = lane128 - C;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = c0 + e <= t ? v[e] : 0.f;
+      st_row32_bf16(Ps, 64, t, c0, v);
+    }
+  }
+  ok = publish_ok(ok);
+  // 2. X (float32 over Ws and TT), then the bf16 X image into Ws and T' = bf16(X beta) into both
+  //    halves of TT; every thread reads its 16 entries of X before any is overwritten
+  {
+    float* Xf = reinterpret_cast<float*>(Ws);
+    invert_unit_lower(A, Xf, Xf + 64 * XS, tid);
+    float xv[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int idx = tid + NP * e, t = idx >> 6, j = idx & 63;
+      xv[e] = (j >> 4) > (t >> 4) ? 0.f : Xf[t * XS + j];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int idx = tid + NP * e, t = idx >> 6, j = idx & 63;
+      const bf16 xb = __float2bfloat16_rn(xv[e]);
+      const bf16 tb = __float2bfloat16_rn(__bfloat162float(xb) * bsm[j]);
+      *reinterpret_cast<bf16*>(Ws + sw_offset(64, t, j)) = xb;
+      *reinterpret_cast<bf16*>(TT + sw_offset(128, t, j)) = tb;
+      *reinterpret_cast<bf16*>(TT + sw_offset(128, t + 64, j)) = tb;
+    }
+  }
+  ok = publish_ok(ok);
+  // 3. the X, P and T' images; U = [T'; T'] V (columns 0-127), W = [T'; T'] K (128-255)
+  if (tid == 0) {
+    bulk_store(img + PREP_X, Ws, TILE_TT);
+    bulk_store(img + PREP_P, Ps, TILE_TT);
+    bulk_store(img + PREP_T, TT, TILE_TT);
+    bulk_commit();
+    if (ok) {
+      mma_seq<4, 0, 128, 1, 64>(tm, sTT, sV, idesc_bf16(128, 128, 0, 1), 0u);
+      mma_seq<4, 0, 128, 1, 128>(tm + 128, sTT, sKQ, idesc_bf16(128, 128, 0, 1), 0u);
+      umma_commit(&bar);
+    }
+    bulk_wait_read();  // Ws (the X image) is rewritten with W below
+  }
+  if (ok) ok = mma_wait(&bar, phase, status);
+  __syncthreads();
+  {
+    // lanes 0-63 (the first copy of the token rows) read U, lanes 64-127 read W; the two warps of
+    // a lane quarter split the 128 columns
+    const int t = lane128 & 63;
+    const bool w_rows = lane128 >= 64;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
       float v[32];
-      tmem_ld32(taddr(tm, warp * 32, c0), v);
+      const int c0 = half * 64 + 32 * k;
+      tmem_ld32(lane_tm + (uint32_t)((w_rows ? 128 : 0) + c0), v);
       tmem_wait_ld();
-      if (row < C) {
-#pragma unroll
-        for (int e = 0; e < 32; ++e) A[row * 65 + c0 + e] = c0 + e < row ? bsm[row] * v[e] : 0.f;
-      } else {
-        const int t = row - C;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) v[e] = c0 + e <= t ? v[e] : 0.f;
-        st_row32_bf16(Ps, 64, t, c0, v);
-      }
+      st_row32_bf16(w_rows ? Ws : Vt, 64, t, c0, v);
     }
   }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tm, 64);
-  if (!ok) return;
-  if (tid < 64) {
-    const int j = tid;
-    float x[64];
-#pragma unroll
-    for (int t = 0; t < 64; ++t) {
-      float acc = (t == j) ? 1.f : 0.f;
-#pragma unroll
-      for (int s = 0; s < t; ++s) acc = fmaf(-A[t * 65 + s], x[s], acc);
-      x[t] = acc;
+  ok = publish_ok(ok);
+  // 4. the U image; M = -W^T K (columns 0-127), P W (M=64, columns 128-255)
+  if (tid == 0) {
+    bulk_store(img + PREP_U, Vt, TILE_TD);
+    bulk_commit();
+    if (ok) {
+      mma_seq<4, 1, 64, 1, 128>(tm, sW, sKQ, idesc_bf16(128, 128, 1, 1, 1), 0u);
+      mma_seq<4, 0, 64, 1, 64>(tm + 128, sP, sW, idesc_bf16(64, 128, 0, 1), 0u);
+      umma_commit(&bar);
     }
-#pragma unroll
-    for (int t = 0; t < 64; ++t) *reinterpret_cast<bf16*>(Xs + sw_offset(64, t, j)) = __float2bfloat16_rn(x[t]);
   }
+  if (ok) ok = mma_wait(&bar, phase, status);
   __syncthreads();
-  scale_columns_twice(TTs, Xs, bsm, tid, NT);
+  {
+    // M row i = lane: columns [64 half, 64 half + 64) are atom `half` of the M image
+    uint8_t* Ma = half ? M1 : M0;
+    const int t = quarter * 16 + (lane & 15);  // P W row of this lane (M=64 layout, lanes 0-15)
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      float m[32], pw[32];
+      tmem_ld32(lane_tm + (uint32_t)(half * 64 + 32 * k), m);
+      tmem_ld32(lane_tm + (uint32_t)(128 + half * 64 + 32 * k), pw);
+      tmem_wait_ld();
+      st_row32_bf16(Ma, 128, lane128, 32 * k, m);
+      if (lane < 16) sub_row32_bf16(KQ, 128, 64 + t, half * 64 + 32 * k, pw);  // Q' = Q - P W
+    }
+  }
   fence_async_smem();
   __syncthreads();
   if (tid == 0) {
-    bulk_store(xt + (size_t)blockIdx.x * PREP_BYTES, Xs, PREP_BYTES);
+    bulk_store(img + PREP_Q, KQ + TILE_TD / 2, TILE_TD / 2);  // Q' columns 0-63: rows 64-127 of atom 0
+    bulk_store(img + PREP_Q + TILE_TD / 2, KQ + TILE_JI / 2 + TILE_TD / 2, TILE_TD / 2);
+    bulk_store(img + PREP_M, M0, TILE_JI / 2);
+    bulk_store(img + PREP_M + TILE_JI / 2, M1, TILE_JI / 2);
     bulk_commit();
-    bulk_wait_all();
+    bulk_wait_read();  // shared memory stays valid until the copies have read it
   }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tm, 256);
 }
 
 // ------------------------------------------------------------------------------------------
-// forward: one CTA (256 threads) per (b, h). H^T lives in tensor memory (lane j = value index,
-// column i = key index); the chunk's products run in the "rows t" form with the token rows
-// duplicated over both halves of the 128 lanes, so all eight warps share every readout:
-//   [U | W] = [T'; T'] [V | K]         (N = 256, issued during the previous chunk)
-//   X = [W; W] H,  O = Q H              (batch B)  -> delta = U - X        (rows t)
-//   H^T += delta^T K                    (batch C1) -> bf16 copy of H for the next chunk
-//   O += P delta, [U | W] of chunk c+1  (batch C2) -> O stored, W of chunk c+1 staged
-// Warp w reads lane quarter w % 4; the two warps of a quarter split the columns (w / 4).
+// forward: one CTA per (b, h) walks its chunks. H^T lives in tensor memory (fp32, lane j = value
+// index, column i = key index) and, for the products, as the bf16 tile Hs [j][i]:
+//   H^T += Hs M + U^T K,  O = Q' Hs    (one commit: Q' Hs has read Hs when H^T is complete)
+//   O += P U                           (M=64, double-buffered in tensor memory)
+// Warp 8 issues every product and load; warps 0-7 read H^T back into Hs and O into the staging
+// tile Ot, warp w reading lane quarter w % 4 and the two warps of a quarter splitting the columns
+// (w / 4); thread 0 copies Hs (the checkpoint) and Ot out with bulk stores. The O readout of chunk c-1 overlaps
+// the chain products of chunk c. Mbarriers order the two roles; every wait is bounded.
 // ------------------------------------------------------------------------------------------
-constexpr int NT2 = 256;
+constexpr int NT2 = 256;         // threads of the sequential backward
+constexpr int NF = 288;          // forward: eight reading warps and the issuing warp
+constexpr int NR = 256;          // the forward's reading threads
 struct FwdSmem {
-  // per-chunk input set: [V | K] adjacent (the MN-major B operand [V | K]), Q, then P and
-  // [T'; T'] (128 rows x 64) as the prep wrote them
-  static constexpr uint32_t Vt = 0, Kt = TILE_TD, Qt = 2 * TILE_TD, Pt = 3 * TILE_TD, TT = Pt + TILE_TT;
-  static constexpr uint32_t SET = TT + TILE_JT;  // 72 KB
-  static constexpr uint32_t WW = 2 * SET,            // [W; W] 128 rows x 128
-      Ha = WW + TILE_JI,                             // H^T bf16 [j][i]
-      Dr = Ha + TILE_JI,                             // delta rows [t][j]
-      END = Dr + TILE_TD;
+  // per-chunk set: P, then [U | Q' | M] in the prep image's order (one bulk copy), then K
+  static constexpr uint32_t Pt = 0, Ut = TILE_TT, Qt = Ut + TILE_TD, Mt = Qt + TILE_TD, Kt = Mt + TILE_JI;
+  static constexpr uint32_t SET = Kt + TILE_TD;                                  // 88 KB
+  static constexpr uint32_t Hs = 2 * SET, Ot = Hs + TILE_JI, END = Ot + TILE_TD;  // 224 KB
 };
-constexpr int F_H = 0, F_U = 128, F_W = 256, F_X = 256, F_O = 384;
+constexpr int F_H = 0, F_O = 128;  // O of chunk c at columns F_O + 128 (c & 1)
 
 struct ChunkAt {
   int t0, valid;
@@ -257,326 +417,259 @@ __device__ __forceinline__ ChunkAt chunk_at(int b, int c, int T) {
   return a;
 }
 
-__global__ void __launch_bounds__(NT2, 1) scan_fwd_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap omap,
-    const bf16* __restrict__ beta, const float* __restrict__ s0, const uint8_t* __restrict__ xt,
-    float* __restrict__ sn, uint8_t* __restrict__ hck, int T, int H, int D,
-    int NC, int* status) {
+// bounded wait by one thread; a timeout ORs `code` into the status word
+__device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t& phase, int* status, int code) {
+  const bool ok = mbar_wait(bar, phase);
+  phase ^= 1u;
+  if (!ok) atomicOr(status, code);
+  return ok;
+}
+
+__global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap omap,
+    const float* __restrict__ s0, const uint8_t* __restrict__ xt, float* __restrict__ sn,
+    uint8_t* __restrict__ hck, int T, int H, int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *WW = sm + FwdSmem::WW, *Ha = sm + FwdSmem::Ha, *Dr = sm + FwdSmem::Dr;
-  __shared__ uint64_t barB, barH, barC, lbar[2];
+  uint8_t *Hs = sm + FwdSmem::Hs, *Ot = sm + FwdSmem::Ot;
+  __shared__ uint64_t barH, barO[2], barOR[2], barHs, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quarter = warp & 3, half = warp >> 2;
-  const int lane128 = quarter * 32 + lane;   // this thread's tensor-memory lane
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  uint32_t lphase[2] = {0u, 0u};
   auto set = [&](int c) { return sm + (uint32_t)(c & 1) * FwdSmem::SET; };
-  auto load_chunk = [&](int c) {
-    const ChunkAt a = chunk_at(b, c, T);
-    uint8_t* s = set(c);
-    if (tid == 0) {
-      uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + PREP_BYTES - PREP_P);
-      tma_tile(s + FwdSmem::Vt, &vmap, lb, h, a.t0, b);
-      tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
-      tma_tile(s + FwdSmem::Qt, &qmap, lb, h, a.t0, b);
-      bulk_load(s + FwdSmem::Pt, xt + ((size_t)bh * NC + c) * PREP_BYTES + PREP_P, PREP_BYTES - PREP_P, lb);
-    }
-  };
-  auto wait_chunk = [&](int c) -> bool {
-    const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
-    lphase[c & 1] ^= 1u;
-    if (!r && tid == 0) atomicOr(status, 4);
-    return r;
-  };
   if (tid == 0) {
-    mbar_init(&barB, 1); mbar_init(&barH, 1); mbar_init(&barC, 1);
+    mbar_init(&barH, 1); mbar_init(&barO[0], 1); mbar_init(&barO[1], 1);
+    mbar_init(&barOR[0], NR); mbar_init(&barOR[1], NR); mbar_init(&barHs, NR);
     mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
     mbar_fence_init();
   }
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
   __syncthreads();
-  if (NC > 0) load_chunk(0);
   tc_fence_after();
   const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
-  // H^T row j = column j of the initial state (warps 0-3; warps 4-7 idle here)
-  if (half == 0) column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, lane128, lane_tm, F_H, Ha);
-  const uint32_t sWW = smem_u32(WW), sH = smem_u32(Ha), sD = smem_u32(Dr);
-  const uint32_t id_uw = idesc_bf16(128, 256, 0, 1);  // [T';T'] (K) x [V|K] (MN)
-  const uint32_t id_xo = idesc_bf16(128, 128, 0, 0);  // X = [W;W] H: both K-major
-  const uint32_t id_qh = idesc_bf16(64, 128, 0, 0);   // O = Q H
-  const uint32_t id_hk = idesc_bf16(128, 128, 1, 1);  // H^T += delta^T K: both MN-major
-  const uint32_t id_pd = idesc_bf16(64, 128, 0, 1);   // O += P delta
-  // token row of this thread in the duplicated "rows t" layout, and its 32-column slice
-  const int trow = lane128 & 63;
-  const int upper = lane128 >> 6;  // 0: lanes 0-63, 1: lanes 64-127
-  auto readout_w = [&]() {         // W rows (duplicated lanes) -> [W; W]
-    const int c0 = half * 64;
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      float v[32];
-      tmem_ld32(lane_tm + (uint32_t)(F_W + c0 + 32 * k), v);
-      tmem_wait_ld();
-      st_row32_bf16(WW, 128, upper * 64 + trow, c0 + 32 * k, v);
-    }
-  };
-  uint32_t pB = 0, pH = 0, pC = 0;
-  bool ok = true;
-  if (NC > 0) {
-    ok = wait_chunk(0);
-    publish();
-    if (tid == 0) {
-      mma_seq<4, 0, 128, 1, 64>(tm + F_U, smem_u32(set(0) + FwdSmem::TT), smem_u32(set(0) + FwdSmem::Vt), id_uw, 0u);
-      umma_commit(&barC);
-    }
-    ok = mma_wait(&barC, pC, status) && ok;
-    if (NC > 1) load_chunk(1);
-    readout_w();
-    publish();
-  }
-  for (int c = 0; c < NC && ok; ++c) {
-    const ChunkAt a = chunk_at(b, c, T);
-    const bool more = c + 1 < NC;
-    if (tid == 0) {  // checkpoint H_c (the bf16 copy the chunk's products read)
-      bulk_store(hck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
-      bulk_commit();
-    }
-    const uint32_t sQ = smem_u32(set(c) + FwdSmem::Qt), sK = smem_u32(set(c) + FwdSmem::Kt);
-    const uint32_t sP = smem_u32(set(c) + FwdSmem::Pt);
-    if (tid == 0) {
-      mma_seq<8, 0, 128, 0, 128>(tm + F_X, sWW, sH, id_xo, 0u);  // X = [W;W] H
-      umma_commit(&barB);
-      mma_seq<8, 0, 64, 0, 128>(tm + F_O, sQ, sH, id_qh, 0u);    // O = Q H (waited on with C2)
-    }
-    ok = mma_wait(&barB, pB, status) && ok;
-    {
-      // delta = U - X, rows t (Dr was released by the previous chunk's O store before the
-      // barrier that ended that chunk); lanes 0-63 take columns 0-63, lanes 64-127 columns 64-127
-      const int c0 = upper * 64 + half * 32;
-      float u[32], x[32];
-      tmem_ld32(lane_tm + (uint32_t)(F_U + c0), u);
-      tmem_ld32(lane_tm + (uint32_t)(F_X + c0), x);
-      tmem_wait_ld();
-#pragma unroll
-      for (int e = 0; e < 32; ++e) u[e] -= x[e];
-      st_row32_bf16(Dr, 64, trow, c0, u);
-    }
-    if (more) ok = wait_chunk(c + 1) && ok;
-    if (tid == 0) bulk_wait_read();  // the checkpoint has left Ha before it is rewritten
-    publish();
-    if (tid == 0 && ok) {
-      mma_seq<4, 1, 64, 1, 64>(tm + F_H, sD, sK, id_hk, 1u);     // H^T += delta^T K
-      umma_commit(&barH);
-      mma_seq<4, 0, 64, 1, 64>(tm + F_O, sP, sD, id_pd, 1u);     // O += P delta
-      if (more)
-        mma_seq<4, 0, 128, 1, 64>(tm + F_U, smem_u32(set(c + 1) + FwdSmem::TT), smem_u32(set(c + 1) + FwdSmem::Vt), id_uw, 0u);
-      umma_commit(&barC);
-    }
-    ok = ok && mma_wait(&barH, pH, status);
-    {
-      // H^T row j -> bf16 Ha (and the final state)
-      const int c0 = half * 64;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        float v[32];
-        tmem_ld32(lane_tm + (uint32_t)(F_H + c0 + 32 * k), v);
-        tmem_wait_ld();
-        st_row32_bf16(Ha, 128, lane128, c0 + 32 * k, v);
-        if (!more && lane128 < D) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c0 + 32 * k + e < D) sn[(int64_t)bh * D * D + (int64_t)(c0 + 32 * k + e) * D + lane128] = v[e];
+  if (warp == 8) {
+    // ---------------- issuing warp (lane 0) ----------------
+    if (lane == 0) {
+      auto load_chunk = [&](int c) {
+        const ChunkAt a = chunk_at(b, c, T);
+        uint8_t* s = set(c);
+        uint64_t* lb = &lbar[c & 1];
+        const uint8_t* img = xt + ((size_t)bh * NC + c) * PREP_BYTES;
+        mbar_arrive_expect_tx(lb, FwdSmem::SET);
+        bulk_load(s + FwdSmem::Pt, img + PREP_P, TILE_TT, lb);
+        bulk_load(s + FwdSmem::Ut, img + PREP_U, 2 * TILE_TD + TILE_JI, lb);
+        tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
+      };
+      if (NC > 0) load_chunk(0);
+      if (NC > 1) load_chunk(1);
+      uint32_t pl[2] = {0u, 0u}, pOR[2] = {0u, 0u}, pO[2] = {0u, 0u}, pHs = 0;
+      const uint32_t sH = smem_u32(Hs);
+      for (int c = 0; c < NC; ++c) {
+        if (!wait_or_flag(&lbar[c & 1], pl[c & 1], status, 4)) break;
+        if (!wait_or_flag(&barHs, pHs, status, 2)) break;                          // Hs = H_c
+        if (c >= 2 && !wait_or_flag(&barOR[c & 1], pOR[c & 1], status, 2)) break;  // O of c-2 read
+        tc_fence_after();
+        const uint8_t* s = set(c);
+        const uint32_t sU = smem_u32(s + FwdSmem::Ut), dO = tm + F_O + 128 * (c & 1);
+        mma_seq<8, 0, 128, 1, 128>(tm + F_H, sH, smem_u32(s + FwdSmem::Mt), idesc_bf16(128, 128, 0, 1), 1u);
+        mma_seq<8, 0, 64, 0, 128>(dO, smem_u32(s + FwdSmem::Qt), sH, idesc_bf16(64, 128, 0, 0), 0u);
+        mma_seq<4, 1, 64, 1, 64>(tm + F_H, sU, smem_u32(s + FwdSmem::Kt), idesc_bf16(128, 128, 1, 1), 1u);
+        umma_commit(&barH);
+        mma_seq<4, 0, 64, 1, 64>(dO, smem_u32(s + FwdSmem::Pt), sU, idesc_bf16(64, 128, 0, 1), 1u);
+        umma_commit(&barO[c & 1]);
+        if (c + 2 < NC) {  // the set is free once every product of chunk c is done
+          if (!wait_or_flag(&barO[c & 1], pO[c & 1], status, 2)) break;
+          load_chunk(c + 2);
         }
       }
     }
-    ok = ok && mma_wait(&barC, pC, status);
-    if (c + 2 < NC) load_chunk(c + 2);  // set (c & 1) is free: every product of chunk c is done
-    {
-      // O rows (M=64 layout: lanes 0-15 of each quarter hold t = 16 quarter + lane) staged in
-      // Dr (free once the state update has completed) for one TMA store
-      const int t = quarter * 16 + (lane & 15);
-      const int c0 = half * 64;
+    __syncwarp();
+  } else {
+    // ---------------- reading warps 0-7 ----------------
+    const int quarter = warp & 3, half = warp >> 2;
+    const int lane128 = quarter * 32 + lane;  // this thread's tensor-memory lane
+    const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
+    // H^T row j = column j of the initial state (warps 0-3); its bf16 copy is the first checkpoint
+    if (half == 0) column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, lane128, lane_tm, F_H, Hs);
+    fence_async_smem();
+    bar_sync_named(1, NR);
+    if (tid == 0 && NC > 0) {
+      bulk_store(hck + (size_t)bh * NC * TILE_JI, Hs, TILE_JI);
+      bulk_commit();
+    }
+    tc_fence_before();
+    mbar_arrive(&barHs);
+    uint32_t pH = 0, pO[2] = {0u, 0u};
+    bool ok = true;
+    // O of chunk c: tensor memory -> registers -> Ot (M=64 layout: lanes 0-15 of each quarter
+    // hold the token rows) -> one TMA store
+    auto out_rows = [&](int c) -> bool {
+      if (!wait_or_flag(&barO[c & 1], pO[c & 1], status, 2)) return false;
+      tc_fence_after();
+      float v[64];
+      const uint32_t col = (uint32_t)(F_O + 128 * (c & 1) + half * 64);
+      tmem_ld32(lane_tm + col, *reinterpret_cast<float(*)[32]>(v));
+      tmem_ld32(lane_tm + col + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&barOR[c & 1]);
+      if (tid == 0) bulk_wait_read_but_newest();  // the previous O store has left Ot
+      bar_sync_named(1, NR);
+      if (lane < 16) {
+        st_row32_bf16(Ot, 64, quarter * 16 + lane, half * 64, v);
+        st_row32_bf16(Ot, 64, quarter * 16 + lane, half * 64 + 32, v + 32);
+      }
+      fence_async_smem();
+      bar_sync_named(1, NR);
+      if (tid == 0) {
+        const ChunkAt a = chunk_at(b, c, T);
+        tma_store_4d(&omap, Ot, 0, h, a.t0, b);
+        if (D > 64) tma_store_4d(&omap, Ot + TILE_TD / 2, 64, h, a.t0, b);
+        bulk_commit();
+      }
+      return true;
+    };
+    for (int c = 0; c < NC && ok; ++c) {
+      if (c > 0 && !(ok = out_rows(c - 1))) break;
+      if (!(ok = wait_or_flag(&barH, pH, status, 2))) break;
+      tc_fence_after();
+      if (tid == 0) {  // the checkpoint of H_c has left Hs (the newest group, O of c - 1, may not)
+        if (c == 0) bulk_wait_read();
+        else bulk_wait_read_but_newest();
+      }
+      bar_sync_named(1, NR);
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         float v[32];
-        tmem_ld32(lane_tm + (uint32_t)(F_O + c0 + 32 * k), v);
+        const int c0 = half * 64 + 32 * k;
+        tmem_ld32(lane_tm + (uint32_t)(F_H + c0), v);
         tmem_wait_ld();
-        if (lane < 16) st_row32_bf16(Dr, 64, t, c0 + 32 * k, v);
+        st_row32_bf16(Hs, 128, lane128, c0, v);
+        if (c + 1 == NC && lane128 < D) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (c0 + e < D) sn[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + lane128] = v[e];
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&barHs);
+      if (c + 1 < NC) {  // checkpoint H_{c+1} for chunk c + 1 while the next products run
+        bar_sync_named(1, NR);
+        if (tid == 0) {
+          bulk_store(hck + ((size_t)bh * NC + c + 1) * TILE_JI, Hs, TILE_JI);
+          bulk_commit();
+        }
       }
     }
-    if (more) readout_w();
-    fence_async_smem();
-    __syncthreads();
-    if (tid == 0) {
-      tma_store_4d(&omap, Dr, 0, h, a.t0, b);
-      if (D > 64) tma_store_4d(&omap, Dr + TILE_TD / 2, 64, h, a.t0, b);
-      bulk_commit();
-      bulk_wait_read();  // Dr is rewritten by the next chunk's delta readout
+    if (ok && NC > 0) out_rows(NC - 1);
+    if (NC == 0 && half == 0) {
+      const int j = lane128;
+      if (j < D)
+        for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = s0[(int64_t)bh * D * D + (int64_t)i * D + j];
     }
-    publish();
+    if (tid == 0) bulk_wait_all();
   }
-  if (NC == 0 && half == 0) {
-    const int j = lane128;
-    if (j < D)
-      for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = s0[(int64_t)bh * D * D + (int64_t)i * D + j];
-  }
-  if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tm, 512);
 }
 
 // ------------------------------------------------------------------------------------------
-// backward, sequential (256 threads): the dH^T chain in tensor memory, in reverse chunk order,
-// checkpointing the bf16 dH_{c+1} per chunk:
-//   B:  ddelta^T = dH^T K^T;  [ddelta^T | dH^T] += dO^T [P | Q]    (N = 192)
-//   C1: dH^T -= ddelta^T W                                          -> bf16 copy of dH
-//   C2: W of chunk c-1 = T' K                                       -> staged for the next C1
+// backward, sequential (256 threads): the dH^T chain in tensor memory in reverse chunk order,
+//   dH^T_c = dH^T_{c+1} + dHs M^T + dO^T Q'      (12 k-steps; dHs = bf16 dH^T_{c+1})
+// dHs is double-buffered, so its bulk-copied checkpoint never waits on the chain.
 // ------------------------------------------------------------------------------------------
 struct DhSmem {
-  // per-chunk input set: T', then P immediately before Q (the MN-major B operand [P | Q]), K, dO
-  static constexpr uint32_t Tt = 0, Pt = TILE_TT, Qt = 2 * TILE_TT, Kt = Qt + TILE_TD, Gt = Kt + TILE_TD;
+  // per-chunk set: [Q' | M] as the prep image holds them, then dO
+  static constexpr uint32_t Qt = 0, Mt = TILE_TD, Gt = Mt + TILE_JI;
   static constexpr uint32_t SET = Gt + TILE_TD;  // 64 KB
-  static constexpr uint32_t Wk = 2 * SET, Ha = Wk + TILE_TD, Da = Ha + TILE_JI, END = Da + TILE_JT;
+  static constexpr int NSET = 2;
+  static constexpr uint32_t Ha = NSET * SET, END = Ha + 2 * TILE_JI;  // 192 KB
 };
-constexpr int G_D = 0, G_H = 64, G_W = 192;
+constexpr int G_H = 0;
 
 __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    const __grid_constant__ CUtensorMap gmap, const bf16* __restrict__ beta,
-    const uint8_t* __restrict__ xt, const float* __restrict__ dsn,
+    const __grid_constant__ CUtensorMap gmap, const uint8_t* __restrict__ xt, const float* __restrict__ dsn,
     float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Wk = sm + DhSmem::Wk, *Ha = sm + DhSmem::Ha, *Da = sm + DhSmem::Da;
-  __shared__ uint64_t barB, barH, barC, lbar[2];
+  uint8_t* Ha = sm + DhSmem::Ha;
+  __shared__ uint64_t barH, lbar[DhSmem::NSET];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, half = warp >> 2;
   const int lane128 = quarter * 32 + lane;
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  uint32_t lphase[2] = {0u, 0u};
-  auto set = [&](int c) { return sm + (uint32_t)(c & 1) * DhSmem::SET; };
-  auto load_chunk = [&](int c) {
+  uint32_t lphase[DhSmem::NSET] = {0u, 0u}, pH = 0;
+  auto set = [&](int c) { return sm + (uint32_t)(c % DhSmem::NSET) * DhSmem::SET; };
+  auto load_chunk = [&](int c) {  // thread 0
     const ChunkAt a = chunk_at(b, c, T);
     uint8_t* s = set(c);
-    if (tid == 0) {
-      uint64_t* lb = &lbar[c & 1];
-      mbar_arrive_expect_tx(lb, 3 * TILE_TD + 2 * TILE_TT);
-      const uint8_t* pre = xt + ((size_t)bh * NC + c) * PREP_BYTES;
-      bulk_load(s + DhSmem::Tt, pre + PREP_T, TILE_TT, lb);
-      bulk_load(s + DhSmem::Pt, pre + PREP_P, TILE_TT, lb);
-      tma_tile(s + DhSmem::Qt, &qmap, lb, h, a.t0, b);
-      tma_tile(s + DhSmem::Kt, &kmap, lb, h, a.t0, b);
-      tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
-    }
+    uint64_t* lb = &lbar[c % DhSmem::NSET];
+    mbar_arrive_expect_tx(lb, DhSmem::SET);
+    bulk_load(s + DhSmem::Qt, xt + ((size_t)bh * NC + c) * PREP_BYTES + PREP_Q, TILE_TD + TILE_JI, lb);
+    tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
   };
   auto wait_chunk = [&](int c) -> bool {
-    const bool r = mbar_wait(&lbar[c & 1], lphase[c & 1]);
-    lphase[c & 1] ^= 1u;
+    const int k = c % DhSmem::NSET;
+    const bool r = mbar_wait(&lbar[k], lphase[k]);
+    lphase[k] ^= 1u;
     if (!r && tid == 0) atomicOr(status, 4);
     return r;
   };
   if (tid == 0) {
-    mbar_init(&barB, 1); mbar_init(&barH, 1); mbar_init(&barC, 1);
-    mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
+    mbar_init(&barH, 1);
+    for (int k = 0; k < DhSmem::NSET; ++k) mbar_init(&lbar[k], 1);
     mbar_fence_init();
   }
-  if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
+  if (warp == 0) { tmem_alloc(&tbase, 128); tmem_relinquish(); }
   __syncthreads();
-  if (NC > 0) load_chunk(NC - 1);
+  if (tid == 0)
+    for (int k = 1; k <= DhSmem::NSET && NC - k >= 0; ++k) load_chunk(NC - k);
   tc_fence_after();
   const uint32_t tm = tbase;
   const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
-  if (half == 0)
-    column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, lane128, lane_tm, G_H, Ha);
-  const uint32_t sW = smem_u32(Wk), sH = smem_u32(Ha), sD = smem_u32(Da);
-  const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);       // ddelta^T = dH^T K^T
-  const uint32_t id_opq = idesc_bf16(128, 192, 1, 1);     // [ddelta^T | dH^T] += dO^T [P | Q]
-  const uint32_t id_dw = idesc_bf16(128, 128, 0, 1, 1);   // dH^T -= ddelta^T W
-  const uint32_t id_tk = idesc_bf16(64, 128, 0, 1);       // W = T' K
-  auto readout_w = [&]() {  // W rows (M=64 layout) -> Wk [t][i]
-    const int t = quarter * 16 + (lane & 15);
-    const int c0 = half * 64;
+  auto dhs = [&](int c) { return Ha + (uint32_t)(c & 1) * TILE_JI; };  // dH_{c+1}, read by chunk c
+  if (half == 0 && NC > 0)
+    column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, lane128, lane_tm, G_H,
+                            dhs(NC - 1));
+  bool ok = publish_ok(true);
+  for (int c = NC - 1; c >= 0 && ok; --c) {
+    uint8_t* hb = dhs(c);
+    if (tid == 0) {  // checkpoint dH_{c+1} for chunk c
+      bulk_store(dhck + ((size_t)bh * NC + c) * TILE_JI, hb, TILE_JI);
+      bulk_commit();
+    }
+    ok = wait_chunk(c) && ok;
+    if (tid == 0 && ok) {
+      const uint8_t* s = set(c);
+      mma_seq<8, 0, 128, 0, 128>(tm + G_H, smem_u32(hb), smem_u32(s + DhSmem::Mt), idesc_bf16(128, 128, 0, 0), 1u);  // += dHs M^T
+      mma_seq<4, 1, 64, 1, 64>(tm + G_H, smem_u32(s + DhSmem::Gt), smem_u32(s + DhSmem::Qt),
+                               idesc_bf16(128, 128, 1, 1), 1u);                                          // += dO^T Q'
+      umma_commit(&barH);
+    }
+    if (ok) ok = mma_wait(&barH, pH, status);
+    if (tid == 0) {
+      if (ok && c - DhSmem::NSET >= 0) load_chunk(c - DhSmem::NSET);  // set of chunk c is free
+      bulk_wait_read_but_newest();  // the checkpoint of chunk c + 1 has left the other buffer
+    }
+    __syncthreads();
+    uint8_t* nb = dhs(c - 1);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       float v[32];
-      tmem_ld32(lane_tm + (uint32_t)(G_W + c0 + 32 * k), v);
+      const int c0 = half * 64 + 32 * k;
+      tmem_ld32(lane_tm + (uint32_t)(G_H + c0), v);
       tmem_wait_ld();
-      if (lane < 16) st_row32_bf16(Wk, 64, t, c0 + 32 * k, v);
-    }
-  };
-  uint32_t pB = 0, pH = 0, pC = 0;
-  bool ok = true;
-  if (NC > 0) {
-    ok = wait_chunk(NC - 1);
-    publish();
-    if (tid == 0) {
-      mma_seq<4, 0, 64, 1, 64>(tm + G_W, smem_u32(set(NC - 1) + DhSmem::Tt), smem_u32(set(NC - 1) + DhSmem::Kt),
-                               id_tk, 0u);
-      umma_commit(&barC);
-    }
-    ok = mma_wait(&barC, pC, status) && ok;
-    if (NC > 1) load_chunk(NC - 2);
-    readout_w();
-    publish();
-  }
-  for (int c = NC - 1; c >= 0 && ok; --c) {
-    const bool more = c > 0;
-    if (tid == 0) {  // checkpoint dH_{c+1}
-      bulk_store(dhck + ((size_t)bh * NC + c) * TILE_JI, Ha, TILE_JI);
-      bulk_commit();
-    }
-    const uint32_t sK = smem_u32(set(c) + DhSmem::Kt), sP = smem_u32(set(c) + DhSmem::Pt);
-    const uint32_t sG = smem_u32(set(c) + DhSmem::Gt);
-    if (tid == 0) {
-      mma_seq<8, 0, 128, 0, 64>(tm + G_D, sH, sK, id_hk, 0u);   // ddelta^T = dH^T K^T
-      mma_seq<4, 1, 64, 1, 64>(tm + G_D, sG, sP, id_opq, 1u);   // [ddelta^T | dH^T] += dO^T [P | Q]
-      umma_commit(&barB);
-    }
-    ok = mma_wait(&barB, pB, status) && ok;
-    {
-      const int c0 = half * 32;
-      float v[32];
-      tmem_ld32(lane_tm + (uint32_t)(G_D + c0), v);
-      tmem_wait_ld();
-      st_row32_bf16(Da, 128, lane128, c0, v);  // ddelta^T row j
-    }
-    if (more) ok = wait_chunk(c - 1) && ok;
-    if (tid == 0) bulk_wait_read();
-    publish();
-    if (tid == 0 && ok) {
-      mma_seq<4, 0, 128, 1, 64>(tm + G_H, sD, sW, id_dw, 1u);   // dH^T -= ddelta^T W
-      umma_commit(&barH);
-      if (more)
-        mma_seq<4, 0, 64, 1, 64>(tm + G_W, smem_u32(set(c - 1) + DhSmem::Tt), smem_u32(set(c - 1) + DhSmem::Kt),
-                                 id_tk, 0u);
-      umma_commit(&barC);
-    }
-    ok = ok && mma_wait(&barH, pH, status);
-    {
-      const int c0 = half * 64;
+      st_row32_bf16(nb, 128, lane128, c0, v);
+      if (c == 0 && lane128 < D) {
 #pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        float v[32];
-        tmem_ld32(lane_tm + (uint32_t)(G_H + c0 + 32 * k), v);
-        tmem_wait_ld();
-        st_row32_bf16(Ha, 128, lane128, c0 + 32 * k, v);
-        if (c == 0 && lane128 < D) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c0 + 32 * k + e < D) ds0[(int64_t)bh * D * D + (int64_t)(c0 + 32 * k + e) * D + lane128] = v[e];
-        }
+        for (int e = 0; e < 32; ++e)
+          if (c0 + e < D) ds0[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + lane128] = v[e];
       }
     }
-    ok = ok && mma_wait(&barC, pC, status);
-    if (c >= 2) load_chunk(c - 2);  // set (c & 1) is free: every product of chunk c is done
-    if (more) readout_w();
-    publish();
+    ok = publish_ok(ok);
   }
   if (NC == 0 && half == 0) {
     const int j = lane128;
@@ -587,7 +680,7 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
   if (tid == 0) bulk_wait_all();
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tm, 512);
+  if (warp == 0) tmem_dealloc(tm, 128);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -911,17 +1004,16 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
     if ((rc = make_token_map(&qm, q, B, T, H, D)) || (rc = make_token_map(&km, k, B, T, H, D)) ||
         (rc = make_token_map(&vm, v, B, T, H, D)) || (rc = make_token_map(&om, o, B, T, H, D)))
       return rc;
-    const size_t sp = smem_bytes(PREP_BYTES + 64 * 65 * 4);
+    const size_t sp = smem_bytes(PrepSmem::END);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp), "prep attr");
-    scan_prep_kernel<<<B * H * NC, NT, sp, st>>>(qm, km, (const bf16*)beta, xt, T, H, D, NC, status);
+    scan_prep_kernel<<<B * H * NC, NP, sp, st>>>(qm, km, vm, (const bf16*)beta, xt, T, H, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 prep");
   } else {
     memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm));
   }
   const size_t sf = smem_bytes(FwdSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sf), "fwd attr");
-  scan_fwd_kernel<<<B * H, NT2, sf, st>>>(qm, km, vm, om, (const bf16*)beta,
-                                         state0, xt, state_n, hck, T, H, D, NC, status);
+  scan_fwd_kernel<<<B * H, NF, sf, st>>>(km, om, state0, xt, state_n, hck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 fwd");
   return VB_OK;
 }
@@ -952,8 +1044,7 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   }
   const size_t sd = smem_bytes(DhSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd), "dh attr");
-  scan_dh_kernel<<<B * H, NT2, sd, st>>>(qm, km, gm, (const bf16*)beta, xt,
-                                        dstate_n, dstate0, dhck, T, H, D, NC, status);
+  scan_dh_kernel<<<B * H, NT2, sd, st>>>(gm, xt, dstate_n, dstate0, dhck, T, H, D, NC, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 dh");
   if (NC > 0) {
     const size_t sg = smem_bytes(GrSmem::END);
