@@ -701,30 +701,25 @@ constexpr int R_DP = 64, R_DW = 128, R_DV = 256, R_DT = 384;                    
 constexpr int R_DQ = 128, R_Y = 256, R_Z = 320, R_DK = 128;                       // batches 4-7
 
 constexpr int NG = 256;  // threads of the local-gradient kernel: two warps per lane quadrant
+// one [64 t][128] bf16 tile to (b, h, tokens t0..) of a [B, T, H, D] tensor (rows past T and
+// columns past D are not written)
+__device__ __forceinline__ void store_tile(const CUtensorMap* map, const uint8_t* tile, int h, int t0, int b, int D) {
+  tma_store_4d(map, tile, 0, h, t0, b);
+  if (D > 64) tma_store_4d(map, tile + TILE_TD / 2, 64, h, t0, b);
+  bulk_commit();
+}
 __device__ __forceinline__ void ld32w(uint32_t tm, int col, float (&v)[32]) {
   tmem_ld32(tm + (uint32_t)col, v);
   tmem_wait_ld();
-}
-// row `r` of a float32 accumulator (64 of its columns from `c0`) as bf16 at columns c0.. of a
-// [64 t][128] global row (dq, dk, dv); columns at or past D are skipped
-__device__ __forceinline__ void store_row64(bf16* dst, const float* r, int c0, int D) {
-#pragma unroll
-  for (int i = 0; i < 64; i += 8) {
-    if (c0 + i >= D) break;
-    uint4 w4;
-    w4.x = pack_bf16(r[i], r[i + 1]); w4.y = pack_bf16(r[i + 2], r[i + 3]);
-    w4.z = pack_bf16(r[i + 4], r[i + 5]); w4.w = pack_bf16(r[i + 6], r[i + 7]);
-    *reinterpret_cast<uint4*>(dst + c0 + i) = w4;
-  }
 }
 
 __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap gmap,
-    const bf16* __restrict__ beta, const uint8_t* __restrict__ xt, const uint8_t* __restrict__ hck,
-    const uint8_t* __restrict__ dhck, bf16* __restrict__ dq,
-    bf16* __restrict__ dk, bf16* __restrict__ dv, bf16* __restrict__ dbeta, int T, int H, int D,
-    int NC, int* status) {
+    const __grid_constant__ CUtensorMap dqmap, const __grid_constant__ CUtensorMap dkmap,
+    const __grid_constant__ CUtensorMap dvmap, const bf16* __restrict__ beta, const uint8_t* __restrict__ xt,
+    const uint8_t* __restrict__ hck, const uint8_t* __restrict__ dhck, bf16* __restrict__ dbeta, int T, int H,
+    int D, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t *Qt = sm + GrSmem::Qt, *Kt = sm + GrSmem::Kt, *Vt = sm + GrSmem::Vt, *Gt = sm + GrSmem::Gt;
@@ -737,7 +732,7 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   uint8_t* dGt = Pt;   // [64][64]
   float* scr = reinterpret_cast<float*>(Ht);  // [64][65] floats
   __shared__ float bsm[C], db1[C], db2s[2][C];
-  __shared__ uint64_t bar, lbar;
+  __shared__ uint64_t bar, lbar[3];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // warps w and w + 4 share tensor-memory lane quadrant w % 4 and split the columns (half)
@@ -745,28 +740,38 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   const int lane128 = quarter * 32 + lane;
   const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
   const int t0 = c * C, valid = min(C, T - t0);
-  const int64_t ld = (int64_t)H * D;
   const int64_t row0 = (int64_t)b * T + t0;
   const int trow = quarter * 16 + (lane & 15);  // token row of an M=64 accumulator (lane < 16)
   const bool rowlane = lane < 16;
   const size_t chunk = (size_t)bh * NC + c;
-  if (tid == 0) { mbar_init(&bar, 1); mbar_init(&lbar, 1); mbar_fence_init(); }
-  __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(&lbar, 4 * TILE_TD + 2 * TILE_JI + 3 * TILE_TT);
-    tma_tile(Qt, &qmap, &lbar, h, t0, b);
-    tma_tile(Kt, &kmap, &lbar, h, t0, b);
-    tma_tile(Vt, &vmap, &lbar, h, t0, b);
-    tma_tile(Gt, &gmap, &lbar, h, t0, b);
-    bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar);
-    bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar);
-    bulk_load(Xt, xt + chunk * PREP_BYTES + PREP_X, TILE_TT, &lbar);
-    bulk_load(Pt, xt + chunk * PREP_BYTES + PREP_P, TILE_TT, &lbar);
-    bulk_load(Tt, xt + chunk * PREP_BYTES + PREP_T, TILE_TT, &lbar);
+    mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_init(&lbar[2], 1);
+    mbar_fence_init();
   }
+  __syncthreads();
+  if (tid == 0) {  // in the order of first use: batch 1's operands, batch 2's, then X and Q
+    const uint8_t* pre = xt + chunk * PREP_BYTES;
+    mbar_arrive_expect_tx(&lbar[0], 2 * TILE_TD + TILE_JI + TILE_TT);
+    tma_tile(Kt, &kmap, &lbar[0], h, t0, b);
+    bulk_load(Tt, pre + PREP_T, TILE_TT, &lbar[0]);
+    tma_tile(Vt, &vmap, &lbar[0], h, t0, b);
+    bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar[0]);
+    mbar_arrive_expect_tx(&lbar[1], TILE_TD + TILE_JI + TILE_TT);
+    bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar[1]);
+    tma_tile(Gt, &gmap, &lbar[1], h, t0, b);
+    bulk_load(Pt, pre + PREP_P, TILE_TT, &lbar[1]);
+    mbar_arrive_expect_tx(&lbar[2], TILE_TD + TILE_TT);
+    bulk_load(Xt, pre + PREP_X, TILE_TT, &lbar[2]);
+    tma_tile(Qt, &qmap, &lbar[2], h, t0, b);
+  }
+  auto loaded = [&](int k) -> bool {
+    const bool r = mbar_wait(&lbar[k], 0);
+    if (!r && tid == 0) atomicOr(status, 4);
+    return r;
+  };
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
-  if (!mbar_wait(&lbar, 0) && tid == 0) atomicOr(status, 4);
+  bool ok = loaded(0);
   if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
   publish();
   const uint32_t tm = tbase;
@@ -777,9 +782,8 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   const uint32_t sdP = smem_u32(dPt), sdW = smem_u32(dWt), sdX = smem_u32(dXt), sY = smem_u32(Yt);
   const uint32_t sdG = smem_u32(dGt);
   uint32_t phase = 0;
-  bool ok = true;
-  // batch 1: K K^T, Q K^T, W^T, U^T, ddelta^T = dH'^T K^T
-  if (tid == 0) {
+  // batch 1: K K^T, W^T, U^T, ddelta^T = dH'^T K^T
+  if (tid == 0 && ok) {
     const uint32_t id64 = idesc_bf16(64, 64, 0, 0);
     mma_seq<8, 0, 64, 0, 64>(tm + R_KK, sK, sK, id64, 0u);
     const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
@@ -789,12 +793,13 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     mma_seq<8, 0, 128, 0, 64>(tm + R_DD, sdH, sK, id_hk, 0u);
     umma_commit(&bar);
   }
-  ok = mma_wait(&bar, phase, status);
+  ok = ok && mma_wait(&bar, phase, status);
   {
     float w[32];
     ld32w(lane_tm, R_W + half * 32, w);
     st_row32_bf16(Wr, 128, lane128, half * 32, w);
   }
+  ok = loaded(1) && ok;
   publish();
   // batch 2: X = H^T W^T; ddelta^T += dO^T P
   if (tid == 0 && ok) {
@@ -842,9 +847,10 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     ld64(lane_tm, R_DW + half * 64, r);
     if (rowlane) st_row64_bf16(dWt, 64, trow, half, r);
     ld64(lane_tm, R_DV + half * 64, r);
-    if (rowlane && trow < valid) store_row64(dv + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
+    if (rowlane) st_row64_bf16(Vt, 64, trow, half, r);  // dV staged over V (its products are done)
   }
   publish();
+  if (tid == 0) store_tile(&dvmap, Vt, h, t0, b, D);
   // batch 4: dQ = dO H^T + dP K; dT' += dW K^T
   if (tid == 0 && ok) {
     const uint32_t id_oh = idesc_bf16(64, 128, 0, 1);
@@ -859,7 +865,8 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   {
     float r[64];
     ld64(lane_tm, R_DQ + half * 64, r);
-    if (rowlane && trow < valid) store_row64(dq + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
+    if (rowlane) st_row64_bf16(Gt, 64, trow, half, r);  // dQ staged over dO (its products are done)
+    ok = loaded(2) && ok;
     // dT' row t: dX = dT' diag(beta) (bf16 operand), dT' * X products for dbeta's first part
     float dt[32];
     ld32w(lane_tm, R_DT + half * 32, dt);
@@ -876,6 +883,10 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     }
   }
   publish();
+  if (tid == 0) {
+    store_tile(&dqmap, Gt, h, t0, b, D);
+    bulk_wait_read_but_newest();  // dV has left V, which Y overwrites below
+  }
   if (tid < C) {
     float a = 0.f;
     for (int t = 0; t < C; ++t) a += scr[t * 65 + tid];
@@ -946,10 +957,15 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   {
     float r[64];
     ld64(lane_tm, R_DK + half * 64, r);
-    if (rowlane && trow < valid) store_row64(dk + (row0 + trow) * ld + (int64_t)h * D, r, half * 64, D);
+    if (rowlane) st_row64_bf16(Kt, 64, trow, half, r);  // dK staged over K (its products are done)
   }
+  fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) {
+    store_tile(&dkmap, Kt, h, t0, b, D);
+    bulk_wait_read();
+  }
   if (warp == 0) tmem_dealloc(tm, 512);
 }
 
@@ -1049,8 +1065,11 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   if (NC > 0) {
     const size_t sg = smem_bytes(GrSmem::END);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sg), "grad attr");
-    scan_grad_kernel<<<B * H * NC, NG, sg, st>>>(qm, km, vm, gm, (const bf16*)beta,
-                                                 xt, hck, dhck, (bf16*)dq, (bf16*)dk, (bf16*)dv,
+    CUtensorMap dqm, dkm, dvm;
+    if ((rc = make_token_map(&dqm, dq, B, T, H, D)) || (rc = make_token_map(&dkm, dk, B, T, H, D)) ||
+        (rc = make_token_map(&dvm, dv, B, T, H, D)))
+      return rc;
+    scan_grad_kernel<<<B * H * NC, NG, sg, st>>>(qm, km, vm, gm, dqm, dkm, dvm, (const bf16*)beta, xt, hck, dhck,
                                                  (bf16*)dbeta, T, H, D, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 grad");
   }
