@@ -2,9 +2,10 @@
 // and its gradient vesper/kernels/norm_triton.py:47-82).
 //
 // Forward: one warp per row, the row held in registers (16-byte vector loads when the width
-// allows), one read and one write of the row. Backward: one warp per row for dx; the gain
-// gradient is summed per warp in shared memory, per CTA in warp order, then across CTAs in CTA
-// order by a second kernel: no atomics, the same bits on every run.
+// allows), one read and one write of the row. Backward: one warp per row for dx, the next row's
+// raw 16-byte words in flight and two CTAs of eight warps per SM; the gain gradient is summed per
+// warp in registers, per CTA in warp order, then across CTAs in CTA order by a second kernel: no
+// atomics, the same bits on every run.
 #include <mutex>
 
 #include "common.cuh"
@@ -14,8 +15,8 @@ namespace {
 
 constexpr int WARPS = 8;          // warps per CTA (forward rows in flight; backward warps)
 constexpr int FWD_ROWS_PER_WARP = 2;   // rows each forward warp loads before computing
-constexpr int BWD_WARPS = 4;
-constexpr int BWD_ROWS_PER_WARP = 16;
+constexpr int BWD_WARPS = 8;
+constexpr int BWD_ROWS_PER_WARP = 8;
 constexpr int BWD_ROWS_PER_CTA = BWD_WARPS * BWD_ROWS_PER_WARP;
 
 // 16-byte vector loads of E = 16/sizeof(T) elements; VPL vectors per lane cover 32*E*VPL channels
@@ -30,6 +31,32 @@ __device__ __forceinline__ void load_row(const T* __restrict__ row, int nv, int 
 #pragma unroll
       for (int e = 0; e < E; ++e) v[i][e] = 0.f;
     }
+  }
+}
+
+// the raw 16-byte words of a row (zero past the width) and their conversion to floats
+template <int VPL>
+__device__ __forceinline__ void load_raw(const void* __restrict__ row, int nv, int lane, uint4 (&r)[VPL]) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int vi = lane + 32 * i;
+    r[i] = vi < nv ? __ldg(reinterpret_cast<const uint4*>(row) + vi) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& raw, float (&f)[16 / sizeof(T)]) {
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < (int)(16 / sizeof(T)); ++i) f[i] = to_f32<T>(e[i]);
+}
+// the gain at 16-byte vector vi of a row (E = 16 / sizeof(T) floats)
+template <int E>
+__device__ __forceinline__ void load_gain(const float* __restrict__ w, int vi, float (&g)[E]) {
+  const float4* gp = reinterpret_cast<const float4*>(w + vi * E);
+#pragma unroll
+  for (int q = 0; q < E / 4; ++q) {
+    const float4 g4 = __ldg(gp + q);
+    g[4 * q] = g4.x; g[4 * q + 1] = g4.y; g[4 * q + 2] = g4.z; g[4 * q + 3] = g4.w;
   }
 }
 
@@ -114,13 +141,13 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict
 // while the current one is computed; the gain gradient stays in registers per lane, then is
 // summed over the CTA's warps in warp order into partial[blockIdx.x][width].
 template <typename T, int VPL>
-__global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __restrict__ x,
-                                                                     const float* __restrict__ w,
-                                                                     const T* __restrict__ dy,
-                                                                     const float* __restrict__ inv,
-                                                                     T* __restrict__ dx,
-                                                                     float* __restrict__ partial,
-                                                                     int64_t rows, int width) {
+__global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T* __restrict__ x,
+                                                                        const float* __restrict__ w,
+                                                                        const T* __restrict__ dy,
+                                                                        const float* __restrict__ inv,
+                                                                        T* __restrict__ dx,
+                                                                        float* __restrict__ partial,
+                                                                        int64_t rows, int width) {
   constexpr int E = 16 / sizeof(T);
   extern __shared__ float acc_s[];  // [BWD_WARPS][width]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -131,11 +158,11 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[i][e] = 0.f;
   const int64_t row0 = (int64_t)blockIdx.x * BWD_ROWS_PER_CTA;
-  float xv[2][VPL][E], dv[2][VPL][E];
+  uint4 xr[2][VPL], dr[2][VPL];
   int64_t row = row0 + warp;
   if (row < rows) {
-    load_row<T, VPL>(x + row * width, nv, lane, xv[0]);
-    load_row<T, VPL>(dy + row * width, nv, lane, dv[0]);
+    load_raw<VPL>(x + row * width, nv, lane, xr[0]);
+    load_raw<VPL>(dy + row * width, nv, lane, dr[0]);
   }
 #pragma unroll 2
   for (int k = 0; k < BWD_ROWS_PER_WARP; ++k) {
@@ -144,8 +171,8 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __
     if (row >= rows) break;
     const int64_t nrow = row + BWD_WARPS;
     if (k + 1 < BWD_ROWS_PER_WARP && nrow < rows) {
-      load_row<T, VPL>(x + nrow * width, nv, lane, xv[cur ^ 1]);
-      load_row<T, VPL>(dy + nrow * width, nv, lane, dv[cur ^ 1]);
+      load_raw<VPL>(x + nrow * width, nv, lane, xr[cur ^ 1]);
+      load_raw<VPL>(dy + nrow * width, nv, lane, dr[cur ^ 1]);
     }
     const float iv = __ldg(inv + row);
     float s = 0.f;
@@ -153,8 +180,12 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __
     for (int i = 0; i < VPL; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
+        float xv[E], dv[E], g[E];
+        unpack<T>(xr[cur][i], xv);
+        unpack<T>(dr[cur][i], dv);
+        load_gain<E>(w, vi, g);
 #pragma unroll
-        for (int e = 0; e < E; ++e) s += dv[cur][i][e] * __ldg(w + vi * E + e) * (xv[cur][i][e] * iv);
+        for (int e = 0; e < E; ++e) s += dv[e] * g[e] * (xv[e] * iv);
       }
     }
     const float mean = warp_sum(s) / (float)width;
@@ -162,13 +193,15 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_vec_kernel(const T* __
     for (int i = 0; i < VPL; ++i) {
       const int vi = lane + 32 * i;
       if (vi < nv) {
-        float o[E];
+        float xv[E], dv[E], g[E], o[E];
+        unpack<T>(xr[cur][i], xv);
+        unpack<T>(dr[cur][i], dv);
+        load_gain<E>(w, vi, g);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const float xh = xv[cur][i][e] * iv;
-          const float d = dv[cur][i][e];
-          o[e] = iv * (d * __ldg(w + vi * E + e) - xh * mean);
-          acc[i][e] += d * xh;
+          const float xh = xv[e] * iv;
+          o[e] = iv * (dv[e] * g[e] - xh * mean);
+          acc[i][e] += dv[e] * xh;
         }
         store_vec<T, E>(dx + row * width + vi * E, o);
       }
