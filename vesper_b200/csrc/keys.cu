@@ -17,10 +17,44 @@ namespace {
 constexpr int RUN = 64;        // tokens per warp
 constexpr int WARPS = 4;       // warps per CTA
 
-template <int EPL>
-struct Vec {
-  float v[EPL];
-};
+// EPL consecutive elements at p (aligned to their total size, up to 16 bytes) as one access per
+// 16 bytes, or one narrower access when they are fewer
+template <typename T, int EPL>
+__device__ __forceinline__ void ld_elems(const T* __restrict__ p, float (&out)[EPL]) {
+  constexpr int BYTES = EPL * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+    load_vec<T, EPL>(p, out);
+  } else if constexpr (BYTES == 8) {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f32<T>(e[i]);
+  } else if constexpr (BYTES == 4) {
+    const unsigned raw = __ldg(reinterpret_cast<const unsigned*>(p));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f32<T>(e[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) out[i] = to_f32<T>(p[i]);
+  }
+}
+template <typename T, int EPL>
+__device__ __forceinline__ void st_elems(T* __restrict__ p, const float (&in)[EPL]) {
+  constexpr int BYTES = EPL * (int)sizeof(T);
+  if constexpr (BYTES % 16 == 0) {
+    store_vec<T, EPL>(p, in);
+  } else if constexpr (BYTES == 8 || BYTES == 4) {
+    T e[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) e[i] = from_f32<T>(in[i]);
+    if constexpr (BYTES == 8) *reinterpret_cast<uint2*>(p) = *reinterpret_cast<const uint2*>(e);
+    else *reinterpret_cast<unsigned*>(p) = *reinterpret_cast<const unsigned*>(e);
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) p[i] = from_f32<T>(in[i]);
+  }
+}
 
 // loads EPL channels [c, c+EPL) of row `t` of the filter input (z for t >= 0, else history)
 template <typename T, int EPL>
@@ -31,19 +65,16 @@ __device__ __forceinline__ void load_in(const T* __restrict__ z, const float* __
   for (int e = 0; e < EPL; ++e) out[e] = 0.f;
   if (!live) return;
   if (t >= 0) {
-    const T* p = z + ((int64_t)b * T_ + t) * W + c;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) out[e] = to_f32<T>(p[e]);
+    ld_elems<T, EPL>(z + ((int64_t)b * T_ + t) * W + c, out);
   } else if (t >= -(K - 1)) {
-    const float* p = hist + ((int64_t)b * (K - 1) + (K - 1 + t)) * W + c;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) out[e] = p[e];
+    ld_elems<float, EPL>(hist + ((int64_t)b * (K - 1) + (K - 1 + t)) * W + c, out);
   }
 }
 
-// normalize_keys of one head vector spread over the warp: returns scale, den, sq
+// normalize_keys of one head vector spread over the warp: returns scale, s = u / scale (each
+// quotient computed once and reused by the caller), den, sq
 template <int EPL>
-__device__ __forceinline__ void norm_stats(const float (&u)[EPL], float floor_, float& scale,
+__device__ __forceinline__ void norm_stats(const float (&u)[EPL], float floor_, float& scale, float (&s)[EPL],
                                            float& den, float& sq) {
   float amax = 0.f;
 #pragma unroll
@@ -52,11 +83,48 @@ __device__ __forceinline__ void norm_stats(const float (&u)[EPL], float floor_, 
   float s2 = 0.f;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    const float s = u[e] / scale;
-    s2 += s * s;
+    s[e] = u[e] / scale;
+    s2 += s[e] * s[e];
   }
   sq = warp_sum(s2);
   den = sqrtf(fmaxf(sq, 1.0f));
+}
+
+// EPL channels [c, c+EPL) of key-gradient row t (zero when the row is not needed)
+template <typename T, int EPL>
+__device__ __forceinline__ void load_g(const T* __restrict__ gk, int b, int t, int T_, int W, int c, bool need,
+                                       float (&out)[EPL]) {
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) out[e] = 0.f;
+  if (!need || t < 0 || t >= T_) return;
+  ld_elems<T, EPL>(gk + ((int64_t)b * T_ + t) * W + c, out);
+}
+
+// the filter input's gradient du of one token from its window w[r] = row t - r and its key
+// gradient g (the normalisation's backward: (g / den - s (g . s) / den^3 [sq >= 1]) / scale)
+template <int EPL, int K>
+__device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float (&w)[K][EPL], const float (&g)[EPL],
+                                         float floor_, float (&du)[EPL]) {
+  float u[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    float a = 0.f;
+#pragma unroll
+    for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], w[r][e], a);
+    u[e] = a;
+  }
+  float scale, s[EPL], den, sq;
+  norm_stats<EPL>(u, floor_, scale, s, den, sq);
+  float dot = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) dot += g[e] * s[e];
+  dot = warp_sum(dot);
+  const float q = dot / (den * den * den);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float through = sq >= 1.0f ? s[e] * q : 0.f;
+    du[e] = (g[e] / den - through) / scale;
+  }
 }
 
 template <typename T, int EPL, int K>
@@ -92,12 +160,13 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
       for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[r][e], a);
       u[e] = a;
     }
-    float scale, den, sq;
-    norm_stats<EPL>(u, floor_, scale, den, sq);
+    float scale, s[EPL], den, sq;
+    norm_stats<EPL>(u, floor_, scale, s, den, sq);
     if (live) {
-      T* p = out + ((int64_t)b * T_ + t) * W + c;
+      float o[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) p[e] = from_f32<T>((u[e] / scale) / den);
+      for (int e = 0; e < EPL; ++e) o[e] = s[e] / den;
+      st_elems<T, EPL>(out + ((int64_t)b * T_ + t) * W + c, o);
     }
 #pragma unroll
     for (int r = K - 1; r > 0; --r)
@@ -136,52 +205,21 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
   // before the step for token t the window holds the rows of step t + 1: win[r] = row t + 1 - r
 #pragma unroll
   for (int r = 0; r < K; ++r) load_in<T, EPL>(z, hist, b, thi + 1 - r, T_, W, K, c, live && r > 0, win[r]);
-  for (int t = thi; t >= t0; --t) {
-    // slide one row older: win[r] = row t - r; only the oldest row is new
-#pragma unroll
-    for (int r = 0; r < K - 1; ++r)
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) win[r][e] = win[r + 1][e];
-    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, win[K - 1]);
-    float u[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      float a = 0.f;
-#pragma unroll
-      for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[r][e], a);
-      u[e] = a;
-    }
-    float scale, den, sq;
-    norm_stats<EPL>(u, floor_, scale, den, sq);
-    float g[EPL];
-    if (live) {
-      const T* p = gk + ((int64_t)b * T_ + t) * W + c;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) g[e] = to_f32<T>(p[e]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) g[e] = 0.f;
-    }
-    float dot = 0.f;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) dot += g[e] * (u[e] / scale);
-    dot = warp_sum(dot);
+  // tokens go in pairs: the two tokens' input gradients (their reductions independent) are formed
+  // together, then each enters the ring in turn, in the order of a one-token walk
+  auto step = [&](int t, const float (&du)[EPL], const float (&w)[K][EPL]) {
     // shift the gradient ring: dring[r] <- du at t + r
 #pragma unroll
     for (int r = K - 1; r > 0; --r)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) dring[r][e] = dring[r - 1][e];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      const float s = u[e] / scale;
-      const float through = sq >= 1.0f ? s * (dot / (den * den * den)) : 0.f;
-      dring[0][e] = (g[e] / den - through) / scale;
-    }
+    for (int e = 0; e < EPL; ++e) dring[0][e] = du[e];
     if (t < t1) {
 #pragma unroll
       for (int r = 0; r < K; ++r)
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) dt[r][e] = fmaf(dring[0][e], win[r][e], dt[r][e]);
+        for (int e = 0; e < EPL; ++e) dt[r][e] = fmaf(dring[0][e], w[r][e], dt[r][e]);
       float o[EPL];
 #pragma unroll
       for (int e = 0; e < EPL; ++e) {
@@ -191,11 +229,36 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
           if (t + r < T_) a = fmaf(tp[r][e], dring[r][e], a);
         o[e] = a;
       }
-      if (live) {
-        T* p = dz + ((int64_t)b * T_ + t) * W + c;
+      if (live) st_elems<T, EPL>(dz + ((int64_t)b * T_ + t) * W + c, o);
+    }
+  };
+  for (int t = thi; t >= t0; t -= 2) {
+    const bool two = t - 1 >= t0;
+    // token t's window: win[r] = row t - r (one row older than before); token t - 1's: wb
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) p[e] = from_f32<T>(o[e]);
-      }
+    for (int r = 0; r < K - 1; ++r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) win[r][e] = win[r + 1][e];
+    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, win[K - 1]);
+    float wb[K][EPL];
+#pragma unroll
+    for (int r = 0; r < K - 1; ++r)
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) wb[r][e] = win[r + 1][e];
+    load_in<T, EPL>(z, hist, b, t - K, T_, W, K, c, live && two, wb[K - 1]);
+    float ga[EPL], gb[EPL];
+    load_g<T, EPL>(gk, b, t, T_, W, c, live, ga);
+    load_g<T, EPL>(gk, b, t - 1, T_, W, c, live && two, gb);
+    float da[EPL], db[EPL];
+    token_du<EPL, K>(tp, win, ga, floor_, da);
+    token_du<EPL, K>(tp, wb, gb, floor_, db);
+    step(t, da, win);
+    if (two) {
+#pragma unroll
+      for (int r = 0; r < K; ++r)
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) win[r][e] = wb[r][e];
+      step(t - 1, db, win);
     }
   }
   if (live) {
@@ -297,6 +360,8 @@ extern "C" int vb_keys_fwd(const void* z, const float* hist, const float* taps, 
   if (rc) return rc;
   if (B == 0 || T == 0) return VB_OK;
   VB_REQUIRE(z && taps && keys && (hist || taps_count == 1), "keys_fwd: null pointer");
+  VB_REQUIRE(aligned16(z) && aligned16(keys) && (!hist || aligned16(hist)),
+             "keys_fwd: z, keys and history must start on 16-byte boundaries");
   const int hd = width / heads;
   cudaStream_t st = (cudaStream_t)stream;
   return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
@@ -328,6 +393,8 @@ extern "C" int vb_keys_bwd(const void* z, const float* hist, const float* taps, 
   }
   VB_REQUIRE(z && taps && grad_keys && grad_z && grad_taps && workspace && (hist || taps_count == 1),
              "keys_bwd: null pointer");
+  VB_REQUIRE(aligned16(z) && aligned16(grad_keys) && aligned16(grad_z) && (!hist || aligned16(hist)),
+             "keys_bwd: z, the key gradient, dz and history must start on 16-byte boundaries");
   const int hd = width / heads;
   return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
     return VB_KEYS_EPL_DISPATCH(hd, EPL, [&]() -> int {

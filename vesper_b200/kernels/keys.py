@@ -21,6 +21,12 @@ KEY_NORM_FLOOR = 1e-6  # vesper/recurrence.py:27
 SUPPORTED = (torch.float32, torch.bfloat16, torch.float16)
 
 
+def _aligned(t: Tensor) -> Tensor:
+    """``t`` contiguous and starting on a 16-byte boundary (the kernels' vector accesses)."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def fused_keys(z: Tensor, history: Tensor, taps: Tensor, heads: int) -> Tensor:
     """Normalized keys ``[b, n, heads, d / heads]`` in ``z``'s dtype (``z [b, n, d]`` on CUDA)."""
     if z.device.type != "cuda":
@@ -34,7 +40,7 @@ def fused_keys(z: Tensor, history: Tensor, taps: Tensor, heads: int) -> Tensor:
     if taps.shape != (count, d) or history.shape != (b, count - 1, d):
         msg = f"taps {tuple(taps.shape)} / history {tuple(history.shape)} do not fit z {tuple(z.shape)}"
         raise ContractError(msg)
-    out: Tensor = _FusedKeys.apply(z.contiguous(), history, taps, heads)
+    out: Tensor = _FusedKeys.apply(_aligned(z), history, taps, heads)
     return out
 
 
@@ -70,7 +76,7 @@ def keys_backward(
 class _FusedKeys(torch.autograd.Function):
     @staticmethod
     def forward(ctx, z: Tensor, history: Tensor, taps: Tensor, heads: int) -> Tensor:  # type: ignore[override]
-        hist = history.to(torch.float32).contiguous()
+        hist = _aligned(history.to(torch.float32))
         wide = taps.to(torch.float32).contiguous()
         k = keys_forward(z, hist, wide, heads, KEY_NORM_FLOOR)
         ctx.save_for_backward(z, hist, wide)
@@ -84,7 +90,7 @@ class _FusedKeys(torch.autograd.Function):
         z, hist, wide = ctx.saved_tensors
         want_hist = bool(ctx.needs_input_grad[1])
         grad_z, grad_taps, grad_hist = keys_backward(
-            z, hist, wide, grad_k.contiguous().to(z.dtype), ctx.heads, KEY_NORM_FLOOR, want_hist
+            z, hist, wide, _aligned(grad_k.to(z.dtype)), ctx.heads, KEY_NORM_FLOOR, want_hist
         )
         gh = grad_hist.to(ctx.history_dtype) if grad_hist is not None else None
         return grad_z, gh, grad_taps.to(ctx.taps_dtype), None
