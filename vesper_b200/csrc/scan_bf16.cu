@@ -67,20 +67,6 @@ __device__ __forceinline__ void ld64(uint32_t tm, int col, float (&v)[64]) {
   tmem_wait_ld();
 }
 
-// Column j of a float32 [D][D] matrix (zero-padded to 128) -> tensor-memory row and bf16 tile row
-__device__ __forceinline__ void column_to_tmem_and_tile(const float* mat, int D, int j, uint32_t lane_tm,
-                                                        int col, uint8_t* tile) {
-#pragma unroll
-  for (int c0 = 0; c0 < DP; c0 += 32) {
-    float v[32];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = (mat != nullptr && c0 + e < D && j < D) ? mat[(int64_t)(c0 + e) * D + j] : 0.f;
-    tmem_st32(lane_tm + (uint32_t)(col + c0), v);
-    st_row32_bf16(tile, 128, j, c0, v);
-  }
-  tmem_wait_st();
-}
-
 // One MMA of K = 16 * STEPS, D (+)= A x B: the k-step descriptors are the step-0 descriptor plus a
 // compile-time offset (the start-address field counts 16-byte units), so each step costs one
 // add and the issue. A_MN / B_MN select the MN-major form (tile rows = K index) over the K-major
@@ -385,25 +371,33 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
 }
 
 // ------------------------------------------------------------------------------------------
-// forward: one CTA per (b, h) walks its chunks. H^T lives in tensor memory (fp32, lane j = value
-// index, column i = key index) and, for the products, as the bf16 tile Hs [j][i]:
-//   H^T += Hs M + U^T K,  O = Q' Hs    (one commit: Q' Hs has read Hs when H^T is complete)
-//   O += P U                           (M=64, double-buffered in tensor memory)
-// Warp 8 issues every product and load; warps 0-7 read H^T back into Hs and O into the staging
-// tile Ot, warp w reading lane quarter w % 4 and the two warps of a quarter splitting the columns
-// (w / 4); thread 0 copies Hs (the checkpoint) and Ot out with bulk stores. The O readout of chunk c-1 overlaps
-// the chain products of chunk c. Mbarriers order the two roles; every wait is bounded.
+// forward: two CTAs per (b, h) walk its chunks, each owning half of the value index j (rows of
+// H^T): H^T_J lives in tensor memory (fp32, M=64 layout: row r at lane 32 (r / 16) + r % 16,
+// column i = key index) and, for the products, as the bf16 tile Hs [64 j][128 i]:
+//   H^T_J += Hs M + U_J^T K,  O_J = Q' Hs   (one commit: Q' Hs has read Hs when H^T_J is complete)
+//   O_J += P U_J                            (M=64 x N=64, double-buffered in tensor memory)
+// Splitting the value index halves what each SM stores per chunk (its half of the checkpoint and
+// of O) and spreads a sequence's copies over two SMs; M, K, Q' and P are read by both (the second
+// read mostly from L2). Warp 8 issues every product and load; warps 0-7 read H^T_J back into Hs
+// and O_J into the staging tile Ot (lanes 0-15 of warp w's quarter w % 4, the two warps of a
+// quarter splitting the columns); thread 0 copies Hs (the checkpoint) and Ot out with bulk
+// stores. The O readout of chunk c-1 overlaps the chain products of chunk c. Mbarriers order the
+// two roles; every wait is bounded.
 // ------------------------------------------------------------------------------------------
 constexpr int NT2 = 256;         // threads of the sequential backward
 constexpr int NF = 288;          // forward: eight reading warps and the issuing warp
 constexpr int NR = 256;          // the forward's reading threads
+constexpr uint32_t TILE_HALF = 64 * 128 * 2;  // [64 j][128 i]
+constexpr uint32_t TILE_OJ = 64 * 64 * 2;     // [64 t][64 j]
 struct FwdSmem {
-  // per-chunk set: P, then [U | Q' | M] in the prep image's order (one bulk copy), then K
-  static constexpr uint32_t Pt = 0, Ut = TILE_TT, Qt = Ut + TILE_TD, Mt = Qt + TILE_TD, Kt = Mt + TILE_JI;
-  static constexpr uint32_t SET = Kt + TILE_TD;                                  // 88 KB
-  static constexpr uint32_t Hs = 2 * SET, Ot = Hs + TILE_JI, END = Ot + TILE_TD;  // 224 KB
+  // per-chunk set: P, this CTA's half of U (one 64-column atom), then [Q' | M] in the prep
+  // image's order (one bulk copy), then K
+  static constexpr uint32_t Pt = 0, Ut = TILE_TT, Qt = Ut + TILE_OJ, Mt = Qt + TILE_TD, Kt = Mt + TILE_JI;
+  static constexpr uint32_t SET = Kt + TILE_TD;                                     // 80 KB
+  static constexpr uint32_t Hs = 2 * SET, Ot = Hs + TILE_HALF, Zt = Ot + TILE_OJ;
+  static constexpr uint32_t END = Zt + TILE_HALF / 2;  // 192 KB; Zt: zeros for the padding half
 };
-constexpr int F_H = 0, F_O = 128;  // O of chunk c at columns F_O + 128 (c & 1)
+constexpr int F_H = 0, F_O = 128;  // O of chunk c at columns F_O + 64 (c & 1)
 
 struct ChunkAt {
   int t0, valid;
@@ -425,17 +419,52 @@ __device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t& phase, int
   return ok;
 }
 
+// the 64-row half jh of a [128 j][128 i] state image: two 8 KB pieces (one per 64-column atom);
+// with a single value half (d <= 64) rows 64-127 are padding, stored as zeros from the 8 KB
+// zero tile `zero` (the local-gradient kernel multiplies over all 128 rows)
+__device__ __forceinline__ void store_state_half(uint8_t* img, const uint8_t* half_tile, int jh, int halves,
+                                                 const uint8_t* zero) {
+  bulk_store(img + (uint32_t)jh * (TILE_HALF / 2), half_tile, TILE_HALF / 2);
+  bulk_store(img + TILE_JI / 2 + (uint32_t)jh * (TILE_HALF / 2), half_tile + TILE_HALF / 2, TILE_HALF / 2);
+  if (halves == 1) {
+    bulk_store(img + TILE_HALF / 2, zero, TILE_HALF / 2);
+    bulk_store(img + TILE_JI / 2 + TILE_HALF / 2, zero, TILE_HALF / 2);
+  }
+}
+// zeros an 8 KB shared tile (all threads of the caller's group, before a proxy fence and barrier)
+__device__ __forceinline__ void zero_tile8k(uint8_t* tile, int t, int n) {
+  for (int i = t; i < (int)(TILE_HALF / 2 / 16); i += n) reinterpret_cast<uint4*>(tile)[i] = make_uint4(0u, 0u, 0u, 0u);
+}
+
+// Row jl (0..63) of a state half in the M=64 layout: column j = 64 jh + jl of the float32 [D][D]
+// matrix (zero past D) into tensor memory at column `col`, and as bf16 into row jl of the
+// [64][128] tile. Warps 0-3 call it; lanes 16-31 write unused tensor-memory lanes and no tile row.
+__device__ __forceinline__ void state_row_m64(const float* mat, int D, int jh, uint32_t lane_tm, int col,
+                                              uint8_t* tile) {
+  const int lane = threadIdx.x & 31, jl = 16 * ((threadIdx.x >> 5) & 3) + (lane & 15);
+  const int j = lane < 16 ? 64 * jh + jl : D;
+#pragma unroll
+  for (int c0 = 0; c0 < DP; c0 += 32) {
+    float v[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) v[e] = (mat != nullptr && c0 + e < D && j < D) ? mat[(int64_t)(c0 + e) * D + j] : 0.f;
+    tmem_st32(lane_tm + (uint32_t)(col + c0), v);
+    if (lane < 16) st_row32_bf16(tile, 64, jl, c0, v);
+  }
+  tmem_wait_st();
+}
+
 __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap omap,
     const float* __restrict__ s0, const uint8_t* __restrict__ xt, float* __restrict__ sn,
-    uint8_t* __restrict__ hck, int T, int H, int D, int NC, int* status) {
+    uint8_t* __restrict__ hck, int T, int H, int D, int NC, int halves, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Hs = sm + FwdSmem::Hs, *Ot = sm + FwdSmem::Ot;
+  uint8_t *Hs = sm + FwdSmem::Hs, *Ot = sm + FwdSmem::Ot, *Zt = sm + FwdSmem::Zt;
   __shared__ uint64_t barH, barO[2], barOR[2], barHs, lbar[2];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
+  const int bh = blockIdx.x / halves, jh = blockIdx.x % halves, b = bh / H, h = bh % H;
   auto set = [&](int c) { return sm + (uint32_t)(c & 1) * FwdSmem::SET; };
   if (tid == 0) {
     mbar_init(&barH, 1); mbar_init(&barO[0], 1); mbar_init(&barO[1], 1);
@@ -443,7 +472,7 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
     mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
     mbar_fence_init();
   }
-  if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
+  if (warp == 0) { tmem_alloc(&tbase, 256); tmem_relinquish(); }
   __syncthreads();
   tc_fence_after();
   const uint32_t tm = tbase;
@@ -457,7 +486,8 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
         const uint8_t* img = xt + ((size_t)bh * NC + c) * PREP_BYTES;
         mbar_arrive_expect_tx(lb, FwdSmem::SET);
         bulk_load(s + FwdSmem::Pt, img + PREP_P, TILE_TT, lb);
-        bulk_load(s + FwdSmem::Ut, img + PREP_U, 2 * TILE_TD + TILE_JI, lb);
+        bulk_load(s + FwdSmem::Ut, img + PREP_U + (uint32_t)jh * TILE_OJ, TILE_OJ, lb);
+        bulk_load(s + FwdSmem::Qt, img + PREP_Q, TILE_TD + TILE_JI, lb);
         tma_tile(s + FwdSmem::Kt, &kmap, lb, h, a.t0, b);
       };
       if (NC > 0) load_chunk(0);
@@ -470,12 +500,12 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
         if (c >= 2 && !wait_or_flag(&barOR[c & 1], pOR[c & 1], status, 2)) break;  // O of c-2 read
         tc_fence_after();
         const uint8_t* s = set(c);
-        const uint32_t sU = smem_u32(s + FwdSmem::Ut), dO = tm + F_O + 128 * (c & 1);
-        mma_seq<8, 0, 128, 1, 128>(tm + F_H, sH, smem_u32(s + FwdSmem::Mt), idesc_bf16(128, 128, 0, 1), 1u);
-        mma_seq<8, 0, 64, 0, 128>(dO, smem_u32(s + FwdSmem::Qt), sH, idesc_bf16(64, 128, 0, 0), 0u);
-        mma_seq<4, 1, 64, 1, 64>(tm + F_H, sU, smem_u32(s + FwdSmem::Kt), idesc_bf16(128, 128, 1, 1), 1u);
+        const uint32_t sU = smem_u32(s + FwdSmem::Ut), dO = tm + F_O + 64 * (c & 1);
+        mma_seq<8, 0, 64, 1, 128>(tm + F_H, sH, smem_u32(s + FwdSmem::Mt), idesc_bf16(64, 128, 0, 1), 1u);
+        mma_seq<8, 0, 64, 0, 64>(dO, smem_u32(s + FwdSmem::Qt), sH, idesc_bf16(64, 64, 0, 0), 0u);
+        mma_seq<4, 1, 64, 1, 64>(tm + F_H, sU, smem_u32(s + FwdSmem::Kt), idesc_bf16(64, 128, 1, 1), 1u);
         umma_commit(&barH);
-        mma_seq<4, 0, 64, 1, 64>(dO, smem_u32(s + FwdSmem::Pt), sU, idesc_bf16(64, 128, 0, 1), 1u);
+        mma_seq<4, 0, 64, 1, 64>(dO, smem_u32(s + FwdSmem::Pt), sU, idesc_bf16(64, 64, 0, 1), 1u);
         umma_commit(&barO[c & 1]);
         if (c + 2 < NC) {  // the set is free once every product of chunk c is done
           if (!wait_or_flag(&barO[c & 1], pO[c & 1], status, 2)) break;
@@ -487,44 +517,39 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
   } else {
     // ---------------- reading warps 0-7 ----------------
     const int quarter = warp & 3, half = warp >> 2;
-    const int lane128 = quarter * 32 + lane;  // this thread's tensor-memory lane
+    const int jl = quarter * 16 + (lane & 15);  // this lane's row of the M=64 accumulators
+    const bool rowlane = lane < 16;
     const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
-    // H^T row j = column j of the initial state (warps 0-3); its bf16 copy is the first checkpoint
-    if (half == 0) column_to_tmem_and_tile(s0 + (int64_t)bh * D * D, D, lane128, lane_tm, F_H, Hs);
+    // H^T_J from the initial state (warps 0-3); its bf16 copy is the first checkpoint
+    if (half == 0) state_row_m64(s0 + (int64_t)bh * D * D, D, jh, lane_tm, F_H, Hs);
+    zero_tile8k(Zt, tid, NR);
     fence_async_smem();
     bar_sync_named(1, NR);
     if (tid == 0 && NC > 0) {
-      bulk_store(hck + (size_t)bh * NC * TILE_JI, Hs, TILE_JI);
+      store_state_half(hck + (size_t)bh * NC * TILE_JI, Hs, jh, halves, Zt);
       bulk_commit();
     }
     tc_fence_before();
     mbar_arrive(&barHs);
     uint32_t pH = 0, pO[2] = {0u, 0u};
     bool ok = true;
-    // O of chunk c: tensor memory -> registers -> Ot (M=64 layout: lanes 0-15 of each quarter
-    // hold the token rows) -> one TMA store
+    // O_J of chunk c: tensor memory -> registers -> Ot -> one TMA store
     auto out_rows = [&](int c) -> bool {
       if (!wait_or_flag(&barO[c & 1], pO[c & 1], status, 2)) return false;
       tc_fence_after();
-      float v[64];
-      const uint32_t col = (uint32_t)(F_O + 128 * (c & 1) + half * 64);
-      tmem_ld32(lane_tm + col, *reinterpret_cast<float(*)[32]>(v));
-      tmem_ld32(lane_tm + col + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+      float v[32];
+      tmem_ld32(lane_tm + (uint32_t)(F_O + 64 * (c & 1) + half * 32), v);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&barOR[c & 1]);
       if (tid == 0) bulk_wait_read_but_newest();  // the previous O store has left Ot
       bar_sync_named(1, NR);
-      if (lane < 16) {
-        st_row32_bf16(Ot, 64, quarter * 16 + lane, half * 64, v);
-        st_row32_bf16(Ot, 64, quarter * 16 + lane, half * 64 + 32, v + 32);
-      }
+      if (rowlane) st_row32_bf16(Ot, 64, jl, half * 32, v);
       fence_async_smem();
       bar_sync_named(1, NR);
       if (tid == 0) {
         const ChunkAt a = chunk_at(b, c, T);
-        tma_store_4d(&omap, Ot, 0, h, a.t0, b);
-        if (D > 64) tma_store_4d(&omap, Ot + TILE_TD / 2, 64, h, a.t0, b);
+        tma_store_4d(&omap, Ot, 64 * jh, h, a.t0, b);
         bulk_commit();
       }
       return true;
@@ -544,11 +569,14 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
         const int c0 = half * 64 + 32 * k;
         tmem_ld32(lane_tm + (uint32_t)(F_H + c0), v);
         tmem_wait_ld();
-        st_row32_bf16(Hs, 128, lane128, c0, v);
-        if (c + 1 == NC && lane128 < D) {
+        if (rowlane) {
+          st_row32_bf16(Hs, 64, jl, c0, v);
+          const int j = 64 * jh + jl;
+          if (c + 1 == NC && j < D) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (c0 + e < D) sn[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + lane128] = v[e];
+            for (int e = 0; e < 32; ++e)
+              if (c0 + e < D) sn[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + j] = v[e];
+          }
         }
       }
       fence_async_smem();
@@ -557,14 +585,14 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
       if (c + 1 < NC) {  // checkpoint H_{c+1} for chunk c + 1 while the next products run
         bar_sync_named(1, NR);
         if (tid == 0) {
-          bulk_store(hck + ((size_t)bh * NC + c + 1) * TILE_JI, Hs, TILE_JI);
+          store_state_half(hck + ((size_t)bh * NC + c + 1) * TILE_JI, Hs, jh, halves, Zt);
           bulk_commit();
         }
       }
     }
     if (ok && NC > 0) out_rows(NC - 1);
-    if (NC == 0 && half == 0) {
-      const int j = lane128;
+    if (NC == 0 && half == 0 && rowlane) {
+      const int j = 64 * jh + jl;
       if (j < D)
         for (int i = 0; i < D; ++i) sn[(int64_t)bh * D * D + (int64_t)i * D + j] = s0[(int64_t)bh * D * D + (int64_t)i * D + j];
     }
@@ -572,36 +600,39 @@ __global__ void __launch_bounds__(NF, 1) scan_fwd_kernel(
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tm, 512);
+  if (warp == 0) tmem_dealloc(tm, 256);
 }
 
 // ------------------------------------------------------------------------------------------
-// backward, sequential (256 threads): the dH^T chain in tensor memory in reverse chunk order,
-//   dH^T_c = dH^T_{c+1} + dHs M^T + dO^T Q'      (12 k-steps; dHs = bf16 dH^T_{c+1})
-// dHs is double-buffered, so its bulk-copied checkpoint never waits on the chain.
+// backward, sequential (256 threads): two CTAs per (b, h), each owning half of the value index j,
+// walk the dH^T chain in tensor memory (M=64 layout) in reverse chunk order,
+//   dH^T_J += dHs M^T + dO_J^T Q'      (12 k-steps; dHs = bf16 dH^T_{J, c+1}, [64 j][128 i])
+// dHs is double-buffered, so its bulk-copied half of the checkpoint never waits on the chain;
+// three input sets are in flight.
 // ------------------------------------------------------------------------------------------
 struct DhSmem {
-  // per-chunk set: [Q' | M] as the prep image holds them, then dO
+  // per-chunk set: [Q' | M] as the prep image holds them, then this CTA's 64 columns of dO
   static constexpr uint32_t Qt = 0, Mt = TILE_TD, Gt = Mt + TILE_JI;
-  static constexpr uint32_t SET = Gt + TILE_TD;  // 64 KB
-  static constexpr int NSET = 2;
-  static constexpr uint32_t Ha = NSET * SET, END = Ha + 2 * TILE_JI;  // 192 KB
+  static constexpr uint32_t SET = Gt + TILE_OJ;  // 56 KB
+  static constexpr int NSET = 3;
+  static constexpr uint32_t Ha = NSET * SET, Zt = Ha + 2 * TILE_HALF, END = Zt + TILE_HALF / 2;  // 208 KB
 };
 constexpr int G_H = 0;
 
 __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     const __grid_constant__ CUtensorMap gmap, const uint8_t* __restrict__ xt, const float* __restrict__ dsn,
-    float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int* status) {
+    float* __restrict__ ds0, uint8_t* __restrict__ dhck, int T, int H, int D, int NC, int halves, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t* Ha = sm + DhSmem::Ha;
+  uint8_t *Ha = sm + DhSmem::Ha, *Zt = sm + DhSmem::Zt;
   __shared__ uint64_t barH, lbar[DhSmem::NSET];
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quarter = warp & 3, half = warp >> 2;
-  const int lane128 = quarter * 32 + lane;
-  const int bh = blockIdx.x, b = bh / H, h = bh % H;
-  uint32_t lphase[DhSmem::NSET] = {0u, 0u}, pH = 0;
+  const int jl = quarter * 16 + (lane & 15);  // this lane's row of the M=64 accumulator
+  const bool rowlane = lane < 16;
+  const int bh = blockIdx.x / halves, jh = blockIdx.x % halves, b = bh / H, h = bh % H;
+  uint32_t lphase[DhSmem::NSET] = {0u, 0u, 0u}, pH = 0;
   auto set = [&](int c) { return sm + (uint32_t)(c % DhSmem::NSET) * DhSmem::SET; };
   auto load_chunk = [&](int c) {  // thread 0
     const ChunkAt a = chunk_at(b, c, T);
@@ -609,7 +640,7 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     uint64_t* lb = &lbar[c % DhSmem::NSET];
     mbar_arrive_expect_tx(lb, DhSmem::SET);
     bulk_load(s + DhSmem::Qt, xt + ((size_t)bh * NC + c) * PREP_BYTES + PREP_Q, TILE_TD + TILE_JI, lb);
-    tma_tile(s + DhSmem::Gt, &gmap, lb, h, a.t0, b);
+    tma_load_4d(s + DhSmem::Gt, &gmap, lb, 64 * jh, h, a.t0, b);
   };
   auto wait_chunk = [&](int c) -> bool {
     const int k = c % DhSmem::NSET;
@@ -630,23 +661,23 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
   tc_fence_after();
   const uint32_t tm = tbase;
   const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
-  auto dhs = [&](int c) { return Ha + (uint32_t)(c & 1) * TILE_JI; };  // dH_{c+1}, read by chunk c
+  auto dhs = [&](int c) { return Ha + (uint32_t)(c & 1) * TILE_HALF; };  // dH_{c+1}, read by chunk c
   if (half == 0 && NC > 0)
-    column_to_tmem_and_tile(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, lane128, lane_tm, G_H,
-                            dhs(NC - 1));
+    state_row_m64(dsn != nullptr ? dsn + (int64_t)bh * D * D : nullptr, D, jh, lane_tm, G_H, dhs(NC - 1));
+  zero_tile8k(Zt, tid, NT2);
   bool ok = publish_ok(true);
   for (int c = NC - 1; c >= 0 && ok; --c) {
     uint8_t* hb = dhs(c);
-    if (tid == 0) {  // checkpoint dH_{c+1} for chunk c
-      bulk_store(dhck + ((size_t)bh * NC + c) * TILE_JI, hb, TILE_JI);
+    if (tid == 0) {  // checkpoint dH_{c+1} for chunk c (this CTA's half)
+      store_state_half(dhck + ((size_t)bh * NC + c) * TILE_JI, hb, jh, halves, Zt);
       bulk_commit();
     }
     ok = wait_chunk(c) && ok;
     if (tid == 0 && ok) {
       const uint8_t* s = set(c);
-      mma_seq<8, 0, 128, 0, 128>(tm + G_H, smem_u32(hb), smem_u32(s + DhSmem::Mt), idesc_bf16(128, 128, 0, 0), 1u);  // += dHs M^T
+      mma_seq<8, 0, 64, 0, 128>(tm + G_H, smem_u32(hb), smem_u32(s + DhSmem::Mt), idesc_bf16(64, 128, 0, 0), 1u);  // += dHs M^T
       mma_seq<4, 1, 64, 1, 64>(tm + G_H, smem_u32(s + DhSmem::Gt), smem_u32(s + DhSmem::Qt),
-                               idesc_bf16(128, 128, 1, 1), 1u);                                          // += dO^T Q'
+                               idesc_bf16(64, 128, 1, 1), 1u);                                          // += dO^T Q'
       umma_commit(&barH);
     }
     if (ok) ok = mma_wait(&barH, pH, status);
@@ -662,17 +693,20 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
       const int c0 = half * 64 + 32 * k;
       tmem_ld32(lane_tm + (uint32_t)(G_H + c0), v);
       tmem_wait_ld();
-      st_row32_bf16(nb, 128, lane128, c0, v);
-      if (c == 0 && lane128 < D) {
+      if (rowlane) {
+        st_row32_bf16(nb, 64, jl, c0, v);
+        const int j = 64 * jh + jl;
+        if (c == 0 && j < D) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (c0 + e < D) ds0[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + lane128] = v[e];
+          for (int e = 0; e < 32; ++e)
+            if (c0 + e < D) ds0[(int64_t)bh * D * D + (int64_t)(c0 + e) * D + j] = v[e];
+        }
       }
     }
     ok = publish_ok(ok);
   }
-  if (NC == 0 && half == 0) {
-    const int j = lane128;
+  if (NC == 0 && half == 0 && rowlane) {
+    const int j = 64 * jh + jl;
     if (j < D)
       for (int i = 0; i < D; ++i)
         ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = dsn ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
@@ -1028,8 +1062,9 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
     memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm));
   }
   const size_t sf = smem_bytes(FwdSmem::END);
+  const int halves = D > 64 ? 2 : 1;  // value halves: the second is all padding when D <= 64
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sf), "fwd attr");
-  scan_fwd_kernel<<<B * H, NF, sf, st>>>(km, om, state0, xt, state_n, hck, T, H, D, NC, status);
+  scan_fwd_kernel<<<B * H * halves, NF, sf, st>>>(km, om, state0, xt, state_n, hck, T, H, D, NC, halves, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 fwd");
   return VB_OK;
 }
@@ -1060,7 +1095,8 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
   }
   const size_t sd = smem_bytes(DhSmem::END);
   VB_CUDA_CHECK(cudaFuncSetAttribute(scan_dh_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sd), "dh attr");
-  scan_dh_kernel<<<B * H, NT2, sd, st>>>(gm, xt, dstate_n, dstate0, dhck, T, H, D, NC, status);
+  const int halves = D > 64 ? 2 : 1;  // value halves: the second is all padding when D <= 64
+  scan_dh_kernel<<<B * H * halves, NT2, sd, st>>>(gm, xt, dstate_n, dstate0, dhck, T, H, D, NC, halves, status);
   VB_LAUNCH_CHECK("delta_scan_bf16 dh");
   if (NC > 0) {
     const size_t sg = smem_bytes(GrSmem::END);
