@@ -84,11 +84,11 @@ __device__ __forceinline__ void mma_seq(uint32_t d, uint32_t a, uint32_t b, uint
   }
 }
 
-// all threads: bounded wait on the MMA barrier; flips the phase
+// all threads: bounded wait on the MMA barrier; flips the phase; any thread that gives up flags it
 __device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t& phase, int* status) {
   const bool ok = mbar_wait(bar, phase);
   phase ^= 1u;
-  if (!ok && threadIdx.x == 0) atomicOr(status, 2);
+  if (!ok) atomicOr(status, 2);
   tc_fence_after();
   return ok;
 }
@@ -646,7 +646,7 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
     const int k = c % DhSmem::NSET;
     const bool r = mbar_wait(&lbar[k], lphase[k]);
     lphase[k] ^= 1u;
-    if (!r && tid == 0) atomicOr(status, 4);
+    if (!r) atomicOr(status, 4);
     return r;
   };
   if (tid == 0) {
@@ -681,11 +681,11 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
       umma_commit(&barH);
     }
     if (ok) ok = mma_wait(&barH, pH, status);
-    if (tid == 0) {
-      if (ok && c - DhSmem::NSET >= 0) load_chunk(c - DhSmem::NSET);  // set of chunk c is free
-      bulk_wait_read_but_newest();  // the checkpoint of chunk c + 1 has left the other buffer
-    }
+    if (tid == 0) bulk_wait_read_but_newest();  // the checkpoint of chunk c + 1 has left the other buffer
     __syncthreads();
+    // the set of chunk c is free; it is re-armed only now that every thread has waited on its
+    // load barrier (re-armed earlier, a late waiter could see the barrier two phases on and stall)
+    if (tid == 0 && ok && c - DhSmem::NSET >= 0) load_chunk(c - DhSmem::NSET);
     uint8_t* nb = dhs(c - 1);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -800,7 +800,7 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
   }
   auto loaded = [&](int k) -> bool {
     const bool r = mbar_wait(&lbar[k], 0);
-    if (!r && tid == 0) atomicOr(status, 4);
+    if (!r) atomicOr(status, 4);
     return r;
   };
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
