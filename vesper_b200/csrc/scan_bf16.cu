@@ -921,16 +921,16 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     store_tile(&dqmap, Gt, h, t0, b, D);
     bulk_wait_read_but_newest();  // dV has left V, which Y overwrites below
   }
-  if (tid < C) {
-    float a = 0.f;
-    for (int t = 0; t < C; ++t) a += scr[t * 65 + tid];
-    db1[tid] = a;
-  }
-  // batch 5: Y = dX X^T
+  // batch 5: Y = dX X^T (issued before the dbeta column sums below, which do not feed it)
   if (tid == 0 && ok) {
     const uint32_t id = idesc_bf16(64, 64, 0, 0);
     mma_seq<4, 0, 64, 0, 64>(tm + R_Y, sdX, sX, id, 0u);
     umma_commit(&bar);
+  }
+  if (tid < C) {
+    float a = 0.f;
+    for (int t = 0; t < C; ++t) a += scr[t * 65 + tid];
+    db1[tid] = a;
   }
   ok = ok && mma_wait(&bar, phase, status);
   {
