@@ -17,12 +17,13 @@
 // memory; the head dimension is zero-padded to 128 inside the tiles):
 //   prep     chunk-parallel: K K^T and Q K^T, the unit-lower-triangular solve for X (float32,
 //            one thread per column), then U, W, M, Q'; a bf16 tile image per chunk.
-//   forward  one CTA per sequence walks its chunks; H^T lives in tensor memory (fp32, 128 lanes =
-//            value index j, 128 columns = key index i). The bf16 copy of H_c that fed the chunk's
-//            products is checkpointed (the backward reuses it, no recomputation of the chain).
-//   backward one CTA per sequence walks the chunks in reverse for the state gradient,
-//            checkpointing the bf16 dH_{c+1}; then a chunk-parallel kernel forms every local
-//            gradient from (H_c, dH_{c+1}) in one pass: dq, dk, dv, dbeta.
+//   forward  two CTAs per sequence (one per half of the value index j) walk its chunks; H^T
+//            lives in tensor memory (fp32, rows = value index j, columns = key index i). The bf16
+//            copy of H_c that fed the chunk's products is checkpointed (the backward reuses it, no
+//            recomputation of the chain).
+//   backward two CTAs per sequence walk the chunks in reverse for the state gradient,
+//            checkpointing the bf16 dH_{c+1}; then one persistent CTA per SM forms every local
+//            gradient of a chunk from (H_c, dH_{c+1}) in five product stages: dq, dk, dv, dbeta.
 // Waits on the tensor core are bounded (2 s): a timeout sets bit 1 of *status and the kernel
 // leaves after releasing its tensor memory.
 #include <cstring>
@@ -718,21 +719,37 @@ __global__ void __launch_bounds__(NT2, 1) scan_dh_kernel(
 }
 
 // ------------------------------------------------------------------------------------------
-// backward, chunk-parallel: every local gradient of one chunk from (H_c, dH_{c+1})
+// backward, chunk-parallel: every local gradient of one chunk from (H_c, dH_{c+1}).
+// With R = V - K H_c (so delta = T' R), the chunk's gradients are five dependent product stages:
+//   1  (K H)^T, ddelta^T = dH'^T K^T + dO^T P                         -> R^T = V^T - (K H)^T
+//   2  delta^T = R^T T'^T, dW = -ddelta H^T, dV = T'^T ddelta, dT' = ddelta R^T
+//   3  dP = dO delta^T (causal), Y = dX X^T (dX = dT' diag(beta)), dQ = dO H^T, dK = delta dH'^T
+//   4  Z = X^T Y and Z^T = Y^T X, K K^T, dQ += dP K, dK += dP^T Q + T'^T dW
+//   5  dK += dG K  (dG = diag(beta) dA symmetrised, dA = -Z strictly lower)
+// dT' = dU V^T + dW K^T = ddelta (V - K H)^T needs no dW, and dV and dQ are read out while
+// later stages run. One persistent CTA per SM walks chunks blockIdx.x, blockIdx.x + gridDim.x,
+// ...: the next chunk's tiles stream into regions the current chunk has finished with, and its
+// stage 1 runs while the current chunk's dQ and dK are read out. Regions (K and Q trade places
+// between successive chunks of a CTA, so that the next K lands one stage early):
+//   dH' 32 KB (read by stages 1, 3), H 32 KB (1-3), V 16 KB (stage 1 and its readout),
+//   dO 16 KB (1, 3), P 8 KB (1)            -> the next chunk's after stages 1 and 3
+//   Q 16 KB (4) -> next K after stage 4;  T' 8 KB (2, 4), X 8 KB (2-4) -> next after stage 4
+//   K 16 KB (1, 4, 5) -> next Q after stage 5
 // ------------------------------------------------------------------------------------------
 struct GrSmem {
-  static constexpr uint32_t Qt = 0, Kt = Qt + TILE_TD, Vt = Kt + TILE_TD, Gt = Vt + TILE_TD,
-                            Ht = Gt + TILE_TD, dHt = Ht + TILE_JI, Xt = dHt + TILE_JI,
-                            Tt = Xt + TILE_TT, Pt = Tt + TILE_TT, Dt = Pt + TILE_TT,
-                            dDt = Dt + TILE_JT, Wr = dDt + TILE_JT, dPt = Wr + TILE_JT,
-                            END = dPt + TILE_TT;
-  // reuse: dW [t][i] over Wr (W^T is dead once H^T W^T is formed), dX over dDt (dead after dT'),
-  // Y over Vt (dead after dT'), dGs over Pt (dead after ddelta), float scratch over Ht (dead
-  // after dQ and dW)
+  static constexpr uint32_t DH = 0, HH = DH + TILE_JI, VV = HH + TILE_JI, GG = VV + TILE_TD, KA = GG + TILE_TD,
+                            KB = KA + TILE_TD, PP = KB + TILE_TD, TT = PP + TILE_TT, XX = TT + TILE_TT,
+                            Rt = XX + TILE_TT, dD = Rt + TILE_JT, Dt = dD + TILE_JT, Wd = Dt + TILE_JT,
+                            END = Wd + TILE_TD;
+  // reuse: R^T -> dX (+0) and dG (+8 KB); ddelta^T -> dV staging; delta^T -> dP (+0) and Y (+8 KB)
+  // -> dK staging; dW -> dQ staging
 };
-constexpr int R_KK = 0, R_W = 128, R_U = 192, R_DD = 256, R_X = 320;   // batches 1-2
-constexpr int R_DP = 64, R_DW = 128, R_DV = 256, R_DT = 384;                      // batch 3
-constexpr int R_DQ = 128, R_Y = 256, R_Z = 320, R_DK = 128;                       // batches 4-7
+// tensor-memory columns (512 allocated); a stage's results are read out before a later stage
+// writes their columns (dV and dQ, read out while stages 3 and 5 run, stay clear of them)
+constexpr int C_RT = 256, C_DDT = 320;                         // stage 1 (M=128)
+constexpr int C_DELTA = 0, C_DTP = 64, C_DW = 128, C_DV = 256;  // stage 2 (delta^T M=128, rest M=64)
+constexpr int C_DP = 0, C_Y = 64, C_DQ = 128, C_DK = 384;       // stage 3 (M=64)
+constexpr int C_Z = 0, C_KK = 64, C_ZT = 256;                  // stage 4 (M=64)
 
 constexpr int NG = 256;  // threads of the local-gradient kernel: two warps per lane quadrant
 // one [64 t][128] bf16 tile to (b, h, tokens t0..) of a [B, T, H, D] tensor (rows past T and
@@ -746,6 +763,26 @@ __device__ __forceinline__ void ld32w(uint32_t tm, int col, float (&v)[32]) {
   tmem_ld32(tm + (uint32_t)col, v);
   tmem_wait_ld();
 }
+// one step of a recursive-halving sum over lanes l and l ^ o: the lane with bit o set keeps the
+// upper M entries, the other the lower M, each adding its partner's copy of them
+template <int M>
+__device__ __forceinline__ void halve_sum(float (&v)[32], int lane, int o) {
+  const bool up = (lane & o) != 0;
+#pragma unroll
+  for (int i = 0; i < M; ++i) {
+    const float send = up ? v[i] : v[i + M];
+    const float keep = up ? v[i + M] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+  }
+}
+// v[0..31] summed over the 16 lanes of each half-warp (all 32 lanes take part): lane l ends with
+// the sums of entries 2 (l % 16) and 2 (l % 16) + 1 in v[0] and v[1]
+__device__ __forceinline__ void halfwarp_sums(float (&v)[32], int lane) {
+  halve_sum<16>(v, lane, 8);
+  halve_sum<8>(v, lane, 4);
+  halve_sum<4>(v, lane, 2);
+  halve_sum<2>(v, lane, 1);
+}
 
 __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
@@ -753,253 +790,316 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const __grid_constant__ CUtensorMap dqmap, const __grid_constant__ CUtensorMap dkmap,
     const __grid_constant__ CUtensorMap dvmap, const bf16* __restrict__ beta, const uint8_t* __restrict__ xt,
     const uint8_t* __restrict__ hck, const uint8_t* __restrict__ dhck, bf16* __restrict__ dbeta, int T, int H,
-    int D, int NC, int* status) {
+    int D, int NC, int total, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
-  uint8_t *Qt = sm + GrSmem::Qt, *Kt = sm + GrSmem::Kt, *Vt = sm + GrSmem::Vt, *Gt = sm + GrSmem::Gt;
-  uint8_t *Ht = sm + GrSmem::Ht, *dHt = sm + GrSmem::dHt, *Xt = sm + GrSmem::Xt, *Tt = sm + GrSmem::Tt;
-  uint8_t *Pt = sm + GrSmem::Pt, *Dt = sm + GrSmem::Dt, *dDt = sm + GrSmem::dDt, *Wr = sm + GrSmem::Wr;
-  uint8_t *dPt = sm + GrSmem::dPt;
-  uint8_t* dWt = Wr;   // [64 t][128 i] fits the 16 KB of Wr
-  uint8_t* dXt = dDt;  // [64][64]
-  uint8_t* Yt = Vt;    // [64][64]
-  uint8_t* dGt = Pt;   // [64][64]
-  float* scr = reinterpret_cast<float*>(Ht);  // [64][65] floats
-  __shared__ float bsm[C], db1[C], db2s[2][C];
-  __shared__ uint64_t bar, lbar[3];
+  uint8_t *Vt = sm + GrSmem::VV, *Xt = sm + GrSmem::XX, *Rt = sm + GrSmem::Rt, *dDt = sm + GrSmem::dD;
+  uint8_t *Dt = sm + GrSmem::Dt, *Wd = sm + GrSmem::Wd;
+  uint8_t *dXt = Rt, *dGt = Rt + TILE_TT, *dVt = dDt, *dPt = Dt, *Yt = Dt + TILE_TT, *dKt = Dt, *dQt = Wd;
+  __shared__ float bsm[C], db1[C], db2s[2][C], part[4][C];
+  __shared__ uint64_t bar, bar1, la, lb;
   __shared__ uint32_t tbase;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // warps w and w + 4 share tensor-memory lane quadrant w % 4 and split the columns (half)
   const int quarter = warp & 3, half = warp >> 2;
-  const int lane128 = quarter * 32 + lane;
-  const int c = blockIdx.x % NC, bh = blockIdx.x / NC, b = bh / H, h = bh % H;
-  const int t0 = c * C, valid = min(C, T - t0);
-  const int64_t row0 = (int64_t)b * T + t0;
+  const int lane128 = quarter * 32 + lane;      // row of an M=128 accumulator
   const int trow = quarter * 16 + (lane & 15);  // token row of an M=64 accumulator (lane < 16)
   const bool rowlane = lane < 16;
-  const size_t chunk = (size_t)bh * NC + c;
   if (tid == 0) {
-    mbar_init(&bar, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1); mbar_init(&lbar[2], 1);
+    // bar: stages 2-5; bar1: stage 1; la: V, P | dH', H, dO | K (three arrivals); lb: T', X | Q
+    mbar_init(&bar, 1); mbar_init(&bar1, 1); mbar_init(&la, 3); mbar_init(&lb, 2);
     mbar_fence_init();
   }
-  __syncthreads();
-  if (tid == 0) {  // in the order of first use: batch 1's operands, batch 2's, then X and Q
-    const uint8_t* pre = xt + chunk * PREP_BYTES;
-    mbar_arrive_expect_tx(&lbar[0], 2 * TILE_TD + TILE_JI + TILE_TT);
-    tma_tile(Kt, &kmap, &lbar[0], h, t0, b);
-    bulk_load(Tt, pre + PREP_T, TILE_TT, &lbar[0]);
-    tma_tile(Vt, &vmap, &lbar[0], h, t0, b);
-    bulk_load(dHt, dhck + chunk * TILE_JI, TILE_JI, &lbar[0]);
-    mbar_arrive_expect_tx(&lbar[1], TILE_TD + TILE_JI + TILE_TT);
-    bulk_load(Ht, hck + chunk * TILE_JI, TILE_JI, &lbar[1]);
-    tma_tile(Gt, &gmap, &lbar[1], h, t0, b);
-    bulk_load(Pt, pre + PREP_P, TILE_TT, &lbar[1]);
-    mbar_arrive_expect_tx(&lbar[2], TILE_TD + TILE_TT);
-    bulk_load(Xt, pre + PREP_X, TILE_TT, &lbar[2]);
-    tma_tile(Qt, &qmap, &lbar[2], h, t0, b);
-  }
-  auto loaded = [&](int k) -> bool {
-    const bool r = mbar_wait(&lbar[k], 0);
-    if (!r) atomicOr(status, 4);
-    return r;
-  };
-  const bf16 bv = fetch_beta(beta + h, row0, H, valid);
   if (warp == 0) { tmem_alloc(&tbase, 512); tmem_relinquish(); }
-  bool ok = loaded(0);
-  if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
-  publish();
-  const uint32_t tm = tbase;
-  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
-  const uint32_t sQ = smem_u32(Qt), sK = smem_u32(Kt), sV = smem_u32(Vt), sG = smem_u32(Gt);
-  const uint32_t sH = smem_u32(Ht), sdH = smem_u32(dHt), sX = smem_u32(Xt), sT = smem_u32(Tt);
-  const uint32_t sP = smem_u32(Pt), sD = smem_u32(Dt), sdD = smem_u32(dDt), sW = smem_u32(Wr);
-  const uint32_t sdP = smem_u32(dPt), sdW = smem_u32(dWt), sdX = smem_u32(dXt), sY = smem_u32(Yt);
-  const uint32_t sdG = smem_u32(dGt);
-  uint32_t phase = 0;
-  // batch 1: K K^T, W^T, U^T, ddelta^T = dH'^T K^T
-  if (tid == 0 && ok) {
-    const uint32_t id64 = idesc_bf16(64, 64, 0, 0);
-    mma_seq<8, 0, 64, 0, 64>(tm + R_KK, sK, sK, id64, 0u);
-    const uint32_t id_tn = idesc_bf16(128, 64, 1, 0);
-    mma_seq<4, 1, 64, 0, 64>(tm + R_W, sK, sT, id_tn, 0u);
-    mma_seq<4, 1, 64, 0, 64>(tm + R_U, sV, sT, id_tn, 0u);
-    const uint32_t id_hk = idesc_bf16(128, 64, 0, 0);
-    mma_seq<8, 0, 128, 0, 64>(tm + R_DD, sdH, sK, id_hk, 0u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float w[32];
-    ld32w(lane_tm, R_W + half * 32, w);
-    st_row32_bf16(Wr, 128, lane128, half * 32, w);
-  }
-  ok = loaded(1) && ok;
-  publish();
-  // batch 2: X = H^T W^T; ddelta^T += dO^T P
-  if (tid == 0 && ok) {
-    const uint32_t id_hw = idesc_bf16(128, 64, 0, 1);
-    mma_seq<8, 0, 128, 1, 128>(tm + R_X, sH, sW, id_hw, 0u);
-    const uint32_t id_op = idesc_bf16(128, 64, 1, 1);
-    mma_seq<4, 1, 64, 1, 64>(tm + R_DD, sG, sP, id_op, 1u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float u[32], x[32];
-    tmem_ld32(lane_tm + (uint32_t)(R_U + half * 32), u);
-    tmem_ld32(lane_tm + (uint32_t)(R_X + half * 32), x);
-    tmem_wait_ld();
-#pragma unroll
-    for (int s = 0; s < 32; ++s) u[s] -= x[s];
-    st_row32_bf16(Dt, 128, lane128, half * 32, u);  // delta^T [j][t]
-    ld32w(lane_tm, R_DD + half * 32, x);
-    st_row32_bf16(dDt, 128, lane128, half * 32, x);  // ddelta^T [j][t]
-  }
-  publish();
-  // batch 3: dP = dO delta^T; dW = -ddelta H^T; dV = T'^T ddelta; dT' = ddelta V^T
-  if (tid == 0 && ok) {
-    const uint32_t id_dp = idesc_bf16(64, 64, 0, 1);
-    mma_seq<8, 0, 64, 1, 128>(tm + R_DP, sG, sD, id_dp, 0u);
-    const uint32_t id_dw = idesc_bf16(64, 128, 1, 1, 1);
-    mma_seq<8, 1, 128, 1, 128>(tm + R_DW, sdD, sH, id_dw, 0u);
-    const uint32_t id_dv = idesc_bf16(64, 128, 1, 0);
-    mma_seq<4, 1, 64, 0, 128>(tm + R_DV, sT, sdD, id_dv, 0u);
-    const uint32_t id_dt = idesc_bf16(64, 64, 1, 0);
-    mma_seq<8, 1, 128, 0, 64>(tm + R_DT, sdD, sV, id_dt, 0u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float a[32];
-    ld32w(lane_tm, R_DP + half * 32, a);
-    if (rowlane) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) a[e] = half * 32 + e <= trow ? a[e] : 0.f;
-      st_row32_bf16(dPt, 64, trow, half * 32, a);
-    }
-    float r[64];
-    ld64(lane_tm, R_DW + half * 64, r);
-    if (rowlane) st_row64_bf16(dWt, 64, trow, half, r);
-    ld64(lane_tm, R_DV + half * 64, r);
-    if (rowlane) st_row64_bf16(Vt, 64, trow, half, r);  // dV staged over V (its products are done)
-  }
-  publish();
-  if (tid == 0) store_tile(&dvmap, Vt, h, t0, b, D);
-  // batch 4: dQ = dO H^T + dP K; dT' += dW K^T
-  if (tid == 0 && ok) {
-    const uint32_t id_oh = idesc_bf16(64, 128, 0, 1);
-    mma_seq<8, 0, 64, 1, 128>(tm + R_DQ, sG, sH, id_oh, 0u);
-    const uint32_t id_pk = idesc_bf16(64, 128, 0, 1);
-    mma_seq<4, 0, 64, 1, 64>(tm + R_DQ, sdP, sK, id_pk, 1u);
-    const uint32_t id_wk = idesc_bf16(64, 64, 0, 0);
-    mma_seq<8, 0, 64, 0, 64>(tm + R_DT, sdW, sK, id_wk, 1u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float r[64];
-    ld64(lane_tm, R_DQ + half * 64, r);
-    if (rowlane) st_row64_bf16(Gt, 64, trow, half, r);  // dQ staged over dO (its products are done)
-    ok = loaded(2) && ok;
-    // dT' row t: dX = dT' diag(beta) (bf16 operand), dT' * X products for dbeta's first part
-    float dt[32];
-    ld32w(lane_tm, R_DT + half * 32, dt);
-    if (rowlane) {
-      float dx[32];
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int s2 = half * 32 + e;
-        const float xr = __bfloat162float(*reinterpret_cast<const bf16*>(Xt + sw_offset(64, trow, s2)));
-        dx[e] = dt[e] * bsm[s2];
-        scr[trow * 65 + s2] = dt[e] * xr;
-      }
-      st_row32_bf16(dXt, 64, trow, half * 32, dx);
-    }
-  }
-  publish();
-  if (tid == 0) {
-    store_tile(&dqmap, Gt, h, t0, b, D);
-    bulk_wait_read_but_newest();  // dV has left V, which Y overwrites below
-  }
-  // batch 5: Y = dX X^T (issued before the dbeta column sums below, which do not feed it)
-  if (tid == 0 && ok) {
-    const uint32_t id = idesc_bf16(64, 64, 0, 0);
-    mma_seq<4, 0, 64, 0, 64>(tm + R_Y, sdX, sX, id, 0u);
-    umma_commit(&bar);
-  }
-  if (tid < C) {
-    float a = 0.f;
-    for (int t = 0; t < C; ++t) a += scr[t * 65 + tid];
-    db1[tid] = a;
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float y[32];
-    ld32w(lane_tm, R_Y + half * 32, y);
-    if (rowlane) st_row32_bf16(Yt, 64, trow, half * 32, y);
-  }
-  publish();
-  // batch 6: Z = X^T Y; dA = -Z (strictly lower)
-  if (tid == 0 && ok) {
-    const uint32_t id = idesc_bf16(64, 64, 1, 1);
-    mma_seq<4, 1, 64, 1, 64>(tm + R_Z, sX, sY, id, 0u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float z[32], kk[32];
-    tmem_ld32(lane_tm + (uint32_t)(R_Z + half * 32), z);
-    tmem_ld32(lane_tm + (uint32_t)(R_KK + half * 32), kk);
-    tmem_wait_ld();
-    if (rowlane) {
-      const float bt = bsm[trow];
-      float db2 = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const int s2 = half * 32 + e;
-        const float da = s2 < trow ? -z[e] : 0.f;
-        db2 = fmaf(da, kk[e], db2);
-        scr[trow * 65 + s2] = bt * da;  // dG
-      }
-      db2s[half][trow] = db2;
-    }
-  }
-  __syncthreads();
-  if (rowlane) {
-    float g[32];
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      const int s2 = half * 32 + e;
-      g[e] = scr[trow * 65 + s2] + scr[s2 * 65 + trow];
-    }
-    st_row32_bf16(dGt, 64, trow, half * 32, g);
-    if (half == 0 && trow < valid)
-      dbeta[(row0 + trow) * H + h] = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
-  }
-  publish();
-  // batch 7: dK = dP^T Q + delta dH'^T + T'^T dW + (dG + dG^T) K
-  if (tid == 0 && ok) {
-    const uint32_t id_mn = idesc_bf16(64, 128, 1, 1);
-    mma_seq<4, 1, 64, 1, 64>(tm + R_DK, sdP, sQ, id_mn, 0u);
-    mma_seq<8, 1, 128, 1, 128>(tm + R_DK, sD, sdH, id_mn, 1u);
-    mma_seq<4, 1, 64, 1, 64>(tm + R_DK, sT, sdW, id_mn, 1u);
-    const uint32_t id_gk = idesc_bf16(64, 128, 0, 1);
-    mma_seq<4, 0, 64, 1, 64>(tm + R_DK, sdG, sK, id_gk, 1u);
-    umma_commit(&bar);
-  }
-  ok = ok && mma_wait(&bar, phase, status);
-  {
-    float r[64];
-    ld64(lane_tm, R_DK + half * 64, r);
-    if (rowlane) st_row64_bf16(Kt, 64, trow, half, r);  // dK staged over K (its products are done)
-  }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = tbase;
+  const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
+  const uint32_t s0 = smem_u32(sm);
+  const uint32_t sdH = s0 + GrSmem::DH, sH = s0 + GrSmem::HH, sG = s0 + GrSmem::GG;
+  const uint32_t sP = s0 + GrSmem::PP, sT = s0 + GrSmem::TT, sX = s0 + GrSmem::XX, sR = s0 + GrSmem::Rt;
+  const uint32_t sdD = s0 + GrSmem::dD, sD = s0 + GrSmem::Dt, sdW = s0 + GrSmem::Wd;
+  const uint32_t sdX = sR, sdG = sR + TILE_TT, sdP = sD, sY = sD + TILE_TT;
+  // thread 0's account of what it armed or committed and which phases it saw complete: a CTA that
+  // stops early waits (bounded) for its copies and products in flight before it returns
+  int la_arms = 0, la_seen = 0, lb_arms = 0, lb_seen = 0, b1_commits = 0, b1_seen = 0, b_commits = 0, b_seen = 0;
+
+  struct Coord {
+    int b, h, t0;
+  };
+  auto coords = [&](int chunk) -> Coord {
+    const int bh = chunk / NC;
+    return Coord{bh / H, bh % H, (chunk - bh * NC) * C};
+  };
+  auto k_region = [&](int parity) -> uint32_t { return parity ? GrSmem::KB : GrSmem::KA; };
+  auto q_region = [&](int parity) -> uint32_t { return parity ? GrSmem::KA : GrSmem::KB; };
+  // the loads of chunk `chunk` (thread 0), in the order their regions free up
+  auto load_vp = [&](int chunk, const Coord& q) {
+    mbar_arrive_expect_tx(&la, TILE_TD + TILE_TT);
+    tma_tile(Vt, &vmap, &la, q.h, q.t0, q.b);
+    bulk_load(sm + GrSmem::PP, xt + (size_t)chunk * PREP_BYTES + PREP_P, TILE_TT, &la);
+    ++la_arms;
+  };
+  auto load_hg = [&](int chunk, const Coord& q) {
+    mbar_arrive_expect_tx(&la, 2 * TILE_JI + TILE_TD);
+    bulk_load(sm + GrSmem::DH, dhck + (size_t)chunk * TILE_JI, TILE_JI, &la);
+    bulk_load(sm + GrSmem::HH, hck + (size_t)chunk * TILE_JI, TILE_JI, &la);
+    tma_tile(sm + GrSmem::GG, &gmap, &la, q.h, q.t0, q.b);
+    ++la_arms;
+  };
+  auto load_k = [&](const Coord& q, int parity) {
+    mbar_arrive_expect_tx(&la, TILE_TD);
+    tma_tile(sm + k_region(parity), &kmap, &la, q.h, q.t0, q.b);
+    ++la_arms;
+  };
+  auto load_tx = [&](int chunk) {
+    const uint8_t* pre = xt + (size_t)chunk * PREP_BYTES;
+    mbar_arrive_expect_tx(&lb, 2 * TILE_TT);
+    bulk_load(sm + GrSmem::TT, pre + PREP_T, TILE_TT, &lb);
+    bulk_load(Xt, pre + PREP_X, TILE_TT, &lb);
+    ++lb_arms;
+  };
+  auto load_q = [&](const Coord& q, int parity) {
+    mbar_arrive_expect_tx(&lb, TILE_TD);
+    tma_tile(sm + q_region(parity), &qmap, &lb, q.h, q.t0, q.b);
+    ++lb_arms;
+  };
+  // stage 1 of a chunk whose K lives in k_region(parity) (thread 0, after its loads on la)
+  auto issue_s1 = [&](int parity) {
+    const uint32_t sK = s0 + k_region(parity);
+    const uint32_t id = idesc_bf16(128, 64, 0, 0);
+    mma_seq<8, 0, 128, 0, 64>(tm + C_RT, sH, sK, id, 0u);    // (K H)^T [j][t]
+    mma_seq<8, 0, 128, 0, 64>(tm + C_DDT, sdH, sK, id, 0u);  // ddelta^T = dH'^T K^T + dO^T P
+    mma_seq<4, 1, 64, 1, 64>(tm + C_DDT, sG, sP, idesc_bf16(128, 64, 1, 1), 1u);
+    umma_commit(&bar1);
+    ++b1_commits;
+  };
+  auto commit = [&]() {
+    umma_commit(&bar);
+    ++b_commits;
+  };
+  // all threads: the next phase of bar (thread 0's count sets the parity of everyone's)
+  auto wait_mma = [&](bool ok) -> bool {
+    if (!ok) return false;
+    const bool r = mbar_wait(&bar, (uint32_t)(b_seen & 1));
+    if (r) ++b_seen;
+    else atomicOr(status, 2);
+    tc_fence_after();
+    return r;
+  };
+  auto wait_load = [&](uint64_t* lbar, int& seen) -> bool {
+    const bool r = mbar_wait(lbar, (uint32_t)(seen & 1));
+    if (r) ++seen;
+    else atomicOr(status, 4);
+    return r;
+  };
+
+  bool ok = true;
+  int chunk = blockIdx.x;
+  if (tid == 0 && chunk < total) {
+    const Coord q = coords(chunk);
+    load_vp(chunk, q);
+    load_hg(chunk, q);
+    load_k(q, 0);
+    load_tx(chunk);
+    load_q(q, 0);
+    if (wait_load(&la, la_seen)) issue_s1(0);
+    else ok = false;
+  }
+  for (int it = 0; chunk < total; chunk += gridDim.x, ++it) {
+    const int par = it & 1;
+    const int next = chunk + (int)gridDim.x;
+    const bool has_next = next < total;
+    const Coord cur = coords(chunk), nxt = coords(has_next ? next : chunk);
+    const int b = cur.b, h = cur.h, t0 = cur.t0;
+    const int valid = min(C, T - t0);
+    const int64_t row0 = (int64_t)b * T + t0;
+    const uint32_t sK = s0 + k_region(par), sQ = s0 + q_region(par);
+    const bf16 bv = fetch_beta(beta + h, row0, H, valid);
+    // stage 1 was issued before this iteration: R^T = V^T - (K H)^T, ddelta^T
+    if (ok) {
+      const bool r = mbar_wait(&bar1, (uint32_t)(b1_seen & 1));
+      if (r) ++b1_seen;
+      else { ok = false; atomicOr(status, 2); }
+      tc_fence_after();
+    }
+    {
+      float a[32];
+      ld32w(lane_tm, C_RT + half * 32, a);
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        a[e] = __bfloat162float(*reinterpret_cast<const bf16*>(Vt + sw_offset(64, half * 32 + e, lane128))) - a[e];
+      st_row32_bf16(Rt, 128, lane128, half * 32, a);
+      ld32w(lane_tm, C_DDT + half * 32, a);
+      st_row32_bf16(dDt, 128, lane128, half * 32, a);
+    }
+    if (tid < C) bsm[tid] = __bfloat162float(bv);
+    if (tid == 0) bulk_wait_read();  // the previous chunk's dQ and dK stores have left Wd and Dt
+    publish();
+    if (tid == 0 && ok && has_next) load_vp(next, nxt);  // V (also read by the readout above) and P are done
+    // stage 2: delta^T = R^T T'^T; dW = -ddelta H^T; dV = T'^T ddelta; dT' = ddelta R^T
+    if (tid == 0 && ok) {
+      if (wait_load(&lb, lb_seen)) {
+        mma_seq<4, 0, 128, 0, 64>(tm + C_DELTA, sR, sT, idesc_bf16(128, 64, 0, 0), 0u);
+        mma_seq<8, 1, 128, 1, 128>(tm + C_DW, sdD, sH, idesc_bf16(64, 128, 1, 1, 1), 0u);
+        mma_seq<4, 1, 64, 0, 128>(tm + C_DV, sT, sdD, idesc_bf16(64, 128, 1, 0), 0u);
+        mma_seq<8, 1, 128, 1, 128>(tm + C_DTP, sdD, sR, idesc_bf16(64, 64, 1, 1), 0u);
+        commit();
+      } else {
+        ok = false;
+      }
+    }
+    ok = wait_mma(ok);
+    if (tid != 0 && ok) {  // X is read below (thread 0 saw lb before stage 2)
+      const bool r = mbar_wait(&lb, (uint32_t)(lb_seen & 1));
+      if (r) ++lb_seen;
+      else { ok = false; atomicOr(status, 4); }
+    }
+    {
+      float a[32];
+      ld32w(lane_tm, C_DELTA + half * 32, a);
+      st_row32_bf16(Dt, 128, lane128, half * 32, a);  // delta^T [j][t]
+      float r[64];
+      ld64(lane_tm, C_DW + half * 64, r);
+      if (rowlane) st_row64_bf16(Wd, 64, trow, half, r);  // dW [t][i]
+      // dT' row t: dX = dT' diag(beta) (bf16 operand); dbeta's first part sum_t dT'[t][s] X[t][s]
+      float dx[32];
+      ld32w(lane_tm, C_DTP + half * 32, a);
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint4 xw = *reinterpret_cast<const uint4*>(Xt + sw_chunk(64, trow, half * 4 + c8));
+        const bf16* xe = reinterpret_cast<const bf16*>(&xw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int e = 8 * c8 + i;
+          dx[e] = a[e] * bsm[half * 32 + e];
+          a[e] = rowlane ? a[e] * __bfloat162float(xe[i]) : 0.f;
+        }
+      }
+      if (rowlane) st_row32_bf16(dXt, 64, trow, half * 32, dx);
+      halfwarp_sums(a, lane);
+      if (rowlane) {
+        part[quarter][half * 32 + 2 * lane] = a[0];
+        part[quarter][half * 32 + 2 * lane + 1] = a[1];
+      }
+    }
+    publish();
+    // stage 3: dP = dO delta^T; Y = dX X^T; dQ = dO H^T; dK = delta dH'^T
+    if (tid == 0 && ok) {
+      mma_seq<8, 0, 64, 1, 128>(tm + C_DP, sG, sD, idesc_bf16(64, 64, 0, 1), 0u);
+      mma_seq<4, 0, 64, 0, 64>(tm + C_Y, sdX, sX, idesc_bf16(64, 64, 0, 0), 0u);
+      mma_seq<8, 0, 64, 1, 128>(tm + C_DQ, sG, sH, idesc_bf16(64, 128, 0, 1), 0u);
+      mma_seq<8, 1, 128, 1, 128>(tm + C_DK, sD, sdH, idesc_bf16(64, 128, 1, 1), 0u);
+      commit();
+    }
+    if (tid < C) db1[tid] = (part[0][tid] + part[1][tid]) + (part[2][tid] + part[3][tid]);
+    {  // dV, while stage 3 runs: staged over ddelta^T (its products are done)
+      float r[64];
+      ld64(lane_tm, C_DV + half * 64, r);
+      if (rowlane) st_row64_bf16(dVt, 64, trow, half, r);
+    }
+    ok = wait_mma(ok);
+    if (tid == 0 && ok && has_next) load_hg(next, nxt);  // dH', H and dO are done
+    {
+      float a[32];
+      ld32w(lane_tm, C_DP + half * 32, a);
+      if (rowlane) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) a[e] = half * 32 + e <= trow ? a[e] : 0.f;
+        st_row32_bf16(dPt, 64, trow, half * 32, a);
+      }
+      ld32w(lane_tm, C_Y + half * 32, a);
+      if (rowlane) st_row32_bf16(Yt, 64, trow, half * 32, a);
+    }
+    publish();
+    if (tid == 0) store_tile(&dvmap, dVt, h, t0, b, D);
+    // stage 4: Z = X^T Y and its transpose; K K^T; dQ += dP K; dK += dP^T Q + T'^T dW
+    if (tid == 0 && ok) {
+      mma_seq<4, 1, 64, 1, 64>(tm + C_Z, sX, sY, idesc_bf16(64, 64, 1, 1), 0u);
+      mma_seq<4, 1, 64, 1, 64>(tm + C_ZT, sY, sX, idesc_bf16(64, 64, 1, 1), 0u);
+      mma_seq<8, 0, 64, 0, 64>(tm + C_KK, sK, sK, idesc_bf16(64, 64, 0, 0), 0u);
+      mma_seq<4, 0, 64, 1, 64>(tm + C_DQ, sdP, sK, idesc_bf16(64, 128, 0, 1), 1u);
+      const uint32_t id_mn = idesc_bf16(64, 128, 1, 1);
+      mma_seq<4, 1, 64, 1, 64>(tm + C_DK, sdP, sQ, id_mn, 1u);
+      mma_seq<4, 1, 64, 1, 64>(tm + C_DK, sT, sdW, id_mn, 1u);
+      commit();
+    }
+    ok = wait_mma(ok);
+    if (tid == 0 && ok && has_next) {  // Q, T' and X are done: the next K lands in Q's region
+      load_k(nxt, par ^ 1);
+      load_tx(next);
+    }
+    {
+      float z[32], zt[32], kk[32];
+      tmem_ld32(lane_tm + (uint32_t)(C_Z + half * 32), z);
+      tmem_ld32(lane_tm + (uint32_t)(C_ZT + half * 32), zt);
+      tmem_ld32(lane_tm + (uint32_t)(C_KK + half * 32), kk);
+      tmem_wait_ld();
+      if (rowlane) {
+        // dG = diag(beta) dA + (diag(beta) dA)^T has one nonzero term per entry: beta_t dA[t][s]
+        // below the diagonal, beta_s dA[s][t] = -beta_s Z^T[t][s] above it
+        const float bt = bsm[trow];
+        float db2 = 0.f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {  // unconditional loads: a load under the lane test branches
+          const int s2 = half * 32 + e;
+          const float bs = bsm[s2];
+          const float da = s2 < trow ? -z[e] : 0.f;
+          db2 = fmaf(da, kk[e], db2);
+          z[e] = s2 < trow ? bt * da : (s2 > trow ? -bs * zt[e] : 0.f);
+        }
+        st_row32_bf16(dGt, 64, trow, half * 32, z);
+        db2s[half][trow] = db2;
+      }
+    }
+    publish();
+    if (rowlane && half == 0 && trow < valid)
+      dbeta[(row0 + trow) * H + h] = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
+    // stage 5: dK += dG K; then the next chunk's stage 1 (its columns and regions are free)
+    if (tid == 0 && ok) {
+      mma_seq<4, 0, 64, 1, 64>(tm + C_DK, sdG, sK, idesc_bf16(64, 128, 0, 1), 1u);
+      commit();
+      if (has_next) {
+        if (wait_load(&la, la_seen)) issue_s1(par ^ 1);
+        else ok = false;
+      }
+    }
+    {  // dQ, while stage 5 runs: staged over dW (its products are done)
+      float r[64];
+      ld64(lane_tm, C_DQ + half * 64, r);
+      if (rowlane) st_row64_bf16(dQt, 64, trow, half, r);
+    }
+    ok = wait_mma(ok);
+    if (tid == 0) {
+      if (ok && has_next) load_q(nxt, par ^ 1);  // K is done: the next Q lands in its region
+      bulk_wait_read();                           // dV has left ddelta^T's region (next stage 1)
+    }
+    {
+      float r[64];
+      ld64(lane_tm, C_DK + half * 64, r);
+      if (rowlane) st_row64_bf16(dKt, 64, trow, half, r);  // dK staged over dP and Y
+    }
+    ok = publish_ok(ok);
+    if (tid == 0) {
+      store_tile(&dqmap, dQt, h, t0, b, D);
+      store_tile(&dkmap, dKt, h, t0, b, D);
+    }
+    if (!ok) break;
+  }
   if (tid == 0) {
-    store_tile(&dkmap, Kt, h, t0, b, D);
+    // after an early stop: let every armed copy and committed product finish (bounded waits)
+    while (la_arms % 3) { mbar_arrive(&la); ++la_arms; }
+    while (lb_arms % 2) { mbar_arrive(&lb); ++lb_arms; }
+    for (; la_seen < la_arms / 3; ++la_seen) mbar_wait(&la, (uint32_t)(la_seen & 1));
+    for (; lb_seen < lb_arms / 2; ++lb_seen) mbar_wait(&lb, (uint32_t)(lb_seen & 1));
+    for (; b1_seen < b1_commits; ++b1_seen) mbar_wait(&bar1, (uint32_t)(b1_seen & 1));
+    for (; b_seen < b_commits; ++b_seen) mbar_wait(&bar, (uint32_t)(b_seen & 1));
     bulk_wait_read();
   }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (warp == 0) tmem_dealloc(tm, 512);
 }
 
@@ -1105,8 +1205,12 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
     if ((rc = make_token_map(&dqm, dq, B, T, H, D)) || (rc = make_token_map(&dkm, dk, B, T, H, D)) ||
         (rc = make_token_map(&dvm, dv, B, T, H, D)))
       return rc;
-    scan_grad_kernel<<<B * H * NC, NG, sg, st>>>(qm, km, vm, gm, dqm, dkm, dvm, (const bf16*)beta, xt, hck, dhck,
-                                                 (bf16*)dbeta, T, H, D, NC, status);
+    int dev = 0, nsm = 0;
+    VB_CUDA_CHECK(cudaGetDevice(&dev), "grad device");
+    VB_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev), "grad SM count");
+    const int total = B * H * NC;  // one persistent CTA per SM walks the chunks
+    scan_grad_kernel<<<total < nsm ? total : nsm, NG, sg, st>>>(qm, km, vm, gm, dqm, dkm, dvm, (const bf16*)beta, xt,
+                                                                 hck, dhck, (bf16*)dbeta, T, H, D, NC, total, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 grad");
   }
   return VB_OK;
