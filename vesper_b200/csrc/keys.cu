@@ -119,11 +119,14 @@ __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float 
 #pragma unroll
   for (int e = 0; e < EPL; ++e) dot += g[e] * s[e];
   dot = warp_sum(dot);
-  const float q = dot / (den * den * den);
+  // s and sq repeat the forward's quotients exactly (the clamp decision); the gradient's own
+  // quotients are products with one reciprocal of den and one of scale
+  const float rden = 1.0f / den, rscale = 1.0f / scale;
+  const float q = dot * (rden * rden * rden);
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
     const float through = sq >= 1.0f ? s[e] * q : 0.f;
-    du[e] = (g[e] / den - through) / scale;
+    du[e] = (g[e] * rden - through) * rscale;
   }
 }
 
@@ -163,9 +166,10 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
     float scale, s[EPL], den, sq;
     norm_stats<EPL>(u, floor_, scale, s, den, sq);
     if (live) {
+      const float rden = 1.0f / den;  // k = s / den to within an ulp or two of the quotient
       float o[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) o[e] = s[e] / den;
+      for (int e = 0; e < EPL; ++e) o[e] = s[e] * rden;
       st_elems<T, EPL>(out + ((int64_t)b * T_ + t) * W + c, o);
     }
 #pragma unroll

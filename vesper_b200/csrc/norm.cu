@@ -84,15 +84,20 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const T* __rest
 #pragma unroll
       for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(v[r][i][e]));
     const float scale = fmaxf(warp_max(amax), floor_);
+    // one reciprocal per row, then products: z = x / scale and y = z / rms * g to within a few
+    // ulps of the quotients (no decision depends on them), z in [-1, 1] so no product underflows
+    const float rscale = 1.0f / scale;
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i)
 #pragma unroll
       for (int e = 0; e < E; ++e) {
-        const float z = v[r][i][e] / scale;
+        const float z = v[r][i][e] * rscale;
+        v[r][i][e] = z;
         ss += z * z;
       }
     const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
+    const float rrms = 1.0f / rms;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int vi = lane + 32 * i;
@@ -105,7 +110,7 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const T* __rest
           g[4 * q] = g4.x; g[4 * q + 1] = g4.y; g[4 * q + 2] = g4.z; g[4 * q + 3] = g4.w;
         }
 #pragma unroll
-        for (int e = 0; e < E; ++e) o[e] = v[r][i][e] / scale / rms * g[e];
+        for (int e = 0; e < E; ++e) o[e] = v[r][i][e] * (rrms * g[e]);
         store_vec<T, E>(y + row * width + vi * E, o);
       }
     }
@@ -127,13 +132,15 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict
   float amax = 0.f;
   for (int j = lane; j < width; j += 32) amax = fmaxf(amax, fabsf(to_f32<T>(xr[j])));
   const float scale = fmaxf(warp_max(amax), floor_);
+  const float rscale = 1.0f / scale;  // as the vector kernel: one reciprocal per row
   float ss = 0.f;
   for (int j = lane; j < width; j += 32) {
-    const float z = to_f32<T>(xr[j]) / scale;
+    const float z = to_f32<T>(xr[j]) * rscale;
     ss += z * z;
   }
   const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
-  for (int j = lane; j < width; j += 32) yr[j] = from_f32<T>(to_f32<T>(xr[j]) / scale / rms * __ldg(w + j));
+  const float rrms = 1.0f / rms;
+  for (int j = lane; j < width; j += 32) yr[j] = from_f32<T>(to_f32<T>(xr[j]) * rscale * (rrms * __ldg(w + j)));
   if (lane == 0) inv[row] = 1.0f / (scale * rms);
 }
 
