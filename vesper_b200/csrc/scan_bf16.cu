@@ -1045,9 +1045,11 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
         for (int e = 0; e < 32; ++e) {  // unconditional loads: a load under the lane test branches
           const int s2 = half * 32 + e;
           const float bs = bsm[s2];
-          const float da = s2 < trow ? -z[e] : 0.f;
+          // 0/1 masks and products rather than selects between computed values
+          const float lo = s2 < trow ? 1.f : 0.f, hi = s2 > trow ? 1.f : 0.f;
+          const float da = -lo * z[e];
           db2 = fmaf(da, kk[e], db2);
-          z[e] = s2 < trow ? bt * da : (s2 > trow ? -bs * zt[e] : 0.f);
+          z[e] = fmaf(bt, da, -hi * bs * zt[e]);
         }
         st_row32_bf16(dGt, 64, trow, half * 32, z);
         db2s[half][trow] = db2;
