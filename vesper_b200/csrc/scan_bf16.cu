@@ -267,12 +267,13 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
     tmem_wait_ld();
     if (lane128 < C) {
       const int t = lane128;
+      const float bt = bsm[t];  // 0/1 masks and products below, not per-lane selects
 #pragma unroll
-      for (int e = 0; e < 32; ++e) A[t * 65 + c0 + e] = c0 + e < t ? bsm[t] * v[e] : 0.f;
+      for (int e = 0; e < 32; ++e) A[t * 65 + c0 + e] = (c0 + e < t ? 1.f : 0.f) * (bt * v[e]);
     } else {
       const int t = lane128 - C;
 #pragma unroll
-      for (int e = 0; e < 32; ++e) v[e] = c0 + e <= t ? v[e] : 0.f;
+      for (int e = 0; e < 32; ++e) v[e] *= c0 + e <= t ? 1.f : 0.f;
       st_row32_bf16(Ps, 64, t, c0, v);
     }
   }
@@ -286,7 +287,8 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int idx = tid + NP * e, t = idx >> 6, j = idx & 63;
-      xv[e] = (j >> 4) > (t >> 4) ? 0.f : Xf[t * XS + j];
+      const float xf = Xf[t * XS + j];  // loaded unconditionally (entries above the blocks are not written)
+      xv[e] = (j >> 4) > (t >> 4) ? 0.f : xf;
     }
     __syncthreads();
 #pragma unroll
