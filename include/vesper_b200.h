@@ -79,20 +79,24 @@ VB_API int vb_rms_norm_bwd_noalloc(const void *x, const float *weight, const voi
  * u[b,t,j] = sum_r taps[r,j] * full[b, t+K-1-r, j] with full = cat(hist, z) along t, then
  * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's
  * dtype. z, keys: [B,T,W] (keys viewed [B,T,heads,W/heads]); hist: [B,K-1,W] float32;
- * taps: [K,W] float32. Replaces vesper/kernels/keys_triton.py:148-156 (keys_forward) reached from
- * vesper/kernels/keys.py:28-46 (fused_keys) and vesper/column.py:255-289 (RecurrentSublayer.keys). */
-VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void *keys, int B, int T,
-                int width, int heads, int taps_count, float floor_, int dtype, void *stream);
+ * taps: [K,W] float32. stats: [B,heads,T,2] float32 (8-byte aligned) or NULL: per token and head
+ * the scale and den of the normalisation, den negated where the squared norm reaches 1 (where
+ * the clamp passes gradient), for vb_keys_bwd. Replaces vesper/kernels/keys_triton.py:148-156
+ * (keys_forward) reached from vesper/kernels/keys.py:28-46 (fused_keys) and
+ * vesper/column.py:255-289 (RecurrentSublayer.keys). */
+VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void *keys, float *stats,
+                int B, int T, int width, int heads, int taps_count, float floor_, int dtype, void *stream);
 
 VB_API size_t vb_keys_bwd_workspace(int B, int T, int width, int heads, int taps_count);
 
 /* Gradients of sum(keys * grad_keys): grad_z [B,T,W] in z's dtype, grad_taps [K,W] float32
- * (fixed-order), grad_hist [B,K-1,W] float32 (skipped when NULL). Replaces
+ * (fixed-order), grad_hist [B,K-1,W] float32 (skipped when NULL). stats: vb_keys_fwd's output for
+ * the same inputs, or NULL to recompute the statistics (slower). Replaces
  * vesper/kernels/keys_triton.py:159-177 (keys_backward) and vesper/kernels/keys.py:67-78
  * (_history_gradient). */
 VB_API int vb_keys_bwd(const void *z, const float *hist, const float *taps, const void *grad_keys,
-                void *grad_z, float *grad_taps, float *grad_hist, void *workspace, int B, int T,
-                int width, int heads, int taps_count, float floor_, int dtype, void *stream);
+                const float *stats, void *grad_z, float *grad_taps, float *grad_hist, void *workspace,
+                int B, int T, int width, int heads, int taps_count, float floor_, int dtype, void *stream);
 
 /* ---- delta-rule scan, float32 (token-serial) --------------------------------------------------
  * H_t = H_{t-1} + beta_t k_t (v_t - H_{t-1}^T k_t)^T, o_t = H_t^T q_t, H read as [key, value].

@@ -13,7 +13,7 @@ import torch
 
 import oracle
 from conftest import golden, golden_names
-from vesper_b200.kernels.keys import fused_keys
+from vesper_b200.kernels.keys import KEY_NORM_FLOOR, fused_keys, keys_backward, keys_forward
 
 pytestmark = pytest.mark.gpu
 CUDA = torch.device("cuda")
@@ -92,3 +92,28 @@ def test_no_history_gradient_unless_asked_and_captured_equals_eager() -> None:
         graph.replay()
         torch.cuda.synchronize()
         assert all(torch.equal(a, b) for a, b in zip(out, eager[0], strict=True))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_saved_statistics_give_the_recomputed_gradients_at_the_clamp_boundary(dtype: torch.dtype) -> None:
+    """The backward fed the forward's per-token statistics matches the one that recomputes them,
+    also where a head's filtered key is one-hot (squared norm exactly one, gradient through)."""
+    g = torch.Generator().manual_seed(11)
+    b, n, width, heads, count = 2, 150, 256, 2, 4
+    z = torch.randn(b, n, width, generator=g)
+    z[0, 10:14, :128] = 0.0
+    z[0, 13, 5] = 3.0  # u[0, 13] of head 0 = taps[0, 5] * 3 at channel 5 only
+    hist = torch.randn(b, count - 1, width, generator=g).to(CUDA)
+    taps = (torch.randn(count, width, generator=g) * 0.5).to(CUDA)
+    zc = z.to(CUDA, dtype)
+    grad_k = torch.randn(b, n, heads, width // heads, generator=g).to(CUDA, dtype)
+    stats = torch.empty(b, heads, n, 2, device=CUDA)
+    keys_forward(zc, hist, taps, heads, KEY_NORM_FLOOR, stats)
+    assert bool((stats[0, 0, 13, 1] < 0).item()) and float(stats[0, 0, 13, 1].abs()) == 1.0
+    with_stats = keys_backward(zc, hist, taps, grad_k, heads, KEY_NORM_FLOOR, True, stats)
+    recomputed = keys_backward(zc, hist, taps, grad_k, heads, KEY_NORM_FLOOR, True, None)
+    for got, want in zip(with_stats, recomputed, strict=True):
+        w = want.double().cpu().numpy()
+        bound = 2e-5 if dtype == torch.float32 else 8e-3
+        np.testing.assert_allclose(got.double().cpu().numpy(), w, rtol=bound, atol=bound * np.abs(w).max())
+

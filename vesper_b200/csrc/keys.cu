@@ -6,7 +6,10 @@
 // every element of z is read from HBM once (plus K-1 rows of overlap per run), and the key is
 // written once. The backward walks its run in reverse with the next K-1 input gradients in
 // registers, recomputing the filter output, and fuses dz, the taps' gradient (per-warp partial
-// sums, reduced in a fixed order) and the history's gradient into the same pass.
+// sums, reduced in a fixed order) and the history's gradient into the same pass. The forward can
+// save each token's normalisation statistics (scale and den, 8 bytes per token and head); the
+// backward then skips recomputing them (two warp reductions, a square root and the exact
+// quotients per token) and takes the clamp decision from them.
 #include "common.cuh"
 
 namespace vb {
@@ -101,10 +104,12 @@ __device__ __forceinline__ void load_g(const T* __restrict__ gk, int b, int t, i
 }
 
 // the filter input's gradient du of one token from its window w[r] = row t - r and its key
-// gradient g (the normalisation's backward: (g / den - s (g . s) / den^3 [sq >= 1]) / scale)
-template <int EPL, int K>
+// gradient g (the normalisation's backward: (g / den - s (g . s) / den^3 [sq >= 1]) / scale).
+// STATS: the forward's (scale, den) of the token, den negated when sq >= 1 (the clamp
+// decision, taken from the forward's exact quotients); otherwise they are recomputed here.
+template <int EPL, int K, bool STATS>
 __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float (&w)[K][EPL], const float (&g)[EPL],
-                                         float floor_, float (&du)[EPL]) {
+                                         float floor_, float2 stat, float (&du)[EPL]) {
   float u[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
@@ -113,19 +118,31 @@ __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float 
     for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], w[r][e], a);
     u[e] = a;
   }
-  float scale, s[EPL], den, sq;
-  norm_stats<EPL>(u, floor_, scale, s, den, sq);
+  float scale, s[EPL], den, rscale;
+  bool clamped;
+  if constexpr (STATS) {
+    scale = stat.x;
+    den = fabsf(stat.y);
+    clamped = stat.y < 0.f;
+    rscale = 1.0f / scale;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s[e] = u[e] * rscale;  // within an ulp of u / scale: gradient only
+  } else {
+    float sq;
+    norm_stats<EPL>(u, floor_, scale, s, den, sq);  // the forward's exact quotients (the clamp)
+    clamped = sq >= 1.0f;
+    rscale = 1.0f / scale;
+  }
   float dot = 0.f;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) dot += g[e] * s[e];
   dot = warp_sum(dot);
-  // s and sq repeat the forward's quotients exactly (the clamp decision); the gradient's own
-  // quotients are products with one reciprocal of den and one of scale
-  const float rden = 1.0f / den, rscale = 1.0f / scale;
+  // the gradient's own quotients are products with one reciprocal of den and one of scale
+  const float rden = 1.0f / den;
   const float q = dot * (rden * rden * rden);
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
-    const float through = sq >= 1.0f ? s[e] * q : 0.f;
+    const float through = clamped ? s[e] * q : 0.f;
     du[e] = (g[e] * rden - through) * rscale;
   }
 }
@@ -134,8 +151,9 @@ template <typename T, int EPL, int K>
 __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restrict__ z,
                                                               const float* __restrict__ hist,
                                                               const float* __restrict__ taps,
-                                                              T* __restrict__ out, int B, int T_,
-                                                              int W, int heads, int runs,
+                                                              T* __restrict__ out,
+                                                              float2* __restrict__ stats, int B,
+                                                              int T_, int W, int heads, int runs,
                                                               float floor_) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5);
@@ -151,6 +169,7 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
     for (int e = 0; e < EPL; ++e) tp[r][e] = live ? __ldg(taps + (int64_t)r * W + c + e) : 0.f;
   const int t0 = run * RUN, t1 = min(T_, t0 + RUN);
   float win[K][EPL];  // win[r] = input row t - r
+  float2 st_pair = make_float2(0.f, 0.f);
 #pragma unroll
   for (int r = 1; r < K; ++r) load_in<T, EPL>(z, hist, b, t0 - r, T_, W, K, c, live, win[r]);
   for (int t = t0; t < t1; ++t) {
@@ -172,6 +191,12 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
       for (int e = 0; e < EPL; ++e) o[e] = s[e] * rden;
       st_elems<T, EPL>(out + ((int64_t)b * T_ + t) * W + c, o);
     }
+    // (scale, den), den negated where the clamp passes gradient: token t's pair waits in lane
+    // (t - t0) % 32, and each 32 tokens leave as one contiguous warp store ([B, heads, T, 2])
+    const int slot = (t - t0) & 31;
+    if (lane == slot) st_pair = make_float2(scale, sq >= 1.0f ? -den : den);
+    if (stats != nullptr && (slot == 31 || t + 1 == t1) && lane <= slot)
+      stats[((int64_t)b * heads + head) * T_ + (t - slot + lane)] = st_pair;
 #pragma unroll
     for (int r = K - 1; r > 0; --r)
 #pragma unroll
@@ -179,11 +204,12 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
   }
 }
 
-// Backward over one run in reverse. partial: [B * runs, K, W] taps-gradient partial sums.
-template <typename T, int EPL, int K>
+// Backward over one run in reverse. partial: [B * runs, K, W] taps-gradient partial sums; stats:
+// the forward's per-token (scale, +-den) when STATS, else recomputed.
+template <typename T, int EPL, int K, bool STATS>
 __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
     const T* __restrict__ z, const float* __restrict__ hist, const float* __restrict__ taps,
-    const T* __restrict__ gk, T* __restrict__ dz, float* __restrict__ dhist,
+    const T* __restrict__ gk, const float2* __restrict__ stats, T* __restrict__ dz, float* __restrict__ dhist,
     float* __restrict__ partial, int B, int T_, int W, int heads, int runs, float floor_) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * WARPS + (threadIdx.x >> 5);
@@ -253,9 +279,15 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
     float ga[EPL], gb[EPL];
     load_g<T, EPL>(gk, b, t, T_, W, c, live, ga);
     load_g<T, EPL>(gk, b, t - 1, T_, W, c, live && two, gb);
+    float2 sa = make_float2(1.f, 1.f), sb = sa;
+    if constexpr (STATS) {
+      const float2* st_row = stats + ((int64_t)b * heads + head) * T_;
+      sa = __ldg(st_row + t);
+      if (two) sb = __ldg(st_row + t - 1);
+    }
     float da[EPL], db[EPL];
-    token_du<EPL, K>(tp, win, ga, floor_, da);
-    token_du<EPL, K>(tp, wb, gb, floor_, db);
+    token_du<EPL, K, STATS>(tp, win, ga, floor_, sa, da);
+    token_du<EPL, K, STATS>(tp, wb, gb, floor_, sb, db);
     step(t, da, win);
     if (two) {
 #pragma unroll
@@ -291,15 +323,16 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
 }
 
 template <typename T, int EPL>
-int launch_fwd(const void* z, const float* hist, const float* taps, void* out, int B, int T_, int W,
-               int heads, int K, float floor_, cudaStream_t st) {
+int launch_fwd(const void* z, const float* hist, const float* taps, void* out, float* stats, int B, int T_,
+               int W, int heads, int K, float floor_, cudaStream_t st) {
   const int runs = (T_ + RUN - 1) / RUN;
   const int warps = B * heads * runs;
   const int ctas = (warps + WARPS - 1) / WARPS;
 #define VB_KEYS_FWD(KK)                                                                          \
   case KK:                                                                                       \
-    keys_fwd_kernel<T, EPL, KK><<<ctas, WARPS * 32, 0, st>>>((const T*)z, hist, taps, (T*)out, B, \
-                                                             T_, W, heads, runs, floor_);        \
+    keys_fwd_kernel<T, EPL, KK><<<ctas, WARPS * 32, 0, st>>>((const T*)z, hist, taps, (T*)out,  \
+                                                             (float2*)stats, B, T_, W, heads,   \
+                                                             runs, floor_);                     \
     break;
   switch (K) {
     VB_KEYS_FWD(1) VB_KEYS_FWD(2) VB_KEYS_FWD(3) VB_KEYS_FWD(4)
@@ -312,17 +345,22 @@ int launch_fwd(const void* z, const float* hist, const float* taps, void* out, i
 }
 
 template <typename T, int EPL>
-int launch_bwd(const void* z, const float* hist, const float* taps, const void* gk, void* dz,
-               float* dtaps, float* dhist, float* partial, int B, int T_, int W, int heads, int K,
-               float floor_, cudaStream_t st) {
+int launch_bwd(const void* z, const float* hist, const float* taps, const void* gk, const float* stats,
+               void* dz, float* dtaps, float* dhist, float* partial, int B, int T_, int W, int heads,
+               int K, float floor_, cudaStream_t st) {
   const int runs = (T_ + RUN - 1) / RUN;
   const int warps = B * heads * runs;
   const int ctas = (warps + WARPS - 1) / WARPS;
-#define VB_KEYS_BWD(KK)                                                                           \
-  case KK:                                                                                        \
-    keys_bwd_kernel<T, EPL, KK><<<ctas, WARPS * 32, 0, st>>>((const T*)z, hist, taps, (const T*)gk, \
-                                                             (T*)dz, dhist, partial, B, T_, W,    \
-                                                             heads, runs, floor_);                \
+#define VB_KEYS_BWD(KK)                                                                            \
+  case KK:                                                                                         \
+    if (stats != nullptr)                                                                          \
+      keys_bwd_kernel<T, EPL, KK, true><<<ctas, WARPS * 32, 0, st>>>(                              \
+          (const T*)z, hist, taps, (const T*)gk, (const float2*)stats, (T*)dz, dhist, partial, B, T_, \
+          W, heads, runs, floor_);                                                                 \
+    else                                                                                           \
+      keys_bwd_kernel<T, EPL, KK, false><<<ctas, WARPS * 32, 0, st>>>(                             \
+          (const T*)z, hist, taps, (const T*)gk, nullptr, (T*)dz, dhist, partial, B, T_, W, heads, \
+          runs, floor_);                                                                           \
     break;
   switch (K) {
     VB_KEYS_BWD(1) VB_KEYS_BWD(2) VB_KEYS_BWD(3) VB_KEYS_BWD(4)
@@ -357,8 +395,8 @@ using namespace vb;
     { constexpr int EPL = 8; return __VA_ARGS__(); }               \
   }()
 
-extern "C" int vb_keys_fwd(const void* z, const float* hist, const float* taps, void* keys, int B,
-                           int T, int width, int heads, int taps_count, float floor_, int dtype,
+extern "C" int vb_keys_fwd(const void* z, const float* hist, const float* taps, void* keys, float* stats,
+                           int B, int T, int width, int heads, int taps_count, float floor_, int dtype,
                            void* stream) {
   int rc = check_shape(B, T, width, heads, taps_count);
   if (rc) return rc;
@@ -366,11 +404,12 @@ extern "C" int vb_keys_fwd(const void* z, const float* hist, const float* taps, 
   VB_REQUIRE(z && taps && keys && (hist || taps_count == 1), "keys_fwd: null pointer");
   VB_REQUIRE(aligned16(z) && aligned16(keys) && (!hist || aligned16(hist)),
              "keys_fwd: z, keys and history must start on 16-byte boundaries");
+  VB_REQUIRE(((uintptr_t)stats & 7u) == 0, "keys_fwd: stats must start on an 8-byte boundary");
   const int hd = width / heads;
   cudaStream_t st = (cudaStream_t)stream;
   return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
     return VB_KEYS_EPL_DISPATCH(hd, EPL, [&]() -> int {
-      return launch_fwd<Tt, EPL>(z, hist, taps, keys, B, T, width, heads, taps_count, floor_, st);
+      return launch_fwd<Tt, EPL>(z, hist, taps, keys, stats, B, T, width, heads, taps_count, floor_, st);
     });
   });
 }
@@ -382,9 +421,9 @@ extern "C" size_t vb_keys_bwd_workspace(int B, int T, int width, int heads, int 
 }
 
 extern "C" int vb_keys_bwd(const void* z, const float* hist, const float* taps, const void* grad_keys,
-                           void* grad_z, float* grad_taps, float* grad_hist, void* workspace, int B,
-                           int T, int width, int heads, int taps_count, float floor_, int dtype,
-                           void* stream) {
+                           const float* stats, void* grad_z, float* grad_taps, float* grad_hist,
+                           void* workspace, int B, int T, int width, int heads, int taps_count,
+                           float floor_, int dtype, void* stream) {
   int rc = check_shape(B, T, width, heads, taps_count);
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
@@ -399,10 +438,11 @@ extern "C" int vb_keys_bwd(const void* z, const float* hist, const float* taps, 
              "keys_bwd: null pointer");
   VB_REQUIRE(aligned16(z) && aligned16(grad_keys) && aligned16(grad_z) && (!hist || aligned16(hist)),
              "keys_bwd: z, the key gradient, dz and history must start on 16-byte boundaries");
+  VB_REQUIRE(((uintptr_t)stats & 7u) == 0, "keys_bwd: stats must start on an 8-byte boundary");
   const int hd = width / heads;
   return VB_DISPATCH_DTYPE(dtype, Tt, [&]() -> int {
     return VB_KEYS_EPL_DISPATCH(hd, EPL, [&]() -> int {
-      return launch_bwd<Tt, EPL>(z, hist, taps, grad_keys, grad_z, grad_taps, grad_hist,
+      return launch_bwd<Tt, EPL>(z, hist, taps, grad_keys, stats, grad_z, grad_taps, grad_hist,
                                  (float*)workspace, B, T, width, heads, taps_count, floor_, st);
     });
   });

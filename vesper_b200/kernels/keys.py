@@ -6,7 +6,9 @@ of mstampfli/vesper-preview. ``u[t] = sum_r taps[r] * z[t - r]`` with the chunk'
 arithmetic, the key in ``z``'s dtype, ``[b, n, heads, d/heads]``. The backward is the reference's
 own gradient (the normalisation's scale held constant, the clamp at a squared norm of one passing
 gradient at and above it); the taps' gradient is summed in a fixed order and the history's is
-formed only when the history requires one. Kernels: ``vb_keys_fwd`` / ``vb_keys_bwd``.
+formed only when the history requires one. The forward saves each token's normalisation
+statistics (scale and den, 8 bytes per token and head) for the backward, which then does not
+recompute them. Kernels: ``vb_keys_fwd`` / ``vb_keys_bwd``.
 """
 
 from __future__ import annotations
@@ -44,19 +46,33 @@ def fused_keys(z: Tensor, history: Tensor, taps: Tensor, heads: int) -> Tensor:
     return out
 
 
-def keys_forward(z: Tensor, hist: Tensor, taps: Tensor, heads: int, floor: float) -> Tensor:
+def keys_forward(
+    z: Tensor, hist: Tensor, taps: Tensor, heads: int, floor: float, stats: Tensor | None = None
+) -> Tensor:
+    """Keys ``[b, n, heads, d/heads]``; ``stats`` (float32 ``[b, heads, n, 2]``) receives each
+    token's normalisation scale and den (den negated where the clamp passes gradient)."""
     b, n, width = z.shape
     out = torch.empty(b, n, heads, width // heads, dtype=z.dtype, device=z.device)
     _lib.call(
-        "vb_keys_fwd", z.data_ptr(), hist.data_ptr(), taps.data_ptr(), out.data_ptr(), b, n, width,
-        heads, int(taps.shape[0]), floor, _lib.DTYPE_CODE[z.dtype], _lib.stream(z.device),
+        "vb_keys_fwd", z.data_ptr(), hist.data_ptr(), taps.data_ptr(), out.data_ptr(),
+        _lib.ptr(stats), b, n, width, heads, int(taps.shape[0]), floor, _lib.DTYPE_CODE[z.dtype],
+        _lib.stream(z.device),
     )  # fmt: skip
     return out
 
 
 def keys_backward(
-    z: Tensor, hist: Tensor, taps: Tensor, grad_k: Tensor, heads: int, floor: float, want_hist: bool
+    z: Tensor,
+    hist: Tensor,
+    taps: Tensor,
+    grad_k: Tensor,
+    heads: int,
+    floor: float,
+    want_hist: bool,
+    stats: Tensor | None = None,
 ) -> tuple[Tensor, Tensor, Tensor | None]:
+    """Input, taps and history gradients; ``stats`` from ``keys_forward`` on the same inputs, or
+    None to recompute them."""
     b, n, width = z.shape
     count = int(taps.shape[0])
     grad_z = torch.empty_like(z)
@@ -67,8 +83,8 @@ def keys_backward(
     ws = _lib.workspace(_lib.query("vb_keys_bwd_workspace", b, n, width, heads, count), z.device)
     _lib.call(
         "vb_keys_bwd", z.data_ptr(), hist.data_ptr(), taps.data_ptr(), grad_k.data_ptr(),
-        grad_z.data_ptr(), grad_taps.data_ptr(), _lib.ptr(grad_hist), ws.data_ptr(), b, n, width,
-        heads, count, floor, _lib.DTYPE_CODE[z.dtype], _lib.stream(z.device),
+        _lib.ptr(stats), grad_z.data_ptr(), grad_taps.data_ptr(), _lib.ptr(grad_hist), ws.data_ptr(),
+        b, n, width, heads, count, floor, _lib.DTYPE_CODE[z.dtype], _lib.stream(z.device),
     )  # fmt: skip
     return grad_z, grad_taps, grad_hist
 
@@ -78,8 +94,10 @@ class _FusedKeys(torch.autograd.Function):
     def forward(ctx, z: Tensor, history: Tensor, taps: Tensor, heads: int) -> Tensor:  # type: ignore[override]
         hist = _aligned(history.to(torch.float32))
         wide = taps.to(torch.float32).contiguous()
-        k = keys_forward(z, hist, wide, heads, KEY_NORM_FLOOR)
-        ctx.save_for_backward(z, hist, wide)
+        b, n, _ = z.shape
+        stats = torch.empty(b, heads, n, 2, dtype=torch.float32, device=z.device)
+        k = keys_forward(z, hist, wide, heads, KEY_NORM_FLOOR, stats)
+        ctx.save_for_backward(z, hist, wide, stats)
         ctx.heads = heads
         ctx.history_dtype = history.dtype
         ctx.taps_dtype = taps.dtype
@@ -87,10 +105,10 @@ class _FusedKeys(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_k: Tensor):  # type: ignore[override]
-        z, hist, wide = ctx.saved_tensors
+        z, hist, wide, stats = ctx.saved_tensors
         want_hist = bool(ctx.needs_input_grad[1])
         grad_z, grad_taps, grad_hist = keys_backward(
-            z, hist, wide, _aligned(grad_k.to(z.dtype)), ctx.heads, KEY_NORM_FLOOR, want_hist
+            z, hist, wide, _aligned(grad_k.to(z.dtype)), ctx.heads, KEY_NORM_FLOOR, want_hist, stats
         )
         gh = grad_hist.to(ctx.history_dtype) if grad_hist is not None else None
         return grad_z, gh, grad_taps.to(ctx.taps_dtype), None
