@@ -80,8 +80,8 @@ VB_API int vb_rms_norm_bwd_noalloc(const void *x, const float *weight, const voi
  * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's
  * dtype. z, keys: [B,T,W] (keys viewed [B,T,heads,W/heads]); hist: [B,K-1,W] float32;
  * taps: [K,W] float32. stats: [B,heads,T,2] float32 (8-byte aligned) or NULL: per token and head
- * the scale and den of the normalisation, den negated where the squared norm reaches 1 (where
- * the clamp passes gradient), for vb_keys_bwd. Replaces vesper/kernels/keys_triton.py:148-156
+ * 1/scale and 1/den of the normalisation, the second negated where the squared norm reaches 1
+ * (where the clamp passes gradient), for vb_keys_bwd. Replaces vesper/kernels/keys_triton.py:148-156
  * (keys_forward) reached from vesper/kernels/keys.py:28-46 (fused_keys) and
  * vesper/column.py:255-289 (RecurrentSublayer.keys). */
 VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void *keys, float *stats,

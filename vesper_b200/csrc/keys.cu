@@ -7,9 +7,9 @@
 // written once. The backward walks its run in reverse with the next K-1 input gradients in
 // registers, recomputing the filter output, and fuses dz, the taps' gradient (per-warp partial
 // sums, reduced in a fixed order) and the history's gradient into the same pass. The forward can
-// save each token's normalisation statistics (scale and den, 8 bytes per token and head); the
-// backward then skips recomputing them (two warp reductions, a square root and the exact
-// quotients per token) and takes the clamp decision from them.
+// save each token's normalisation statistics (the reciprocals of scale and den, 8 bytes per token
+// and head); the backward then skips recomputing them (two warp reductions, a square root and
+// every quotient per token) and takes the clamp decision from them.
 #include "common.cuh"
 
 namespace vb {
@@ -105,8 +105,8 @@ __device__ __forceinline__ void load_g(const T* __restrict__ gk, int b, int t, i
 
 // the filter input's gradient du of one token from its window w[r] = row t - r and its key
 // gradient g (the normalisation's backward: (g / den - s (g . s) / den^3 [sq >= 1]) / scale).
-// STATS: the forward's (scale, den) of the token, den negated when sq >= 1 (the clamp
-// decision, taken from the forward's exact quotients); otherwise they are recomputed here.
+// STATS: the forward's (1 / scale, 1 / den) of the token, the second negated when sq >= 1 (the
+// clamp decision, taken from the forward's exact quotients); otherwise they are recomputed here.
 template <int EPL, int K, bool STATS>
 __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float (&w)[K][EPL], const float (&g)[EPL],
                                          float floor_, float2 stat, float (&du)[EPL]) {
@@ -118,27 +118,26 @@ __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float 
     for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], w[r][e], a);
     u[e] = a;
   }
-  float scale, s[EPL], den, rscale;
+  float s[EPL], rscale, rden;
   bool clamped;
   if constexpr (STATS) {
-    scale = stat.x;
-    den = fabsf(stat.y);
+    rscale = stat.x;
+    rden = fabsf(stat.y);
     clamped = stat.y < 0.f;
-    rscale = 1.0f / scale;
 #pragma unroll
     for (int e = 0; e < EPL; ++e) s[e] = u[e] * rscale;  // within an ulp of u / scale: gradient only
   } else {
-    float sq;
+    float scale, den, sq;
     norm_stats<EPL>(u, floor_, scale, s, den, sq);  // the forward's exact quotients (the clamp)
     clamped = sq >= 1.0f;
     rscale = 1.0f / scale;
+    rden = 1.0f / den;
   }
   float dot = 0.f;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) dot += g[e] * s[e];
   dot = warp_sum(dot);
-  // the gradient's own quotients are products with one reciprocal of den and one of scale
-  const float rden = 1.0f / den;
+  // the gradient's own quotients are products with the reciprocals of den and scale
   const float q = dot * (rden * rden * rden);
 #pragma unroll
   for (int e = 0; e < EPL; ++e) {
@@ -184,17 +183,18 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
     }
     float scale, s[EPL], den, sq;
     norm_stats<EPL>(u, floor_, scale, s, den, sq);
+    const float rden = 1.0f / den;  // k = s / den to within an ulp or two of the quotient
     if (live) {
-      const float rden = 1.0f / den;  // k = s / den to within an ulp or two of the quotient
       float o[EPL];
 #pragma unroll
       for (int e = 0; e < EPL; ++e) o[e] = s[e] * rden;
       st_elems<T, EPL>(out + ((int64_t)b * T_ + t) * W + c, o);
     }
-    // (scale, den), den negated where the clamp passes gradient: token t's pair waits in lane
-    // (t - t0) % 32, and each 32 tokens leave as one contiguous warp store ([B, heads, T, 2])
+    // (1 / scale, 1 / den), the second negated where the clamp passes gradient: token t's pair
+    // waits in lane (t - t0) % 32, and each 32 tokens leave as one contiguous warp store
+    // ([B, heads, T, 2])
     const int slot = (t - t0) & 31;
-    if (lane == slot) st_pair = make_float2(scale, sq >= 1.0f ? -den : den);
+    if (lane == slot) st_pair = make_float2(1.0f / scale, sq >= 1.0f ? -rden : rden);
     if (stats != nullptr && (slot == 31 || t + 1 == t1) && lane <= slot)
       stats[((int64_t)b * heads + head) * T_ + (t - slot + lane)] = st_pair;
 #pragma unroll
