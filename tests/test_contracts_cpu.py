@@ -9,6 +9,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+from vesper_b200 import _lib
 from vesper_b200.contracts import ContractError, check_shape
 from vesper_b200.kernels.delta_scan import delta_scan_fused_fp32
 from vesper_b200.kernels.keys import fused_keys
@@ -43,3 +44,17 @@ def test_shape_and_dtype_errors_come_before_the_device_check() -> None:
         delta_scan_fused_fp32(q.bfloat16(), q, q, torch.zeros(1, 8, 2), torch.zeros(1, 2, 16, 16))
     with pytest.raises(ContractError, match="axis"):
         delta_scan_fused_fp32(q, q[:, :4], q, torch.zeros(1, 8, 2), torch.zeros(1, 2, 16, 16))
+
+
+def test_the_key_filter_refuses_statistics_off_an_8_byte_boundary() -> None:
+    """Both key-filter entry points check the statistics buffer on the host before any launch
+    (the addresses below are never dereferenced)."""
+    bf16 = _lib.DTYPE_CODE[torch.bfloat16]
+    aligned, odd = 1 << 20, (1 << 20) + 4
+    with pytest.raises(_lib.KernelError, match="8-byte boundary"):
+        _lib.call("vb_keys_fwd", aligned, aligned, aligned, aligned, odd, 1, 64, 128, 2, 4, 1e-6, bf16, None)
+    with pytest.raises(_lib.KernelError, match="8-byte boundary"):
+        _lib.call(
+            "vb_keys_bwd", aligned, aligned, aligned, aligned, odd, aligned, aligned, None, aligned,
+            1, 64, 128, 2, 4, 1e-6, bf16, None,
+        )  # fmt: skip
