@@ -57,63 +57,117 @@ def scan_algorithmic_bytes(b: int, t: int, h: int, d: int) -> int:
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+    """SM clocks and throttle reasons sampled DURING the timed region.
 
-    FIELDS = (
+    NVML is read from a thread every ``period`` seconds (a sample is an instantaneous reading,
+    so a timed region of a few milliseconds still gets several); the thread has taken its first
+    sample before ``__enter__`` returns. Without NVML it falls back to ``nvidia-smi -lms 100``.
+    Reasons recorded: hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap.
+    """
+
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40}  # fmt: skip
+    SMI_FIELDS = (
         "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
     )
 
-    def __init__(self, gpu: str) -> None:
-        self.gpu = gpu
+    def __init__(self, gpu: str, period: float = 0.002) -> None:
+        self.gpu, self.period = gpu, period
+        self.samples: list[tuple[float, float, set[str]]] = []
         self.proc: subprocess.Popen | None = None
+        self.thread = None
+        self.source = "none"
+
+    def _nvml_handle(self):
+        import pynvml  # nvidia-ml-py
+
+        pynvml.nvmlInit()
+        if self.gpu.startswith("GPU-"):
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(self.gpu)
+        return pynvml, pynvml.nvmlDeviceGetHandleByIndex(int(self.gpu))
 
     def __enter__(self) -> Clocks:
+        import threading
+
+        try:
+            nv, handle = self._nvml_handle()
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - no NVML: the nvidia-smi fallback
+            return self._smi_enter()
+        self.source = "nvml"
+        self.stop = threading.Event()
+        first = threading.Event()
+
+        def poll() -> None:
+            while True:
+                try:
+                    mhz = float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM))
+                    bits = int(get_reasons(handle))
+                    self.samples.append((mhz, max_mhz, {n for n, b in self.REASON_BITS.items() if bits & b}))
+                except Exception:  # noqa: BLE001
+                    pass
+                first.set()
+                if self.stop.wait(self.period):
+                    return
+
+        self.thread = threading.Thread(target=poll, daemon=True)
+        self.thread.start()
+        first.wait(5.0)
+        self.samples.clear()  # the region opens now
+        return self
+
+    def _smi_enter(self) -> Clocks:
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--query-gpu={self.SMI_FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
             )  # fmt: skip
+            self.source = "nvidia-smi"
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc: object) -> None:
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
-        else:
-            self.lines = []
-
-    def summary(self) -> dict:
-        sms, maxes, reasons = [], [], set()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            return
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ln in out.splitlines():
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
+                mhz, mx = float(parts[1]), float(parts[2])
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9], strict=True):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sms:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            self.samples.append((mhz, mx, {n for n, f in zip(names, parts[5:9], strict=True) if f.lower() == "active"}))
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": self.source}
+        reasons: set[str] = set()
+        for _, _, r in self.samples:
+            reasons |= r
         return {
-            "sm_mhz": statistics.median(sms),
-            "sm_max_mhz": max(maxes),
+            "sm_mhz": statistics.median(s[0] for s in self.samples),
+            "sm_max_mhz": max(s[1] for s in self.samples),
             "reasons": sorted(reasons),
-            "samples": len(sms),
+            "samples": len(self.samples),
+            "source": self.source,
         }
 
 
@@ -340,10 +394,18 @@ def run_ours(args) -> None:
     del inp, sets, leaves, host, outs_host, results, o, grads, saved
     torch.cuda.empty_cache()
     train = None if args.no_train else train_leg(args, device, world, rank, local)
+    torch.cuda.empty_cache()
+    config3 = None if args.no_config3 else config3_leg(device, world, args.steps)
+    torch.cuda.empty_cache()
+    config1 = config1_leg(device, args.steps) if rank == 0 else None
 
     # --- CPU baseline: the oracle (float64 C port of the reference path) on rank 0 at N=1 ------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle
+
+        oracle.set_threads(oracle.usable_cores())
         cpu = cpu_sample()
 
     if rank == 0:
@@ -358,6 +420,7 @@ def run_ours(args) -> None:
                 "sharding": "each rank its own (batch x head) units, no collective", "graph": "CUDA graph replay",
             },
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "train_step": train,
+            "config1": config1, "config3": config3,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks.summary(),
@@ -366,6 +429,220 @@ def run_ours(args) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+C1 = (2, 512, 4, 64)  # config 1: B, T, H, d (fp32 scan)
+
+
+def scan_f32_algorithmic_bytes(b: int, t: int, h: int, d: int) -> int:
+    """HBM bytes of the fp32 scan fwd+bwd: (44d+12) per token-head (float32 I/O) + 5 state passes."""
+    return b * t * h * (44 * d + 12) + b * h * 5 * 4 * d * d
+
+
+def config1_leg(device, steps: int) -> dict:
+    """Config 1: ``delta_scan_fused_fp32`` forward+backward at B=2, T=512, H=4, d=64 in float32.
+
+    q, k ~ N(0,1) then L2-normalised per head, v ~ N(0,1), beta = sigmoid(N(0,1)), S0 = 0, the
+    loss sum(o * g) with g ~ N(0,1), seed 0. Reports microseconds per forward+backward through the
+    public entry point (autograd included) and of the two kernels alone (CUDA events on their
+    stream), and the kernels' fraction of the HBM roofline (far from it by nature: 8 sequences,
+    each walked token by token).
+    """
+    import torch
+    import torch.nn.functional as F  # noqa: N812
+
+    from vesper_b200.kernels.delta_scan import check_status, delta_scan_fused_fp32, scan_f32_backward, scan_f32_forward
+
+    b, t, h, d = C1
+    g = torch.Generator(device=device).manual_seed(0)
+    q = F.normalize(torch.randn(b, t, h, d, device=device, generator=g), dim=-1)
+    k = F.normalize(torch.randn(b, t, h, d, device=device, generator=g), dim=-1)
+    v = torch.randn(b, t, h, d, device=device, generator=g)
+    beta = torch.sigmoid(torch.randn(b, t, h, device=device, generator=g))
+    s0 = torch.zeros(b, h, d, d, device=device)
+    gout = torch.randn(b, t, h, d, device=device, generator=g)
+    leaves = [x.detach().requires_grad_() for x in (q, k, v, beta, s0)]
+
+    def api() -> None:
+        o, _ = delta_scan_fused_fp32(*leaves)
+        torch.autograd.grad([o], leaves, [gout])
+
+    def kernels() -> None:
+        _, _, resid = scan_f32_forward(q, k, v, beta, s0, True)
+        scan_f32_backward(q, k, v, beta, s0, resid, gout, None)
+
+    reps = max(20, min(steps, 200))
+    out = {}
+    for name, fn in (("api", api), ("kernels", kernels)):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        out[name] = e0.elapsed_time(e1) / reps * 1e3  # us
+    check_status(device)
+    algo = scan_f32_algorithmic_bytes(b, t, h, d)
+    peak = peaks().get("hbm_gbs") or 6650.0
+    achieved = algo / (out["kernels"] / 1e6) / 1e9
+    return {
+        "metric": "delta-scan fwd+bwd, fp32 (config 1)", "value": round(b * t / (out["api"] / 1e6), 1),
+        "unit": "tokens/s", "us_per_fwd_bwd": round(out["api"], 2), "kernel_us_per_fwd_bwd": round(out["kernels"], 2),
+        "steps": reps, "dtype": "f32",
+        "config": {"workload": "config 1: delta_scan_fused_fp32 fwd+bwd", "B": b, "T": t, "H": h, "d": d},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 5), "traffic": None, "algorithmic_bytes": algo,
+                     "kernel": "scan_f32_fwd_kernel + scan_f32_bwd_kernel",
+                     "note": "8 sequences walked token by token: latency-bound, not a bandwidth figure"},
+    }  # fmt: skip
+
+
+C3 = {"B": 16, "T": 2048, "d": 512, "heads": 8, "head_dim": 64, "kv_groups": 4, "window": 512, "ffn_mult": 3}
+
+
+def _kernel_group(name: str) -> str:
+    n = name.lower()
+    for key, group in (("scan_", "delta-scan"), ("attn_", "attention"), ("keys_", "key filter"),
+                       ("rms_", "rmsnorm"), ("column_sum", "rmsnorm"), ("select_rows", "copy-forward/compaction"),
+                       ("gather_rows", "copy-forward/compaction"), ("expand_rows", "copy-forward/compaction"),
+                       ("compact_", "copy-forward/compaction"), ("relu", "relu^2"), ("rotary", "rotary"),
+                       ("gemm", "gemm (cuBLAS)"), ("cutlass", "gemm (cuBLAS)"), ("nvjet", "gemm (cuBLAS)"),
+                       ("xmma", "gemm (cuBLAS)"), ("cublas", "gemm (cuBLAS)")):  # fmt: skip
+        if key in n:
+            return group
+    return "torch elementwise/other"
+
+
+def column_bounds(b: int, t: int) -> dict[str, tuple[str, float]]:
+    """Per kernel group of one column fwd+bwd at config 3: (bound, algorithmic bytes or flops)."""
+    d, h, dk, w, hidden = C3["d"], C3["heads"], C3["head_dim"], C3["window"], C3["ffn_mult"] * C3["d"]
+    hkv = h // C3["kv_groups"]
+    tokens = b * t
+    linear = 4 * d * d + h * d + d * d + 2 * d * hkv * dk + d * d + 2 * d * hidden  # every weight matrix
+    w_eff = sum(min(i + 1, w) for i in range(t))
+    attn_fwd = b * h * 4 * dk * w_eff
+    return {
+        "gemm (cuBLAS)": ("tensor", 6.0 * tokens * linear),
+        "attention": ("tensor", 3.5 * attn_fwd),
+        "delta-scan": ("hbm", float(scan_algorithmic_bytes(b, t, h, dk))),
+        "key filter": ("hbm", float(tokens * (10 * d + 16 * h))),
+        # the residual stream is float32: forward reads 4d and writes the bf16 output 2d, backward
+        # reads x 4d and dy 2d and writes dx 4d, plus the row statistic both ways; three norms
+        "rmsnorm": ("hbm", float(3 * tokens * (16 * d + 8))),
+    }
+
+
+def config3_leg(device, world: int, steps: int) -> dict:
+    """Config 3: one column forward+backward in bf16 at d_model 512 (8 x 64 heads, kv_groups 4,
+    window 512, relu^2 FFN of 1536), B=16, T=2048 per GPU, weights ~ N(0, 0.02), inputs ~ N(0,1).
+
+    The step (``Column.step`` under bf16 autocast, the loss sum(y * g), gradients of x and every
+    parameter) is captured as one CUDA graph and replayed; each rank runs its own 16 rows (batch
+    sharding, weak scaling, no collective). Per kernel group: device time from one profiled eager
+    step and its algorithmic bound (bytes at the HBM peak or flops at the bf16 tensor peak); the
+    column total against the sum of those bounds.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from vesper_b200 import _lib
+    from vesper_b200.column import Column, ColumnShape, init_column_state, set_scan
+
+    b, t, d = C3["B"], C3["T"], C3["d"]
+    shape = ColumnShape(d=d, heads=C3["heads"], kv_groups=C3["kv_groups"], head_dim=C3["head_dim"],
+                        window=C3["window"], rotary_base=10000.0, ffn_mult=C3["ffn_mult"], block=64, key_conv=4)  # fmt: skip
+    gen = torch.Generator().manual_seed(3)
+    col = Column(shape, gen)
+    with torch.no_grad():
+        for name, p in col.named_parameters():
+            if p.dim() == 2 and "conv_k" not in name:
+                p.copy_(0.02 * torch.randn(p.shape, generator=gen))
+    col = col.to(device)
+    set_scan(col, "fused")
+    g = torch.Generator(device=device).manual_seed(5 + int(os.environ.get("RANK", "0")))
+    x = torch.randn(b, t, d, device=device, generator=g).requires_grad_()
+    up = torch.randn(b, t, d, device=device, generator=g)
+    pos = torch.arange(t, device=device).expand(b, t).contiguous()
+    params = list(col.parameters())
+
+    def step():
+        state = init_column_state(shape, b, 1, torch.bfloat16, device)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y, _, _ = col.step(x, pos, state, 0)
+        return torch.autograd.grad([(y.float() * up).sum()], [x, *params])
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream(device).wait_stream(side)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    reps = max(3, min(steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        tt = torch.tensor([ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    _lib.check_status(device)
+    del graph
+    # per kernel group: one eager step under the profiler (device times of every kernel)
+    groups: dict[str, float] = {}
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize(device)
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time_total > 0:
+                grp = _kernel_group(ev.name)
+                groups[grp] = groups.get(grp, 0.0) + ev.device_time_total / 1e3  # ms
+    except Exception as exc:  # noqa: BLE001 - the breakdown is optional
+        groups = {"error": str(exc)[:200]}
+    pk = peaks()
+    hbm = pk.get("hbm_gbs") or 6650.0
+    tensor = pk.get("bf16_tflops") or 1590.0
+    rows = {}
+    bound_sum = 0.0
+    for grp, (kind, amount) in column_bounds(b, t).items():
+        bound_ms = amount / (hbm * 1e9 if kind == "hbm" else tensor * 1e12) * 1e3
+        bound_sum += bound_ms
+        meas = groups.get(grp)
+        rows[grp] = {"bound": kind, "ms": None if meas is None else round(meas, 4), "bound_ms": round(bound_ms, 4),
+                     "frac": None if not meas else round(bound_ms / meas, 4)}  # fmt: skip
+    for grp, meas in groups.items():
+        if grp not in rows and isinstance(meas, float):
+            rows[grp] = {"bound": None, "ms": round(meas, 4), "bound_ms": None, "frac": None}
+    return {
+        "metric": "one column fwd+bwd tokens/s (config 3)", "value": round(world * b * t / (ms / 1e3), 1),
+        "unit": "tokens/s", "n_gpus": world, "ms_per_step": round(ms, 4), "steps": reps, "scaling": "weak",
+        "dtype": "bf16 autocast", "data": "synthetic (N(0,1) inputs, N(0,0.02) weights)",
+        "config": {"workload": "config 3: Column.step fwd+bwd, captured graph", **C3, "parallelism": f"batch x{world}",
+                   "ffn": "relu^2 (the reference has no SwiGLU)"},
+        "kernels": rows, "bound_sum_ms": round(bound_sum, 4),
+        "roofline": {"bound": "mixed", "achieved_ms": round(ms, 4), "bound_ms": round(bound_sum, 4),
+                     "frac": round(bound_sum / ms, 4), "peak_hbm_gbs": hbm, "peak_bf16_tflops": tensor,
+                     "note": "column time against the sum of its kernel groups' roofline times"},
+    }  # fmt: skip
 
 
 TRAIN_B, TRAIN_T = 32, 2048  # config 4: rows of 2048 tokens per GPU
@@ -480,6 +757,10 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+
+    oracle.set_threads(oracle.usable_cores())  # torchrun exports OMP_NUM_THREADS=1
     samples = []
     for _ in range(max(1, args.warmup_ref)):
         cpu_sample(1)
@@ -512,6 +793,7 @@ def main() -> None:
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--no-train", action="store_true", help="skip the config-4 training-step leg")
+    p.add_argument("--no-config3", action="store_true", help="skip the config-3 one-column leg")
     p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")

@@ -47,6 +47,8 @@ def lib() -> ctypes.CDLL:
         _lib.vo_window_attn_fwd.argtypes = [i, i, i, i, i, i, i, p, p, p, p, p]
         _lib.vo_window_attn_bwd.argtypes = [i, i, i, i, i, i, i, p, p, p, p, p, p, p]
         _lib.vo_num_threads.restype = ctypes.c_int
+        _lib.vo_set_threads.argtypes = [i]
+        _lib.vo_set_threads.restype = ctypes.c_int
     return _lib
 
 
@@ -61,6 +63,19 @@ def _ptr(a: np.ndarray | None):
 def threads() -> int:
     """OpenMP threads the oracle uses (``OMP_NUM_THREADS`` or all cores)."""
     return int(lib().vo_num_threads())
+
+
+def set_threads(n: int) -> int:
+    """Use ``n`` OpenMP threads from now on (overriding ``OMP_NUM_THREADS``); returns the count."""
+    return int(lib().vo_set_threads(int(n)))
+
+
+def usable_cores() -> int:
+    """The CPUs this process may run on (its affinity mask), whatever ``OMP_NUM_THREADS`` says."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
 KEY_NORM_FLOOR = 1e-6  # recurrence.py:27

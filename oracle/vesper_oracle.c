@@ -427,3 +427,16 @@ int vo_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Sets the OpenMP thread count of every later call (n < 1 leaves it unchanged); returns the
+ * count in effect. A launcher such as torchrun exports OMP_NUM_THREADS=1, which a timed CPU
+ * baseline must override with the cores the process may actually use. */
+int vo_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}

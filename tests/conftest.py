@@ -43,8 +43,36 @@ def rel(a: np.ndarray, b: np.ndarray) -> float:
 
 
 def max_rel(a: np.ndarray, b: np.ndarray) -> float:
-    """Largest elementwise error relative to the reference's largest magnitude."""
+    """Largest elementwise error relative to the reference's largest magnitude (normwise)."""
     a64, b64 = np.asarray(a, np.float64), np.asarray(b, np.float64)
     scale = np.abs(b64).max() if b64.size else 0.0
     err = np.abs(a64 - b64).max() if b64.size else 0.0
     return float(err / scale) if scale > 0 else float(err)
+
+
+# The per-element reading of the north star's "2e-2 max relative": every element's error is
+# measured against its own reference magnitude, floored at ELEM_FLOOR times the tensor's RMS, so
+# an element near zero (whose absolute error is set by the magnitudes it was summed from, not by
+# its own) is held to the tensor's typical scale instead of an unbounded ratio.
+ELEM_FLOOR = 1.0
+
+
+def elem_rel(a: np.ndarray, b: np.ndarray, floor: float = ELEM_FLOOR) -> float:
+    """Largest per-element relative error ``|a - b| / max(|b|, floor * rms(b))``."""
+    a64, b64 = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    if b64.size == 0:
+        return 0.0
+    rms = float(np.sqrt(np.mean(np.square(b64))))
+    den = np.maximum(np.abs(b64), floor * rms)
+    err = np.abs(a64 - b64)
+    if rms == 0.0:
+        return float(err.max())
+    return float((err / den).max())
+
+
+def error_report(a: np.ndarray, b: np.ndarray) -> str:
+    """The three readings of one comparison as a line (relative L2, normwise max, per element)."""
+    return (
+        f"rel {rel(a, b):.2e} normwise {max_rel(a, b):.2e} "
+        f"elem(floor rms) {elem_rel(a, b):.2e} elem(floor 0.5 rms) {elem_rel(a, b, 0.5):.2e}"
+    )

@@ -22,7 +22,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("VESPER_REF", "/root/reference"))
+if "VESPER_REF" not in os.environ:
+    sys.exit("set VESPER_REF to a checkout of the reference (mstampfli/vesper-preview)")
+REF = Path(os.environ["VESPER_REF"])
 sys.dont_write_bytecode = True
 sys.path.insert(0, str(REF))
 

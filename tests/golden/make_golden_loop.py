@@ -23,11 +23,14 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("VESPER_REF", "/root/reference"))
+if "VESPER_REF" not in os.environ:
+    sys.exit("set VESPER_REF to a checkout of the reference (mstampfli/vesper-preview)")
+REF = Path(os.environ["VESPER_REF"])
 sys.dont_write_bytecode = True
 sys.path.insert(0, str(REF))
 
 from vesper.attention import KVCache  # noqa: E402
+from vesper.embedding import TiedEmbedding  # noqa: E402
 from vesper.column import Carry, Column, ColumnShape, ColumnState, Projections  # noqa: E402
 from vesper.loop import CdfRule, HaltingHead, Loop  # noqa: E402
 from vesper.recurrence import normalize_keys  # noqa: E402
@@ -176,7 +179,57 @@ def loop_fixtures() -> None:
         )  # fmt: skip
 
 
+# config 4's looped model: d=512, 8 heads x 64, kv_groups 4, window 512,
+# relu^2 FFN of 3 x d, block 64, key filter of 4 taps, 13 columns, 8 passes, ACT with epsilon 0.01
+# and the random-init halting head, vocabulary 32000; reduced to B x T = 2 x 96 tokens so the float64
+# reference runs on a CPU in about a minute
+C4_SHAPE = ColumnShape(d=512, heads=8, kv_groups=4, head_dim=64, window=512, rotary_base=10000.0, ffn_mult=3,
+                       block=64, key_conv=4)  # fmt: skip
+C4_COLUMNS, C4_TMAX, C4_VOCAB, C4_B, C4_N, C4_SEED = 13, 8, 32000, 2, 128, 0
+
+
+def config4_fixture() -> None:
+    """The config-4 model's pass counts: embedding, 13 columns and the halting head drawn in the
+    model's order from seed 0 (``vesper/model.py:49-56``), token ids uniform over the vocabulary."""
+    g = torch.Generator().manual_seed(C4_SEED)
+    emb = TiedEmbedding(C4_VOCAB, C4_SHAPE.d, g)
+    cols = [Column(C4_SHAPE, g) for _ in range(C4_COLUMNS)]
+    loop = Loop(cols, HaltingHead(C4_SHAPE.d, g), C4_SHAPE.d, C4_TMAX, 0.01)
+    sums = {**{f"sum.embedding.{k}": v for k, v in ((k[4:], v) for k, v in _param_sums(emb).items())},
+            **_param_sums(loop)}  # fmt: skip
+    emb, loop = emb.to(F64), loop.to(F64)
+    tokens = torch.randint(0, C4_VOCAB, (C4_B, C4_N), generator=torch.Generator().manual_seed(C4_SEED + 1))
+    pos = torch.arange(C4_N).expand(C4_B, C4_N).contiguous()
+    d, hkv, dk = C4_SHAPE.d, C4_SHAPE.kv_heads, C4_SHAPE.head_dim
+    states = [ColumnState(
+        h=tuple(torch.zeros(C4_B, C4_SHAPE.heads, dk, dk, dtype=F64) for _ in range(C4_TMAX)),
+        kv=tuple(KVCache(torch.zeros(C4_B, 0, hkv, dk, dtype=F64), torch.zeros(C4_B, 0, hkv, dk, dtype=F64),
+                         torch.zeros(C4_B, 0, dtype=torch.long), C4_SHAPE.window) for _ in range(C4_TMAX)),
+        key_history=tuple(torch.zeros(C4_B, C4_SHAPE.key_history, d, dtype=F64) for _ in range(C4_TMAX)),
+    ) for _ in range(C4_COLUMNS)]  # fmt: skip
+    with torch.no_grad():
+        res = loop.forward(emb.embed(tokens), pos, states)
+        head, eps = loop.halting_head(), loop.halt_epsilon
+        cum = torch.zeros(C4_B, C4_N, dtype=F64)
+        margins = []
+        for t in range(C4_TMAX - 1):
+            p = head.probability(res.per_pass[t], t)
+            margins.append(cum + p - (1.0 - eps))
+            cum = cum + p
+        mg = torch.stack(margins)
+        live = mg[torch.stack([res.n_iters > t for t in range(C4_TMAX - 1)])]
+        print("config4 n_iters histogram", torch.bincount(res.n_iters.flatten(), minlength=C4_TMAX + 1).tolist(),
+              "min |margin|", float(live.abs().min()))  # fmt: skip
+    _save("loop_config4", tokens=tokens, pos=pos, n_iters=res.n_iters, margins=mg, y=res.y.float(), ponder=res.ponder,
+          **sums)  # fmt: skip
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    column_fixture()
-    loop_fixtures()
+    which = set(sys.argv[1:]) or {"column", "loop", "config4"}
+    if "column" in which:
+        column_fixture()
+    if "loop" in which:
+        loop_fixtures()
+    if "config4" in which:
+        config4_fixture()

@@ -3,7 +3,8 @@
 The truth is the reference in float64 fed the same bfloat16-valued inputs. The kernel's licence is
 its bfloat16 intermediates: the reference's bound is 1.5e-2 relative L2 on outputs, the final state
 and all five gradients (vesper tests/test_delta_scan_fused.py:34), and the north star's is 2e-2
-max-relative (largest error over the largest reference magnitude); both are checked.
+max-relative (largest error over the largest reference magnitude); both are checked, and the
+per-element reading (each error against max(|want|, rms(want))) within 1e-1.
 """
 
 from __future__ import annotations
@@ -13,7 +14,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import golden, golden_names, max_rel, rel
+from conftest import elem_rel, error_report, golden, golden_names, max_rel, rel
 from vesper_b200.contracts import ContractError
 from vesper_b200.kernels.delta_scan import check_status, delta_scan_fused
 
@@ -22,6 +23,7 @@ CUDA = torch.device("cuda")
 BF16 = torch.bfloat16
 TOL = 1.5e-2
 TOL_MAX = 2e-2
+ELEM_TOL = 1e-1  # per element against max(|want|, rms(want)): the far tail of the bf16 rounding
 
 
 def _inputs(b, n, h, d, seed=0, state_scale=0.5):
@@ -46,8 +48,10 @@ def _fwd_bwd(q, k, v, beta, s0, d_o, d_s):
 
 
 def _assert_close(got, want, name):
+    print(f"{name}: {error_report(got, want)}")
     assert rel(got, want) < TOL, (name, rel(got, want))
     assert max_rel(got, want) < TOL_MAX, (name, max_rel(got, want))
+    assert elem_rel(got, want) < ELEM_TOL, (name, elem_rel(got, want))
 
 
 @pytest.mark.parametrize("name", golden_names("scan_"))

@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import oracle
-from conftest import golden, golden_names, max_rel, rel
+from conftest import elem_rel, error_report, golden, golden_names, max_rel, rel
 from vesper_b200 import _lib
 from vesper_b200.contracts import ContractError
 from vesper_b200.kernels.window_attn import window_attention, window_attention_active
@@ -76,8 +76,10 @@ def _oracle(q, keys, values, window, d_o):
 
 def _assert_matches(got, want, names=("o", "dq", "dkeys", "dvalues")):
     for a, b, what in zip(got, want, names, strict=True):
+        print(f"{what}: {error_report(a, b)}")
         assert rel(a, b) < 1e-2, (what, rel(a, b))
         assert max_rel(a, b) < 2e-2, (what, max_rel(a, b))
+        assert elem_rel(a, b) < 1e-1, (what, elem_rel(a, b))
 
 
 @pytest.mark.parametrize(

@@ -65,8 +65,25 @@ def test_two_calls_in_a_row_match_the_workspace_entry_point(dtype: torch.dtype) 
         torch.testing.assert_close(got_dg, want_dg, rtol=TOL, atol=TOL)
 
 
-def test_a_call_beyond_the_fixed_scratch_is_refused() -> None:
-    rows, width = 65 * 1024 + 64, 1024  # one partial row more than the array holds
+def test_a_call_one_row_beyond_the_fixed_scratch_is_refused() -> None:
+    # at width 1024 the array holds the partial sums of 65536 rows (1024 blocks of 64 rows); one
+    # row more needs a 1025th block of partial sums: refused before any pointer is touched
+    rows, width = 65536 + 1, 1024
     with pytest.raises(_lib.KernelError, match="fixed scratch"):
         _lib.call("vb_rms_norm_bwd_noalloc", None, None, None, None, None, None, rows, width,
                   _lib.DTYPE_CODE[torch.float32], _lib.stream(CUDA))
+
+
+def test_a_call_that_fills_the_fixed_scratch_exactly_is_accepted_and_matches() -> None:
+    # 65536 rows at width 1024: every one of the array's 2^20 partial sums is written and read
+    g = torch.Generator(device=CUDA).manual_seed(4)
+    rows, width = 65536, 1024
+    x = torch.randn(rows, width, device=CUDA, generator=g).to(torch.bfloat16)
+    w = 1 + 0.1 * torch.randn(width, device=CUDA, generator=g)
+    dy = torch.randn(rows, width, device=CUDA, generator=g).to(torch.bfloat16)
+    inv = _forward(x, w)
+    want_dx, want_dg = _with_workspace(x, w, dy, inv)
+    got_dx, got_dg = _without_allocation(x, w, dy, inv)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got_dx.float(), want_dx.float(), rtol=TOL, atol=TOL)
+    torch.testing.assert_close(got_dg, want_dg, rtol=TOL, atol=TOL)

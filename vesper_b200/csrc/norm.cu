@@ -397,7 +397,6 @@ extern "C" int vb_rms_norm_bwd(const void* x, const float* weight, const void* d
     return VB_OK;
   }
   VB_REQUIRE(x && weight && dy && inv && dx && dweight && workspace, "rms_norm_bwd: null pointer");
-  const int ctas = bwd_ctas(rows);
   return launch_bwd(x, weight, dy, inv, dx, dweight, (float*)workspace, rows, width, dtype, st);
 }
 
