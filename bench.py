@@ -2,8 +2,9 @@
 
 One step = the fused key pipeline + RMSNorm + bf16 delta scan, forward and backward, on
 B=8, H=8, T=4096, d=128 (width 1024): ``x -> fused_rms_norm -> fused_keys -> delta_scan_fused``
-with q, v, beta and the upstream gradient as further inputs, then the backward through all three
-(gradients of x, the gain, the taps, q, v and beta). Synthetic inputs with the config's
+with q, v, the write-strength logits (beta = sigmoid(logits) formed inside the scan's kernels)
+and the upstream gradient as further inputs, then the backward through all three (gradients of
+x, the gain, the taps, q, v and the logits). Synthetic inputs with the config's
 distributions. Inputs are far larger than L2 (about 1 GB per step), so no flush is needed.
 
 A second leg times config 4, the looped d512 model's training step (13 columns x 8 passes with ACT
@@ -189,7 +190,8 @@ def make_inputs(device, seed: int):
     x = torch.randn(B, T, WIDTH, device=device, generator=g).bfloat16()
     q = torch.nn.functional.normalize(torch.randn(B, T, H, D, device=device, generator=g), dim=-1).bfloat16()
     v = torch.randn(B, T, H, D, device=device, generator=g).bfloat16()
-    beta = torch.sigmoid(torch.randn(B, T, H, device=device, generator=g)).bfloat16()
+    # the write-strength logits (beta = sigmoid of them, formed inside the scan's kernels)
+    beta = torch.randn(B, T, H, device=device, generator=g).bfloat16()
     d_o = torch.randn(B, T, H, D, device=device, generator=g).bfloat16()
     taps = 0.5 * torch.randn(TAPS, WIDTH, device=device, generator=g)
     gain = torch.ones(WIDTH, device=device)
@@ -209,7 +211,7 @@ def step(inp, leaves):
     x, q, v, beta, gain, taps = leaves
     xn = fused_rms_norm(x, gain, 1e-3, 1e-6)
     k = fused_keys(xn, inp["hist"], taps, H)
-    o, _ = delta_scan_fused(q, k, v, beta, inp["s0"])
+    o, _ = delta_scan_fused(q, k, v, beta, inp["s0"], from_logits=True)
     grads = torch.autograd.grad([o], [x, q, v, beta, gain, taps], [inp["d_o"]])
     return o, grads
 
@@ -284,17 +286,17 @@ def run_ours(args) -> None:
     # --- roofline of the dominant kernel group: delta-scan fwd+bwd, CUDA events on its stream ---
     q, k, v, beta, s0 = inp["q"], inp["x"].view(B, T, H, D), inp["v"], inp["beta"], inp["s0"]
     k = torch.nn.functional.normalize(k.float(), dim=-1).bfloat16()
-    _, _, saved = scan_bf16_forward(q, k, v, beta, s0)
+    _, _, saved = scan_bf16_forward(q, k, v, beta, s0, True)
     reps = max(5, min(args.steps, 50))
     for _ in range(3):
-        scan_bf16_forward(q, k, v, beta, s0)
-        scan_bf16_backward(q, k, v, beta, saved, inp["d_o"], None)
+        scan_bf16_forward(q, k, v, beta, s0, True)
+        scan_bf16_backward(q, k, v, beta, saved, inp["d_o"], None, True)
     torch.cuda.synchronize(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        _, _, saved = scan_bf16_forward(q, k, v, beta, s0)
-        scan_bf16_backward(q, k, v, beta, saved, inp["d_o"], None)
+        _, _, saved = scan_bf16_forward(q, k, v, beta, s0, True)
+        scan_bf16_backward(q, k, v, beta, saved, inp["d_o"], None, True)
     e1.record()
     torch.cuda.synchronize(device)
     scan_ms = e0.elapsed_time(e1) / reps
@@ -722,7 +724,7 @@ def cpu_sample(rows: int = 1) -> dict:
     q = rng.standard_normal((rows, T, H, D))
     q /= np.linalg.norm(q, axis=-1, keepdims=True)
     v = rng.standard_normal((rows, T, H, D))
-    beta = 1 / (1 + np.exp(-rng.standard_normal((rows, T, H))))
+    beta = 1 / (1 + np.exp(-rng.standard_normal((rows, T, H))))  # write_strength of N(0,1) logits
     d_o = rng.standard_normal((rows, T, H, D))
     s0 = np.zeros((rows, H, D, D))
     t0 = time.perf_counter()

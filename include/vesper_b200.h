@@ -118,6 +118,24 @@ VB_API int vb_delta_scan_f32_bwd(const float *q, const float *k, const float *v,
                           float *dstate0, void *workspace, int B, int T, int H, int D,
                           void *stream);
 
+/* The same scan taking the write-strength LOGITS: beta = sigmoid(beta_logits + shift) is formed
+ * inside the kernels (shift: [B,T] float32, one value per token shared by the heads, or NULL = 0;
+ * -inf gives an exact zero write), and the backward returns the logits' gradient
+ * dlogits = (dbeta * (1 - beta)) * beta in `dlogits`. Replaces vesper/recurrence.py:34-88
+ * (write_strength: sigmoid(logits), with the modulator's odds shift ln(1 + alpha m)) fused with
+ * the scan, as called from vesper/column.py:236-253 (RecurrentSublayer.project). */
+VB_API int vb_delta_scan_f32_fwd_logits(const float *q, const float *k, const float *v,
+                                        const float *beta_logits, const float *shift,
+                                        const float *state0, float *o, float *state_n, float *resid,
+                                        int B, int T, int H, int D, void *stream);
+
+VB_API int vb_delta_scan_f32_bwd_logits(const float *q, const float *k, const float *v,
+                                        const float *beta_logits, const float *shift,
+                                        const float *state0, const float *resid, const float *dout,
+                                        const float *dstate_n, float *dq, float *dk, float *dv,
+                                        float *dlogits, float *dstate0, void *workspace, int B,
+                                        int T, int H, int D, void *stream);
+
 /* ---- delta-rule scan, bfloat16 (chunked WY form on tcgen05) -----------------------------------
  * The same recurrence as above with bf16 q, k, v, beta, o [B,T,H,D] / [B,T,H] and float32
  * state0, state_n [B,H,D,D]; 64-token chunks, D <= 128 and a multiple of 8, 16-byte aligned
@@ -142,6 +160,23 @@ VB_API int vb_delta_scan_bf16_bwd(const void *q, const void *k, const void *v, c
                                   void *dq, void *dk, void *dv, void *dbeta, float *dstate0,
                                   void *workspace, int *status, int B, int T, int H, int D,
                                   void *stream);
+
+/* The bf16 scan taking the write-strength logits (bf16 [B,T,H]) and an optional per-token float32
+ * shift [B,T]: beta = bf16(sigmoid(float(logit) + shift)) as torch.sigmoid rounds its bf16
+ * output, and dlogits = bf16((float(bf16(dbeta)) * (1 - beta)) * beta) as torch's bf16
+ * sigmoid_backward forms it. Replaces vesper/recurrence.py:34-88 (write_strength) fused with
+ * vesper/kernels/delta_scan.py:132-153 (delta_scan_fused). */
+VB_API int vb_delta_scan_bf16_fwd_logits(const void *q, const void *k, const void *v,
+                                         const void *beta_logits, const float *shift,
+                                         const float *state0, void *o, float *state_n, void *saved,
+                                         int *status, int B, int T, int H, int D, void *stream);
+
+VB_API int vb_delta_scan_bf16_bwd_logits(const void *q, const void *k, const void *v,
+                                         const void *beta_logits, const float *shift,
+                                         const void *saved, const void *dout,
+                                         const float *dstate_n, void *dq, void *dk, void *dv,
+                                         void *dlogits, float *dstate0, void *workspace,
+                                         int *status, int B, int T, int H, int D, void *stream);
 
 /* ---- windowed attention ------------------------------------------------------------------
  * Softmax attention of q [B,NQ,H,DK] over keys, values [B,L,HKV,DK] (bf16 or f16 by `dtype`,

@@ -69,13 +69,20 @@ class _Report:
         assert not self.bad, self.bad
 
 
+def _logit(beta: np.ndarray) -> np.ndarray:
+    b = np.asarray(beta, np.float64)
+    return np.log(b) - np.log1p(-b)
+
+
 def _column_run(f: dict[str, np.ndarray], bf16: bool):
     col = Column(SHAPE, torch.Generator().manual_seed(SEED))
     _check_sums(col, f)
     col = col.to(CUDA)
     set_scan(col, "fused" if bf16 else "fused-fp32")
     names = ("x", "h1", "ck", "cv", "hist", "rec_z", "rec_k", "rec_v", "rec_beta", "attn_k", "attn_v")
-    leaves = {k: _t(f[k]).requires_grad_() for k in names}
+    # this build carries the write strength as its logits (the scan forms the sigmoid): the
+    # fixture's carried beta enters as logit(beta)
+    leaves = {k: _t(_logit(f[k]) if k == "rec_beta" else f[k]).requires_grad_() for k in names}
     b = leaves["x"].shape[0]
     cold = init_column_state(SHAPE, b, 2, torch.float32, CUDA)
     state = ColumnState(
@@ -106,9 +113,15 @@ def test_column_step_with_a_carry_matches_the_reference(bf16: bool) -> None:
     assert np.array_equal(new.kv[1].pos.cpu().numpy(), f["kv_pos"])
     for k, w in (("rec_z", "w_z"), ("rec_k", "w_k"), ("rec_v", "w_v"), ("rec_beta", "w_beta"),
                  ("attn_k", "w_ak"), ("attn_v", "w_av")):  # fmt: skip
-        _close(getattr(written, k), f[w], f"written {k}")
+        got = getattr(written, k)
+        # the written write strength is its logits here: beta is their sigmoid
+        _close(torch.sigmoid(got.float()) if k == "rec_beta" else got, f[w], f"written {k}")
+    carried_beta = f["rec_beta"].astype(np.float64)
     for k, t in leaves.items():
-        _close(t.grad, f[f"dleaf.{k}"], f"grad {k}")
+        want = f[f"dleaf.{k}"]
+        if k == "rec_beta":  # the gradient of the carried logits: dbeta * beta (1 - beta)
+            want = want * carried_beta * (1.0 - carried_beta)
+        _close(t.grad, want, f"grad {k}")
     for k, p in col.named_parameters():
         _close(p.grad, f[f"grad.{k}"], f"grad {k}")
     _close.check()

@@ -3,10 +3,12 @@
 This is exactly the chain ``bench.py`` times (``fused_rms_norm`` -> ``fused_keys`` ->
 ``delta_scan_fused``, forward and backward) at BASELINE config 2's full size: B=8, H=8, T=4096,
 d=128, width 1024. Unlike the bench it carries a nonzero initial state, a nonzero key history and
-a nonzero state gradient, so every state path the column uses is exercised. The GPU runs all eight
+a nonzero state gradient, so every state path the column uses is exercised. As in the bench, the
+scan takes the write-strength logits and forms beta = sigmoid(logits) in its kernels; the oracle
+is fed the reference's write_strength of the same logits. The GPU runs all eight
 batch rows; the float64 oracle (the reference's pure-PyTorch float32 path restated) checks two of
 them in full: the output, the final state and the gradients of x, the gain, the taps, the history,
-q, v, beta and the initial state.
+q, v, the logits and the initial state.
 
 Bounds, the bf16 mode's: 1.5e-2 relative L2 (the reference's own test bound for its bf16 scan,
 vesper tests/test_delta_scan_fused.py:34) and 2e-2 normwise max-relative (the north star's "max
@@ -18,6 +20,7 @@ is asserted within ``ELEM_TOL`` = 1e-1 and every reading is printed.
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
@@ -46,7 +49,7 @@ def _inputs(seed: int = 21):
     hist = torch.randn(B, TAPS - 1, W, generator=g)
     q = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=g), dim=-1).to(BF16)
     v = torch.randn(B, T, H, D, generator=g).to(BF16)
-    beta = torch.sigmoid(torch.randn(B, T, H, generator=g)).to(BF16)
+    beta = torch.randn(B, T, H, generator=g).to(BF16)  # the write-strength logits
     s0 = 0.1 * torch.randn(B, H, D, D, generator=g)
     d_o = torch.randn(B, T, H, D, generator=g)
     d_s = torch.randn(B, H, D, D, generator=g)
@@ -59,7 +62,7 @@ def test_config2_chain_forward_and_every_gradient_match_the_oracle() -> None:
     lx, lg, lt, lh, lq, lv, lb, ls = leaves
     xn = fused_rms_norm(lx, lg, 1e-3, 1e-6)
     k = fused_keys(xn, lh, lt, H)
-    o, sn = delta_scan_fused(lq, k, lv, lb, ls)
+    o, sn = delta_scan_fused(lq, k, lv, lb, ls, from_logits=True)
     ((o.float() * d_o.to(CUDA)).sum() + (sn * d_s.to(CUDA)).sum()).backward()
     torch.cuda.synchronize()
     check_status(CUDA)
@@ -68,7 +71,7 @@ def test_config2_chain_forward_and_every_gradient_match_the_oracle() -> None:
         "dx": lx.grad.float().cpu().numpy(), "dgain": lg.grad.cpu().numpy(),
         "dtaps": lt.grad.cpu().numpy(), "dhist": lh.grad.cpu().numpy(),
         "dq": lq.grad.float().cpu().numpy(), "dv": lv.grad.float().cpu().numpy(),
-        "dbeta": lb.grad.float().cpu().numpy(), "ds0": ls.grad.cpu().numpy(),
+        "dlogits": lb.grad.float().cpu().numpy(), "ds0": ls.grad.cpu().numpy(),
     }  # fmt: skip
     del leaves, lx, lg, lt, lh, lq, lv, lb, ls, xn, k, o, sn
     rows = list(ROWS)
@@ -76,7 +79,8 @@ def test_config2_chain_forward_and_every_gradient_match_the_oracle() -> None:
     xr = x[rows].double().numpy()
     g64, t64 = gain.double().numpy(), taps.double().numpy()
     hr = hist[rows].double().numpy()
-    qr, vr, br = (t[rows].double().numpy() for t in (q, v, beta))
+    qr, vr, lr = (t[rows].double().numpy() for t in (q, v, beta))
+    br = 1.0 / (1.0 + np.exp(-lr))  # write_strength
     sr, dor, dsr = s0[rows].double().numpy(), d_o[rows].double().numpy(), d_s[rows].double().numpy()
     xn_w, _ = oracle.rms_norm(xr, g64)
     k_w = oracle.keys(xn_w, hr, t64, H)
@@ -86,7 +90,8 @@ def test_config2_chain_forward_and_every_gradient_match_the_oracle() -> None:
     dx_w, dg_w = oracle.rms_norm_grads(xr, g64, dz_w)
     # every quantity here is a function of its own batch row; the gain's and the taps' gradients,
     # which sum over all rows, are checked by the next test on a batch of two rows
-    want = {"o": o_w, "state": s_w, "dx": dx_w, "dhist": dh_w, "dq": dq_w, "dv": dv_w, "dbeta": db_w, "ds0": ds_w}
+    want = {"o": o_w, "state": s_w, "dx": dx_w, "dhist": dh_w, "dq": dq_w, "dv": dv_w,
+            "dlogits": db_w * br * (1.0 - br), "ds0": ds_w}  # fmt: skip
     report, bad = [], []
     for name, w in want.items():
         g_rows = got[name][rows]
@@ -106,12 +111,13 @@ def test_config2_chain_gain_and_taps_gradients_match_the_oracle_on_a_two_row_bat
     lx, lg, lt, lh, lq, lv, lb, ls = leaves
     xn = fused_rms_norm(lx, lg, 1e-3, 1e-6)
     k = fused_keys(xn, lh, lt, H)
-    o, sn = delta_scan_fused(lq, k, lv, lb, ls)
+    o, sn = delta_scan_fused(lq, k, lv, lb, ls, from_logits=True)
     ((o.float() * d_o.to(CUDA)).sum() + (sn * d_s.to(CUDA)).sum()).backward()
     torch.cuda.synchronize()
     check_status(CUDA)
     xr, g64, t64, hr = x.double().numpy(), gain.double().numpy(), taps.double().numpy(), hist.double().numpy()
-    qr, vr, br, sr = (t.double().numpy() for t in (q, v, beta, s0))
+    qr, vr, sr = (t.double().numpy() for t in (q, v, s0))
+    br = 1.0 / (1.0 + np.exp(-beta.double().numpy()))
     xn_w, _ = oracle.rms_norm(xr, g64)
     k_w = oracle.keys(xn_w, hr, t64, H)
     _, dk_w, _, _, _ = oracle.delta_scan_grads(qr, k_w, vr, br, sr, d_o.double().numpy(), d_s.double().numpy())

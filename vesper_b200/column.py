@@ -5,8 +5,10 @@ key filter, delta-rule scan), windowed attention, the feed-forward ``W_2 relu(W_
 classes keep the reference's parameter names, shapes and initialization draws, so a reference
 ``state_dict`` loads unchanged, and its per-pass state (``ColumnState``), its copy-forward
 (``Carry`` / ``Projections``) and its ``step`` contract. What runs differs: RMSNorm, the key filter,
-the scan and the attention are this package's sm_100a kernels (no reference scan: the reference's
-``delta_scan_chunked`` is the oracle the tests compare with), the copy-forward merges are one
+the scan (which forms the write strength ``sigmoid(W_beta x)`` inside its kernels, so the carried
+``rec_beta`` holds logits) and the attention are this package's sm_100a kernels (no reference
+scan: the reference's ``delta_scan_chunked`` is the oracle the tests compare with), the
+copy-forward merges are one
 multi-tensor select per merge point, and with a carry the attention computes the active queries
 only (the halted ones' outputs are discarded by the loop anyway). Projections stay cuBLAS GEMMs.
 """
@@ -63,7 +65,12 @@ class ColumnShape:
 
 @dataclass(frozen=True)
 class Projections:
-    """What a chunk writes into a pass's states per position (``vesper/column.py:122-137``)."""
+    """What a chunk writes into a pass's states per position (``vesper/column.py:122-137``).
+
+    ``rec_beta`` holds the write-strength LOGITS ``W_beta x`` here, not ``beta``: the scan forms
+    ``beta = sigmoid(logits)`` inside its kernels (``from_logits``), so a halted token's carried
+    write strength is carried as the logits it was computed from (the same ``beta`` results).
+    """
 
     rec_z: Tensor
     rec_k: Tensor
@@ -189,15 +196,22 @@ class RecurrentSublayer(nn.Module):
             bound = 1.0 / math.sqrt(shape.key_conv)
             self.conv_k = nn.Parameter(torch.rand(shape.key_conv, d, generator=generator) * (2 * bound) - bound)
 
-    def project(self, x: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-        """``q, v [b,n,h,dk]``, the key input ``z = W_k x [b,n,d]`` and ``beta = sigmoid(W_beta x)``."""
+    def project_logits(self, x: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        """``q, v [b,n,h,dk]``, the key input ``z = W_k x [b,n,d]`` and the write-strength logits
+        ``W_beta x [b,n,h]``, which the scan turns into ``beta`` inside its kernels."""
         dims: Dims = {}
         check_shape("x", x, ("b", "n", "d"), dims)
         b, n = dims["b"], dims["n"]
         q = F.linear(x, self.w_q).view(b, n, self.heads, self.head_dim)
         z = F.linear(x, self.w_k)
         v = F.linear(x, self.w_v).view(b, n, self.heads, self.head_dim)
-        return q, z, v, torch.sigmoid(F.linear(x, self.w_beta))
+        return q, z, v, F.linear(x, self.w_beta)
+
+    def project(self, x: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        """``q, v [b,n,h,dk]``, ``z = W_k x [b,n,d]`` and ``beta = sigmoid(W_beta x)``
+        (``vesper/column.py:236-253``); the column itself uses ``project_logits``."""
+        q, z, v, logits = self.project_logits(x)
+        return q, z, v, torch.sigmoid(logits)
 
     def keys(self, z: Tensor, history: Tensor) -> tuple[Tensor, Tensor]:
         """Normalized keys from the filter over ``(history, z)`` and the next history
@@ -214,18 +228,21 @@ class RecurrentSublayer(nn.Module):
         tail = z[:, max(0, n - (width - 1)) :].to(compute)
         return k, torch.cat([history.to(compute)[:, n:], tail], dim=1)
 
-    def scan(self, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor) -> tuple[Tensor, Tensor]:
-        """The scan (``scan_impl``) with autocast off, then ``W_o`` in the activation dtype."""
+    def scan(self, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, *,
+             from_logits: bool = False) -> tuple[Tensor, Tensor]:  # fmt: skip
+        """The scan (``scan_impl``) with autocast off, then ``W_o`` in the activation dtype;
+        ``from_logits``: ``beta`` holds the write-strength logits (the kernels form the sigmoid)."""
         kernel = delta_scan_fused if self.scan_impl == "fused" else delta_scan_fused_fp32
         dtype = FUSED_INPUT_DTYPES[self.scan_impl]
         with torch.autocast(device_type=q.device.type, enabled=False):
-            o, new_state = kernel(q.to(dtype), k.to(dtype), v.to(dtype), beta.to(dtype), state.to(STATE_DTYPE))
+            o, new_state = kernel(q.to(dtype), k.to(dtype), v.to(dtype), beta.to(dtype), state.to(STATE_DTYPE),
+                                  from_logits=from_logits)  # fmt: skip
         return F.linear(o.to(q.dtype).flatten(2), self.w_o), new_state
 
     def forward(self, x: Tensor, state: Tensor, history: Tensor) -> tuple[Tensor, Tensor, Tensor]:
-        q, z, v, beta = self.project(x)
+        q, z, v, logits = self.project_logits(x)
         k, history_next = self.keys(z, history)
-        y, state_next = self.scan(q, k, v, beta, state)
+        y, state_next = self.scan(q, k, v, logits, state, from_logits=True)
         return y, state_next, history_next
 
 
@@ -311,7 +328,7 @@ class Column(nn.Module):
             check_shape("carry.attn_k", p.attn_k, ("b", "n", "hkv", "dk"), dims)
             check_shape("carry.attn_v", p.attn_v, ("b", "n", "hkv", "dk"), dims)
 
-        q, z, v, beta = self.rec.project(self.norm_rec.forward(x))
+        q, z, v, beta = self.rec.project_logits(self.norm_rec.forward(x))  # beta: the logits
         if carry is not None:
             (z,) = select_rows(carry.active, [z], [carry.projections.rec_z.to(z.dtype)])
         k, history_next = self.rec.keys(z, history)
@@ -319,7 +336,7 @@ class Column(nn.Module):
             p = carry.projections
             k, v, beta = select_rows(carry.active, [k, v, beta],
                                      [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
-        r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index])
+        r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index], from_logits=True)
         x = x + r
 
         aq, ak, av = self.attn.project(self.norm_attn.forward(x), pos)

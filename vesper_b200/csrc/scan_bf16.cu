@@ -55,6 +55,21 @@ __device__ __forceinline__ bf16 fetch_beta(const bf16* __restrict__ beta, int64_
   return (t < C && t < valid) ? beta[(row0 + t) * H] : __float2bfloat16_rn(0.f);
 }
 
+// the additive shift of this thread's token (threads < 64) for the write-strength logits, or 0
+__device__ __forceinline__ float fetch_shift(const float* __restrict__ shift, int64_t row0, int valid) {
+  const int t = threadIdx.x;
+  return (shift != nullptr && t < C && t < valid) ? shift[row0 + t] : 0.f;
+}
+
+// The write strength the scan uses: `raw` itself, or with `logit` set the reference's
+// write_strength, beta = sigmoid(raw + shift) rounded to bf16 as torch.sigmoid's bf16 output is
+// (1 / (1 + exp(-x)) in float32, vesper/recurrence.py:34-88).
+__device__ __forceinline__ float beta_value(bf16 raw, int logit, float shift) {
+  if (!logit) return __bfloat162float(raw);
+  const float x = __bfloat162float(raw) + shift;
+  return __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-x))));
+}
+
 // TMA loads of one [64 token][128 d] tile (two 64-channel boxes) of chunk t0 of (b, h)
 __device__ __forceinline__ void tma_tile(uint8_t* tile, const CUtensorMap* map, uint64_t* bar, int h, int t0, int b) {
   tma_load_4d(tile, map, bar, 0, h, t0, b);
@@ -215,8 +230,8 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
 
 __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ beta, uint8_t* __restrict__ xt, int T,
-    int H, int NC, int* status) {
+    const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ beta, const float* __restrict__ shift,
+    int logit, uint8_t* __restrict__ xt, int T, int H, int NC, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t *KQ = sm + PrepSmem::KQ, *Vt = sm + PrepSmem::Vt, *Ws = sm + PrepSmem::Ws, *TT = sm + PrepSmem::TT;
@@ -245,10 +260,11 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
     tma_tile(Vt, &vmap, &lbar, h, t0, b);
   }
   const bf16 bv = fetch_beta(beta + h, row0, H, valid);
+  const float bsh = logit ? fetch_shift(shift, row0, valid) : 0.f;
   if (warp == 0) { tmem_alloc(&tbase, 256); tmem_relinquish(); }
   bool ok = mbar_wait(&lbar, 0);
   if (!ok) atomicOr(status, 4);
-  if (tid < C) bsm[tid] = __bfloat162float(bv);  // after the tile wait: both loads in flight together
+  if (tid < C) bsm[tid] = beta_value(bv, logit, bsh);  // after the tile wait: both loads in flight together
   ok = publish_ok(ok);
   const uint32_t tm = tbase;
   const uint32_t lane_tm = taddr(tm, quarter * 32, 0);
@@ -790,9 +806,9 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
     const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap gmap,
     const __grid_constant__ CUtensorMap dqmap, const __grid_constant__ CUtensorMap dkmap,
-    const __grid_constant__ CUtensorMap dvmap, const bf16* __restrict__ beta, const uint8_t* __restrict__ xt,
-    const uint8_t* __restrict__ hck, const uint8_t* __restrict__ dhck, bf16* __restrict__ dbeta, int T, int H,
-    int D, int NC, int total, int* status) {
+    const __grid_constant__ CUtensorMap dvmap, const bf16* __restrict__ beta, const float* __restrict__ shift,
+    int logit, const uint8_t* __restrict__ xt, const uint8_t* __restrict__ hck, const uint8_t* __restrict__ dhck,
+    bf16* __restrict__ dbeta, int T, int H, int D, int NC, int total, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
   uint8_t *Vt = sm + GrSmem::VV, *Xt = sm + GrSmem::XX, *Rt = sm + GrSmem::Rt, *dDt = sm + GrSmem::dD;
@@ -919,6 +935,7 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     const int64_t row0 = (int64_t)b * T + t0;
     const uint32_t sK = s0 + k_region(par), sQ = s0 + q_region(par);
     const bf16 bv = fetch_beta(beta + h, row0, H, valid);
+    const float bsh = logit ? fetch_shift(shift, row0, valid) : 0.f;
     // stage 1 was issued before this iteration: R^T = V^T - (K H)^T, ddelta^T
     if (ok) {
       const bool r = mbar_wait(&bar1, (uint32_t)(b1_seen & 1));
@@ -936,7 +953,7 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
       ld32w(lane_tm, C_DDT + half * 32, a);
       st_row32_bf16(dDt, 128, lane128, half * 32, a);
     }
-    if (tid < C) bsm[tid] = __bfloat162float(bv);
+    if (tid < C) bsm[tid] = beta_value(bv, logit, bsh);
     if (tid == 0) bulk_wait_read();  // the previous chunk's dQ and dK stores have left Wd and Dt
     publish();
     if (tid == 0 && ok && has_next) load_vp(next, nxt);  // V (also read by the readout above) and P are done
@@ -1058,8 +1075,13 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
       }
     }
     publish();
-    if (rowlane && half == 0 && trow < valid)
-      dbeta[(row0 + trow) * H + h] = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
+    if (rowlane && half == 0 && trow < valid) {
+      const bf16 db = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
+      // with logits, the gradient through the sigmoid as torch's bf16 sigmoid_backward forms it
+      // from the bf16 dbeta and beta: (dbeta * (1 - beta)) * beta in float32, rounded to bf16
+      const float bt = bsm[trow];
+      dbeta[(row0 + trow) * H + h] = logit ? __float2bfloat16_rn((__bfloat162float(db) * (1.0f - bt)) * bt) : db;
+    }
     // stage 5: dK += dG K; then the next chunk's stage 1 (its columns and regions are free)
     if (tid == 0 && ok) {
       mma_seq<4, 0, 64, 1, 64>(tm + C_DK, sdG, sK, idesc_bf16(64, 128, 0, 1), 1u);
@@ -1140,9 +1162,10 @@ extern "C" size_t vb_delta_scan_bf16_bwd_workspace(int B, int T, int H, int D) {
   return n > 0 ? n : 16;
 }
 
-extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* v, const void* beta,
-                                      const float* state0, void* o, float* state_n, void* saved,
-                                      int* status, int B, int T, int H, int D, void* stream) {
+namespace {
+int scan_bf16_fwd(const void* q, const void* k, const void* v, const void* beta, const float* shift, int logit,
+                  const float* state0, void* o, float* state_n, void* saved, int* status, int B, int T, int H,
+                  int D, void* stream) {
   const void* ptrs[] = {q, k, v, o, saved};
   int rc = check(ptrs, 5, B, T, H, D);
   if (rc) return rc;
@@ -1160,7 +1183,7 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
       return rc;
     const size_t sp = smem_bytes(PrepSmem::END);
     VB_CUDA_CHECK(cudaFuncSetAttribute(scan_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sp), "prep attr");
-    scan_prep_kernel<<<B * H * NC, NP, sp, st>>>(qm, km, vm, (const bf16*)beta, xt, T, H, NC, status);
+    scan_prep_kernel<<<B * H * NC, NP, sp, st>>>(qm, km, vm, (const bf16*)beta, shift, logit, xt, T, H, NC, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 prep");
   } else {
     memset(&qm, 0, sizeof(qm)); memset(&km, 0, sizeof(km)); memset(&vm, 0, sizeof(vm));
@@ -1173,11 +1196,10 @@ extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* 
   return VB_OK;
 }
 
-extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* v, const void* beta,
-                                      const void* saved, const void* dout, const float* dstate_n,
-                                      void* dq, void* dk, void* dv, void* dbeta, float* dstate0,
-                                      void* workspace, int* status, int B, int T, int H, int D,
-                                      void* stream) {
+int scan_bf16_bwd(const void* q, const void* k, const void* v, const void* beta, const float* shift, int logit,
+                  const void* saved, const void* dout, const float* dstate_n, void* dq, void* dk, void* dv,
+                  void* dbeta, float* dstate0, void* workspace, int* status, int B, int T, int H, int D,
+                  void* stream) {
   const void* ptrs[] = {q, k, v, saved, dout, dq, dk, dv, workspace};
   int rc = check(ptrs, 9, B, T, H, D);
   if (rc) return rc;
@@ -1213,9 +1235,42 @@ extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* 
     VB_CUDA_CHECK(cudaGetDevice(&dev), "grad device");
     VB_CUDA_CHECK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev), "grad SM count");
     const int total = B * H * NC;  // one persistent CTA per SM walks the chunks
-    scan_grad_kernel<<<total < nsm ? total : nsm, NG, sg, st>>>(qm, km, vm, gm, dqm, dkm, dvm, (const bf16*)beta, xt,
-                                                                 hck, dhck, (bf16*)dbeta, T, H, D, NC, total, status);
+    scan_grad_kernel<<<total < nsm ? total : nsm, NG, sg, st>>>(qm, km, vm, gm, dqm, dkm, dvm, (const bf16*)beta,
+                                                                 shift, logit, xt, hck, dhck, (bf16*)dbeta, T, H,
+                                                                 D, NC, total, status);
     VB_LAUNCH_CHECK("delta_scan_bf16 grad");
   }
   return VB_OK;
+}
+}  // namespace
+
+extern "C" int vb_delta_scan_bf16_fwd(const void* q, const void* k, const void* v, const void* beta,
+                                      const float* state0, void* o, float* state_n, void* saved,
+                                      int* status, int B, int T, int H, int D, void* stream) {
+  return scan_bf16_fwd(q, k, v, beta, nullptr, 0, state0, o, state_n, saved, status, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_bf16_bwd(const void* q, const void* k, const void* v, const void* beta,
+                                      const void* saved, const void* dout, const float* dstate_n,
+                                      void* dq, void* dk, void* dv, void* dbeta, float* dstate0,
+                                      void* workspace, int* status, int B, int T, int H, int D,
+                                      void* stream) {
+  return scan_bf16_bwd(q, k, v, beta, nullptr, 0, saved, dout, dstate_n, dq, dk, dv, dbeta, dstate0, workspace,
+                       status, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_bf16_fwd_logits(const void* q, const void* k, const void* v, const void* beta_logits,
+                                             const float* shift, const float* state0, void* o, float* state_n,
+                                             void* saved, int* status, int B, int T, int H, int D, void* stream) {
+  VB_REQUIRE(B == 0 || H == 0 || beta_logits != nullptr, "delta_scan_bf16_fwd_logits: null logits");
+  return scan_bf16_fwd(q, k, v, beta_logits, shift, 1, state0, o, state_n, saved, status, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_bf16_bwd_logits(const void* q, const void* k, const void* v, const void* beta_logits,
+                                             const float* shift, const void* saved, const void* dout,
+                                             const float* dstate_n, void* dq, void* dk, void* dv, void* dlogits,
+                                             float* dstate0, void* workspace, int* status, int B, int T, int H,
+                                             int D, void* stream) {
+  return scan_bf16_bwd(q, k, v, beta_logits, shift, 1, saved, dout, dstate_n, dq, dk, dv, dlogits, dstate0,
+                       workspace, status, B, T, H, D, stream);
 }

@@ -13,6 +13,17 @@
 namespace vb {
 namespace {
 
+// The write strength of token row `row` ((b*T + t)*H + h; `tok` = b*T + t): beta itself, or with
+// `logit` set the reference's write_strength, sigmoid(logit + shift[tok]) = 1 / (1 + exp(-x)) in
+// float32 as torch.sigmoid forms it (vesper/recurrence.py:34-88).
+__device__ __forceinline__ float beta_at(const float* __restrict__ beta, const float* __restrict__ shift, int logit,
+                                         int64_t row, int64_t tok) {
+  const float raw = __ldg(beta + row);
+  if (!logit) return raw;
+  const float x = raw + (shift != nullptr ? __ldg(shift + tok) : 0.f);
+  return 1.0f / (1.0f + expf(-x));
+}
+
 constexpr int NWARP = 8;          // warps per CTA
 constexpr int CPW = 4;            // value columns per warp
 constexpr int BV = NWARP * CPW;   // value columns per CTA
@@ -20,8 +31,8 @@ constexpr int BV = NWARP * CPW;   // value columns per CTA
 template <int NI>
 __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-    const float* __restrict__ beta, const float* __restrict__ s0, float* __restrict__ o,
-    float* __restrict__ sn, float* __restrict__ resid, int T, int H, int D) {
+    const float* __restrict__ beta, const float* __restrict__ shift, int logit, const float* __restrict__ s0,
+    float* __restrict__ o, float* __restrict__ sn, float* __restrict__ resid, int T, int H, int D) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int jb = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
   const int j0 = jb * BV + warp * CPW;
@@ -49,7 +60,7 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
     }
 #pragma unroll
     for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? __ldg(v + row * D + j0 + c) : 0.f;
-    const float bt = __ldg(beta + row);
+    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
     float red[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
@@ -131,6 +142,7 @@ __device__ __forceinline__ void cta_sum_store(float (&part)[NI], float* red, flo
 template <int NI>
 __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ beta,
+    const float* __restrict__ shift, int logit,
     const float* __restrict__ s0, const float* __restrict__ resid, const float* __restrict__ dout,
     const float* __restrict__ dsn, float* __restrict__ dv, float* __restrict__ ds0,
     float* __restrict__ part, int B, int T, int H, int D) {
@@ -167,7 +179,7 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
       gg[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
       rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
     }
-    const float bt = __ldg(beta + row);
+    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
 #pragma unroll
     for (int m = 0; m < NI; ++m)
 #pragma unroll
@@ -243,7 +255,7 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
       rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
       dr[c] = ok ? dv[row * D + j0 + c] : 0.f;
     }
-    const float bt = __ldg(beta + row);
+    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
     float hd[NI];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
@@ -272,14 +284,17 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
 }
 
 // Per (b, t, h): sums the column-block partials in order; dk = beta * Gr - H dr, dbeta = k . Gr.
+// With logits, dbeta is the gradient of the logits: (dbeta * (1 - beta)) * beta, the order of
+// torch's sigmoid_backward.
 __global__ void scan_f32_finish_kernel(const float* __restrict__ k, const float* __restrict__ beta,
+                                       const float* __restrict__ shift, int logit,
                                        const float* __restrict__ part, float* __restrict__ dq,
                                        float* __restrict__ dk, float* __restrict__ dbeta,
-                                       int64_t rows, int D, int NJB) {
+                                       int64_t rows, int H, int D, int NJB) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= rows) return;
-  const float bt = beta[row];
+  const float bt = beta_at(beta, shift, logit, row, row / H);
   float dotk = 0.f;
   for (int i = lane; i < D; i += 32) {
     float gr = 0.f, hd = 0.f, qd = 0.f;
@@ -293,7 +308,7 @@ __global__ void scan_f32_finish_kernel(const float* __restrict__ k, const float*
     dotk = fmaf(k[row * D + i], gr, dotk);
   }
   dotk = warp_sum(dotk);
-  if (lane == 0) dbeta[row] = dotk;
+  if (lane == 0) dbeta[row] = logit ? (dotk * (1.0f - bt)) * bt : dotk;
 }
 
 int njb(int D) { return (D + BV - 1) / BV; }
@@ -318,9 +333,10 @@ int check(int B, int T, int H, int D) {
 
 using namespace vb;
 
-extern "C" int vb_delta_scan_f32_fwd(const float* q, const float* k, const float* v, const float* beta,
-                                     const float* state0, float* o, float* state_n, float* resid,
-                                     int B, int T, int H, int D, void* stream) {
+namespace {
+int scan_f32_fwd(const float* q, const float* k, const float* v, const float* beta, const float* shift, int logit,
+                 const float* state0, float* o, float* state_n, float* resid, int B, int T, int H, int D,
+                 void* stream) {
   int rc = check(B, T, H, D);
   if (rc) return rc;
   if (B == 0 || H == 0) return VB_OK;
@@ -328,10 +344,26 @@ extern "C" int vb_delta_scan_f32_fwd(const float* q, const float* k, const float
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(njb(D), B * H);
   return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    scan_f32_fwd_kernel<NI><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, state0, o, state_n, resid, T, H, D);
+    scan_f32_fwd_kernel<NI><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, shift, logit, state0, o, state_n, resid,
+                                                         T, H, D);
     VB_LAUNCH_CHECK("delta_scan_f32_fwd");
     return VB_OK;
   });
+}
+
+}  // namespace
+
+extern "C" int vb_delta_scan_f32_fwd(const float* q, const float* k, const float* v, const float* beta,
+                                     const float* state0, float* o, float* state_n, float* resid,
+                                     int B, int T, int H, int D, void* stream) {
+  return scan_f32_fwd(q, k, v, beta, nullptr, 0, state0, o, state_n, resid, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_f32_fwd_logits(const float* q, const float* k, const float* v,
+                                            const float* beta_logits, const float* shift, const float* state0,
+                                            float* o, float* state_n, float* resid, int B, int T, int H, int D,
+                                            void* stream) {
+  return scan_f32_fwd(q, k, v, beta_logits, shift, 1, state0, o, state_n, resid, B, T, H, D, stream);
 }
 
 extern "C" size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D) {
@@ -339,12 +371,11 @@ extern "C" size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D) {
   return 3 * (size_t)njb(D > 0 ? D : 1) * (rows > 0 ? rows : 1) * (size_t)(D > 0 ? D : 1) * sizeof(float);
 }
 
-extern "C" int vb_delta_scan_f32_bwd(const float* q, const float* k, const float* v, const float* beta,
-                                     const float* state0, const float* resid, const float* dout,
-                                     const float* dstate_n, float* dq, float* dk, float* dv,
-                                     float* dbeta, float* dstate0, void* workspace, int B, int T,
-                                     int H, int D, void* stream) {
-  (void)v;
+namespace {
+int scan_f32_bwd(const float* q, const float* k, const float* beta, const float* shift, int logit,
+                 const float* state0, const float* resid, const float* dout, const float* dstate_n, float* dq,
+                 float* dk, float* dv, float* dbeta, float* dstate0, void* workspace, int B, int T, int H, int D,
+                 void* stream) {
   int rc = check(B, T, H, D);
   if (rc) return rc;
   if (B == 0 || H == 0) return VB_OK;
@@ -355,15 +386,36 @@ extern "C" int vb_delta_scan_f32_bwd(const float* q, const float* k, const float
   const size_t smem = sizeof(float) * NWARP * D;
   float* part = (float*)workspace;
   return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    scan_f32_bwd_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, beta, state0, resid, dout, dstate_n,
-                                                            dv, dstate0, part, B, T, H, D);
+    scan_f32_bwd_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, beta, shift, logit, state0, resid, dout,
+                                                            dstate_n, dv, dstate0, part, B, T, H, D);
     VB_LAUNCH_CHECK("delta_scan_f32_bwd");
     const int64_t rows = (int64_t)B * T * H;
     if (rows > 0) {
-      scan_f32_finish_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(k, beta, part, dq, dk, dbeta, rows,
-                                                                    D, njb(D));
+      scan_f32_finish_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(k, beta, shift, logit, part, dq, dk, dbeta,
+                                                                    rows, H, D, njb(D));
       VB_LAUNCH_CHECK("delta_scan_f32_finish");
     }
     return VB_OK;
   });
+}
+}  // namespace
+
+extern "C" int vb_delta_scan_f32_bwd(const float* q, const float* k, const float* v, const float* beta,
+                                     const float* state0, const float* resid, const float* dout,
+                                     const float* dstate_n, float* dq, float* dk, float* dv,
+                                     float* dbeta, float* dstate0, void* workspace, int B, int T,
+                                     int H, int D, void* stream) {
+  (void)v;
+  return scan_f32_bwd(q, k, beta, nullptr, 0, state0, resid, dout, dstate_n, dq, dk, dv, dbeta, dstate0,
+                      workspace, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_f32_bwd_logits(const float* q, const float* k, const float* v,
+                                            const float* beta_logits, const float* shift, const float* state0,
+                                            const float* resid, const float* dout, const float* dstate_n, float* dq,
+                                            float* dk, float* dv, float* dlogits, float* dstate0, void* workspace,
+                                            int B, int T, int H, int D, void* stream) {
+  (void)v;
+  return scan_f32_bwd(q, k, beta_logits, shift, 1, state0, resid, dout, dstate_n, dq, dk, dv, dlogits, dstate0,
+                      workspace, B, T, H, D, stream);
 }

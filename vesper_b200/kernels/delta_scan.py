@@ -18,6 +18,12 @@ states checkpointed in the forward and reused by the backward.
 ``delta_scan_fused_fp32``: float32 throughout, token by token (``vb_delta_scan_f32_*``).
 
 Zero tokens return ``(q, state)`` with the same state object, as the reference does.
+
+``from_logits=True`` takes the write strength as its logits ``W_beta x`` instead and forms
+``beta = sigmoid(logits + shift)`` inside the kernels (the reference's ``write_strength``,
+``vesper/recurrence.py:34-88``, with the modulator's per-token odds shift from
+``modulation_shift``); the backward returns the logits' gradient. The result is bit-identical to
+``torch.sigmoid`` followed by the scan: no separate sigmoid pass over beta and its gradient.
 """
 
 from __future__ import annotations
@@ -69,6 +75,35 @@ def _checked_length(
     return dims["n"]
 
 
+def modulation_shift(logits: Tensor, m: Tensor, alpha: float) -> Tensor:
+    """The per-token odds shift ``ln(1 + alpha m)`` [b, n] float32 that ``write_strength`` adds to
+    the logits (``vesper/recurrence.py:34-88``), ``-inf`` where the factor is zero (an exact zero
+    write and gradient). Same validation and messages as the reference."""
+    if not 0.0 <= alpha < float("inf"):
+        msg = f"alpha must be finite and non-negative, got {alpha}"
+        raise ValueError(msg)
+    dims: Dims = {}
+    check_shape("logits", logits, ("b", "n", "h"), dims)
+    check_shape("m", m, ("b", "n"), dims)
+    factor = 1.0 + alpha * m.to(torch.float32)
+    if bool((factor < 0).any().item()):
+        msg = f"1 + alpha m must not be negative; alpha {alpha}, smallest m {m.min().item()}"
+        raise ValueError(msg)
+    return torch.where(factor > 0, torch.log(factor.clamp_min(torch.finfo(torch.float32).tiny)),
+                       torch.full_like(factor, float("-inf"))).contiguous()  # fmt: skip
+
+
+def _checked_shift(shift: Tensor | None, q: Tensor) -> Tensor | None:
+    if shift is None:
+        return None
+    b, n = q.shape[0], q.shape[1]
+    check_shape("shift", shift, ("b", "n"), {"b": b, "n": n}, torch.float32)
+    if shift.device != q.device:
+        msg = f"shift is on {shift.device}, q on {q.device}"
+        raise ContractError(msg)
+    return shift.contiguous()
+
+
 # the device status word the bf16 scan's kernels report a timeout through (shared by the library)
 status_word = _lib.status_word
 check_status = _lib.check_status
@@ -78,30 +113,36 @@ check_status = _lib.check_status
 
 
 def scan_bf16_forward(
-    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
-) -> tuple[Tensor, Tensor, Tensor]:
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, from_logits: bool = False,
+    shift: Tensor | None = None,
+) -> tuple[Tensor, Tensor, Tensor]:  # fmt: skip
     b, n, h, d = q.shape
     o = torch.empty_like(q)
     sn = torch.empty_like(state)
     saved = _lib.workspace(_lib.query("vb_delta_scan_bf16_saved_bytes", b, n, h, d), q.device)
+    head = ("vb_delta_scan_bf16_fwd_logits", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+            _lib.ptr(shift)) if from_logits else (
+            "vb_delta_scan_bf16_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr())  # fmt: skip
     _lib.call(
-        "vb_delta_scan_bf16_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
-        state.data_ptr(), o.data_ptr(), sn.data_ptr(), saved.data_ptr(),
+        *head, state.data_ptr(), o.data_ptr(), sn.data_ptr(), saved.data_ptr(),
         status_word(q.device).data_ptr(), b, n, h, d, _lib.stream(q.device),
     )  # fmt: skip
     return o, sn, saved
 
 
 def scan_bf16_backward(
-    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, saved: Tensor, d_o: Tensor, d_sn: Tensor | None
-) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, saved: Tensor, d_o: Tensor, d_sn: Tensor | None,
+    from_logits: bool = False, shift: Tensor | None = None,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
     b, n, h, d = q.shape
     dq, dk, dv, dbeta = (torch.empty_like(t) for t in (q, k, v, beta))
     ds0 = torch.empty(b, h, d, d, dtype=torch.float32, device=q.device)
     ws = _lib.workspace(_lib.query("vb_delta_scan_bf16_bwd_workspace", b, n, h, d), q.device)
+    head = ("vb_delta_scan_bf16_bwd_logits", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+            _lib.ptr(shift)) if from_logits else (
+            "vb_delta_scan_bf16_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr())  # fmt: skip
     _lib.call(
-        "vb_delta_scan_bf16_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
-        saved.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(), dk.data_ptr(),
+        *head, saved.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(), dk.data_ptr(),
         dv.data_ptr(), dbeta.data_ptr(), ds0.data_ptr(), ws.data_ptr(),
         status_word(q.device).data_ptr(), b, n, h, d, _lib.stream(q.device),
     )  # fmt: skip
@@ -110,32 +151,38 @@ def scan_bf16_backward(
 
 class _ScanBF16(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor):  # type: ignore[override]
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, from_logits: bool,  # type: ignore[override]
+                shift: Tensor | None):  # fmt: skip
         q, k, v, beta, state = (t.contiguous() for t in (q, k, v, beta, state))
-        o, sn, saved = scan_bf16_forward(q, k, v, beta, state)
+        o, sn, saved = scan_bf16_forward(q, k, v, beta, state, from_logits, shift)
+        ctx.from_logits = from_logits
         if any(ctx.needs_input_grad):
-            ctx.save_for_backward(q, k, v, beta, saved)
+            ctx.save_for_backward(q, k, v, beta, saved, shift)
         return o, sn
 
     @staticmethod
     def backward(ctx, d_o: Tensor | None, d_sn: Tensor | None):  # type: ignore[override]
-        q, k, v, beta, saved = ctx.saved_tensors
+        q, k, v, beta, saved, shift = ctx.saved_tensors
         d_o = torch.zeros_like(q) if d_o is None else d_o.contiguous().to(torch.bfloat16)
         d_sn = None if d_sn is None else d_sn.contiguous().to(torch.float32)
-        return scan_bf16_backward(q, k, v, beta, saved, d_o, d_sn)
+        grads = scan_bf16_backward(q, k, v, beta, saved, d_o, d_sn, ctx.from_logits, shift)
+        return (*grads, None, None)
 
 
 def delta_scan_fused(
-    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
-) -> tuple[Tensor, Tensor]:
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, *, from_logits: bool = False,
+    shift: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:  # fmt: skip
     """Apply ``n`` tokens to the state with the chunked bfloat16 kernels (the reference's form).
 
     Args:
         q: ``[b, n, h, dk]`` queries, bfloat16, on a CUDA device.
         k: ``[b, n, h, dk]`` keys, bfloat16, L2 norm at most one.
         v: ``[b, n, h, dk]`` values, bfloat16.
-        beta: ``[b, n, h]`` write strengths in [0, 1], bfloat16.
+        beta: ``[b, n, h]`` write strengths in [0, 1], bfloat16 (their logits with ``from_logits``).
         state: ``[b, h, dk, dk]`` the state before the first token, float32.
+        from_logits: ``beta`` holds the logits; the kernels form ``sigmoid(beta + shift)``.
+        shift: optional ``[b, n]`` float32 per-token shift of the logits (``modulation_shift``).
 
     Returns:
         ``(o, state_n)``: ``o [b, n, h, dk]`` in bfloat16 and the state after the last token in
@@ -154,7 +201,10 @@ def delta_scan_fused(
             else f"head dimension {q.shape[-1]} must be a multiple of 8"
         )
         raise ContractError(msg)
-    o, sn = _ScanBF16.apply(q, k, v, beta, state)
+    if shift is not None and not from_logits:
+        msg = "shift applies to write-strength logits: pass from_logits=True"
+        raise ContractError(msg)
+    o, sn = _ScanBF16.apply(q, k, v, beta, state, bool(from_logits), _checked_shift(shift, q))
     return o, sn
 
 
@@ -162,15 +212,18 @@ def delta_scan_fused(
 
 
 def scan_f32_forward(
-    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, keep_resid: bool
-) -> tuple[Tensor, Tensor, Tensor | None]:
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, keep_resid: bool, from_logits: bool = False,
+    shift: Tensor | None = None,
+) -> tuple[Tensor, Tensor, Tensor | None]:  # fmt: skip
     b, n, h, d = q.shape
     o = torch.empty_like(q)
     sn = torch.empty_like(state)
     resid = torch.empty_like(v) if keep_resid else None
+    head = ("vb_delta_scan_f32_fwd_logits", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+            _lib.ptr(shift)) if from_logits else (
+            "vb_delta_scan_f32_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr())  # fmt: skip
     _lib.call(
-        "vb_delta_scan_f32_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
-        state.data_ptr(), o.data_ptr(), sn.data_ptr(), _lib.ptr(resid), b, n, h, d,
+        *head, state.data_ptr(), o.data_ptr(), sn.data_ptr(), _lib.ptr(resid), b, n, h, d,
         _lib.stream(q.device),
     )  # fmt: skip
     return o, sn, resid
@@ -178,15 +231,17 @@ def scan_f32_forward(
 
 def scan_f32_backward(
     q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, resid: Tensor,
-    d_o: Tensor, d_sn: Tensor | None,
+    d_o: Tensor, d_sn: Tensor | None, from_logits: bool = False, shift: Tensor | None = None,
 ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:  # fmt: skip
     b, n, h, d = q.shape
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dbeta, ds0 = torch.empty_like(beta), torch.empty_like(state)
     ws = _lib.workspace(_lib.query("vb_delta_scan_f32_bwd_workspace", b, n, h, d), q.device)
+    head = ("vb_delta_scan_f32_bwd_logits", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
+            _lib.ptr(shift)) if from_logits else (
+            "vb_delta_scan_f32_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr())  # fmt: skip
     _lib.call(
-        "vb_delta_scan_f32_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), beta.data_ptr(),
-        state.data_ptr(), resid.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(),
+        *head, state.data_ptr(), resid.data_ptr(), d_o.data_ptr(), _lib.ptr(d_sn), dq.data_ptr(),
         dk.data_ptr(), dv.data_ptr(), dbeta.data_ptr(), ds0.data_ptr(), ws.data_ptr(), b, n, h, d,
         _lib.stream(q.device),
     )  # fmt: skip
@@ -195,34 +250,41 @@ def scan_f32_backward(
 
 class _ScanF32(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor):  # type: ignore[override]
+    def forward(ctx, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, from_logits: bool,  # type: ignore[override]
+                shift: Tensor | None):  # fmt: skip
         q, k, v, beta, state = (t.contiguous() for t in (q, k, v, beta, state))
         keep = any(ctx.needs_input_grad)
-        o, sn, resid = scan_f32_forward(q, k, v, beta, state, keep)
+        o, sn, resid = scan_f32_forward(q, k, v, beta, state, keep, from_logits, shift)
+        ctx.from_logits = from_logits
         if keep:
-            ctx.save_for_backward(q, k, v, beta, state, resid)
+            ctx.save_for_backward(q, k, v, beta, state, resid, shift)
         return o, sn
 
     @staticmethod
     def backward(ctx, d_o: Tensor | None, d_sn: Tensor | None):  # type: ignore[override]
-        q, k, v, beta, state, resid = ctx.saved_tensors
+        q, k, v, beta, state, resid, shift = ctx.saved_tensors
         d_o = torch.zeros_like(q) if d_o is None else d_o.contiguous().to(torch.float32)
         d_sn = None if d_sn is None else d_sn.contiguous().to(torch.float32)
-        grads = scan_f32_backward(q, k, v, beta, state, resid, d_o, d_sn)
-        return grads
+        grads = scan_f32_backward(q, k, v, beta, state, resid, d_o, d_sn, ctx.from_logits, shift)
+        return (*grads, None, None)
 
 
 def delta_scan_fused_fp32(
-    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor
-) -> tuple[Tensor, Tensor]:
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, *, from_logits: bool = False,
+    shift: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:  # fmt: skip
     """Apply ``n`` tokens to the state in float32 (the reference's precision).
 
     Returns ``(o [b, n, h, dk], state_n)`` in float32; with no tokens, ``(q, state)``.
+    ``from_logits`` / ``shift``: as for ``delta_scan_fused``.
 
     Raises:
         ContractError: on a shape, dtype or device mismatch, or a head dimension above 256.
     """
     if _checked_length(q, k, v, beta, state, FP32_INPUT_DTYPE) == 0:
         return q, state
-    o, sn = _ScanF32.apply(q, k, v, beta, state)
+    if shift is not None and not from_logits:
+        msg = "shift applies to write-strength logits: pass from_logits=True"
+        raise ContractError(msg)
+    o, sn = _ScanF32.apply(q, k, v, beta, state, bool(from_logits), _checked_shift(shift, q))
     return o, sn
