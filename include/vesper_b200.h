@@ -163,8 +163,8 @@ VB_API int vb_delta_scan_bf16_bwd(const void *q, const void *k, const void *v, c
 
 /* The bf16 scan taking the write-strength logits (bf16 [B,T,H]) and an optional per-token float32
  * shift [B,T]: beta = bf16(sigmoid(float(logit) + shift)) as torch.sigmoid rounds its bf16
- * output, and dlogits = bf16((float(bf16(dbeta)) * (1 - beta)) * beta) as torch's bf16
- * sigmoid_backward forms it. Replaces vesper/recurrence.py:34-88 (write_strength) fused with
+ * output, and dlogits = bf16(dbeta) * (1 - beta) * beta with every intermediate rounded to bf16,
+ * as torch's bf16 sigmoid_backward forms it (bit-identical to sigmoid then the scan). Replaces vesper/recurrence.py:34-88 (write_strength) fused with
  * vesper/kernels/delta_scan.py:132-153 (delta_scan_fused). */
 VB_API int vb_delta_scan_bf16_fwd_logits(const void *q, const void *k, const void *v,
                                          const void *beta_logits, const float *shift,

@@ -102,6 +102,24 @@ def test_config2_full_size_matches_the_oracle_on_sampled_sequences() -> None:
             _assert_close(got[sl], want, key)
 
 
+@pytest.mark.parametrize("d", [256, 192, 20])
+def test_head_dimensions_beyond_the_chunked_tiles_match_the_oracle(d: int) -> None:
+    # the contract's dk <= 256 (vesper/kernels/delta_scan.py:28-31): widths the 128-wide chunked
+    # tiles do not take run the token-serial float32 kernel, exact to float32 rounding
+    b, n, h = 2, 150, 2
+    q, k, v, beta, s0 = _inputs(b, n, h, d, seed=d)
+    g = torch.Generator().manual_seed(d + 1)
+    d_o, d_s = torch.randn(b, n, h, d, generator=g), torch.randn(b, h, d, d, generator=g)
+    o, s, grads = _fwd_bwd(q, k, v, beta, s0, d_o, d_s)
+    args = [t.float().numpy() for t in (q, k, v, beta, s0)]
+    o_w, s_w = oracle.delta_scan(*args)
+    g_w = oracle.delta_scan_grads(*args, d_o.numpy(), d_s.numpy())
+    _assert_close(o, o_w, "o")
+    _assert_close(s, s_w, "state")
+    for got, want, key in zip(grads, g_w, ("dq", "dk", "dv", "dbeta", "ds0"), strict=True):
+        _assert_close(got, want, key)
+
+
 def test_a_carried_state_continues_the_sequence_and_no_tokens_change_nothing() -> None:
     q, k, v, beta, s0 = (t.to(CUDA) for t in _inputs(2, 130, 3, 16))
     o_ref, s_ref = delta_scan_fused(q, k, v, beta, s0)

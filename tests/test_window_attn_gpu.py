@@ -145,7 +145,9 @@ def test_contract_violations_are_refused_before_any_launch() -> None:
     q = torch.zeros(1, 8, 4, 64, dtype=BF16, device=CUDA)
     kv = torch.zeros(1, 8, 2, 64, dtype=BF16, device=CUDA)
     with pytest.raises(ContractError, match="dtype"):
-        window_attention(q.float(), kv.float(), kv.float(), 8)
+        window_attention(q.double(), kv.double(), kv.double(), 8)
+    with pytest.raises(ContractError, match="dtype"):
+        window_attention(q.float(), kv, kv, 8)
     with pytest.raises(ContractError, match="CUDA only"):
         window_attention(q.cpu(), kv.cpu(), kv.cpu(), 8)
     with pytest.raises(ContractError, match="multiple of 16"):
@@ -190,3 +192,60 @@ def test_repeats_bitwise_and_equals_itself_captured() -> None:
         torch.cuda.synchronize()
         assert all(torch.equal(a, b) for a, b in zip(out, eager[0], strict=True))
     _lib.check_status(CUDA)
+
+
+# ---- float32: the reference's float32 path, on CUDA cores at float32 rounding -----------------------
+
+F32_TOL = 1e-5
+
+
+@pytest.mark.parametrize("name", golden_names("attn_"))
+def test_float32_output_and_gradients_match_the_reference_at_float32_rounding(name: str) -> None:
+    f = golden(name)
+    window = int(f["window"])
+    q = torch.from_numpy(f["q"]).float()
+    keys = torch.from_numpy(np.concatenate([f["ck"], f["k"]], axis=1)).float()
+    values = torch.from_numpy(np.concatenate([f["cv"], f["v"]], axis=1)).float()
+    m = f["ck"].shape[1]
+    o, dq, dkeys, dvalues = _run(q, keys, values, window, torch.from_numpy(f["up"]))
+    pairs = [(o, f["o"], "o"), (dq, f["dq"], "dq"), (dkeys[:, m:], f["dk"], "dk"), (dvalues[:, m:], f["dv"], "dv"),
+             (dkeys[:, :m], f["dck"], "dcache_k"), (dvalues[:, :m], f["dcv"], "dcache_v")]  # fmt: skip
+    for got, want, what in pairs:
+        if want.size:
+            assert rel(got, want) < F32_TOL, (what, rel(got, want))
+            assert max_rel(got, want) < 1e-4, (what, max_rel(got, want))
+
+
+@pytest.mark.parametrize(("b", "n", "m", "window", "dk"), [(2, 300, 0, 512, 64), (2, 200, 100, 64, 64),
+                                                        (1, 130, 7, 1, 32), (2, 100, 20, 50, 128)])  # fmt: skip
+def test_float32_matches_the_oracle(b: int, n: int, m: int, window: int, dk: int) -> None:
+    q, keys, values, d_o = _inputs(b, n, m, 8, 2, dk, seed=n + window, dtype=torch.float32)
+    got = _run(q, keys, values, window, d_o)
+    for a, w, what in zip(got, _oracle(q, keys, values, window, d_o), ("o", "dq", "dkeys", "dvalues"), strict=True):
+        assert rel(a, w) < F32_TOL, (what, rel(a, w))
+
+
+def test_float32_compacted_rows_equal_the_dense_rows() -> None:
+    b, n, m, h, hkv, dk, window = 2, 300, 32, 4, 2, 64, 100
+    q, keys, values, d_o = _inputs(b, n, m, h, hkv, dk, seed=21, dtype=torch.float32)
+    g = torch.Generator().manual_seed(22)
+    active = torch.rand(b, n, generator=g) < torch.tensor([[0.5], [0.1]])
+    counts = active.sum(1).to(torch.int32)
+    qc = torch.zeros(b, n, h, dk)
+    dc = torch.zeros(b, n, h, dk)
+    qpos = torch.zeros(b, n, dtype=torch.int32)
+    d_dense = torch.zeros_like(d_o)
+    for i in range(b):
+        idx = active[i].nonzero().flatten()
+        qc[i, : len(idx)] = q[i, idx]
+        dc[i, : len(idx)] = d_o[i, idx]
+        qpos[i, : len(idx)] = (idx + m).to(torch.int32)
+        d_dense[i, idx] = d_o[i, idx]
+    dense = _run(q, keys, values, window, d_dense)
+    comp = _run(qc, keys, values, window, dc, qpos=qpos, counts=counts)
+    for i in range(b):
+        c = int(counts[i])
+        idx = active[i].nonzero().flatten().numpy()
+        assert rel(comp[0][i, :c], dense[0][i, idx]) < F32_TOL and rel(comp[1][i, :c], dense[1][i, idx]) < F32_TOL
+        assert not np.any(comp[0][i, c:]) and not np.any(comp[1][i, c:])
+    assert rel(comp[2], dense[2]) < F32_TOL and rel(comp[3], dense[3]) < F32_TOL

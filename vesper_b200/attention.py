@@ -4,10 +4,11 @@ mstampfli/vesper-preview): rotary GQA projections, exact softmax over the last `
 Same parameters (``w_q, w_k, w_v, w_o``), layouts and cache semantics as the reference's
 ``WindowedAttention`` (``vesper/attention.py:219-407``) and ``KVCache`` / ``kv_cache_push``
 (``:30-175``); ``rotary`` (``:178-217``) is one kernel each way (``vesper_b200.kernels.rotary``).
-In bfloat16 or float16 the softmax runs in the tcgen05 kernel (``vesper_b200.kernels.window_attn``) over the cache rows and the chunk directly;
-given the loop's compaction of the active tokens, it computes only their queries. float32 keeps
-the reference's blocked, masked attention (as the reference does), run by torch on the device.
-The decode ring (``RingKVCache``) is not part of this build.
+In bfloat16 or float16 the softmax runs in the tcgen05 kernel (``vesper_b200.kernels.window_attn``)
+over the cache rows and the chunk directly, in float32 in the same entry points' FFMA kernel (the
+reference's float32 mode, its blocked masked softmax, at float32 rounding); given the loop's
+compaction of the active tokens, either computes only their queries. The decode ring
+(``RingKVCache``) is not part of this build.
 """
 
 from __future__ import annotations
@@ -24,7 +25,7 @@ from vesper_b200.kernels.compact import Compaction, expand_rows, gather_rows
 from vesper_b200.kernels.rotary import rotary
 from vesper_b200.kernels.window_attn import window_attention, window_attention_active
 
-WINDOW_KERNEL_DTYPES = (torch.bfloat16, torch.float16)  # float32 keeps the blocked path
+WINDOW_KERNEL_DTYPES = (torch.bfloat16, torch.float16, torch.float32)  # tcgen05 / float32 FFMA kernels
 
 
 @dataclass(frozen=True, slots=True)
@@ -140,42 +141,20 @@ class WindowedAttention(nn.Module):
         if q.device.type != "cuda":
             msg = f"the windowed attention runs on CUDA only, got {q.device}"
             raise ContractError(msg)
-        if q.dtype in WINDOW_KERNEL_DTYPES:
-            kpos = torch.cat([cache.pos, pos], dim=1)
-            require((kpos[:, 1:] - kpos[:, :-1] == 1).all(), "attend: cache and chunk positions must be consecutive")
-            keys = torch.cat([cache.k.to(q.dtype), k.to(q.dtype)], dim=1)
-            vals = torch.cat([cache.v.to(q.dtype), v.to(q.dtype)], dim=1)
-            if compaction is None:
-                o = window_attention(q, keys, vals, w)
-            else:
-                (qc,) = gather_rows(compaction, [q])
-                oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
-                (o,) = expand_rows(compaction, [oc])
-            return self.output(o), kv_cache_push(cache, k, v, pos)
-        return self.output(self._blocked(q, k, v, pos, cache)), kv_cache_push(cache, k, v, pos)
-
-    def _blocked(self, q: Tensor, k: Tensor, v: Tensor, pos: Tensor, cache: KVCache) -> Tensor:
-        """The reference's float32 path (``vesper/attention.py:384-407``): query blocks of
-        ``window`` tokens, each over at most three windows of keys, under the position mask."""
-        n, w = q.shape[1], self.window
-        outs: list[Tensor] = []
-        for s in range(0, n, w):
-            e = min(s + w, n)
-            first = max(0, s - w + 1)
-            if s < w:
-                keys = torch.cat([cache.k, k[:, first:e]], dim=1)
-                vals = torch.cat([cache.v, v[:, first:e]], dim=1)
-                kpos = torch.cat([cache.pos, pos[:, first:e]], dim=1)
-            else:
-                keys, vals, kpos = k[:, first:e], v[:, first:e], pos[:, first:e]
-            qpos = pos[:, s:e]
-            allowed = (kpos[:, None, :] <= qpos[:, :, None]) & (kpos[:, None, :] > qpos[:, :, None] - w)
-            block = F.scaled_dot_product_attention(
-                q[:, s:e].transpose(1, 2), keys.transpose(1, 2), vals.transpose(1, 2),
-                attn_mask=allowed[:, None, :, :], enable_gqa=True,
-            )  # fmt: skip
-            outs.append(block.transpose(1, 2))
-        return torch.cat(outs, dim=1)
+        if q.dtype not in WINDOW_KERNEL_DTYPES:
+            msg = f"q: dtype must be one of {WINDOW_KERNEL_DTYPES}, got {q.dtype}"
+            raise ContractError(msg)
+        kpos = torch.cat([cache.pos, pos], dim=1)
+        require((kpos[:, 1:] - kpos[:, :-1] == 1).all(), "attend: cache and chunk positions must be consecutive")
+        keys = torch.cat([cache.k.to(q.dtype), k.to(q.dtype)], dim=1)
+        vals = torch.cat([cache.v.to(q.dtype), v.to(q.dtype)], dim=1)
+        if compaction is None:
+            o = window_attention(q, keys, vals, w)
+        else:
+            (qc,) = gather_rows(compaction, [q])
+            oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
+            (o,) = expand_rows(compaction, [oc])
+        return self.output(o), kv_cache_push(cache, k, v, pos)
 
     def forward(self, x: Tensor, pos: Tensor, cache: KVCache) -> tuple[Tensor, KVCache]:
         """``project`` then ``attend``."""

@@ -1078,9 +1078,12 @@ __global__ void __launch_bounds__(NG, 1) scan_grad_kernel(
     if (rowlane && half == 0 && trow < valid) {
       const bf16 db = __float2bfloat16_rn(db1[trow] + db2s[0][trow] + db2s[1][trow]);
       // with logits, the gradient through the sigmoid as torch's bf16 sigmoid_backward forms it
-      // from the bf16 dbeta and beta: (dbeta * (1 - beta)) * beta in float32, rounded to bf16
+      // from the bf16 dbeta and beta: dbeta * (1 - beta) * beta with every intermediate rounded
+      // to bf16 (its bf16 arithmetic), so the fused result equals sigmoid-then-scan bit for bit
       const float bt = bsm[trow];
-      dbeta[(row0 + trow) * H + h] = logit ? __float2bfloat16_rn((__bfloat162float(db) * (1.0f - bt)) * bt) : db;
+      const float one_minus = __bfloat162float(__float2bfloat16_rn(1.0f - bt));
+      const float t = __bfloat162float(__float2bfloat16_rn(__bfloat162float(db) * one_minus));
+      dbeta[(row0 + trow) * H + h] = logit ? __float2bfloat16_rn(t * bt) : db;
     }
     // stage 5: dK += dG K; then the next chunk's stage 1 (its columns and regions are free)
     if (tid == 0 && ok) {

@@ -634,7 +634,8 @@ int check(const char* what, int B, int NQ, int L, int H, int HKV, int DK, int wi
   VB_REQUIRE(DK % 16 == 0 && DK >= 16 && DK <= 128, "%s: head dimension %d must be a multiple of 16 in [16, 128]",
              what, DK);
   VB_REQUIRE(window >= 1, "%s: window %d must be at least 1", what, window);
-  VB_REQUIRE(dtype == VB_BF16 || dtype == VB_F16, "%s: dtype must be bfloat16 or float16", what);
+  VB_REQUIRE(dtype == VB_BF16 || dtype == VB_F16 || dtype == VB_F32, "%s: dtype must be bfloat16, float16 or float32",
+             what);
   VB_REQUIRE(qpos != nullptr || L >= NQ, "%s: dense queries need L >= NQ (L=%d, NQ=%d)", what, L, NQ);
   VB_REQUIRE(L < (1 << 29) && NQ < (1 << 29), "%s: length exceeds 2^29", what);
   return VB_OK;
@@ -660,6 +661,14 @@ int dispatch(int DK, int dtype, F&& f) {
 }
 
 }  // namespace
+
+// float32 attention on CUDA cores (window_attn_f32.cu)
+int window_attn_f32_fwd(const float* q, const int* qpos, const int* counts, const float* keys, const float* values,
+                        float* o, float* lse, int B, int NQ, int L, int H, int HKV, int DK, int window,
+                        cudaStream_t st);
+int window_attn_f32_bwd(const float* q, const int* qpos, const int* counts, const float* keys, const float* values,
+                        const float* o, const float* lse, const float* dout, float* dq, float* dkeys, float* dvalues,
+                        float* delta, int B, int NQ, int L, int H, int HKV, int DK, int window, cudaStream_t st);
 }  // namespace vb
 
 using namespace vb;
@@ -672,6 +681,9 @@ extern "C" int vb_window_attn_fwd(const void* q, const int* qpos, const int* cou
   if (B == 0 || NQ == 0) return VB_OK;
   VB_REQUIRE(q && keys && values && o && lse && status, "window_attn_fwd: null pointer");
   VB_REQUIRE(L > 0, "window_attn_fwd: no keys for %d queries", NQ);
+  if (dtype == VB_F32)
+    return window_attn_f32_fwd((const float*)q, qpos, counts, (const float*)keys, (const float*)values, (float*)o, lse,
+                               B, NQ, L, H, HKV, DK, window, (cudaStream_t)stream);
   const bool f16 = dtype == VB_F16;
   CUtensorMap qm, km, vm;
   if ((rc = make_token_map(&qm, q, B, NQ, H, DK, f16)) || (rc = make_token_map(&km, keys, B, L, HKV, DK, f16)) ||
@@ -709,12 +721,17 @@ extern "C" int vb_window_attn_bwd(const void* q, const int* qpos, const int* cou
   cudaStream_t st = (cudaStream_t)stream;
   if (B == 0 || L == 0) return VB_OK;
   VB_REQUIRE(dkeys && dvalues, "window_attn_bwd: null pointer");
+  const size_t esize = dtype == VB_F32 ? 4 : 2;
   if (NQ == 0) {
-    VB_CUDA_CHECK(cudaMemsetAsync(dkeys, 0, (size_t)B * L * HKV * DK * 2, st), "window_attn_bwd");
-    VB_CUDA_CHECK(cudaMemsetAsync(dvalues, 0, (size_t)B * L * HKV * DK * 2, st), "window_attn_bwd");
+    VB_CUDA_CHECK(cudaMemsetAsync(dkeys, 0, (size_t)B * L * HKV * DK * esize, st), "window_attn_bwd");
+    VB_CUDA_CHECK(cudaMemsetAsync(dvalues, 0, (size_t)B * L * HKV * DK * esize, st), "window_attn_bwd");
     return VB_OK;
   }
   VB_REQUIRE(q && keys && values && o && lse && dout && dq && workspace && status, "window_attn_bwd: null pointer");
+  if (dtype == VB_F32)
+    return window_attn_f32_bwd((const float*)q, qpos, counts, (const float*)keys, (const float*)values,
+                               (const float*)o, lse, (const float*)dout, (float*)dq, (float*)dkeys, (float*)dvalues,
+                               (float*)workspace, B, NQ, L, H, HKV, DK, window, st);
   VB_REQUIRE(aligned16(o) && aligned16(dq) && aligned16(dkeys) && aligned16(dvalues),
              "window_attn_bwd: tensor not 16-byte aligned");
   const bool f16 = dtype == VB_F16;

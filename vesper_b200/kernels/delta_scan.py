@@ -35,7 +35,8 @@ from vesper_b200 import _lib
 from vesper_b200.contracts import ContractError, Dims, check_shape
 
 MAX_HEAD_DIM = 256
-BF16_MAX_HEAD_DIM = 128  # the chunked kernel pads the head dimension to one 128-wide tile
+BF16_MAX_HEAD_DIM = 128  # the chunked kernel pads the head dimension to one 128-wide tile; wider
+# heads (up to MAX_HEAD_DIM) take the token-serial float32 kernel
 INPUT_DTYPE = torch.bfloat16  # delta_scan_fused's q, k, v, beta
 FP32_INPUT_DTYPE = torch.float32  # delta_scan_fused_fp32's q, k, v, beta
 STATE_DTYPE = torch.float32
@@ -188,22 +189,25 @@ def delta_scan_fused(
         ``(o, state_n)``: ``o [b, n, h, dk]`` in bfloat16 and the state after the last token in
         float32. With no tokens, the empty query tensor and the unchanged state.
 
+    Head dimensions up to 128 that are multiples of 8 run the chunked tcgen05 kernels; the others
+    the contract allows (up to 256) run the token-serial float32 kernels on float32 copies.
+
     Raises:
-        ContractError: on a shape, dtype or device mismatch, or a head dimension above the
-            kernel's bound (128 for this chunked kernel; ``delta_scan_fused_fp32`` takes 256).
+        ContractError: on a shape, dtype or device mismatch, or a head dimension above 256.
     """
     if _checked_length(q, k, v, beta, state, INPUT_DTYPE) == 0:
         return q, state
-    if q.shape[-1] > BF16_MAX_HEAD_DIM or q.shape[-1] % 8 != 0:
-        msg = (
-            f"head dimension {q.shape[-1]} exceeds the chunked kernel's {BF16_MAX_HEAD_DIM}"
-            if q.shape[-1] > BF16_MAX_HEAD_DIM
-            else f"head dimension {q.shape[-1]} must be a multiple of 8"
-        )
-        raise ContractError(msg)
     if shift is not None and not from_logits:
         msg = "shift applies to write-strength logits: pass from_logits=True"
         raise ContractError(msg)
+    if q.shape[-1] > BF16_MAX_HEAD_DIM or q.shape[-1] % 8 != 0:
+        # head dimensions the chunked tiles do not take (above 128, or not a multiple of 8; the
+        # contract allows up to 256): the token-serial float32 kernel on float32 copies of the
+        # inputs, the output back in bfloat16 (exact float32 arithmetic, slower per token)
+        f32 = torch.float32
+        o, sn = delta_scan_fused_fp32(q.to(f32), k.to(f32), v.to(f32), beta.to(f32), state, from_logits=from_logits,
+                                      shift=shift)  # fmt: skip
+        return o.to(INPUT_DTYPE), sn
     o, sn = _ScanBF16.apply(q, k, v, beta, state, bool(from_logits), _checked_shift(shift, q))
     return o, sn
 

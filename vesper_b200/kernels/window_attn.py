@@ -16,8 +16,10 @@ each batch are live. Padding rows get zero output and no gradient, so buffers si
 case keep a captured graph's shapes static while the kernels read the live count.
 
 Forward and backward run on tcgen05 tensor cores (``vb_window_attn_fwd`` / ``_bwd``): online
-softmax in float32 over 128-key tiles, deterministic gradients (no atomics). Inputs are bfloat16
-or float16, as the reference's kernel path takes.
+softmax in float32 over 128-key tiles, deterministic gradients (no atomics), for bfloat16 or
+float16 inputs, as the reference's kernel path takes. float32 inputs (the reference's float32
+path, its blocked masked softmax) run on CUDA cores in float32 FFMA arithmetic through the same
+entry points, so float32 parity holds at float32 rounding.
 """
 
 from __future__ import annotations
@@ -28,7 +30,7 @@ from torch import Tensor
 from vesper_b200 import _lib
 from vesper_b200.contracts import ContractError, Dims, check_shape, require_cuda
 
-WINDOW_DTYPES = (torch.bfloat16, torch.float16)
+WINDOW_DTYPES = (torch.bfloat16, torch.float16, torch.float32)
 MAX_HEAD_DIM = 128
 
 
