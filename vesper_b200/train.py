@@ -165,7 +165,18 @@ class TrainStep:
         self.templates: list[ColumnState] = self.model.init_states(self.b, torch.bfloat16, dev)
         self.state = state_tensors(self.templates)
         self.steps = 0
+        self.filled = False  # the attention windows have their steady shape (after the first chunk)
         self.outputs: list[Tensor] | None = None
+
+    def adopt_states(self, states: list[ColumnState]) -> None:
+        """Take steady-state carried states (a restored checkpoint's) before the first step."""
+        if self.graph is not None:
+            msg = "the step is captured: carried states can only be copied into it"
+            raise ValueError(msg)
+        self.templates = [_detached(s) for s in states]
+        self.state = [t.to(self.device).clone() for t in state_tensors(self.templates)]
+        self.templates = with_state_tensors(self.templates, self.state)
+        self.filled = True
 
     def load(self, tokens: Tensor, targets: Tensor, mask: Tensor | None = None) -> None:
         self.tokens.copy_(tokens, non_blocking=True)
@@ -191,7 +202,7 @@ class TrainStep:
         return [total.detach(), parts["ntp"].detach(), parts["ponder"].detach(), norm, result.n_iters]
 
     def _eager(self) -> list[Tensor]:
-        if self.steps == 0:
+        if not self.filled:
             # the first chunk fills the attention windows: afterwards every state has its steady
             # shape, which the static state tensors (and the capture) take
             self.bucket.zero()
@@ -212,6 +223,7 @@ class TrainStep:
         self.opt.step()
         self.templates = [_detached(s) for s in result.states]
         self.state = [t.clone() for t in state_tensors(self.templates)]
+        self.filled = True
         self.pos.add_(self.n)
         return [total.detach(), parts["ntp"].detach(), parts["ponder"].detach(), norm, result.n_iters]
 
@@ -230,6 +242,18 @@ class TrainStep:
         self.steps += 1
         assert self.bucket.views_intact(), "a gradient left the bucket"
         return out
+
+    def save(self, path) -> object:
+        """Write a checkpoint (``vesper_b200.checkpoint.save``; every rank calls it)."""
+        from vesper_b200 import checkpoint  # noqa: PLC0415
+
+        return checkpoint.save(path, self)
+
+    def restore(self, path) -> dict[str, object]:
+        """Load a checkpoint in place (``vesper_b200.checkpoint.restore``)."""
+        from vesper_b200 import checkpoint  # noqa: PLC0415
+
+        return checkpoint.restore(path, self)
 
     def release(self) -> None:
         """Drop the graph (it holds the NCCL all-reduce) before the process group goes."""
