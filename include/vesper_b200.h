@@ -250,6 +250,22 @@ VB_API int vb_relu_square_bwd(const void *z, const void *dy, void *dz, long long
 VB_API int vb_rotary(const void *x, const long long *pos, const double *inv_freq, void *y,
                      long long tokens, int heads, int dk, int backward, int dtype, void *stream);
 
+/* ---- the head's per-row next-token loss (linear_nll's row steps) ---------------------------
+ * logits: [rows, V] of `dtype` with row stride `stride` (elements); targets: [rows] int64 in
+ * [0, V). vb_nll_row_stats writes float32 top[r] = max_j x[r,j], log_total[r] =
+ * log sum_j exp(x[r,j] - top[r]) and nll[r] = (top[r] - x[r,target]) + log_total[r].
+ * vb_nll_row_grad overwrites the logits in place with
+ * grad[r] * (exp((x - top[r]) - log_total[r]) - onehot(target)), computed in float32.
+ * Replaces vesper/kernels/nll_triton.py:24-103 (row_stats, row_grad_), the row steps of
+ * vesper/kernels/nll.py:48-169 (linear_nll). */
+VB_API int vb_nll_row_stats(const void *logits, int64_t stride, const int64_t *targets, float *top,
+                            float *log_total, float *nll, int64_t rows, int V, int dtype,
+                            void *stream);
+
+VB_API int vb_nll_row_grad(void *logits, int64_t stride, const int64_t *targets, const float *top,
+                           const float *log_total, const float *grad, int64_t rows, int V,
+                           int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

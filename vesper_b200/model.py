@@ -3,10 +3,10 @@ mstampfli/vesper-preview): tied embedding, the loop of columns, final norm, tied
 objective (mean next-token loss over the loss positions plus ``lambda_h`` times the mean ponder).
 
 Same parameters and initialization draws as the reference's ``Vesper`` (embedding, then the
-columns, then the halting head), so its ``state_dict`` loads. The head and the loss are one
-cuBLAS GEMM and torch's cross-entropy per slice of positions (the reference's fused
-``linear_nll`` is outside this build's path); the objective keeps static shapes (every position
-is scored, the ones outside the mask are replaced before the head), so the step can be captured.
+columns, then the halting head), so its ``state_dict`` loads. The head's loss is ``linear_nll``
+per slice of positions (the reference's fused head: cuBLAS matmuls around this library's row
+kernels, no float32 vocabulary logits); the objective keeps static shapes (every position is
+scored, the ones outside the mask are replaced before the head), so the step can be captured.
 """
 
 from __future__ import annotations
@@ -20,6 +20,7 @@ from torch import Tensor, nn
 
 from vesper_b200.column import Column, ColumnShape, ColumnState, RMSNorm, init_column_state
 from vesper_b200.contracts import Dims, check_ids, check_shape
+from vesper_b200.kernels.nll import linear_nll
 from vesper_b200.loop import ExitRule, HaltingHead, Loop, LoopResult
 
 
@@ -74,14 +75,26 @@ class Vesper(nn.Module):
         width = -(-(b * n) // max(slices, 1))
         summed = torch.zeros((), dtype=torch.float32, device=rows.device)
         for s in range(0, b * n, width):
-            x = self.norm_out.forward(rows[None, s : s + width])[0]
-            losses = F.cross_entropy(self.embedding.logits(x).float(), tgt[s : s + width], reduction="none")
+            losses = token_losses(self, rows[s : s + width], tgt[s : s + width])
             summed = summed + torch.where(keep[s : s + width], losses, 0.0).sum()
         count = mask.sum()
         ntp = summed / count
         ponder = torch.where(mask, result.ponder, 0.0).sum() / count
         total = ntp + lambda_h * ponder
         return total, {"ntp": ntp, "ponder": lambda_h * ponder}
+
+
+def token_losses(model: Vesper, y: Tensor, targets: Tensor, *, keep_logits: bool = False) -> Tensor:
+    """Per-token losses ``[...]`` of positions ``y [..., d]`` through the head
+    (``vesper/model.py:314-342``): the head's norm, then ``linear_nll`` over the tied embedding,
+    which keeps no float32 vocabulary logits."""
+    lead = tuple(f"lead{i}" for i in range(y.dim() - 1))
+    dims: Dims = {}
+    check_shape("y", y, (*lead, "d"), dims)
+    check_shape("targets", targets, lead, dims)
+    x = model.norm_out.forward(y.reshape(1, -1, y.shape[-1]))[0]
+    losses = linear_nll(x, model.embedding.weight, targets.reshape(-1), keep_logits=keep_logits)
+    return losses.view(targets.shape)
 
 
 def count_parameters(model: nn.Module) -> int:
