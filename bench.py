@@ -399,6 +399,8 @@ def run_ours(args) -> None:
     torch.cuda.empty_cache()
     config3 = None if args.no_config3 else config3_leg(device, world, args.steps)
     torch.cuda.empty_cache()
+    config5 = None if args.no_config5 else config5_leg(device, world, rank)
+    torch.cuda.empty_cache()
     config1 = config1_leg(device, args.steps) if rank == 0 else None
 
     # --- CPU baseline: the oracle (float64 C port of the reference path) on rank 0 at N=1 ------
@@ -422,7 +424,7 @@ def run_ours(args) -> None:
                 "sharding": "each rank its own (batch x head) units, no collective", "graph": "CUDA graph replay",
             },
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "train_step": train,
-            "config1": config1, "config3": config3,
+            "config1": config1, "config3": config3, "config5": config5,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks.summary(),
@@ -647,6 +649,78 @@ def config3_leg(device, world: int, steps: int) -> dict:
     }  # fmt: skip
 
 
+C5 = {"B": 64, "T": 16384, "decode_steps": 256, "chunk": 2048}  # config 5, the whole job's batch
+
+
+def config5_leg(device, world: int, rank: int) -> dict:
+    """Config 5: long-context inference of the config-4 model in bf16, B=64 rows sharded by batch
+    over the ranks (64 / N rows each, strong scaling): a T=16384-token prefill (chunked forward,
+    2048 tokens a chunk, carried states), then 256 greedy one-token decode steps carrying each
+    head's 64 x 64 state, the key histories and the ring windows (one captured graph per step).
+    Every token runs all 8 passes (the reference decoder's fixed depth, ``DenseRule``). Token ids
+    uniform over [0, 32000). Tokens/s = 64 x (16384 + 256) / the max over ranks of the time.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from vesper_b200 import _lib
+    from vesper_b200.decode import BatchedDecoder
+    from vesper_b200.model import Vesper
+    from vesper_b200.train import VESPER_S
+
+    cfg = VESPER_S
+    b = C5["B"] // world
+    model = Vesper(cfg.shape, cfg.vocab, cfg.columns, cfg.t_max, cfg.halt_epsilon,
+                   torch.Generator().manual_seed(0)).to(device)  # fmt: skip
+    from vesper_b200.column import set_scan
+
+    set_scan(model, "fused")
+    g = torch.Generator(device=device).manual_seed(500 + rank)
+    prompt = torch.randint(0, cfg.vocab, (b, C5["T"]), device=device, generator=g)
+    dec = BatchedDecoder(model, cfg.t_max, cfg.vocab, b, torch.bfloat16, warm=2)
+    # warm-up on a short prompt: the kernels, the allocator and the step's capture
+    dec.prefill(prompt[:, : C5["chunk"]], chunk=C5["chunk"])
+    tok = prompt[:, :1]
+    for _ in range(4):
+        tok, _ = dec.step(tok)
+    torch.cuda.synchronize(device)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    ev[0].record()
+    last = dec.prefill(prompt, chunk=C5["chunk"])
+    ev[1].record()
+    tok = last.argmax(-1)
+    for _ in range(C5["decode_steps"]):
+        tok, _ = dec.step(tok)
+    ev[2].record()
+    torch.cuda.synchronize(device)
+    pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+    if world > 1:
+        t = torch.tensor([pre_ms, dec_ms, pre_ms + dec_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_ms, dec_ms, total_ms = (float(x) for x in t.tolist())
+    else:
+        total_ms = pre_ms + dec_ms
+    _lib.check_status(device)
+    dec.release()
+    steps = C5["decode_steps"]
+    total_b = b * world
+    return {
+        "metric": "long-context inference tokens/s (config 5)",
+        "value": round(total_b * (C5["T"] + steps) / (total_ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "scaling": "strong", "dtype": "bf16 autocast", "data": "synthetic (token ids uniform over [0, 32000))",
+        "prefill": {"tokens_per_s": round(total_b * C5["T"] / (pre_ms / 1e3), 1), "ms": round(pre_ms, 2)},
+        "decode": {"tokens_per_s": round(total_b * steps / (dec_ms / 1e3), 1), "ms_per_step": round(dec_ms / steps, 4),
+                   "steps": steps},
+        "config": {"workload": "config 5: prefill T=16384 then 256 greedy decode steps", "B": total_b,
+                   "rows_per_gpu": b, "T": C5["T"], "prefill_chunk": C5["chunk"], "passes": cfg.t_max,
+                   "exit_rule": "dense (every token all passes, the reference decoder's fixed depth)",
+                   "parallelism": f"batch x{world}", "decode_graph": "one captured CUDA graph per step"},
+    }  # fmt: skip
+
+
 TRAIN_B, TRAIN_T = 32, 2048  # config 4: rows of 2048 tokens per GPU
 
 
@@ -796,6 +870,7 @@ def main() -> None:
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     p.add_argument("--no-train", action="store_true", help="skip the config-4 training-step leg")
     p.add_argument("--no-config3", action="store_true", help="skip the config-3 one-column leg")
+    p.add_argument("--no-config5", action="store_true", help="skip the config-5 inference leg")
     p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")

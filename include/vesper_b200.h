@@ -136,6 +136,18 @@ VB_API int vb_delta_scan_f32_bwd_logits(const float *q, const float *k, const fl
                                         float *dlogits, float *dstate0, void *workspace, int B,
                                         int T, int H, int D, void *stream);
 
+/* One token per (batch, head) applied to the float32 state: the decode step
+ * H' = H + beta k (v - H^T k)^T, o = H'^T q, for q, k, v [B,H,D] and beta [B,H] of `dtype`
+ * (VB_F32 or VB_BF16; bf16 beta, or the sigmoid of bf16 logits with `from_logits`, rounded to
+ * bf16 as the chunked kernels round it), shift [B] float32 or NULL, o [B,H,D] of `dtype`.
+ * state0 and state_n [B,H,D,D] float32 may be the same buffer (an in-place step). D <= 256.
+ * Replaces vesper/recurrence.py:143-163 (delta_scan_step, one token of delta_update + read) as
+ * the batched decode of vesper/decode.py:29-46 (decode_step) reaches it. */
+VB_API int vb_delta_scan_step(const void *q, const void *k, const void *v, const void *beta,
+                              const float *shift, int from_logits, const float *state0,
+                              float *state_n, void *o, int B, int H, int D, int dtype,
+                              void *stream);
+
 /* ---- delta-rule scan, bfloat16 (chunked WY form on tcgen05) -----------------------------------
  * The same recurrence as above with bf16 q, k, v, beta, o [B,T,H,D] / [B,T,H] and float32
  * state0, state_n [B,H,D,D]; 64-token chunks, D <= 128 and a multiple of 8, 16-byte aligned
@@ -249,6 +261,18 @@ VB_API int vb_relu_square_bwd(const void *z, const void *dy, void *dz, long long
  * Replaces the op sequence of vesper/attention.py:178-217 (rotary). */
 VB_API int vb_rotary(const void *x, const long long *pos, const double *inv_freq, void *y,
                      long long tokens, int heads, int dk, int backward, int dtype, void *stream);
+
+/* ---- one-token decoding attention over a ring window ---------------------------------------
+ * q [B,H,DK] (one token per row), k_new, v_new [B,HKV,DK], the ring k, v [B,W,HKV,DK], pos
+ * [B,W] int64, valid [B,W] bytes, the new tokens' positions pos [B] int64; o [B,H,DK]. Every
+ * element tensor is of `dtype`. The token attends the valid slots with p - window < pos <= p and
+ * itself (scale 1/sqrt(DK), head h reading key head h / (H / HKV), H / HKV <= 8, DK <= 128), then
+ * is written IN PLACE into slot p % W (k, v, pos, valid). Replaces vesper/attention.py:298-338
+ * (attend_ring) with :109-139 (kv_ring_write), batched over the rows of a decode step. */
+VB_API int vb_ring_attend(const void *q, const void *k_new, const void *v_new, void *ring_k,
+                          void *ring_v, int64_t *ring_pos, uint8_t *ring_valid, const int64_t *pos,
+                          void *o, int B, int W, int H, int HKV, int DK, int window, int dtype,
+                          void *stream);
 
 /* ---- the head's per-row next-token loss (linear_nll's row steps) ---------------------------
  * logits: [rows, V] of `dtype` with row stride `stride` (elements); targets: [rows] int64 in

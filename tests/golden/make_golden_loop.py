@@ -224,12 +224,56 @@ def config4_fixture() -> None:
           **sums)  # fmt: skip
 
 
+def decode_fixture() -> None:
+    """The reference's one-token decoding (``vesper/decode.py:29-46`` ``decode_step``: the loop at a
+    fixed depth under ``DenseRule`` over ``RingKVCache`` windows, the head on the token) fed two
+    rows token by token: each row's prompt, then its greedy continuation. Float64 on the CPU; the
+    embedding, columns, halting head and output norm drawn in the model's order from the seed."""
+    from vesper.column import RMSNorm as RefRMSNorm  # noqa: PLC0415
+    from vesper.column import init_column_state  # noqa: PLC0415
+    from vesper.loop import DenseRule  # noqa: PLC0415
+
+    columns, t_max, vocab, depth, prompt, gen = 2, 3, 256, 2, 24, 8
+    g = torch.Generator().manual_seed(SEED)
+    emb = TiedEmbedding(vocab, SHAPE.d, g)
+    cols = [Column(SHAPE, g) for _ in range(columns)]
+    loop = Loop(cols, HaltingHead(SHAPE.d, g), SHAPE.d, t_max, 0.01)
+    norm_out = RefRMSNorm(SHAPE.d)
+    sums = {**{f"sum.embedding.{k[4:]}": v for k, v in _param_sums(emb).items()}, **_param_sums(loop)}
+    with torch.no_grad():
+        loop.u.copy_(0.5 * torch.randn(t_max, SHAPE.d, generator=torch.Generator().manual_seed(SEED + 2)))
+    emb, loop, norm_out = emb.to(F64), loop.to(F64), norm_out.to(F64)
+    prompts = torch.randint(0, vocab, (2, prompt), generator=torch.Generator().manual_seed(SEED + 4))
+    logits_all, ids_all = [], []
+    with torch.no_grad():
+        for row in range(2):
+            states = [init_column_state(SHAPE, 1, t_max, F64, torch.device("cpu"), ring=True) for _ in range(columns)]
+            seq = prompts[row].tolist()
+            row_logits = []
+            for i in range(prompt + gen):
+                token = torch.tensor([[seq[i]]])
+                res = loop.forward(emb.embed(token), torch.tensor([[i]]), states, passes=depth,
+                                   exit_rule=DenseRule())  # fmt: skip
+                states = list(res.states)
+                logits = emb.logits(norm_out.forward(res.y[:, -1:]))[0, 0]
+                row_logits.append(logits)
+                if i + 1 >= prompt and len(seq) < prompt + gen:
+                    seq.append(int(logits.argmax()))
+            logits_all.append(torch.stack(row_logits))
+            ids_all.append(torch.tensor(seq))
+    print("decode fixture generated", [t[prompt:].tolist() for t in ids_all])
+    _save("decode_greedy", tokens=torch.stack(ids_all), logits=torch.stack(logits_all), prompt=prompt, gen=gen,
+          depth=depth, vocab=vocab, columns=columns, t_max=t_max, u=loop.u.detach(), **sums)  # fmt: skip
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
-    which = set(sys.argv[1:]) or {"column", "loop", "config4"}
+    which = set(sys.argv[1:]) or {"column", "loop", "config4", "decode"}
     if "column" in which:
         column_fixture()
     if "loop" in which:
         loop_fixtures()
     if "config4" in which:
         config4_fixture()
+    if "decode" in which:
+        decode_fixture()

@@ -7,8 +7,8 @@ Same parameters (``w_q, w_k, w_v, w_o``), layouts and cache semantics as the ref
 In bfloat16 or float16 the softmax runs in the tcgen05 kernel (``vesper_b200.kernels.window_attn``)
 over the cache rows and the chunk directly, in float32 in the same entry points' FFMA kernel (the
 reference's float32 mode, its blocked masked softmax, at float32 rounding); given the loop's
-compaction of the active tokens, either computes only their queries. The decode ring
-(``RingKVCache``) is not part of this build.
+compaction of the active tokens, either computes only their queries. One-token decoding carries
+a ``RingKVCache`` per pass, attended and written by one batched kernel (``attend_ring``).
 """
 
 from __future__ import annotations
@@ -73,6 +73,50 @@ def kv_cache_push(cache: KVCache, k: Tensor, v: Tensor, pos: Tensor) -> KVCache:
         pos=torch.cat([cache.pos[:, m - keep_old :], pos[:, n - keep_new :]], dim=1),
         window=w,
     )
+
+
+@dataclass(frozen=True, slots=True)
+class RingKVCache:
+    """A fixed-capacity window for one-token decoding (``vesper/attention.py:63-82``): ``k, v
+    [b, window, hkv, dk]`` (keys rotated), ``pos [b, window]`` int64, ``valid [b, window]`` bool.
+    A token at position ``p`` lives in slot ``p % window``; slots are not in age order and
+    visibility is ``valid`` with the window mask on positions. Its shapes never change, so a
+    captured decode step carries it; this build's decode step updates it in place."""
+
+    k: Tensor
+    v: Tensor
+    pos: Tensor
+    valid: Tensor
+    window: int
+
+
+def kv_ring_empty(b: int, hkv: int, dk: int, window: int, dtype: torch.dtype, device: torch.device) -> RingKVCache:
+    """Every slot unwritten: zero keys and values, positions 0, valid False (``vesper/attention.py:85-106``)."""
+    if window < 1:
+        msg = f"window must be at least 1, got {window}"
+        raise ValueError(msg)
+    return RingKVCache(
+        k=torch.zeros(b, window, hkv, dk, dtype=dtype, device=device),
+        v=torch.zeros(b, window, hkv, dk, dtype=dtype, device=device),
+        pos=torch.zeros(b, window, dtype=torch.long, device=device),
+        valid=torch.zeros(b, window, dtype=torch.bool, device=device),
+        window=window,
+    )
+
+
+def ring_from_cache(cache: KVCache) -> RingKVCache:
+    """The ring holding a chronological cache's entries, each in slot ``pos % window`` (the
+    switch from a chunked prefill to one-token decoding)."""
+    b, m, hkv, dk = cache.k.shape
+    ring = kv_ring_empty(b, hkv, dk, cache.window, cache.k.dtype, cache.k.device)
+    if m:
+        slot = cache.pos % cache.window  # [b, m]
+        at = slot[:, :, None, None].expand(b, m, hkv, dk)
+        ring.k.scatter_(1, at, cache.k)
+        ring.v.scatter_(1, at, cache.v)
+        ring.pos.scatter_(1, slot, cache.pos)
+        ring.valid.scatter_(1, slot, torch.ones_like(slot, dtype=torch.bool))
+    return ring
 
 
 class WindowedAttention(nn.Module):
@@ -155,6 +199,42 @@ class WindowedAttention(nn.Module):
             oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
             (o,) = expand_rows(compaction, [oc])
         return self.output(o), kv_cache_push(cache, k, v, pos)
+
+    def attend_ring(self, q: Tensor, k: Tensor, v: Tensor, pos: Tensor, ring: RingKVCache) -> tuple[Tensor, RingKVCache]:
+        """One decoding token per row over its ring and itself (``vesper/attention.py:298-338``):
+        ``q [b,1,h,dk]``, ``k, v [b,1,hkv,dk]``, ``pos [b,1]``. One kernel (``vb_ring_attend``)
+        attends and then writes the token into its slot ``pos % window``: the ring is updated IN
+        PLACE and returned (the decode step's carried buffers)."""
+        dims: Dims = {"hkv": self.kv_heads, "dk": self.head_dim, "h": self.heads, "one": 1, "w": self.window}
+        check_shape("q", q, ("b", "one", "h", "dk"), dims)
+        check_shape("k", k, ("b", "one", "hkv", "dk"), dims)
+        check_shape("v", v, ("b", "one", "hkv", "dk"), dims)
+        check_shape("pos", pos, ("b", "one"), dims, dtype=torch.long)
+        check_shape("ring.k", ring.k, ("b", "w", "hkv", "dk"), dims)
+        check_shape("ring.v", ring.v, ("b", "w", "hkv", "dk"), dims)
+        check_shape("ring.pos", ring.pos, ("b", "w"), dims, dtype=torch.long)
+        check_shape("ring.valid", ring.valid, ("b", "w"), dims, dtype=torch.bool)
+        if ring.window != self.window:
+            msg = f"ring window {ring.window} does not match the layer's {self.window}"
+            raise ContractError(msg)
+        if q.device.type != "cuda":
+            msg = f"the ring attention runs on CUDA only, got {q.device}"
+            raise ContractError(msg)
+        dt = ring.k.dtype
+        if dt not in WINDOW_KERNEL_DTYPES or ring.v.dtype != dt:
+            msg = f"ring: dtype must be one of {WINDOW_KERNEL_DTYPES}, got {dt}"
+            raise ContractError(msg)
+        b = dims["b"]
+        qc, kc, vc = (t.to(dt).contiguous() for t in (q, k, v))
+        o = torch.empty_like(qc)
+        from vesper_b200 import _lib  # noqa: PLC0415
+
+        _lib.call(
+            "vb_ring_attend", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), ring.k.data_ptr(), ring.v.data_ptr(),
+            ring.pos.data_ptr(), ring.valid.data_ptr(), pos.contiguous().data_ptr(), o.data_ptr(), b, self.window,
+            self.heads, self.kv_heads, self.head_dim, self.window, _lib.DTYPE_CODE[dt], _lib.stream(q.device),
+        )  # fmt: skip
+        return self.output(o.to(q.dtype)), ring
 
     def forward(self, x: Tensor, pos: Tensor, cache: KVCache) -> tuple[Tensor, KVCache]:
         """``project`` then ``attend``."""

@@ -24,11 +24,16 @@ import torch
 import torch.nn.functional as F  # noqa: N812
 from torch import Tensor, nn
 
-from vesper_b200.attention import KVCache, WindowedAttention, kv_cache_empty
+from vesper_b200.attention import KVCache, RingKVCache, WindowedAttention, kv_cache_empty, kv_ring_empty
 from vesper_b200.contracts import ContractError, Dims, check_shape
 from vesper_b200.kernels.act import relu_square
 from vesper_b200.kernels.compact import compact_index, select_rows
-from vesper_b200.kernels.delta_scan import delta_scan_fused, delta_scan_fused_fp32, fused_scan_available
+from vesper_b200.kernels.delta_scan import (
+    delta_scan_fused,
+    delta_scan_fused_fp32,
+    delta_scan_step_,
+    fused_scan_available,
+)
 from vesper_b200.kernels.keys import fused_keys
 from vesper_b200.kernels.norm import fused_rms_norm
 
@@ -94,30 +99,39 @@ class ColumnState:
     ``key_history[t] [b,K-1,d]`` (``vesper/column.py:429-441``)."""
 
     h: tuple[Tensor, ...]
-    kv: tuple[KVCache, ...]
+    kv: tuple[KVCache | RingKVCache, ...]
     key_history: tuple[Tensor, ...]
 
 
-def init_column_state(shape: ColumnShape, b: int, t_max: int, dtype: torch.dtype, device: torch.device) -> ColumnState:
+def init_column_state(shape: ColumnShape, b: int, t_max: int, dtype: torch.dtype, device: torch.device, *,
+                      ring: bool = False) -> ColumnState:  # fmt: skip
     """Cold state (``vesper/column.py:444-480``): zero states and histories in
-    ``promote_types(dtype, float32)``, empty windows in ``dtype``."""
+    ``promote_types(dtype, float32)``, empty windows in ``dtype`` (``ring``: unwritten rings for
+    one-token decoding)."""
     if t_max < 1:
         msg = f"t_max must be at least 1, got {t_max}"
         raise ValueError(msg)
     dk = shape.head_dim
     sdt = torch.promote_types(dtype, torch.float32)
+    empty = kv_ring_empty if ring else kv_cache_empty
     return ColumnState(
         h=tuple(torch.zeros(b, shape.heads, dk, dk, dtype=sdt, device=device) for _ in range(t_max)),
-        kv=tuple(kv_cache_empty(b, shape.kv_heads, dk, shape.window, dtype, device) for _ in range(t_max)),
+        kv=tuple(empty(b, shape.kv_heads, dk, shape.window, dtype, device) for _ in range(t_max)),
         key_history=tuple(torch.zeros(b, shape.key_history, shape.d, dtype=sdt, device=device) for _ in range(t_max)),
     )
 
 
 def map_state(state: ColumnState, f: Callable[[Tensor], Tensor]) -> ColumnState:
-    """Every tensor of ``state`` through ``f`` in a fixed order (``vesper/column.py:483-502``)."""
+    """Every tensor of ``state`` through ``f`` in a fixed order (``vesper/column.py:500-517``)."""
+
+    def window(c: KVCache | RingKVCache) -> KVCache | RingKVCache:
+        if isinstance(c, RingKVCache):
+            return RingKVCache(k=f(c.k), v=f(c.v), pos=f(c.pos), valid=f(c.valid), window=c.window)
+        return KVCache(k=f(c.k), v=f(c.v), pos=f(c.pos), window=c.window)
+
     return ColumnState(
         h=tuple(f(h) for h in state.h),
-        kv=tuple(KVCache(k=f(c.k), v=f(c.v), pos=f(c.pos), window=c.window) for c in state.kv),
+        kv=tuple(window(c) for c in state.kv),
         key_history=tuple(f(z) for z in state.key_history),
     )
 
@@ -355,6 +369,34 @@ class Column(nn.Module):
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))
         written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
         return x, ColumnState(h=h, kv=kv, key_history=hist), written
+
+    def step_decode(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int) -> Tensor:
+        """One decoding token per row through pass ``pass_index``'s state, updated IN PLACE.
+
+        What ``step`` computes for ``n = 1`` over a ``RingKVCache`` window (``vesper/column.py:
+        709-812`` with ``attend_ring``), with every carried buffer updated where it lies so a
+        captured decode step needs no copies: the recurrent state by the one-token scan kernel
+        (``delta_scan_step_``, the write strength formed from its logits), the key history shifted
+        by one, the ring written by the attention kernel. ``x [b, 1, d]``, ``pos [b, 1]``.
+        """
+        ring = state.kv[pass_index]
+        if not isinstance(ring, RingKVCache):
+            msg = "step_decode carries a RingKVCache window (init_column_state(..., ring=True))"
+            raise ContractError(msg)
+        history, h = state.key_history[pass_index], state.h[pass_index]
+        q, z, v, logits = self.rec.project_logits(self.norm_rec.forward(x))
+        k, _ = self.rec.keys(z, history)
+        if history.shape[1]:
+            with torch.no_grad():
+                history.copy_(torch.cat([history[:, 1:], z.to(history.dtype)], dim=1))
+        dtype = FUSED_INPUT_DTYPES[self.rec.scan_impl]
+        with torch.autocast(device_type=x.device.type, enabled=False):
+            o = delta_scan_step_(q.to(dtype), k.to(dtype), v.to(dtype), logits.to(dtype), h, from_logits=True)
+        x = x + F.linear(o.to(q.dtype).flatten(2), self.rec.w_o)
+        aq, ak, av = self.attn.project(self.norm_attn.forward(x), pos)
+        a, _ = self.attn.attend_ring(aq, ak, av, pos, ring)
+        x = x + a
+        return x + self.ffn.forward(self.norm_ffn.forward(x))
 
     def forward(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int) -> tuple[Tensor, ColumnState]:
         y, new_state, _ = self.step(x, pos, state, pass_index)

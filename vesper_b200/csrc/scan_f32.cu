@@ -23,16 +23,32 @@ __device__ __forceinline__ float beta_at(const float* __restrict__ beta, const f
   const float x = raw + (shift != nullptr ? __ldg(shift + tok) : 0.f);
   return 1.0f / (1.0f + expf(-x));
 }
+// the same for bfloat16 write strengths: beta (or its logits' sigmoid) rounded to bfloat16, as the
+// chunked bfloat16 kernels and torch.sigmoid's bfloat16 output round it
+__device__ __forceinline__ float beta_at(const __nv_bfloat16* __restrict__ beta, const float* __restrict__ shift,
+                                         int logit, int64_t row, int64_t tok) {
+  const float raw = __bfloat162float(beta[row]);
+  if (!logit) return raw;
+  const float x = raw + (shift != nullptr ? __ldg(shift + tok) : 0.f);
+  return __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-x))));
+}
+__device__ __forceinline__ float ld_in(const float* __restrict__ p) { return __ldg(p); }
+__device__ __forceinline__ float ld_in(const __nv_bfloat16* __restrict__ p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void st_out(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_out(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
 constexpr int NWARP = 8;          // warps per CTA
 constexpr int CPW = 4;            // value columns per warp
 constexpr int BV = NWARP * CPW;   // value columns per CTA
 
-template <int NI>
+// E: the element type of q, k, v, beta and o (float32, or bfloat16 for the decode step); the
+// state and the arithmetic are float32. s0 and sn may be the same buffer (an in-place step): each
+// thread reads its state entries before the loop and writes them after it.
+template <int NI, typename E>
 __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
-    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-    const float* __restrict__ beta, const float* __restrict__ shift, int logit, const float* __restrict__ s0,
-    float* __restrict__ o, float* __restrict__ sn, float* __restrict__ resid, int T, int H, int D) {
+    const E* __restrict__ q, const E* __restrict__ k, const E* __restrict__ v,
+    const E* __restrict__ beta, const float* __restrict__ shift, int logit, const float* s0,
+    E* __restrict__ o, float* sn, float* __restrict__ resid, int T, int H, int D) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int jb = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
   const int j0 = jb * BV + warp * CPW;
@@ -49,17 +65,17 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
   }
   for (int t = 0; t < T; ++t) {
     const int64_t row = (((int64_t)b * T + t) * H + h);
-    const float* kp = k + row * D;
-    const float* qp = q + row * D;
+    const E* kp = k + row * D;
+    const E* qp = q + row * D;
     float kk[NI], qq[NI], vv[CPW];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
       const int i = lane + 32 * m;
-      kk[m] = i < D ? __ldg(kp + i) : 0.f;
-      qq[m] = i < D ? __ldg(qp + i) : 0.f;
+      kk[m] = i < D ? ld_in(kp + i) : 0.f;
+      qq[m] = i < D ? ld_in(qp + i) : 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? __ldg(v + row * D + j0 + c) : 0.f;
+    for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? ld_in(v + row * D + j0 + c) : 0.f;
     const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
     float red[CPW];
 #pragma unroll
@@ -100,7 +116,7 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
         if (lane == c) { ov = red[c]; rv = r[c]; }
       const int j = j0 + lane;
       if (j < D) {
-        o[row * D + j] = ov;
+        st_out(o + row * D + j, ov);
         if (resid) resid[row * D + j] = rv;
       }
     }
@@ -344,8 +360,8 @@ int scan_f32_fwd(const float* q, const float* k, const float* v, const float* be
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(njb(D), B * H);
   return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    scan_f32_fwd_kernel<NI><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, shift, logit, state0, o, state_n, resid,
-                                                         T, H, D);
+    scan_f32_fwd_kernel<NI, float><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, shift, logit, state0, o, state_n,
+                                                                resid, T, H, D);
     VB_LAUNCH_CHECK("delta_scan_f32_fwd");
     return VB_OK;
   });
@@ -364,6 +380,33 @@ extern "C" int vb_delta_scan_f32_fwd_logits(const float* q, const float* k, cons
                                             float* o, float* state_n, float* resid, int B, int T, int H, int D,
                                             void* stream) {
   return scan_f32_fwd(q, k, v, beta_logits, shift, 1, state0, o, state_n, resid, B, T, H, D, stream);
+}
+
+extern "C" int vb_delta_scan_step(const void* q, const void* k, const void* v, const void* beta,
+                                  const float* shift, int from_logits, const float* state0, float* state_n, void* o,
+                                  int B, int H, int D, int dtype, void* stream) {
+  int rc = check(B, 1, H, D);
+  if (rc) return rc;
+  if (B == 0 || H == 0) return VB_OK;
+  VB_REQUIRE(q && k && v && beta && state0 && state_n && o, "delta_scan_step: null pointer");
+  VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16, "delta_scan_step: dtype must be float32 or bfloat16");
+  cudaStream_t st = (cudaStream_t)stream;
+  dim3 grid(njb(D), B * H);
+  const int logit = from_logits ? 1 : 0;
+  return VB_NI_DISPATCH(D, NI, [&]() -> int {
+    if (dtype == VB_F32) {
+      scan_f32_fwd_kernel<NI, float><<<grid, NWARP * 32, 0, st>>>(
+          (const float*)q, (const float*)k, (const float*)v, (const float*)beta, shift, logit, state0, (float*)o,
+          state_n, nullptr, 1, H, D);
+    } else {
+      using bf = __nv_bfloat16;
+      scan_f32_fwd_kernel<NI, bf><<<grid, NWARP * 32, 0, st>>>((const bf*)q, (const bf*)k, (const bf*)v,
+                                                               (const bf*)beta, shift, logit, state0, (bf*)o,
+                                                               state_n, nullptr, 1, H, D);
+    }
+    VB_LAUNCH_CHECK("delta_scan_step");
+    return VB_OK;
+  });
 }
 
 extern "C" size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D) {

@@ -292,3 +292,41 @@ def delta_scan_fused_fp32(
         raise ContractError(msg)
     o, sn = _ScanF32.apply(q, k, v, beta, state, bool(from_logits), _checked_shift(shift, q))
     return o, sn
+
+
+# --- one token, in place (the decode step) ---------------------------------------------------------
+
+
+def delta_scan_step_(
+    q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, *, from_logits: bool = False,
+    shift: Tensor | None = None,
+) -> Tensor:  # fmt: skip
+    """One token per (batch, head) applied to ``state`` IN PLACE; returns ``o``.
+
+    ``delta_scan_step`` of ``vesper/recurrence.py:143-163`` batched for a decode step:
+    ``H' = H + beta k (v - H^T k)^T``, ``o = H'^T q``. ``q, k, v [b, 1, h, dk]`` (or
+    ``[b, h, dk]``) and ``beta [b, 1, h]`` in float32 or bfloat16 (``from_logits``: the logits,
+    ``shift [b, 1]`` optional), ``state [b, h, dk, dk]`` float32, contiguous; ``o`` has ``q``'s
+    shape and dtype. No autograd: the decode step's carried state is updated where it lies.
+    """
+    dt = q.dtype
+    if dt not in (torch.float32, torch.bfloat16):
+        msg = f"q: dtype must be float32 or bfloat16, got {dt}"
+        raise ContractError(msg)
+    b, h, d = q.shape[0], q.shape[-2], q.shape[-1]
+    if q.numel() != b * h * d or k.numel() != b * h * d or v.numel() != b * h * d or beta.numel() != b * h:
+        msg = f"delta_scan_step_: one token per row and head expected, got q {tuple(q.shape)}"
+        raise ContractError(msg)
+    check_shape("state", state, ("b", "h", "dk", "dk"), {"b": b, "h": h, "dk": d}, STATE_DTYPE)
+    if not state.is_contiguous():
+        msg = "state must be contiguous (it is updated in place)"
+        raise ContractError(msg)
+    qc, kc, vc, bc = (t.to(dt).contiguous() for t in (q, k, v, beta))
+    sh = None if shift is None else shift.to(torch.float32).contiguous()
+    o = torch.empty_like(qc)
+    _lib.call(
+        "vb_delta_scan_step", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), bc.data_ptr(), _lib.ptr(sh),
+        1 if from_logits else 0, state.data_ptr(), state.data_ptr(), o.data_ptr(), b, h, d, _lib.DTYPE_CODE[dt],
+        _lib.stream(q.device),
+    )  # fmt: skip
+    return o

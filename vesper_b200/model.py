@@ -54,8 +54,13 @@ class Vesper(nn.Module):
         self.norm_out = RMSNorm(shape.d)
         self.shape, self.columns, self.t_max = shape, columns, t_max
 
-    def init_states(self, b: int, dtype: torch.dtype, device: torch.device) -> list[ColumnState]:
-        return [init_column_state(self.shape, b, self.t_max, dtype, device) for _ in range(self.columns)]
+    def init_states(self, b: int, dtype: torch.dtype, device: torch.device, *, ring: bool = False) -> list[ColumnState]:
+        return [init_column_state(self.shape, b, self.t_max, dtype, device, ring=ring) for _ in range(self.columns)]
+
+    def head(self, y: Tensor) -> Tensor:
+        """Outputs ``[b, n, d]`` to logits ``[b, n, V]``: the output norm, then the tied embedding
+        (``vesper/model.py:128-141``)."""
+        return self.embedding.logits(self.norm_out.forward(y))
 
     def run(self, tokens: Tensor, pos: Tensor, states: Sequence[ColumnState], passes: int | None = None, *,
             recompute: bool = False, exit_rule: ExitRule | None = None) -> LoopResult:  # fmt: skip
