@@ -10,11 +10,13 @@
 // and rewritten afterwards with the new key, value, position and valid flag, so the CTAs of one
 // row never read what another is writing.
 //
-// One CTA of eight warps per (row, key head): the warps split the ring's slots and each walks its
-// share for every query head of the group at once (a slot's key and value are loaded once, with
-// lane l holding elements l, l + 32, ... of each DK-vector; the group's scores are warp sums in
-// flight together), keeping a running float32 (max, sum, output) per head; the warps' partial
-// results are then merged in a fixed order.
+// One CTA of 256 threads per (row, key head), in three phases over the W + 1 candidate keys (the
+// ring's slots and the new token, index W): (1) each thread takes whole slots and forms the
+// group's scores from the slot's key row (16-byte vector loads of eight elements; the queries are
+// in shared memory), -inf for a slot that is not visible; (2) warp g reduces head g's scores to their max
+// and sum and turns them into probabilities; (3) each thread owns output elements (head, channel)
+// and sums probability x value over the keys in slot order, the value rows read coalesced.
+// Deterministic (fixed-order sums), no atomics.
 #include <cmath>
 #include <type_traits>
 
@@ -23,113 +25,115 @@
 namespace vb {
 namespace {
 
-constexpr int NE = 4;      // DK <= 128
-constexpr int WARPS = 8;   // slot-splitting warps per CTA
-constexpr int GMAX = 8;    // query heads per key head
+constexpr int NT = 256;
+constexpr int GMAX = 8;     // query heads per key head
+constexpr int WMAX = 1024;  // ring slots
+constexpr int DKMAX = 128;
 
+// eight consecutive elements (16-byte aligned) as floats
+__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), c = *reinterpret_cast<const float4*>(p + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
+}
 template <typename E>
-__device__ __forceinline__ void load_row(const E* __restrict__ p, int DK, float (&x)[NE]) {
-  const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void load8(const E* p, float (&x)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const E* e = reinterpret_cast<const E*>(&raw);
 #pragma unroll
-  for (int e = 0; e < NE; ++e) {
-    const int d = lane + 32 * e;
-    x[e] = d < DK ? to_f32<E>(p[d]) : 0.f;
-  }
+  for (int i = 0; i < 8; ++i) x[i] = to_f32<E>(e[i]);
 }
 
-template <typename E, int G>
-__global__ void __launch_bounds__(WARPS * 32) ring_attn_kernel(
+template <typename E>
+__global__ void __launch_bounds__(NT) ring_attn_kernel(
     const E* __restrict__ q, const E* __restrict__ k_new, const E* __restrict__ v_new, E* ring_k, E* ring_v,
     int64_t* ring_pos, uint8_t* ring_valid, const int64_t* __restrict__ pos, E* __restrict__ o, int W, int H,
     int HKV, int DK, int window, float scale) {
-  __shared__ float sm_m[WARPS][G], sm_l[WARPS][G], sm_acc[WARPS][G][32 * NE];
-  const int b = blockIdx.x, kh = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  extern __shared__ float smem[];
+  const int G = H / HKV;
+  float* qs = smem;             // [G][DK]
+  float* ps = smem + G * DK;    // [G][W + 1]
+  const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int64_t p = pos[b];
   const int own = (int)(p % W);
-  float qv[G][NE], m[G], l[G], acc[G][NE];
+  for (int e = tid; e < G * DK; e += NT) qs[e] = to_f32<E>(q[((int64_t)b * H + kh * G) * DK + e]);
+  __syncthreads();
+  // (1) scores
+  for (int s = tid; s <= W; s += NT) {
+    const E* krow;
+    bool vis;
+    if (s == W) {
+      krow = k_new + ((int64_t)b * HKV + kh) * DK;
+      vis = true;
+    } else {
+      vis = s != own && ring_valid[(int64_t)b * W + s];
+      if (vis) {
+        const int64_t kp = ring_pos[(int64_t)b * W + s];
+        vis = kp <= p && kp > p - window;
+      }
+      krow = ring_k + (((int64_t)b * W + s) * HKV + kh) * DK;
+    }
+    float acc[GMAX];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    load_row(q + ((int64_t)b * H + kh * G + g) * DK, DK, qv[g]);
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+    for (int g = 0; g < GMAX; ++g) acc[g] = 0.f;
+    if (vis) {
+      for (int d0 = 0; d0 < DK; d0 += 8) {
+        float kv[8];
+        load8(krow + d0, kv);
 #pragma unroll
-    for (int e = 0; e < NE; ++e) acc[g][e] = 0.f;
-  }
-  auto visit = [&](const float (&kv)[NE], const float (&vv)[NE]) {
-    float s[G];
+        for (int g = 0; g < GMAX; ++g) {
+          if (g < G) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float a = 0.f;
-#pragma unroll
-      for (int e = 0; e < NE; ++e) a = fmaf(qv[g][e], kv[e], a);
-      s[g] = a;
+            for (int i = 0; i < 8; ++i) acc[g] = fmaf(qs[g * DK + d0 + i], kv[i], acc[g]);
+          }
+        }
+      }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int g = 0; g < G; ++g) s[g] += __shfl_xor_sync(0xffffffffu, s[g], off);
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float sc = s[g] * scale;
-      const float mn = fmaxf(m[g], sc);
-      const float c = expf(m[g] - mn), pj = expf(sc - mn);
-      l[g] = fmaf(l[g], c, pj);
-#pragma unroll
-      for (int e = 0; e < NE; ++e) acc[g][e] = fmaf(acc[g][e], c, pj * vv[e]);
-      m[g] = mn;
+    for (int g = 0; g < GMAX; ++g)
+      if (g < G) ps[g * (W + 1) + s] = vis ? acc[g] * scale : -INFINITY;
+  }
+  __syncthreads();
+  // (2) probabilities, head g by warp g
+  if (warp < G) {
+    float* row = ps + warp * (W + 1);
+    float m = -INFINITY;
+    for (int s = lane; s <= W; s += 32) m = fmaxf(m, row[s]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int s = lane; s <= W; s += 32) {
+      const float e = row[s] == -INFINITY ? 0.f : expf(row[s] - m);
+      row[s] = e;
+      l += e;
     }
-  };
-  float kv[NE], vv[NE];
-  if (warp == 0) {  // the new token: always visible
-    load_row(k_new + ((int64_t)b * HKV + kh) * DK, DK, kv);
-    load_row(v_new + ((int64_t)b * HKV + kh) * DK, DK, vv);
-    visit(kv, vv);
+    l = warp_sum(l);
+    const float inv = 1.0f / l;
+    for (int s = lane; s <= W; s += 32) row[s] *= inv;
   }
-  for (int slot = warp; slot < W; slot += WARPS) {
-    if (slot == own || !ring_valid[(int64_t)b * W + slot]) continue;
-    const int64_t kp = ring_pos[(int64_t)b * W + slot];
-    if (kp > p || kp <= p - window) continue;
-    const int64_t base = (((int64_t)b * W + slot) * HKV + kh) * DK;
-    load_row(ring_k + base, DK, kv);
-    load_row(ring_v + base, DK, vv);
-    visit(kv, vv);
-  }
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
-#pragma unroll
-    for (int e = 0; e < NE; ++e) sm_acc[warp][g][lane + 32 * e] = acc[g][e];
-  }
-  __syncthreads();  // every warp has read the ring and left its partial result
-  if (warp < G) {  // warp g merges head g's partials in warp order
-    const int g = warp;
-    float M = -INFINITY;
-    for (int w = 0; w < WARPS; ++w) M = fmaxf(M, sm_m[w][g]);
-    float L = 0.f, out[NE] = {0.f, 0.f, 0.f, 0.f};
-    for (int w = 0; w < WARPS; ++w) {
-      const float f = sm_m[w][g] == -INFINITY ? 0.f : expf(sm_m[w][g] - M);
-      L = fmaf(sm_l[w][g], f, L);
-#pragma unroll
-      for (int e = 0; e < NE; ++e) out[e] = fmaf(sm_acc[w][g][lane + 32 * e], f, out[e]);
+  __syncthreads();
+  // (3) outputs: element (g, d) = sum_s p[g][s] v[s][d]
+  for (int e = tid; e < G * DK; e += NT) {
+    const int g = e / DK, d = e % DK;
+    const float* row = ps + g * (W + 1);
+    float acc = row[W] * to_f32<E>(v_new[((int64_t)b * HKV + kh) * DK + d]);
+    const E* vcol = ring_v + ((int64_t)b * W * HKV + kh) * DK + d;
+#pragma unroll 8
+    for (int s = 0; s < W; ++s) {
+      const float pr = row[s];
+      if (pr != 0.f) acc = fmaf(pr, to_f32<E>(vcol[(int64_t)s * HKV * DK]), acc);
     }
-    const float inv = 1.0f / L;
-#pragma unroll
-    for (int e = 0; e < NE; ++e) {
-      const int d = lane + 32 * e;
-      if (d < DK) o[((int64_t)b * H + kh * G + g) * DK + d] = from_f32<E>(out[e] * inv);
-    }
+    o[((int64_t)b * H + kh * G + g) * DK + d] = from_f32<E>(acc);
   }
-  if (warp == WARPS - 1) {  // the new token takes its slot (no warp of any CTA reads that slot)
+  __syncthreads();  // every thread has read the ring
+  // the new token takes its slot (no CTA of this row reads that slot)
+  for (int d = tid; d < DK; d += NT) {
     const int64_t base = (((int64_t)b * W + own) * HKV + kh) * DK;
-    for (int d = lane; d < DK; d += 32) {
-      ring_k[base + d] = k_new[((int64_t)b * HKV + kh) * DK + d];
-      ring_v[base + d] = v_new[((int64_t)b * HKV + kh) * DK + d];
-    }
-    if (kh == 0 && lane == 0) {
-      ring_pos[(int64_t)b * W + own] = p;
-      ring_valid[(int64_t)b * W + own] = 1;
-    }
+    ring_k[base + d] = k_new[((int64_t)b * HKV + kh) * DK + d];
+    ring_v[base + d] = v_new[((int64_t)b * HKV + kh) * DK + d];
+  }
+  if (kh == 0 && tid == 0) {
+    ring_pos[(int64_t)b * W + own] = p;
+    ring_valid[(int64_t)b * W + own] = 1;
   }
 }
 
@@ -143,34 +147,27 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
                               int H, int HKV, int DK, int window, int dtype, void* stream) {
   VB_REQUIRE(B >= 0 && W >= 1 && H >= 1 && HKV >= 1 && H % HKV == 0 && H / HKV <= GMAX,
              "ring_attend: bad shape B=%d W=%d H=%d HKV=%d", B, W, H, HKV);
-  VB_REQUIRE(DK >= 1 && DK <= 32 * NE, "ring_attend: head dimension %d must lie in [1, %d]", DK, 32 * NE);
+  VB_REQUIRE(DK >= 8 && DK <= DKMAX && DK % 8 == 0, "ring_attend: head dimension %d must be a multiple of 8 in [8, %d]",
+             DK, DKMAX);
+  VB_REQUIRE(aligned16(k_new) && aligned16(ring_k), "ring_attend: keys not 16-byte aligned");
   VB_REQUIRE(window >= 1, "ring_attend: window %d must be at least 1", window);
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16 || dtype == VB_F16, "ring_attend: unsupported dtype %d", dtype);
   if (B == 0) return VB_OK;
   VB_REQUIRE(q && k_new && v_new && ring_k && ring_v && ring_pos && ring_valid && pos && o,
              "ring_attend: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
+  VB_REQUIRE(W <= WMAX, "ring_attend: %d slots exceed %d", W, WMAX);
   const dim3 grid(B, HKV);
   const float scale = 1.0f / sqrtf((float)DK);
   const int G = H / HKV;
+  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1));
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    auto launch = [&](auto gc) -> int {
-      constexpr int GG = decltype(gc)::value;
-      ring_attn_kernel<T, GG><<<grid, WARPS * 32, 0, st>>>((const T*)q, (const T*)k_new, (const T*)v_new,
-                                                           (T*)ring_k, (T*)ring_v, ring_pos, ring_valid, pos, (T*)o,
-                                                           W, H, HKV, DK, window, scale);
-      VB_LAUNCH_CHECK("ring_attend");
-      return VB_OK;
-    };
-    switch (G) {
-      case 1: return launch(std::integral_constant<int, 1>{});
-      case 2: return launch(std::integral_constant<int, 2>{});
-      case 3: return launch(std::integral_constant<int, 3>{});
-      case 4: return launch(std::integral_constant<int, 4>{});
-      case 5: return launch(std::integral_constant<int, 5>{});
-      case 6: return launch(std::integral_constant<int, 6>{});
-      case 7: return launch(std::integral_constant<int, 7>{});
-      default: return launch(std::integral_constant<int, 8>{});
-    }
+    VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                  "ring_attend: smem attribute");
+    ring_attn_kernel<T><<<grid, NT, smem, st>>>((const T*)q, (const T*)k_new, (const T*)v_new, (T*)ring_k,
+                                               (T*)ring_v, ring_pos, ring_valid, pos, (T*)o, W, H, HKV, DK, window,
+                                               scale);
+    VB_LAUNCH_CHECK("ring_attend");
+    return VB_OK;
   });
 }

@@ -327,6 +327,71 @@ __global__ void scan_f32_finish_kernel(const float* __restrict__ k, const float*
   if (lane == 0) dbeta[row] = logit ? (dotk * (1.0f - bt)) * bt : dotk;
 }
 
+// ---- the one-token step (decode) -------------------------------------------------------------
+// One CTA of 256 threads per (batch, head): thread t owns the 4-column group j4 = t % (D/4) of
+// rows i = t / (D/4) + s * NS (NS = 256 / (D/4) row slices), so every state access is a coalesced
+// float4. Pass 1 forms a = H^T k and c = H^T q (partials per slice, summed in slice order through
+// shared memory); then r = v - a, o = c + beta (k.q) r (= H'^T q for H' = H + beta k r^T), and
+// pass 2 writes H' (the second read of H comes from L2). D a multiple of 4, at most 256.
+constexpr int ST = 256;
+
+template <typename E>
+__global__ void __launch_bounds__(ST) delta_step_kernel(const E* __restrict__ q, const E* __restrict__ k,
+                                                        const E* __restrict__ v, const E* __restrict__ beta,
+                                                        const float* __restrict__ shift, int logit, const float* s0,
+                                                        float* sn, E* __restrict__ o, int H, int D) {
+  __shared__ float ks[256], qs[256], red[2][ST * 4];
+  const int bh = blockIdx.x, b = bh / H, tid = threadIdx.x;
+  const int quads = D / 4, NS = ST / quads, j4 = tid % quads, slice = tid / quads;
+  const int64_t row = bh;  // token row (b * 1 + 0) * H + h
+  for (int i = tid; i < D; i += ST) {
+    ks[i] = ld_in(k + row * D + i);
+    qs[i] = ld_in(q + row * D + i);
+  }
+  __syncthreads();
+  const float* S = s0 + (int64_t)bh * D * D;
+  float a[4] = {0.f, 0.f, 0.f, 0.f}, c[4] = {0.f, 0.f, 0.f, 0.f};
+  if (slice < NS) {
+    for (int i = slice; i < D; i += NS) {
+      const float4 w = *reinterpret_cast<const float4*>(S + (int64_t)i * D + 4 * j4);
+      const float ki = ks[i], qi = qs[i];
+      a[0] = fmaf(w.x, ki, a[0]); a[1] = fmaf(w.y, ki, a[1]); a[2] = fmaf(w.z, ki, a[2]); a[3] = fmaf(w.w, ki, a[3]);
+      c[0] = fmaf(w.x, qi, c[0]); c[1] = fmaf(w.y, qi, c[1]); c[2] = fmaf(w.z, qi, c[2]); c[3] = fmaf(w.w, qi, c[3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      red[0][slice * D + 4 * j4 + e] = a[e];
+      red[1][slice * D + 4 * j4 + e] = c[e];
+    }
+  }
+  float kq = 0.f;  // k . q, every thread the same fixed-order sum
+  for (int i = 0; i < D; ++i) kq = fmaf(ks[i], qs[i], kq);
+  __syncthreads();
+  const float bt = beta_at(beta, shift, logit, row, (int64_t)b);
+  // r and o for this thread's 4 columns (every slice holds them; slice 0 writes o)
+  float r[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int j = 4 * j4 + e;
+    float aj = 0.f, cj = 0.f;
+    for (int t = 0; t < NS; ++t) {
+      aj += red[0][t * D + j];
+      cj += red[1][t * D + j];
+    }
+    r[e] = ld_in(v + row * D + j) - aj;
+    if (slice == 0) st_out(o + row * D + j, fmaf(bt * kq, r[e], cj));
+  }
+  if (slice < NS) {
+    float* Sn = sn + (int64_t)bh * D * D;
+    for (int i = slice; i < D; i += NS) {
+      float4 w = *reinterpret_cast<const float4*>(S + (int64_t)i * D + 4 * j4);
+      const float bk = bt * ks[i];
+      w.x = fmaf(bk, r[0], w.x); w.y = fmaf(bk, r[1], w.y); w.z = fmaf(bk, r[2], w.z); w.w = fmaf(bk, r[3], w.w);
+      *reinterpret_cast<float4*>(Sn + (int64_t)i * D + 4 * j4) = w;
+    }
+  }
+}
+
 int njb(int D) { return (D + BV - 1) / BV; }
 
 int check(int B, int T, int H, int D) {
@@ -388,25 +453,23 @@ extern "C" int vb_delta_scan_step(const void* q, const void* k, const void* v, c
   int rc = check(B, 1, H, D);
   if (rc) return rc;
   if (B == 0 || H == 0) return VB_OK;
+  VB_REQUIRE(D % 4 == 0, "delta_scan_step: head dimension %d must be a multiple of 4", D);
   VB_REQUIRE(q && k && v && beta && state0 && state_n && o, "delta_scan_step: null pointer");
+  VB_REQUIRE(aligned16(state0) && aligned16(state_n), "delta_scan_step: state not 16-byte aligned");
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16, "delta_scan_step: dtype must be float32 or bfloat16");
   cudaStream_t st = (cudaStream_t)stream;
-  dim3 grid(njb(D), B * H);
   const int logit = from_logits ? 1 : 0;
-  return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    if (dtype == VB_F32) {
-      scan_f32_fwd_kernel<NI, float><<<grid, NWARP * 32, 0, st>>>(
-          (const float*)q, (const float*)k, (const float*)v, (const float*)beta, shift, logit, state0, (float*)o,
-          state_n, nullptr, 1, H, D);
-    } else {
-      using bf = __nv_bfloat16;
-      scan_f32_fwd_kernel<NI, bf><<<grid, NWARP * 32, 0, st>>>((const bf*)q, (const bf*)k, (const bf*)v,
-                                                               (const bf*)beta, shift, logit, state0, (bf*)o,
-                                                               state_n, nullptr, 1, H, D);
-    }
-    VB_LAUNCH_CHECK("delta_scan_step");
-    return VB_OK;
-  });
+  const unsigned grid = (unsigned)(B * H);
+  if (dtype == VB_F32) {
+    delta_step_kernel<float><<<grid, ST, 0, st>>>((const float*)q, (const float*)k, (const float*)v,
+                                                  (const float*)beta, shift, logit, state0, state_n, (float*)o, H, D);
+  } else {
+    using bf = __nv_bfloat16;
+    delta_step_kernel<bf><<<grid, ST, 0, st>>>((const bf*)q, (const bf*)k, (const bf*)v, (const bf*)beta, shift,
+                                               logit, state0, state_n, (bf*)o, H, D);
+  }
+  VB_LAUNCH_CHECK("delta_scan_step");
+  return VB_OK;
 }
 
 extern "C" size_t vb_delta_scan_f32_bwd_workspace(int B, int T, int H, int D) {
