@@ -117,11 +117,18 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
     const float* row = ps + g * (W + 1);
     float acc = row[W] * to_f32<E>(v_new[((int64_t)b * HKV + kh) * DK + d]);
     const E* vcol = ring_v + ((int64_t)b * W * HKV + kh) * DK + d;
-#pragma unroll 8
-    for (int s = 0; s < W; ++s) {
-      const float pr = row[s];
-      if (pr != 0.f) acc = fmaf(pr, to_f32<E>(vcol[(int64_t)s * HKV * DK]), acc);
+    // unconditional loads (a slot that is not visible has probability exactly 0 and finite
+    // values), eight in flight: a load under a test of the probability would serialise them
+    const int64_t stride = (int64_t)HKV * DK;
+    int s = 0;
+    for (; s + 8 <= W; s += 8) {
+      float vv[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) vv[u] = to_f32<E>(vcol[(s + u) * stride]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = fmaf(row[s + u], vv[u], acc);
     }
+    for (; s < W; ++s) acc = fmaf(row[s], to_f32<E>(vcol[s * stride]), acc);
     o[((int64_t)b * H + kh * G + g) * DK + d] = from_f32<E>(acc);
   }
   __syncthreads();  // every thread has read the ring
