@@ -14,8 +14,9 @@
 // ring's slots and the new token, index W): (1) each thread takes whole slots and forms the
 // group's scores from the slot's key row (16-byte vector loads of eight elements; the queries are
 // in shared memory), -inf for a slot that is not visible; (2) warp g reduces head g's scores to their max
-// and sum and turns them into probabilities; (3) each thread owns output elements (head, channel)
-// and sums probability x value over the keys in slot order, the value rows read coalesced.
+// and sum and turns them into probabilities; (3) each warp takes a share of the slots and sums
+// probability x value for every head of the group (lane l holding channels l, l + 32, ...: the
+// value rows read coalesced), and the warps' partial sums are added in warp order.
 // Deterministic (fixed-order sums), no atomics.
 #include <cmath>
 #include <type_traits>
@@ -111,25 +112,45 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
     for (int s = lane; s <= W; s += 32) row[s] *= inv;
   }
   __syncthreads();
-  // (3) outputs: element (g, d) = sum_s p[g][s] v[s][d]
-  for (int e = tid; e < G * DK; e += NT) {
-    const int g = e / DK, d = e % DK;
-    const float* row = ps + g * (W + 1);
-    float acc = row[W] * to_f32<E>(v_new[((int64_t)b * HKV + kh) * DK + d]);
-    const E* vcol = ring_v + ((int64_t)b * W * HKV + kh) * DK + d;
-    // unconditional loads (a slot that is not visible has probability exactly 0 and finite
-    // values), eight in flight: a load under a test of the probability would serialise them
-    const int64_t stride = (int64_t)HKV * DK;
-    int s = 0;
-    for (; s + 8 <= W; s += 8) {
-      float vv[8];
+  // (3) outputs: warp w sums its share of the slots (s = w, w + 8, ...) for every head of the
+  // group, lane l holding channels l, l + 32, ...; the warps' partial sums are added in warp order
+  constexpr int NE = DKMAX / 32;
+  float acc[GMAX][NE];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) vv[u] = to_f32<E>(vcol[(s + u) * stride]);
+  for (int g = 0; g < GMAX; ++g)
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc = fmaf(row[s + u], vv[u], acc);
+    for (int e = 0; e < NE; ++e) acc[g][e] = 0.f;
+  const int64_t stride = (int64_t)HKV * DK;
+  const E* vbase = ring_v + ((int64_t)b * W * HKV + kh) * DK;
+  auto add_row = [&](const E* vrow, int s) {
+    float vv[NE];
+#pragma unroll
+    for (int e = 0; e < NE; ++e) vv[e] = lane + 32 * e < DK ? to_f32<E>(vrow[lane + 32 * e]) : 0.f;
+#pragma unroll
+    for (int g = 0; g < GMAX; ++g) {
+      if (g < G) {
+        const float pr = ps[g * (W + 1) + s];
+#pragma unroll
+        for (int e = 0; e < NE; ++e) acc[g][e] = fmaf(pr, vv[e], acc[g][e]);
+      }
     }
-    for (; s < W; ++s) acc = fmaf(row[s], to_f32<E>(vcol[s * stride]), acc);
-    o[((int64_t)b * H + kh * G + g) * DK + d] = from_f32<E>(acc);
+  };
+  if (warp == 0) add_row(v_new + ((int64_t)b * HKV + kh) * DK, W);
+  // unconditional loads (a slot that is not visible has probability exactly 0 and finite values)
+#pragma unroll 4
+  for (int s = warp; s < W; s += NT / 32) add_row(vbase + s * stride, s);
+  float* part = ps + G * (W + 1);  // [NT/32][G][DK]
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g)
+    if (g < G)
+#pragma unroll
+      for (int e = 0; e < NE; ++e)
+        if (lane + 32 * e < DK) part[(warp * G + g) * DK + lane + 32 * e] = acc[g][e];
+  __syncthreads();
+  for (int e = tid; e < G * DK; e += NT) {
+    float sum = 0.f;
+    for (int w = 0; w < NT / 32; ++w) sum += part[w * G * DK + e];
+    o[((int64_t)b * H + kh * G) * DK + e] = from_f32<E>(sum);
   }
   __syncthreads();  // every thread has read the ring
   // the new token takes its slot (no CTA of this row reads that slot)
@@ -167,7 +188,7 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
   const dim3 grid(B, HKV);
   const float scale = 1.0f / sqrtf((float)DK);
   const int G = H / HKV;
-  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1));
+  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1) + (size_t)(NT / 32) * G * DK);
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
     VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                   "ring_attend: smem attribute");
