@@ -10,10 +10,10 @@
 // and rewritten afterwards with the new key, value, position and valid flag, so the CTAs of one
 // row never read what another is writing.
 //
-// One CTA of 256 threads per (row, key head), in three phases over the W + 1 candidate keys (the
-// ring's slots and the new token, index W): (1) each thread takes whole slots and forms the
-// group's scores from the slot's key row (16-byte vector loads of eight elements; the queries are
-// in shared memory), -inf for a slot that is not visible; (2) warp g reduces head g's scores to their max
+// One CTA of 16 warps per (row, key head), in three phases over the W + 1 candidate keys (the
+// ring's slots and the new token, index W): (1) each warp takes a share of the slots and forms
+// the group's scores for each (lane l holding channels l, l + 32, ... of the queries and the key
+// row; the scores are warp sums), -inf for a slot that is not visible; (2) warp g reduces head g's scores to their max
 // and sum and turns them into probabilities; (3) each warp takes a share of the slots and sums
 // probability x value for every head of the group (lane l holding channels l, l + 32, ...: the
 // value rows read coalesced), and the warps' partial sums are added in warp order.
@@ -26,23 +26,10 @@
 namespace vb {
 namespace {
 
-constexpr int NT = 256;
+constexpr int NT = 512;
 constexpr int GMAX = 8;     // query heads per key head
 constexpr int WMAX = 1024;  // ring slots
 constexpr int DKMAX = 128;
-
-// eight consecutive elements (16-byte aligned) as floats
-__device__ __forceinline__ void load8(const float* p, float (&x)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p), c = *reinterpret_cast<const float4*>(p + 4);
-  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
-}
-template <typename E>
-__device__ __forceinline__ void load8(const E* p, float (&x)[8]) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const E* e = reinterpret_cast<const E*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = to_f32<E>(e[i]);
-}
 
 template <typename E>
 __global__ void __launch_bounds__(NT) ring_attn_kernel(
@@ -59,8 +46,16 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
   const int own = (int)(p % W);
   for (int e = tid; e < G * DK; e += NT) qs[e] = to_f32<E>(q[((int64_t)b * H + kh * G) * DK + e]);
   __syncthreads();
-  // (1) scores
-  for (int s = tid; s <= W; s += NT) {
+  // (1) scores: warp w takes slots w, w + NW, ... (and the new token, index W, for the last warp);
+  // lane l holds channels l, l + 32, ... of the queries (registers) and of each key row, and the
+  // group's G scores are warp sums in flight together
+  constexpr int NE = DKMAX / 32, NW = NT / 32;
+  float qv[GMAX][NE];
+#pragma unroll
+  for (int g = 0; g < GMAX; ++g)
+#pragma unroll
+    for (int e = 0; e < NE; ++e) qv[g][e] = (g < G && lane + 32 * e < DK) ? qs[g * DK + lane + 32 * e] : 0.f;
+  for (int s = warp; s <= W; s += NW) {
     const E* krow;
     bool vis;
     if (s == W) {
@@ -74,25 +69,29 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
       }
       krow = ring_k + (((int64_t)b * W + s) * HKV + kh) * DK;
     }
-    float acc[GMAX];
+    if (!vis) {  // warp-uniform
+      if (lane < G) ps[lane * (W + 1) + s] = -INFINITY;
+      continue;
+    }
+    float kv[NE];
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g) acc[g] = 0.f;
-    if (vis) {
-      for (int d0 = 0; d0 < DK; d0 += 8) {
-        float kv[8];
-        load8(krow + d0, kv);
+    for (int e = 0; e < NE; ++e) kv[e] = lane + 32 * e < DK ? to_f32<E>(krow[lane + 32 * e]) : 0.f;
+    float sc[GMAX];
 #pragma unroll
-        for (int g = 0; g < GMAX; ++g) {
-          if (g < G) {
+    for (int g = 0; g < GMAX; ++g) {
+      float a = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[g] = fmaf(qs[g * DK + d0 + i], kv[i], acc[g]);
-          }
-        }
-      }
+      for (int e = 0; e < NE; ++e) a = fmaf(qv[g][e], kv[e], a);
+      sc[g] = a;
     }
 #pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g)
+        if (g < G) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], off);
+#pragma unroll
     for (int g = 0; g < GMAX; ++g)
-      if (g < G) ps[g * (W + 1) + s] = vis ? acc[g] * scale : -INFINITY;
+      if (g < G && lane == g) ps[g * (W + 1) + s] = sc[g] * scale;
   }
   __syncthreads();
   // (2) probabilities, head g by warp g
@@ -112,9 +111,8 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
     for (int s = lane; s <= W; s += 32) row[s] *= inv;
   }
   __syncthreads();
-  // (3) outputs: warp w sums its share of the slots (s = w, w + 8, ...) for every head of the
+  // (3) outputs: warp w sums its share of the slots (s = w, w + NW, ...) for every head of the
   // group, lane l holding channels l, l + 32, ...; the warps' partial sums are added in warp order
-  constexpr int NE = DKMAX / 32;
   float acc[GMAX][NE];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
@@ -138,8 +136,8 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
   if (warp == 0) add_row(v_new + ((int64_t)b * HKV + kh) * DK, W);
   // unconditional loads (a slot that is not visible has probability exactly 0 and finite values)
 #pragma unroll 4
-  for (int s = warp; s < W; s += NT / 32) add_row(vbase + s * stride, s);
-  float* part = ps + G * (W + 1);  // [NT/32][G][DK]
+  for (int s = warp; s < W; s += NW) add_row(vbase + s * stride, s);
+  float* part = ps + G * (W + 1);  // [NW][G][DK]
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
     if (g < G)
@@ -149,7 +147,7 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
   __syncthreads();
   for (int e = tid; e < G * DK; e += NT) {
     float sum = 0.f;
-    for (int w = 0; w < NT / 32; ++w) sum += part[w * G * DK + e];
+    for (int w = 0; w < NW; ++w) sum += part[w * G * DK + e];
     o[((int64_t)b * H + kh * G) * DK + e] = from_f32<E>(sum);
   }
   __syncthreads();  // every thread has read the ring
@@ -175,9 +173,7 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
                               int H, int HKV, int DK, int window, int dtype, void* stream) {
   VB_REQUIRE(B >= 0 && W >= 1 && H >= 1 && HKV >= 1 && H % HKV == 0 && H / HKV <= GMAX,
              "ring_attend: bad shape B=%d W=%d H=%d HKV=%d", B, W, H, HKV);
-  VB_REQUIRE(DK >= 8 && DK <= DKMAX && DK % 8 == 0, "ring_attend: head dimension %d must be a multiple of 8 in [8, %d]",
-             DK, DKMAX);
-  VB_REQUIRE(aligned16(k_new) && aligned16(ring_k), "ring_attend: keys not 16-byte aligned");
+  VB_REQUIRE(DK >= 1 && DK <= DKMAX, "ring_attend: head dimension %d must lie in [1, %d]", DK, DKMAX);
   VB_REQUIRE(window >= 1, "ring_attend: window %d must be at least 1", window);
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16 || dtype == VB_F16, "ring_attend: unsupported dtype %d", dtype);
   if (B == 0) return VB_OK;
