@@ -46,52 +46,60 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
   const int own = (int)(p % W);
   for (int e = tid; e < G * DK; e += NT) qs[e] = to_f32<E>(q[((int64_t)b * H + kh * G) * DK + e]);
   __syncthreads();
-  // (1) scores: warp w takes slots w, w + NW, ... (and the new token, index W, for the last warp);
-  // lane l holds channels l, l + 32, ... of the queries (registers) and of each key row, and the
-  // group's G scores are warp sums in flight together
-  constexpr int NE = DKMAX / 32, NW = NT / 32;
+  // (1) scores. The visibility of every slot first, from coalesced loads of the positions and
+  // flags (a per-slot chain of dependent loads would serialise the walk); then warp w takes slots
+  // w, w + NW, ... four at a time (the new token is index W): lane l holds channels l, l + 32, ...
+  // of the queries (registers) and of each key row, and the 4 x G scores are warp sums in flight
+  // together. Every key row is loaded (an unwritten slot holds finite zeros); a slot that is not
+  // visible scores -inf.
+  constexpr int NE = DKMAX / 32, NW = NT / 32, U = 4;
+  uint8_t* vis = reinterpret_cast<uint8_t*>(ps + G * (W + 1) + NW * G * DK);  // [W + 1]
+  for (int s = tid; s <= W; s += NT) {
+    bool v = s == W;
+    if (!v && s != own && ring_valid[(int64_t)b * W + s]) {
+      const int64_t kp = ring_pos[(int64_t)b * W + s];
+      v = kp <= p && kp > p - window;
+    }
+    vis[s] = v ? 1 : 0;
+  }
   float qv[GMAX][NE];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
 #pragma unroll
     for (int e = 0; e < NE; ++e) qv[g][e] = (g < G && lane + 32 * e < DK) ? qs[g * DK + lane + 32 * e] : 0.f;
-  for (int s = warp; s <= W; s += NW) {
-    const E* krow;
-    bool vis;
-    if (s == W) {
-      krow = k_new + ((int64_t)b * HKV + kh) * DK;
-      vis = true;
-    } else {
-      vis = s != own && ring_valid[(int64_t)b * W + s];
-      if (vis) {
-        const int64_t kp = ring_pos[(int64_t)b * W + s];
-        vis = kp <= p && kp > p - window;
+  __syncthreads();
+  for (int s0 = warp * U; s0 <= W; s0 += NW * U) {
+    float sc[U][GMAX];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + u;
+      const E* krow = s == W ? k_new + ((int64_t)b * HKV + kh) * DK
+                             : ring_k + (((int64_t)b * W + min(s, W - 1)) * HKV + kh) * DK;
+      float kv[NE];
+#pragma unroll
+      for (int e = 0; e < NE; ++e) kv[e] = (s <= W && lane + 32 * e < DK) ? to_f32<E>(krow[lane + 32 * e]) : 0.f;
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g) {
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < NE; ++e) a = fmaf(qv[g][e], kv[e], a);
+        sc[u][g] = a;
       }
-      krow = ring_k + (((int64_t)b * W + s) * HKV + kh) * DK;
-    }
-    if (!vis) {  // warp-uniform
-      if (lane < G) ps[lane * (W + 1) + s] = -INFINITY;
-      continue;
-    }
-    float kv[NE];
-#pragma unroll
-    for (int e = 0; e < NE; ++e) kv[e] = lane + 32 * e < DK ? to_f32<E>(krow[lane + 32 * e]) : 0.f;
-    float sc[GMAX];
-#pragma unroll
-    for (int g = 0; g < GMAX; ++g) {
-      float a = 0.f;
-#pragma unroll
-      for (int e = 0; e < NE; ++e) a = fmaf(qv[g][e], kv[e], a);
-      sc[g] = a;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-      for (int g = 0; g < GMAX; ++g)
-        if (g < G) sc[g] += __shfl_xor_sync(0xffffffffu, sc[g], off);
+      for (int u = 0; u < U; ++u)
 #pragma unroll
-    for (int g = 0; g < GMAX; ++g)
-      if (g < G && lane == g) ps[g * (W + 1) + s] = sc[g] * scale;
+        for (int g = 0; g < GMAX; ++g)
+          if (g < G) sc[u][g] += __shfl_xor_sync(0xffffffffu, sc[u][g], off);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int s = s0 + u;
+#pragma unroll
+      for (int g = 0; g < GMAX; ++g)
+        if (g < G && lane == g && s <= W) ps[g * (W + 1) + s] = vis[s] ? sc[u][g] * scale : -INFINITY;
+    }
   }
   __syncthreads();
   // (2) probabilities, head g by warp g
@@ -136,7 +144,7 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
   if (warp == 0) add_row(v_new + ((int64_t)b * HKV + kh) * DK, W);
   // unconditional loads (a slot that is not visible has probability exactly 0 and finite values)
 #pragma unroll 4
-  for (int s = warp; s < W; s += NW) add_row(vbase + s * stride, s);
+  for (int s = warp; s < W; s += NW) add_row(vbase + s * stride, s);  // unrolled: four rows in flight
   float* part = ps + G * (W + 1);  // [NW][G][DK]
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
@@ -184,7 +192,8 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
   const dim3 grid(B, HKV);
   const float scale = 1.0f / sqrtf((float)DK);
   const int G = H / HKV;
-  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1) + (size_t)(NT / 32) * G * DK);
+  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1) + (size_t)(NT / 32) * G * DK) +
+                      (size_t)(W + 1);
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
     VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                   "ring_attend: smem attribute");
