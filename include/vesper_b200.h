@@ -267,12 +267,16 @@ VB_API int vb_rotary(const void *x, const long long *pos, const double *inv_freq
  * [B,W] int64, valid [B,W] bytes, the new tokens' positions pos [B] int64; o [B,H,DK]. Every
  * element tensor is of `dtype`. The token attends the valid slots with p - window < pos <= p and
  * itself (scale 1/sqrt(DK), head h reading key head h / (H / HKV), H / HKV <= 8, DK <= 128), then
- * is written IN PLACE into slot p % W (k, v, pos, valid). Replaces vesper/attention.py:298-338
- * (attend_ring) with :109-139 (kv_ring_write), batched over the rows of a decode step. */
+ * is written IN PLACE into slot p % W (k, v, pos, valid). `workspace`
+ * (vb_ring_attend_workspace bytes) holds the partial results of the window's 128-slot ranges.
+ * Replaces vesper/attention.py:298-338 (attend_ring) with :109-139 (kv_ring_write), batched over
+ * the rows of a decode step. */
+VB_API size_t vb_ring_attend_workspace(int B, int W, int H, int HKV, int DK);
+
 VB_API int vb_ring_attend(const void *q, const void *k_new, const void *v_new, void *ring_k,
                           void *ring_v, int64_t *ring_pos, uint8_t *ring_valid, const int64_t *pos,
-                          void *o, int B, int W, int H, int HKV, int DK, int window, int dtype,
-                          void *stream);
+                          void *o, void *workspace, int B, int W, int H, int HKV, int DK, int window,
+                          int dtype, void *stream);
 
 /* ---- the head's per-row next-token loss (linear_nll's row steps) ---------------------------
  * logits: [rows, V] of `dtype` with row stride `stride` (elements); targets: [rows] int64 in

@@ -45,7 +45,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_delta_scan_bf16_bwd_workspace": (_SZ, [_I, _I, _I, _I]),
     "vb_delta_scan_bf16_bwd": (_I, [_P] * 14 + [_I, _I, _I, _I, _P]),
     "vb_nll_row_stats": (_I, [_P, _I64, _P, _P, _P, _P, _I64, _I, _I, _P]),
-    "vb_ring_attend": (_I, [_P] * 9 + [_I] * 7 + [_P]),
+    "vb_ring_attend_workspace": (_SZ, [_I, _I, _I, _I, _I]),
+    "vb_ring_attend": (_I, [_P] * 10 + [_I] * 7 + [_P]),
     "vb_delta_scan_step": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _P]),
     "vb_nll_row_grad": (_I, [_P, _I64, _P, _P, _P, _P, _I64, _I, _I, _P]),
     "vb_delta_scan_f32_fwd_logits": (_I, [_P] * 9 + [_I, _I, _I, _I, _P]),

@@ -229,10 +229,14 @@ class WindowedAttention(nn.Module):
         o = torch.empty_like(qc)
         from vesper_b200 import _lib  # noqa: PLC0415
 
+        ws = _lib.workspace(
+            _lib.query("vb_ring_attend_workspace", b, self.window, self.heads, self.kv_heads, self.head_dim), q.device
+        )
         _lib.call(
             "vb_ring_attend", qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), ring.k.data_ptr(), ring.v.data_ptr(),
-            ring.pos.data_ptr(), ring.valid.data_ptr(), pos.contiguous().data_ptr(), o.data_ptr(), b, self.window,
-            self.heads, self.kv_heads, self.head_dim, self.window, _lib.DTYPE_CODE[dt], _lib.stream(q.device),
+            ring.pos.data_ptr(), ring.valid.data_ptr(), pos.contiguous().data_ptr(), o.data_ptr(), ws.data_ptr(), b,
+            self.window, self.heads, self.kv_heads, self.head_dim, self.window, _lib.DTYPE_CODE[dt],
+            _lib.stream(q.device),
         )  # fmt: skip
         return self.output(o.to(q.dtype)), ring
 

@@ -10,13 +10,13 @@
 // and rewritten afterwards with the new key, value, position and valid flag, so the CTAs of one
 // row never read what another is writing.
 //
-// One CTA of 16 warps per (row, key head), in three phases over the W + 1 candidate keys (the
-// ring's slots and the new token, index W): (1) each warp takes a share of the slots and forms
-// the group's scores for each (lane l holding channels l, l + 32, ... of the queries and the key
-// row; the scores are warp sums), -inf for a slot that is not visible; (2) warp g reduces head g's scores to their max
-// and sum and turns them into probabilities; (3) each warp takes a share of the slots and sums
-// probability x value for every head of the group (lane l holding channels l, l + 32, ...: the
-// value rows read coalesced), and the warps' partial sums are added in warp order.
+// A row's window is split into ranges of 128 slots, one CTA of eight warps per (row, key head,
+// range) so that enough warps keep loads in flight: (1) the warps share the range's candidates
+// and form the group's scores for each (lane l holding channels l, l + 32, ... of the queries and
+// the key row; the scores are warp sums), -inf for a slot that is not visible; (2) warp g reduces
+// head g's scores to the range's max and the unnormalised weights and their sum; (3) the warps
+// share the candidates again for weight x value (the value rows read coalesced). A second kernel
+// merges the ranges in order per (row, key head) and then writes the new token into its slot.
 // Deterministic (fixed-order sums), no atomics.
 #include <cmath>
 #include <type_traits>
@@ -26,58 +26,69 @@
 namespace vb {
 namespace {
 
-constexpr int NT = 512;
+constexpr int NT = 256;
 constexpr int GMAX = 8;     // query heads per key head
 constexpr int WMAX = 1024;  // ring slots
 constexpr int DKMAX = 128;
 
+constexpr int SPLIT_SLOTS = 128;  // ring slots per CTA: a row's window is split over several CTAs
+
+int splits(int W) { return (W + SPLIT_SLOTS - 1) / SPLIT_SLOTS; }
+
+// Partial attention of one (row, key head, slot range): the range's slots (and, for the last
+// range, the new token), written as each head's local max m, local sum l and unnormalised output
+// acc [DK] to part [B][HKV][nsplit][G][DK + 2].
 template <typename E>
-__global__ void __launch_bounds__(NT) ring_attn_kernel(
-    const E* __restrict__ q, const E* __restrict__ k_new, const E* __restrict__ v_new, E* ring_k, E* ring_v,
-    int64_t* ring_pos, uint8_t* ring_valid, const int64_t* __restrict__ pos, E* __restrict__ o, int W, int H,
-    int HKV, int DK, int window, float scale) {
+__global__ void __launch_bounds__(NT) ring_attn_part_kernel(
+    const E* __restrict__ q, const E* __restrict__ k_new, const E* __restrict__ v_new, const E* __restrict__ ring_k,
+    const E* __restrict__ ring_v, const int64_t* __restrict__ ring_pos, const uint8_t* __restrict__ ring_valid,
+    const int64_t* __restrict__ pos, float* __restrict__ part, int W, int H, int HKV, int DK, int window,
+    float scale) {
   extern __shared__ float smem[];
-  const int G = H / HKV;
-  float* qs = smem;             // [G][DK]
-  float* ps = smem + G * DK;    // [G][W + 1]
-  const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
+  const int G = H / HKV, nsplit = gridDim.z;
+  const int b = blockIdx.x, kh = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  const int lo = z * SPLIT_SLOTS, hi = min(W, lo + SPLIT_SLOTS);
+  const bool last = z == nsplit - 1;
+  const int L = hi - lo + (last ? 1 : 0);  // candidates: local index i is slot lo + i, or the new token
+  float* qs = smem;                   // [G][DK]
+  float* ps = smem + G * DK;          // [G][L]
+  constexpr int NE = DKMAX / 32, NW = NT / 32, U = 4;
+  float* red = ps + G * L;            // [NW][G][DK]
+  uint8_t* vis = reinterpret_cast<uint8_t*>(red + NW * G * DK);  // [L]
   const int64_t p = pos[b];
   const int own = (int)(p % W);
+  auto slot_of = [&](int i) { return i < hi - lo ? lo + i : W; };
   for (int e = tid; e < G * DK; e += NT) qs[e] = to_f32<E>(q[((int64_t)b * H + kh * G) * DK + e]);
-  __syncthreads();
-  // (1) scores. The visibility of every slot first, from coalesced loads of the positions and
-  // flags (a per-slot chain of dependent loads would serialise the walk); then warp w takes slots
-  // w, w + NW, ... four at a time (the new token is index W): lane l holds channels l, l + 32, ...
-  // of the queries (registers) and of each key row, and the 4 x G scores are warp sums in flight
-  // together. Every key row is loaded (an unwritten slot holds finite zeros); a slot that is not
-  // visible scores -inf.
-  constexpr int NE = DKMAX / 32, NW = NT / 32, U = 4;
-  uint8_t* vis = reinterpret_cast<uint8_t*>(ps + G * (W + 1) + NW * G * DK);  // [W + 1]
-  for (int s = tid; s <= W; s += NT) {
+  // the visibility of every candidate from one coalesced pass (a per-slot chain of dependent
+  // loads would serialise the walk)
+  for (int i = tid; i < L; i += NT) {
+    const int s = slot_of(i);
     bool v = s == W;
     if (!v && s != own && ring_valid[(int64_t)b * W + s]) {
       const int64_t kp = ring_pos[(int64_t)b * W + s];
       v = kp <= p && kp > p - window;
     }
-    vis[s] = v ? 1 : 0;
+    vis[i] = v ? 1 : 0;
   }
+  __syncthreads();
+  // (1) scores: warp w takes candidates w*U .. w*U + U-1, then NW*U on; lane l holds channels
+  // l, l + 32, ... of the queries and of each key row; the U x G scores are warp sums in flight
+  // together; every key row is loaded (an unwritten slot holds finite zeros)
   float qv[GMAX][NE];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
 #pragma unroll
     for (int e = 0; e < NE; ++e) qv[g][e] = (g < G && lane + 32 * e < DK) ? qs[g * DK + lane + 32 * e] : 0.f;
-  __syncthreads();
-  for (int s0 = warp * U; s0 <= W; s0 += NW * U) {
+  for (int i0 = warp * U; i0 < L; i0 += NW * U) {
     float sc[U][GMAX];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int s = s0 + u;
-      const E* krow = s == W ? k_new + ((int64_t)b * HKV + kh) * DK
-                             : ring_k + (((int64_t)b * W + min(s, W - 1)) * HKV + kh) * DK;
+      const int i = i0 + u, s = slot_of(min(i, L - 1));
+      const E* krow = s == W ? k_new + ((int64_t)b * HKV + kh) * DK : ring_k + (((int64_t)b * W + s) * HKV + kh) * DK;
       float kv[NE];
 #pragma unroll
-      for (int e = 0; e < NE; ++e) kv[e] = (s <= W && lane + 32 * e < DK) ? to_f32<E>(krow[lane + 32 * e]) : 0.f;
+      for (int e = 0; e < NE; ++e) kv[e] = (i < L && lane + 32 * e < DK) ? to_f32<E>(krow[lane + 32 * e]) : 0.f;
 #pragma unroll
       for (int g = 0; g < GMAX; ++g) {
         float a = 0.f;
@@ -95,75 +106,100 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
           if (g < G) sc[u][g] += __shfl_xor_sync(0xffffffffu, sc[u][g], off);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int s = s0 + u;
+      const int i = i0 + u;
 #pragma unroll
       for (int g = 0; g < GMAX; ++g)
-        if (g < G && lane == g && s <= W) ps[g * (W + 1) + s] = vis[s] ? sc[u][g] * scale : -INFINITY;
+        if (g < G && lane == g && i < L) ps[g * L + i] = vis[i] ? sc[u][g] * scale : -INFINITY;
     }
   }
   __syncthreads();
-  // (2) probabilities, head g by warp g
+  // (2) head g (warp g): the local max and the unnormalised weights exp(score - max), their sum
+  float* stats = part + ((((int64_t)b * HKV + kh) * nsplit + z) * G) * (DK + 2);
   if (warp < G) {
-    float* row = ps + warp * (W + 1);
+    float* row = ps + warp * L;
     float m = -INFINITY;
-    for (int s = lane; s <= W; s += 32) m = fmaxf(m, row[s]);
+    for (int i = lane; i < L; i += 32) m = fmaxf(m, row[i]);
     m = warp_max(m);
     float l = 0.f;
-    for (int s = lane; s <= W; s += 32) {
-      const float e = row[s] == -INFINITY ? 0.f : expf(row[s] - m);
-      row[s] = e;
+    for (int i = lane; i < L; i += 32) {
+      const float e = row[i] == -INFINITY ? 0.f : expf(row[i] - m);
+      row[i] = e;
       l += e;
     }
     l = warp_sum(l);
-    const float inv = 1.0f / l;
-    for (int s = lane; s <= W; s += 32) row[s] *= inv;
+    if (lane == 0) {
+      stats[warp * (DK + 2) + DK] = m;
+      stats[warp * (DK + 2) + DK + 1] = l;
+    }
   }
   __syncthreads();
-  // (3) outputs: warp w sums its share of the slots (s = w, w + NW, ...) for every head of the
-  // group, lane l holding channels l, l + 32, ...; the warps' partial sums are added in warp order
+  // (3) warp w sums weight x value over its candidates for every head of the group, lane l holding
+  // channels l, l + 32, ...; the warps' partials are added in warp order
   float acc[GMAX][NE];
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
 #pragma unroll
     for (int e = 0; e < NE; ++e) acc[g][e] = 0.f;
-  const int64_t stride = (int64_t)HKV * DK;
-  const E* vbase = ring_v + ((int64_t)b * W * HKV + kh) * DK;
-  auto add_row = [&](const E* vrow, int s) {
+#pragma unroll 4
+  for (int i = warp; i < L; i += NW) {  // unrolled: four value rows in flight
+    const int s = slot_of(i);
+    const E* vrow = s == W ? v_new + ((int64_t)b * HKV + kh) * DK : ring_v + (((int64_t)b * W + s) * HKV + kh) * DK;
     float vv[NE];
 #pragma unroll
     for (int e = 0; e < NE; ++e) vv[e] = lane + 32 * e < DK ? to_f32<E>(vrow[lane + 32 * e]) : 0.f;
 #pragma unroll
     for (int g = 0; g < GMAX; ++g) {
       if (g < G) {
-        const float pr = ps[g * (W + 1) + s];
+        const float pr = ps[g * L + i];
 #pragma unroll
         for (int e = 0; e < NE; ++e) acc[g][e] = fmaf(pr, vv[e], acc[g][e]);
       }
     }
-  };
-  if (warp == 0) add_row(v_new + ((int64_t)b * HKV + kh) * DK, W);
-  // unconditional loads (a slot that is not visible has probability exactly 0 and finite values)
-#pragma unroll 4
-  for (int s = warp; s < W; s += NW) add_row(vbase + s * stride, s);  // unrolled: four rows in flight
-  float* part = ps + G * (W + 1);  // [NW][G][DK]
+  }
 #pragma unroll
   for (int g = 0; g < GMAX; ++g)
     if (g < G)
 #pragma unroll
       for (int e = 0; e < NE; ++e)
-        if (lane + 32 * e < DK) part[(warp * G + g) * DK + lane + 32 * e] = acc[g][e];
+        if (lane + 32 * e < DK) red[(warp * G + g) * DK + lane + 32 * e] = acc[g][e];
   __syncthreads();
   for (int e = tid; e < G * DK; e += NT) {
+    const int g = e / DK, d = e % DK;
     float sum = 0.f;
-    for (int w = 0; w < NW; ++w) sum += part[w * G * DK + e];
-    o[((int64_t)b * H + kh * G) * DK + e] = from_f32<E>(sum);
+    for (int w = 0; w < NW; ++w) sum += red[(w * G + g) * DK + d];
+    stats[g * (DK + 2) + d] = sum;
   }
-  __syncthreads();  // every thread has read the ring
-  // the new token takes its slot (no CTA of this row reads that slot)
-  for (int d = tid; d < DK; d += NT) {
-    const int64_t base = (((int64_t)b * W + own) * HKV + kh) * DK;
-    ring_k[base + d] = k_new[((int64_t)b * HKV + kh) * DK + d];
-    ring_v[base + d] = v_new[((int64_t)b * HKV + kh) * DK + d];
+}
+
+// Merges a (row, key head)'s range partials in range order into the output, then writes the new
+// token into its slot: the partial kernel has finished every read of the ring.
+template <typename E>
+__global__ void ring_attn_merge_kernel(const E* __restrict__ k_new, const E* __restrict__ v_new, E* ring_k, E* ring_v,
+                                       int64_t* ring_pos, uint8_t* ring_valid, const int64_t* __restrict__ pos,
+                                       const float* __restrict__ part, E* __restrict__ o, int nsplit, int W, int H,
+                                       int HKV, int DK) {
+  const int G = H / HKV;
+  const int b = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
+  const float* base = part + (((int64_t)b * HKV + kh) * nsplit) * G * (DK + 2);
+  for (int e = tid; e < G * DK; e += blockDim.x) {
+    const int g = e / DK, d = e % DK;
+    float M = -INFINITY;
+    for (int z = 0; z < nsplit; ++z) M = fmaxf(M, base[((int64_t)z * G + g) * (DK + 2) + DK]);
+    float Lsum = 0.f, out = 0.f;
+    for (int z = 0; z < nsplit; ++z) {
+      const float* st = base + ((int64_t)z * G + g) * (DK + 2);
+      const float f = st[DK] == -INFINITY ? 0.f : expf(st[DK] - M);
+      Lsum = fmaf(st[DK + 1], f, Lsum);
+      out = fmaf(st[d], f, out);
+    }
+    o[((int64_t)b * H + kh * G + g) * DK + d] = from_f32<E>(out / Lsum);
+  }
+  const int64_t p = pos[b];
+  const int own = (int)(p % W);
+  for (int d = tid; d < DK; d += blockDim.x) {
+    const int64_t dst = (((int64_t)b * W + own) * HKV + kh) * DK;
+    ring_k[dst + d] = k_new[((int64_t)b * HKV + kh) * DK + d];
+    ring_v[dst + d] = v_new[((int64_t)b * HKV + kh) * DK + d];
   }
   if (kh == 0 && tid == 0) {
     ring_pos[(int64_t)b * W + own] = p;
@@ -176,31 +212,41 @@ __global__ void __launch_bounds__(NT) ring_attn_kernel(
 
 using namespace vb;
 
+extern "C" size_t vb_ring_attend_workspace(int B, int W, int H, int HKV, int DK) {
+  if (B <= 0 || W <= 0 || H <= 0 || HKV <= 0 || DK <= 0) return 16;
+  return sizeof(float) * (size_t)B * HKV * splits(W) * (H / HKV) * (DK + 2);
+}
+
 extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_new, void* ring_k, void* ring_v,
-                              int64_t* ring_pos, uint8_t* ring_valid, const int64_t* pos, void* o, int B, int W,
-                              int H, int HKV, int DK, int window, int dtype, void* stream) {
+                              int64_t* ring_pos, uint8_t* ring_valid, const int64_t* pos, void* o, void* workspace,
+                              int B, int W, int H, int HKV, int DK, int window, int dtype, void* stream) {
   VB_REQUIRE(B >= 0 && W >= 1 && H >= 1 && HKV >= 1 && H % HKV == 0 && H / HKV <= GMAX,
              "ring_attend: bad shape B=%d W=%d H=%d HKV=%d", B, W, H, HKV);
   VB_REQUIRE(DK >= 1 && DK <= DKMAX, "ring_attend: head dimension %d must lie in [1, %d]", DK, DKMAX);
   VB_REQUIRE(window >= 1, "ring_attend: window %d must be at least 1", window);
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16 || dtype == VB_F16, "ring_attend: unsupported dtype %d", dtype);
+  VB_REQUIRE(W <= WMAX, "ring_attend: %d slots exceed %d", W, WMAX);
   if (B == 0) return VB_OK;
-  VB_REQUIRE(q && k_new && v_new && ring_k && ring_v && ring_pos && ring_valid && pos && o,
+  VB_REQUIRE(q && k_new && v_new && ring_k && ring_v && ring_pos && ring_valid && pos && o && workspace,
              "ring_attend: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  VB_REQUIRE(W <= WMAX, "ring_attend: %d slots exceed %d", W, WMAX);
-  const dim3 grid(B, HKV);
+  const int G = H / HKV, nsplit = splits(W);
   const float scale = 1.0f / sqrtf((float)DK);
-  const int G = H / HKV;
-  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * (W + 1) + (size_t)(NT / 32) * G * DK) +
-                      (size_t)(W + 1);
+  const int L = SPLIT_SLOTS + 1;
+  const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * L + (size_t)(NT / 32) * G * DK) + (size_t)L;
+  float* part = (float*)workspace;
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+    VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_part_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                   "ring_attend: smem attribute");
-    ring_attn_kernel<T><<<grid, NT, smem, st>>>((const T*)q, (const T*)k_new, (const T*)v_new, (T*)ring_k,
-                                               (T*)ring_v, ring_pos, ring_valid, pos, (T*)o, W, H, HKV, DK, window,
-                                               scale);
-    VB_LAUNCH_CHECK("ring_attend");
+    ring_attn_part_kernel<T><<<dim3(B, HKV, nsplit), NT, smem, st>>>(
+        (const T*)q, (const T*)k_new, (const T*)v_new, (const T*)ring_k, (const T*)ring_v, ring_pos, ring_valid, pos,
+        part, W, H, HKV, DK, window, scale);
+    VB_LAUNCH_CHECK("ring_attend part");
+    const int threads = G * DK < 1024 ? ((G * DK + 31) / 32) * 32 : 1024;
+    ring_attn_merge_kernel<T><<<dim3(B, HKV), threads, 0, st>>>((const T*)k_new, (const T*)v_new, (T*)ring_k,
+                                                                 (T*)ring_v, ring_pos, ring_valid, pos, part, (T*)o,
+                                                                 nsplit, W, H, HKV, DK);
+    VB_LAUNCH_CHECK("ring_attend merge");
     return VB_OK;
   });
 }
