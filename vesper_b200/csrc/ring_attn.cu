@@ -38,14 +38,17 @@ int splits(int W) { return (W + SPLIT_SLOTS - 1) / SPLIT_SLOTS; }
 // Partial attention of one (row, key head, slot range): the range's slots (and, for the last
 // range, the new token), written as each head's local max m, local sum l and unnormalised output
 // acc [DK] to part [B][HKV][nsplit][G][DK + 2].
-template <typename E>
+template <typename E, int GC, int NEC>
 __global__ void __launch_bounds__(NT) ring_attn_part_kernel(
     const E* __restrict__ q, const E* __restrict__ k_new, const E* __restrict__ v_new, const E* __restrict__ ring_k,
     const E* __restrict__ ring_v, const int64_t* __restrict__ ring_pos, const uint8_t* __restrict__ ring_valid,
     const int64_t* __restrict__ pos, float* __restrict__ part, int W, int H, int HKV, int DK, int window,
     float scale) {
   extern __shared__ float smem[];
-  const int G = H / HKV, nsplit = gridDim.z;
+  // GC: the query heads per key head, NEC: channels per lane (ceil(DK / 32)), both compile-time so
+  // that no lane computes for a head or a channel that does not exist
+  constexpr int G = GC, GMAX = GC, NE = NEC;
+  const int nsplit = gridDim.z;
   const int b = blockIdx.x, kh = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
   const int lo = z * SPLIT_SLOTS, hi = min(W, lo + SPLIT_SLOTS);
@@ -53,7 +56,7 @@ __global__ void __launch_bounds__(NT) ring_attn_part_kernel(
   const int L = hi - lo + (last ? 1 : 0);  // candidates: local index i is slot lo + i, or the new token
   float* qs = smem;                   // [G][DK]
   float* ps = smem + G * DK;          // [G][L]
-  constexpr int NE = DKMAX / 32, NW = NT / 32, U = 4;
+  constexpr int NW = NT / 32, U = 4;
   float* red = ps + G * L;            // [NW][G][DK]
   uint8_t* vis = reinterpret_cast<uint8_t*>(red + NW * G * DK);  // [L]
   const int64_t p = pos[b];
@@ -235,13 +238,39 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
   const int L = SPLIT_SLOTS + 1;
   const size_t smem = sizeof(float) * ((size_t)G * DK + (size_t)G * L + (size_t)(NT / 32) * G * DK) + (size_t)L;
   float* part = (float*)workspace;
+  const int ne = (DK + 31) / 32;
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_part_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                  "ring_attend: smem attribute");
-    ring_attn_part_kernel<T><<<dim3(B, HKV, nsplit), NT, smem, st>>>(
-        (const T*)q, (const T*)k_new, (const T*)v_new, (const T*)ring_k, (const T*)ring_v, ring_pos, ring_valid, pos,
-        part, W, H, HKV, DK, window, scale);
-    VB_LAUNCH_CHECK("ring_attend part");
+    auto part_launch = [&](auto gc, auto nec) -> int {
+      constexpr int GG = decltype(gc)::value, NN = decltype(nec)::value;
+      VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_part_kernel<T, GG, NN>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                    "ring_attend: smem attribute");
+      ring_attn_part_kernel<T, GG, NN><<<dim3(B, HKV, nsplit), NT, smem, st>>>(
+          (const T*)q, (const T*)k_new, (const T*)v_new, (const T*)ring_k, (const T*)ring_v, ring_pos, ring_valid,
+          pos, part, W, H, HKV, DK, window, scale);
+      VB_LAUNCH_CHECK("ring_attend part");
+      return VB_OK;
+    };
+    auto by_ne = [&](auto gc) -> int {
+      switch (ne) {
+        case 1: return part_launch(gc, std::integral_constant<int, 1>{});
+        case 2: return part_launch(gc, std::integral_constant<int, 2>{});
+        case 3: return part_launch(gc, std::integral_constant<int, 3>{});
+        default: return part_launch(gc, std::integral_constant<int, 4>{});
+      }
+    };
+    int rc = VB_OK;
+    switch (G) {
+      case 1: rc = by_ne(std::integral_constant<int, 1>{}); break;
+      case 2: rc = by_ne(std::integral_constant<int, 2>{}); break;
+      case 3: rc = by_ne(std::integral_constant<int, 3>{}); break;
+      case 4: rc = by_ne(std::integral_constant<int, 4>{}); break;
+      case 5: rc = by_ne(std::integral_constant<int, 5>{}); break;
+      case 6: rc = by_ne(std::integral_constant<int, 6>{}); break;
+      case 7: rc = by_ne(std::integral_constant<int, 7>{}); break;
+      default: rc = by_ne(std::integral_constant<int, 8>{}); break;
+    }
+    if (rc) return rc;
     const int threads = G * DK < 1024 ? ((G * DK + 31) / 32) * 32 : 1024;
     ring_attn_merge_kernel<T><<<dim3(B, HKV), threads, 0, st>>>((const T*)k_new, (const T*)v_new, (T*)ring_k,
                                                                  (T*)ring_v, ring_pos, ring_valid, pos, part, (T*)o,

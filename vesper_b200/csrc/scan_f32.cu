@@ -63,20 +63,26 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
       S[m][c] = (i < D && j < D) ? s0p[(int64_t)i * D + j] : 0.f;
     }
   }
-  for (int t = 0; t < T; ++t) {
+  // the token's inputs are loaded one token ahead (their latency overlaps the current token's
+  // reductions, which are the sequential chain)
+  float kk[NI], qq[NI], vv[CPW], bt = 0.f;
+  auto load_token = [&](int t, float (&k_)[NI], float (&q_)[NI], float (&v_)[CPW], float& b_) {
     const int64_t row = (((int64_t)b * T + t) * H + h);
-    const E* kp = k + row * D;
-    const E* qp = q + row * D;
-    float kk[NI], qq[NI], vv[CPW];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
       const int i = lane + 32 * m;
-      kk[m] = i < D ? ld_in(kp + i) : 0.f;
-      qq[m] = i < D ? ld_in(qp + i) : 0.f;
+      k_[m] = i < D ? ld_in(k + row * D + i) : 0.f;
+      q_[m] = i < D ? ld_in(q + row * D + i) : 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? ld_in(v + row * D + j0 + c) : 0.f;
-    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+    for (int c = 0; c < CPW; ++c) v_[c] = (j0 + c < D) ? ld_in(v + row * D + j0 + c) : 0.f;
+    b_ = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+  };
+  if (T > 0) load_token(0, kk, qq, vv, bt);
+  for (int t = 0; t < T; ++t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    float kn[NI], qn[NI], vn[CPW], bn = 0.f;
+    if (t + 1 < T) load_token(t + 1, kn, qn, vn, bn);
     float red[CPW];
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
@@ -119,6 +125,13 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_kernel(
         st_out(o + row * D + j, ov);
         if (resid) resid[row * D + j] = rv;
       }
+    }
+    if (t + 1 < T) {
+#pragma unroll
+      for (int m = 0; m < NI; ++m) { kk[m] = kn[m]; qq[m] = qn[m]; }
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) vv[c] = vn[c];
+      bt = bn;
     }
   }
   float* snp = sn + (int64_t)bh * D * D;
@@ -180,22 +193,29 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
       G[m][c] = (dsn && i < D && j < D) ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
     }
   }
-  for (int t = T - 1; t >= 0; --t) {
+  // phase A: a token's inputs are loaded one token ahead (reverse order)
+  auto load_a = [&](int t, float (&k_)[NI], float (&q_)[NI], float (&g_)[CPW], float (&r_)[CPW], float& b_) {
     const int64_t row = (((int64_t)b * T + t) * H + h);
-    float kk[NI], qq[NI], gg[CPW], rr[CPW];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
       const int i = lane + 32 * m;
-      kk[m] = i < D ? __ldg(k + row * D + i) : 0.f;
-      qq[m] = i < D ? __ldg(q + row * D + i) : 0.f;
+      k_[m] = i < D ? __ldg(k + row * D + i) : 0.f;
+      q_[m] = i < D ? __ldg(q + row * D + i) : 0.f;
     }
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
       const bool ok = j0 + c < D;
-      gg[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
-      rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
+      g_[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
+      r_[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
     }
-    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+    b_ = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+  };
+  float kk[NI], qq[NI], gg[CPW], rr[CPW], bt = 0.f;
+  if (T > 0) load_a(T - 1, kk, qq, gg, rr, bt);
+  for (int t = T - 1; t >= 0; --t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    float kn[NI], qn[NI], gn[CPW], rn[CPW], bn = 0.f;
+    if (t > 0) load_a(t - 1, kn, qn, gn, rn, bn);
 #pragma unroll
     for (int m = 0; m < NI; ++m)
 #pragma unroll
@@ -235,6 +255,13 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
     for (int m = 0; m < NI; ++m)
 #pragma unroll
       for (int c = 0; c < CPW; ++c) G[m][c] = fmaf(-kk[m], dr[c], G[m][c]);
+    if (t > 0) {
+#pragma unroll
+      for (int m = 0; m < NI; ++m) { kk[m] = kn[m]; qq[m] = qn[m]; }
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) { gg[c] = gn[c]; rr[c] = rn[c]; }
+      bt = bn;
+    }
   }
 #pragma unroll
   for (int m = 0; m < NI; ++m) {
@@ -256,22 +283,29 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
       S[m][c] = (i < D && j < D) ? s0[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
     }
   }
-  for (int t = 0; t < T; ++t) {
+  // phase B: likewise one token ahead (forward order); dv of this CTA's columns was written above
+  auto load_b = [&](int t, float (&k_)[NI], float (&g_)[CPW], float (&r_)[CPW], float (&d_)[CPW], float& b_) {
     const int64_t row = (((int64_t)b * T + t) * H + h);
-    float kk[NI], gg[CPW], rr[CPW], dr[CPW];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
       const int i = lane + 32 * m;
-      kk[m] = i < D ? __ldg(k + row * D + i) : 0.f;
+      k_[m] = i < D ? __ldg(k + row * D + i) : 0.f;
     }
 #pragma unroll
     for (int c = 0; c < CPW; ++c) {
       const bool ok = j0 + c < D;
-      gg[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
-      rr[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
-      dr[c] = ok ? dv[row * D + j0 + c] : 0.f;
+      g_[c] = ok ? __ldg(dout + row * D + j0 + c) : 0.f;
+      r_[c] = ok ? __ldg(resid + row * D + j0 + c) : 0.f;
+      d_[c] = ok ? dv[row * D + j0 + c] : 0.f;
     }
-    const float bt = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+    b_ = beta_at(beta, shift, logit, row, (int64_t)b * T + t);
+  };
+  float dr[CPW];
+  if (T > 0) load_b(0, kk, gg, rr, dr, bt);
+  for (int t = 0; t < T; ++t) {
+    const int64_t row = (((int64_t)b * T + t) * H + h);
+    float kn[NI], gn[CPW], rn[CPW], dn[CPW], bn = 0.f;
+    if (t + 1 < T) load_b(t + 1, kn, gn, rn, dn, bn);
     float hd[NI];
 #pragma unroll
     for (int m = 0; m < NI; ++m) {
@@ -296,6 +330,13 @@ __global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_kernel(
       dq[m] = a;
     }
     cta_sum_store<NI>(dq, red, part_dq + row * D, D);
+    if (t + 1 < T) {
+#pragma unroll
+      for (int m = 0; m < NI; ++m) kk[m] = kn[m];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) { gg[c] = gn[c]; rr[c] = rn[c]; dr[c] = dn[c]; }
+      bt = bn;
+    }
   }
 }
 
