@@ -19,10 +19,6 @@ namespace {
 
 constexpr int RUN = 64;        // tokens per warp
 constexpr int WARPS = 4;       // warps per CTA
-constexpr int PF = 8;          // rows a warp loads ahead of their use (RUN is a multiple)
-// token pairs the backward loads ahead: fewer for wide lanes or long filters (registers)
-template <int EPL, int K>
-constexpr int pairs_ahead() { return EPL * K <= 16 ? 4 : (EPL * K <= 32 ? 2 : 1); }
 
 // EPL consecutive elements at p (aligned to their total size, up to 16 bytes) as one access per
 // 16 bytes, or one narrower access when they are fewer
@@ -175,19 +171,8 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
   float2 st_pair = make_float2(0.f, 0.f);
 #pragma unroll
   for (int r = 1; r < K; ++r) load_in<T, EPL>(z, hist, b, t0 - r, T_, W, K, c, live, win[r]);
-  // the input rows run PF tokens ahead of their use (pf[i] holds row t0 + i, then + PF, ...): a
-  // warp keeps PF loads in flight instead of waiting on each row's latency in turn
-  float pf[PF][EPL];
-#pragma unroll
-  for (int i = 0; i < PF; ++i) load_in<T, EPL>(z, hist, b, t0 + i, T_, W, K, c, live && t0 + i < t1, pf[i]);
-  for (int tb = t0; tb < t1; tb += PF)
-#pragma unroll
-  for (int i = 0; i < PF; ++i) {
-    const int t = tb + i;
-    if (t >= t1) break;
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) win[0][e] = pf[i][e];
-    load_in<T, EPL>(z, hist, b, t + PF, T_, W, K, c, live && t + PF < t1, pf[i]);
+  for (int t = t0; t < t1; ++t) {
+    load_in<T, EPL>(z, hist, b, t, T_, W, K, c, live, win[0]);
     float u[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
@@ -277,53 +262,29 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
       if (live) st_elems<T, EPL>(dz + ((int64_t)b * T_ + t) * W + c, o);
     }
   };
-  // each pair's loads (two input rows, two key-gradient rows, two statistics) run PB pairs ahead
-  // of their use, so that a warp keeps several rows in flight
-  const float2* st_row = stats != nullptr ? stats + ((int64_t)b * heads + head) * T_ : nullptr;
-  auto fetch = [&](int t, float (&za)[EPL], float (&zb)[EPL], float (&g0)[EPL], float (&g1)[EPL], float2& s0,
-                   float2& s1) {
-    const bool on = t >= t0, two = on && t - 1 >= t0;
-    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live && on, za);
-    load_in<T, EPL>(z, hist, b, t - K, T_, W, K, c, live && two, zb);
-    load_g<T, EPL>(gk, b, t, T_, W, c, live && on, g0);
-    load_g<T, EPL>(gk, b, t - 1, T_, W, c, live && two, g1);
-    s0 = make_float2(1.f, 1.f);
-    s1 = s0;
-    if constexpr (STATS) {
-      if (on) s0 = __ldg(st_row + t);
-      if (two) s1 = __ldg(st_row + t - 1);
-    }
-  };
-  constexpr int PB = pairs_ahead<EPL, K>();
-  float qa[PB][EPL], qb[PB][EPL], qg0[PB][EPL], qg1[PB][EPL];
-  float2 qs0[PB], qs1[PB];
-#pragma unroll
-  for (int i = 0; i < PB; ++i) fetch(thi - 2 * i, qa[i], qb[i], qg0[i], qg1[i], qs0[i], qs1[i]);
-  for (int tbase = thi; tbase >= t0; tbase -= 2 * PB)
-#pragma unroll
-  for (int i = 0; i < PB; ++i) {
-    const int t = tbase - 2 * i;
-    if (t < t0) break;
+  for (int t = thi; t >= t0; t -= 2) {
     const bool two = t - 1 >= t0;
     // token t's window: win[r] = row t - r (one row older than before); token t - 1's: wb
 #pragma unroll
     for (int r = 0; r < K - 1; ++r)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) win[r][e] = win[r + 1][e];
-    float wb[K][EPL], ga[EPL], gb[EPL];
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) {
-      win[K - 1][e] = qa[i][e];
-      wb[K - 1][e] = qb[i][e];
-      ga[e] = qg0[i][e];
-      gb[e] = qg1[i][e];
-    }
-    const float2 sa = qs0[i], sb = qs1[i];
-    fetch(t - 2 * PB, qa[i], qb[i], qg0[i], qg1[i], qs0[i], qs1[i]);
+    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, win[K - 1]);
+    float wb[K][EPL];
 #pragma unroll
     for (int r = 0; r < K - 1; ++r)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) wb[r][e] = win[r + 1][e];
+    load_in<T, EPL>(z, hist, b, t - K, T_, W, K, c, live && two, wb[K - 1]);
+    float ga[EPL], gb[EPL];
+    load_g<T, EPL>(gk, b, t, T_, W, c, live, ga);
+    load_g<T, EPL>(gk, b, t - 1, T_, W, c, live && two, gb);
+    float2 sa = make_float2(1.f, 1.f), sb = sa;
+    if constexpr (STATS) {
+      const float2* st_row = stats + ((int64_t)b * heads + head) * T_;
+      sa = __ldg(st_row + t);
+      if (two) sb = __ldg(st_row + t - 1);
+    }
     float da[EPL], db[EPL];
     token_du<EPL, K, STATS>(tp, win, ga, floor_, sa, da);
     token_du<EPL, K, STATS>(tp, wb, gb, floor_, sb, db);
