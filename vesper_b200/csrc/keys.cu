@@ -93,6 +93,41 @@ __device__ __forceinline__ void norm_stats(const float (&u)[EPL], float floor_, 
   den = sqrtf(fmaxf(sq, 1.0f));
 }
 
+// normalize_keys of one head vector with one reduction of (max |u|, sum u^2) pairs. When the
+// largest magnitude reaches the floor it IS the scale, its own quotient is exactly 1 and the sum
+// of squared quotients is therefore at least 1: the clamp passes gradient with no quotient needed
+// to decide it, and s = u * (1 / scale), sq = (sum u^2) / scale^2 (within an ulp or two of the
+// quotients). Below the floor (a nearly zero vector) the exact quotients decide, as in
+// norm_stats. Returns scale, 1 / scale, s, den, and whether the clamp passes gradient.
+template <int EPL>
+__device__ __forceinline__ void norm_stats_fast(const float (&u)[EPL], float floor_, float& scale, float& rscale,
+                                                float (&s)[EPL], float& den, bool& clamped) {
+  float amax = 0.f, ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    amax = fmaxf(amax, fabsf(u[e]));
+    ss = fmaf(u[e], u[e], ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if (amax >= floor_) {  // warp-uniform
+    scale = amax;
+    rscale = 1.0f / scale;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s[e] = u[e] * rscale;
+    den = sqrtf(fmaxf(ss * rscale * rscale, 1.0f));
+    clamped = true;
+  } else {
+    float sq;
+    norm_stats<EPL>(u, floor_, scale, s, den, sq);
+    rscale = 1.0f / scale;
+    clamped = sq >= 1.0f;
+  }
+}
+
 // EPL channels [c, c+EPL) of key-gradient row t (zero when the row is not needed)
 template <typename T, int EPL>
 __device__ __forceinline__ void load_g(const T* __restrict__ gk, int b, int t, int T_, int W, int c, bool need,
@@ -127,10 +162,8 @@ __device__ __forceinline__ void token_du(const float (&tp)[K][EPL], const float 
 #pragma unroll
     for (int e = 0; e < EPL; ++e) s[e] = u[e] * rscale;  // within an ulp of u / scale: gradient only
   } else {
-    float scale, den, sq;
-    norm_stats<EPL>(u, floor_, scale, s, den, sq);  // the forward's exact quotients (the clamp)
-    clamped = sq >= 1.0f;
-    rscale = 1.0f / scale;
+    float scale, den;
+    norm_stats_fast<EPL>(u, floor_, scale, rscale, s, den, clamped);  // the forward's decision
     rden = 1.0f / den;
   }
   float dot = 0.f;
@@ -181,8 +214,9 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
       for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[r][e], a);
       u[e] = a;
     }
-    float scale, s[EPL], den, sq;
-    norm_stats<EPL>(u, floor_, scale, s, den, sq);
+    float scale, rscale, s[EPL], den;
+    bool clamped;
+    norm_stats_fast<EPL>(u, floor_, scale, rscale, s, den, clamped);
     const float rden = 1.0f / den;  // k = s / den to within an ulp or two of the quotient
     if (live) {
       float o[EPL];
@@ -194,7 +228,7 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
     // waits in lane (t - t0) % 32, and each 32 tokens leave as one contiguous warp store
     // ([B, heads, T, 2])
     const int slot = (t - t0) & 31;
-    if (lane == slot) st_pair = make_float2(1.0f / scale, sq >= 1.0f ? -rden : rden);
+    if (lane == slot) st_pair = make_float2(rscale, clamped ? -rden : rden);
     if (stats != nullptr && (slot == 31 || t + 1 == t1) && lane <= slot)
       stats[((int64_t)b * heads + head) * T_ + (t - slot + lane)] = st_pair;
 #pragma unroll
