@@ -861,6 +861,84 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def breakdown(args) -> None:
+    """Device time per kernel of one leg under torch's profiler (CUPTI activity, no ncu):
+    ``step`` one config-2 step, ``train`` one config-4 training step (eager), ``decode`` one
+    config-5 decode step (a graph replay) after a 1024-token prefill. Prints a table by kernel
+    group and the top kernels. Times under the profiler are not bench values."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    if args.breakdown == "step":
+        inp = make_inputs(device, 1234)
+        leaves = [inp[n].detach().requires_grad_() for n in ("x", "q", "v", "beta", "gain", "taps")]
+        for _ in range(3):
+            step(inp, leaves)
+
+        def run() -> None:
+            step(inp, leaves)
+    elif args.breakdown == "train":
+        from vesper_b200.model import Vesper
+        from vesper_b200.train import VESPER_S, TrainStep
+
+        cfg = VESPER_S
+        model = Vesper(cfg.shape, cfg.vocab, cfg.columns, cfg.t_max, cfg.halt_epsilon,
+                       torch.Generator().manual_seed(0)).to(device)  # fmt: skip
+        trainer = TrainStep(model, cfg, b=TRAIN_B, n=TRAIN_T, warm=10**6)  # eager: kernel names
+        g = torch.Generator(device=device).manual_seed(99)
+        batch = torch.randint(0, cfg.vocab, (TRAIN_B, TRAIN_T + 1), device=device, generator=g)
+        trainer.load(batch[:, :-1], batch[:, 1:])
+        for _ in range(3):
+            trainer.run()
+
+        def run() -> None:
+            trainer.run()
+    else:
+        from vesper_b200.column import set_scan
+        from vesper_b200.decode import BatchedDecoder
+        from vesper_b200.model import Vesper
+        from vesper_b200.train import VESPER_S
+
+        cfg = VESPER_S
+        model = Vesper(cfg.shape, cfg.vocab, cfg.columns, cfg.t_max, cfg.halt_epsilon,
+                       torch.Generator().manual_seed(0)).to(device)  # fmt: skip
+        set_scan(model, "fused")
+        g = torch.Generator(device=device).manual_seed(1)
+        prompt = torch.randint(0, cfg.vocab, (C5["B"], 1024), device=device, generator=g)
+        dec = BatchedDecoder(model, cfg.t_max, cfg.vocab, C5["B"], torch.bfloat16)
+        dec.prefill(prompt, chunk=1024)
+        tok = prompt[:, :1]
+        for _ in range(4):
+            tok, _ = dec.step(tok)
+        state = {"tok": tok}
+
+        def run() -> None:
+            state["tok"], _ = dec.step(state["tok"])
+    torch.cuda.synchronize(device)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        run()
+        torch.cuda.synchronize(device)
+    groups: dict[str, float] = collections.defaultdict(float)
+    kernels: dict[str, list[float]] = collections.defaultdict(lambda: [0.0, 0])
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA and ev.device_time_total > 0:
+            groups[_kernel_group(ev.name)] += ev.device_time_total / 1e3
+            kernels[ev.name[:70]][0] += ev.device_time_total / 1e3
+            kernels[ev.name[:70]][1] += 1
+    total = sum(groups.values())
+    print(f"{args.breakdown}: device time of the kernels {total:.3f} ms")
+    print("| group | ms | share |\n| --- | --- | --- |")
+    for name, ms in sorted(groups.items(), key=lambda kv: -kv[1]):
+        print(f"| {name} | {ms:.3f} | {100 * ms / total:.1f}% |")
+    print("| top kernel | launches | ms |\n| --- | --- | --- |")
+    for name, (ms, n) in sorted(kernels.items(), key=lambda kv: -kv[1][0])[:20]:
+        print(f"| {name.replace('|', '/')} | {n} | {ms:.3f} |")
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -874,10 +952,15 @@ def main() -> None:
     p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")
+    p.add_argument("--breakdown", choices=("step", "train", "decode"), default=None,
+                   help="print one leg's device time per kernel group under torch's profiler, then exit")
     p.add_argument("--steps-ref", type=int, default=0, help="reference samples (default: min(steps, 10))")
     p.add_argument("--warmup-ref", type=int, default=0)
     args = p.parse_args()
     globals()["B"] = args.batch
+    if args.breakdown:
+        breakdown(args)
+        return
     if args.impl == "reference":
         if not args.steps_ref:
             args.steps_ref = min(args.steps, 10)
