@@ -509,7 +509,8 @@ C3 = {"B": 16, "T": 2048, "d": 512, "heads": 8, "head_dim": 64, "kv_groups": 4, 
 
 def _kernel_group(name: str) -> str:
     n = name.lower()
-    for key, group in (("scan_", "delta-scan"), ("attn_", "attention"), ("keys_", "key filter"),
+    for key, group in (("scan_", "delta-scan"), ("delta_step", "delta-scan"), ("attn_", "attention"),
+                       ("nll_", "head loss"), ("keys_", "key filter"),
                        ("rms_", "rmsnorm"), ("column_sum", "rmsnorm"), ("select_rows", "copy-forward/compaction"),
                        ("gather_rows", "copy-forward/compaction"), ("expand_rows", "copy-forward/compaction"),
                        ("compact_", "copy-forward/compaction"), ("relu", "relu^2"), ("rotary", "rotary"),
