@@ -176,12 +176,19 @@ struct PrepSmem {
 constexpr int NP = 256;
 
 // X = (I + A)^-1 for the strictly lower A (float32 [64][65]) into X (float32 [64][68]), 256
-// threads: the four 16 x 16 diagonal blocks by forward substitution (a thread per column), then
-// the blocks below them one block diagonal at a time, X_ij = -X_ii sum_{j <= k < i} A_ik X_kj,
-// each thread a 1 x 4 strip of an output block. Entries above the diagonal blocks are not written.
+// threads, by blocks of 16 in three levels:
+//   1. the four diagonal blocks X_II by forward substitution (a thread per column; the entries
+//      above a block's diagonal come out as zeros);
+//   2. the blocks below them inside each 32 x 32 half: X_10 = -X_11 (A_10 X_00) and
+//      X_32 = -X_33 (A_32 X_22) (the two halves at once, a thread per 1 x 4 strip);
+//   3. the lower-left 32 x 32 block: X[32:, :32] = -X[32:, 32:] (A[32:, :32] X[:32, :32]), every
+//      thread a 1 x 4 strip of each product, the sums running over the blocks that are not zero.
+// Five barriers instead of seven, and each product's dependent chain is at most 32 terms with four
+// independent accumulators per thread. Entries above the diagonal blocks are not written.
 constexpr int XS = 68;  // row stride of X (16-byte aligned rows)
+constexpr int TS = 36;  // row stride of the products' scratch
 __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, float* Tm, int tid) {
-  if (tid < C) {
+  if (tid < C) {  // level 1
     const int o = 16 * (tid >> 4), j = tid & 15;
     float x[16];
 #pragma unroll
@@ -197,35 +204,59 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     }
   }
   __syncthreads();
-  const int jb = tid >> 6, r = (tid >> 2) & 15, q4 = 4 * (tid & 3);
+  // level 2: half hf (0: rows 16-31 x cols 0-15, 1: rows 48-63 x cols 32-47), row r, columns q4..q4+3
+  const int hf = tid >> 6, r2 = (tid >> 2) & 15, q4 = 4 * (tid & 3);
+  const bool l2 = tid < 128;
+  if (l2) {  // T = A_(2hf+1, 2hf) X_(2hf, 2hf)
+    const int ro = 32 * hf + 16, co = 32 * hf;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-  for (int d = 1; d < 4; ++d) {
-    const int i = jb + d;
-    const bool act = i < 4;
-    if (act) {  // T = sum_k A_ik X_kj, rows r, columns q4 .. q4 + 3
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k = jb; k < i; ++k)
-#pragma unroll
-        for (int s = 0; s < 16; ++s) {
-          const float a = A[(16 * i + r) * 65 + 16 * k + s];
-          const float4 x = *reinterpret_cast<const float4*>(X + (16 * k + s) * XS + 16 * jb + q4);
-          t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
-        }
-      *reinterpret_cast<float4*>(Tm + jb * 320 + r * 20 + q4) = t;
+    for (int s = 0; s < 16; ++s) {
+      const float a = A[(ro + r2) * 65 + co + s];
+      const float4 x = *reinterpret_cast<const float4*>(X + (co + s) * XS + co + q4);
+      t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
     }
-    __syncthreads();
-    if (act) {  // X_ij = -X_ii T
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int s = 0; s < 16; ++s) {
-        const float a = X[(16 * i + r) * XS + 16 * i + s];
-        const float4 t = *reinterpret_cast<const float4*>(Tm + jb * 320 + s * 20 + q4);
-        x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
-      }
-      *reinterpret_cast<float4*>(X + (16 * i + r) * XS + 16 * jb + q4) = make_float4(-x.x, -x.y, -x.z, -x.w);
-    }
-    __syncthreads();
+    *reinterpret_cast<float4*>(Tm + (hf * 16 + r2) * TS + q4) = t;
   }
+  __syncthreads();
+  if (l2) {  // X_(2hf+1, 2hf) = -X_(2hf+1, 2hf+1) T
+    const int ro = 32 * hf + 16, co = 32 * hf;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < 16; ++s) {
+      const float a = X[(ro + r2) * XS + ro + s];
+      const float4 t = *reinterpret_cast<const float4*>(Tm + (hf * 16 + s) * TS + q4);
+      x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
+    }
+    *reinterpret_cast<float4*>(X + (ro + r2) * XS + co + q4) = make_float4(-x.x, -x.y, -x.z, -x.w);
+  }
+  __syncthreads();
+  // level 3: row i of the lower 32 rows, columns j4..j4+3 of the left 32 columns
+  const int i3 = tid >> 3, j4 = 4 * (tid & 7);
+  {  // T = A[32:, :32] X[:32, :32]; X[k][j] is zero for k < 16 when j >= 16
+    const int k0 = j4 >= 16 ? 16 : 0;
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int k = k0; k < 32; ++k) {
+      const float a = A[(32 + i3) * 65 + k];
+      const float4 x = *reinterpret_cast<const float4*>(X + k * XS + j4);
+      t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
+    }
+    *reinterpret_cast<float4*>(Tm + i3 * TS + j4) = t;
+  }
+  __syncthreads();
+  {  // X[32:, :32] = -X[32:, 32:] T; X[32 + i][32 + k] is zero for k >= 16 when i < 16
+    const int k1 = i3 < 16 ? 16 : 32;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int k = 0; k < k1; ++k) {
+      const float a = X[(32 + i3) * XS + 32 + k];
+      const float4 t = *reinterpret_cast<const float4*>(Tm + k * TS + j4);
+      x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
+    }
+    *reinterpret_cast<float4*>(X + (32 + i3) * XS + j4) = make_float4(-x.x, -x.y, -x.z, -x.w);
+  }
+  __syncthreads();
 }
 
 __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
