@@ -862,6 +862,31 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def profile_column(args) -> None:
+    """One eager config-3 column forward+backward on ``--batch`` rows after ``--warmup`` warm-ups
+    (a single process, for an ncu capture of the attention kernels at a reduced size)."""
+    import torch
+
+    from vesper_b200.column import Column, ColumnShape, init_column_state, set_scan
+
+    device = torch.device("cuda", 0)
+    b, t, d = args.batch, C3["T"], C3["d"]
+    shape = ColumnShape(d=d, heads=C3["heads"], kv_groups=C3["kv_groups"], head_dim=C3["head_dim"],
+                        window=C3["window"], rotary_base=10000.0, ffn_mult=C3["ffn_mult"], block=64, key_conv=4)  # fmt: skip
+    col = Column(shape, torch.Generator().manual_seed(3)).to(device)
+    set_scan(col, "fused")
+    g = torch.Generator(device=device).manual_seed(5)
+    x = torch.randn(b, t, d, device=device, generator=g).requires_grad_()
+    up = torch.randn(b, t, d, device=device, generator=g)
+    pos = torch.arange(t, device=device).expand(b, t).contiguous()
+    for _ in range(max(args.warmup, 1) + 1):
+        state = init_column_state(shape, b, 1, torch.bfloat16, device)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y, _, _ = col.step(x, pos, state, 0)
+        torch.autograd.grad([(y.float() * up).sum()], [x, *col.parameters()])
+    torch.cuda.synchronize(device)
+
+
 def breakdown(args) -> None:
     """Device time per kernel of one leg under torch's profiler (CUPTI activity, no ncu):
     ``step`` one config-2 step, ``train`` one config-4 training step (eager), ``decode`` one
@@ -953,6 +978,8 @@ def main() -> None:
     p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")
+    p.add_argument("--profile-column", action="store_true",
+                   help="warm up, run one eager config-3 column fwd+bwd of --batch rows, exit (for ncu)")
     p.add_argument("--breakdown", choices=("step", "train", "decode"), default=None,
                    help="print one leg's device time per kernel group under torch's profiler, then exit")
     p.add_argument("--steps-ref", type=int, default=0, help="reference samples (default: min(steps, 10))")
@@ -961,6 +988,9 @@ def main() -> None:
     globals()["B"] = args.batch
     if args.breakdown:
         breakdown(args)
+        return
+    if args.profile_column:
+        profile_column(args)
         return
     if args.impl == "reference":
         if not args.steps_ref:
