@@ -19,6 +19,7 @@ namespace {
 
 constexpr int RUN = 64;        // tokens per warp
 constexpr int WARPS = 4;       // warps per CTA
+constexpr int PF = 8;          // input rows staged ahead of their use (a power of two)
 
 // EPL consecutive elements at p (aligned to their total size, up to 16 bytes) as one access per
 // 16 bytes, or one narrower access when they are fewer
@@ -57,6 +58,26 @@ __device__ __forceinline__ void st_elems(T* __restrict__ p, const float (&in)[EP
 #pragma unroll
     for (int i = 0; i < EPL; ++i) p[i] = from_f32<T>(in[i]);
   }
+}
+
+// ---- staging of input rows through shared memory (cp.async: the copies hold no registers) -----
+template <int BYTES>
+__device__ __forceinline__ void cp_async_bytes(uint32_t dst, const void* src) {
+  static_assert(BYTES == 4 || BYTES == 8 || BYTES == 16, "cp.async copies 4, 8 or 16 bytes");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(dst), "l"(src), "n"(BYTES) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// a lane's EPL elements of T from shared memory as floats
+template <typename T, int EPL>
+__device__ __forceinline__ void ld_staged(const uint8_t* p, float (&out)[EPL]) {
+  const T* e = reinterpret_cast<const T*>(p);
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) out[i] = to_f32<T>(e[i]);
 }
 
 // loads EPL channels [c, c+EPL) of row `t` of the filter input (z for t >= 0, else history)
@@ -204,8 +225,33 @@ __global__ void __launch_bounds__(WARPS * 32) keys_fwd_kernel(const T* __restric
   float2 st_pair = make_float2(0.f, 0.f);
 #pragma unroll
   for (int r = 1; r < K; ++r) load_in<T, EPL>(z, hist, b, t0 - r, T_, W, K, c, live, win[r]);
+  // the run's input rows stream PF rows ahead of their use through a per-warp ring in shared
+  // memory (each lane copies and later reads only its own EPL elements): the copies hold no
+  // registers, so the load latency leaves the per-token chain without costing occupancy
+  constexpr int BYTES = EPL * (int)sizeof(T);
+  constexpr bool STAGED = BYTES == 4 || BYTES == 8 || BYTES == 16;
+  __shared__ __align__(16) uint8_t ring[WARPS][PF][32][STAGED ? BYTES : 16];
+  uint8_t(*mine)[32][STAGED ? BYTES : 16] = ring[threadIdx.x >> 5];
+  auto issue = [&](int t) {
+    if constexpr (STAGED) {
+      if (live && t < t1) cp_async_bytes<BYTES>(smem_addr(mine[(t - t0) & (PF - 1)][lane]), z + ((int64_t)b * T_ + t) * W + c);
+      cp_async_commit_group();
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < PF; ++i) issue(t0 + i);
   for (int t = t0; t < t1; ++t) {
-    load_in<T, EPL>(z, hist, b, t, T_, W, K, c, live, win[0]);
+    if constexpr (STAGED) {
+      cp_async_wait_group<PF - 1>();  // row t's group is the oldest of PF in flight
+      if (live) ld_staged<T, EPL>(mine[(t - t0) & (PF - 1)][lane], win[0]);
+      else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) win[0][e] = 0.f;
+      }
+      issue(t + PF);  // the slot's row has been read into registers
+    } else {
+      load_in<T, EPL>(z, hist, b, t, T_, W, K, c, live, win[0]);
+    }
     float u[EPL];
 #pragma unroll
     for (int e = 0; e < EPL; ++e) {
