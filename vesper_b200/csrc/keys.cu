@@ -342,6 +342,51 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
       if (live) st_elems<T, EPL>(dz + ((int64_t)b * T_ + t) * W + c, o);
     }
   };
+  // the walk's inputs stream PF tokens ahead through a per-warp ring in shared memory: item t
+  // (t = thi, thi - 1, ..., t0) is input row t - K + 1 (history rows, t - K + 1 < 0, are read
+  // directly), key-gradient row t and, with STATS, the token's saved pair (copied by lane 0)
+  constexpr int BYTES = EPL * (int)sizeof(T);
+  constexpr bool STAGED = BYTES == 4 || BYTES == 8 || BYTES == 16;
+  constexpr int SB = STAGED ? BYTES : 16;
+  __shared__ __align__(16) uint8_t ring[WARPS][PF][2][32][SB];
+  __shared__ __align__(8) float2 sring[WARPS][PF];
+  const int wi = threadIdx.x >> 5;
+  const float2* st_row = STATS ? stats + ((int64_t)b * heads + head) * T_ : nullptr;
+  auto issue = [&](int t) {
+    if constexpr (STAGED) {
+      if (t >= t0) {
+        const int slot = (thi - t) & (PF - 1), zr = t - K + 1;
+        if (live && zr >= 0) cp_async_bytes<BYTES>(smem_addr(ring[wi][slot][0][lane]), z + ((int64_t)b * T_ + zr) * W + c);
+        if (live) cp_async_bytes<BYTES>(smem_addr(ring[wi][slot][1][lane]), gk + ((int64_t)b * T_ + t) * W + c);
+        if (STATS && lane == 0) cp_async_bytes<8>(smem_addr(&sring[wi][slot]), st_row + t);
+      }
+      cp_async_commit_group();
+    }
+  };
+  // token t's new window row (t - K + 1), key gradient and saved pair
+  auto take = [&](int t, float (&zrow)[EPL], float (&g)[EPL], float2& stat) {
+    if constexpr (STAGED) {
+      cp_async_wait_group<PF - 1>();  // item t's group is the oldest of PF in flight
+      __syncwarp();                   // lane 0's copy of the pair is visible to the warp
+      const int slot = (thi - t) & (PF - 1), zr = t - K + 1;
+      if (live && zr >= 0) ld_staged<T, EPL>(ring[wi][slot][0][lane], zrow);
+      else load_in<T, EPL>(z, hist, b, zr, T_, W, K, c, live, zrow);
+      if (live) ld_staged<T, EPL>(ring[wi][slot][1][lane], g);
+      else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) g[e] = 0.f;
+      }
+      if constexpr (STATS) stat = sring[wi][slot];
+      __syncwarp();  // every lane has read the slot before it is refilled
+      issue(t - PF);
+    } else {
+      load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, zrow);
+      load_g<T, EPL>(gk, b, t, T_, W, c, live, g);
+      if constexpr (STATS) stat = __ldg(st_row + t);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < PF; ++i) issue(thi - i);
   for (int t = thi; t >= t0; t -= 2) {
     const bool two = t - 1 >= t0;
     // token t's window: win[r] = row t - r (one row older than before); token t - 1's: wb
@@ -349,21 +394,18 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
     for (int r = 0; r < K - 1; ++r)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) win[r][e] = win[r + 1][e];
-    load_in<T, EPL>(z, hist, b, t - K + 1, T_, W, K, c, live, win[K - 1]);
+    float ga[EPL], gb[EPL];
+    float2 sa = make_float2(1.f, 1.f), sb = sa;
+    take(t, win[K - 1], ga, sa);
     float wb[K][EPL];
 #pragma unroll
     for (int r = 0; r < K - 1; ++r)
 #pragma unroll
       for (int e = 0; e < EPL; ++e) wb[r][e] = win[r + 1][e];
-    load_in<T, EPL>(z, hist, b, t - K, T_, W, K, c, live && two, wb[K - 1]);
-    float ga[EPL], gb[EPL];
-    load_g<T, EPL>(gk, b, t, T_, W, c, live, ga);
-    load_g<T, EPL>(gk, b, t - 1, T_, W, c, live && two, gb);
-    float2 sa = make_float2(1.f, 1.f), sb = sa;
-    if constexpr (STATS) {
-      const float2* st_row = stats + ((int64_t)b * heads + head) * T_;
-      sa = __ldg(st_row + t);
-      if (two) sb = __ldg(st_row + t - 1);
+    if (two) take(t - 1, wb[K - 1], gb, sb);
+    else {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) { wb[K - 1][e] = 0.f; gb[e] = 0.f; }
     }
     float da[EPL], db[EPL];
     token_du<EPL, K, STATS>(tp, win, ga, floor_, sa, da);
@@ -377,6 +419,7 @@ __global__ void __launch_bounds__(WARPS * 32) keys_bwd_kernel(
       step(t - 1, db, win);
     }
   }
+  if constexpr (STAGED) cp_async_wait_group<0>();
   if (live) {
     float* p = partial + (((int64_t)b * runs + run) * K) * W + c;
 #pragma unroll
