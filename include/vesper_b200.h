@@ -80,8 +80,8 @@ VB_API int vb_rms_norm_bwd_noalloc(const void *x, const float *weight, const voi
  * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's
  * dtype. z, keys: [B,T,W] (keys viewed [B,T,heads,W/heads]); hist: [B,K-1,W] float32;
  * taps: [K,W] float32. stats: [B,heads,T,2] float32 (8-byte aligned) or NULL: per token and head
- * 1/scale and 1/den of the normalisation, the second negated where the squared norm reaches 1
- * (where the clamp passes gradient), for vb_keys_bwd. Replaces vesper/kernels/keys_triton.py:148-156
+ * r = 1 / max(||u||, floor) (the key is u r) and -1 where the clamp passes gradient (+1 where the
+ * head vector stays below the floor), for vb_keys_bwd. Replaces vesper/kernels/keys_triton.py:148-156
  * (keys_forward) reached from vesper/kernels/keys.py:28-46 (fused_keys) and
  * vesper/column.py:255-289 (RecurrentSublayer.keys). */
 VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void *keys, float *stats,
@@ -90,7 +90,8 @@ VB_API int vb_keys_fwd(const void *z, const float *hist, const float *taps, void
 VB_API size_t vb_keys_bwd_workspace(int B, int T, int width, int heads, int taps_count);
 
 /* Gradients of sum(keys * grad_keys): grad_z [B,T,W] in z's dtype, grad_taps [K,W] float32
- * (fixed-order), grad_hist [B,K-1,W] float32 (skipped when NULL). stats: vb_keys_fwd's output for
+ * (fixed-order), grad_hist [B,K-1,W] float32 (skipped when NULL; 16-byte aligned, as the
+ * workspace). stats: vb_keys_fwd's output for
  * the same inputs, or NULL to recompute the statistics (slower). Replaces
  * vesper/kernels/keys_triton.py:159-177 (keys_backward) and vesper/kernels/keys.py:67-78
  * (_history_gradient). */

@@ -105,11 +105,19 @@ def test_saved_statistics_give_the_recomputed_gradients_at_the_clamp_boundary(dt
     z[0, 13, 5] = 3.0  # u[0, 13] of head 0 = taps[0, 5] * 3 at channel 5 only
     hist = torch.randn(b, count - 1, width, generator=g).to(CUDA)
     taps = (torch.randn(count, width, generator=g) * 0.5).to(CUDA)
+    # u[1, 33] of head 0 has norm 3e-7 at channel 7, below the floor: the clamp holds the gradient
+    z[1, 30:34, :128] = 0.0
+    z[1, 33, 7] = 3e-7 / float(taps[0, 7])
     zc = z.to(CUDA, dtype)
     grad_k = torch.randn(b, n, heads, width // heads, generator=g).to(CUDA, dtype)
     stats = torch.empty(b, heads, n, 2, device=CUDA)
     keys_forward(zc, hist, taps, heads, KEY_NORM_FLOOR, stats)
-    assert bool((stats[0, 0, 13, 1] < 0).item()) and float(stats[0, 0, 13, 1].abs()) == 1.0
+    # stats = (r, -1 where the clamp passes gradient): r = 1 / ||u|| above the floor, 1 / floor below
+    assert float(stats[0, 0, 13, 1]) == -1.0
+    u13 = float(taps[0, 5]) * float(zc[0, 13, 5])
+    assert abs(float(stats[0, 0, 13, 0]) * abs(u13) - 1.0) < 1e-6
+    assert float(stats[1, 0, 33, 1]) == 1.0
+    assert abs(float(stats[1, 0, 33, 0]) * KEY_NORM_FLOOR - 1.0) < 1e-6
     with_stats = keys_backward(zc, hist, taps, grad_k, heads, KEY_NORM_FLOOR, True, stats)
     recomputed = keys_backward(zc, hist, taps, grad_k, heads, KEY_NORM_FLOOR, True, None)
     for got, want in zip(with_stats, recomputed, strict=True):

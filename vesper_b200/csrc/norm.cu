@@ -274,22 +274,33 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_kernel(const T* __rest
   }
 }
 
-// out[j] = sum over p of partial[p][j]: lane <-> column, warp w sums parts w, w+8, ... in order,
-// then the 8 warp sums are added in warp order (a fixed tree: the same bits on every run)
-__global__ void __launch_bounds__(256) column_sum_kernel(const float* __restrict__ partial,
-                                                         float* __restrict__ out, int parts, int width) {
-  __shared__ float acc[8][33];
+// out[j] = sum over p of partial[p][j]: lane <-> column; warp w of 32 sums parts w, w+32, ... into
+// four interleaved accumulators (four loads in flight), then the 32 warp sums are added in warp
+// order (a fixed tree: the same bits on every run)
+constexpr int CS_WARPS = 32;
+__global__ void __launch_bounds__(CS_WARPS * 32) column_sum_kernel(const float* __restrict__ partial,
+                                                                   float* __restrict__ out, int parts, int width) {
+  __shared__ float acc[CS_WARPS][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = blockIdx.x * 32 + lane;
-  float t = 0.f;
-  if (j < width)
-    for (int p = warp; p < parts; p += 8) t += __ldg(partial + (size_t)p * width + j);
-  acc[warp][lane] = t;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (j < width) {
+    const float* p = partial + j;
+    int r = warp;
+    for (; r + 3 * CS_WARPS < parts; r += 4 * CS_WARPS) {
+      a0 += __ldg(p + (size_t)r * width);
+      a1 += __ldg(p + (size_t)(r + CS_WARPS) * width);
+      a2 += __ldg(p + (size_t)(r + 2 * CS_WARPS) * width);
+      a3 += __ldg(p + (size_t)(r + 3 * CS_WARPS) * width);
+    }
+    for (; r < parts; r += CS_WARPS) a0 += __ldg(p + (size_t)r * width);
+  }
+  acc[warp][lane] = (a0 + a1) + (a2 + a3);
   __syncthreads();
   if (warp == 0 && j < width) {
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += acc[w][lane];
+    for (int w = 0; w < CS_WARPS; ++w) s += acc[w][lane];
     out[j] = s;
   }
 }
@@ -321,7 +332,7 @@ int vpl_for(int width) {
 
 // Sums `parts` rows of `partial [parts, width]` in row order into out[width].
 int column_sum(const float* partial, float* out, int parts, int width, cudaStream_t st) {
-  column_sum_kernel<<<(width + 31) / 32, 256, 0, st>>>(partial, out, parts, width);
+  column_sum_kernel<<<(width + 31) / 32, CS_WARPS * 32, 0, st>>>(partial, out, parts, width);
   VB_LAUNCH_CHECK("column_sum");
   return VB_OK;
 }

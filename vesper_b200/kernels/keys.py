@@ -7,8 +7,8 @@ arithmetic, the key in ``z``'s dtype, ``[b, n, heads, d/heads]``. The backward i
 own gradient (the normalisation's scale held constant, the clamp at a squared norm of one passing
 gradient at and above it); the taps' gradient is summed in a fixed order and the history's is
 formed only when the history requires one. The forward saves each token's normalisation
-statistics (the reciprocals of scale and den, 8 bytes per token and head) for the backward,
-which then does not recompute them. Kernels: ``vb_keys_fwd`` / ``vb_keys_bwd``.
+statistics (``r = 1 / max(||u||, floor)`` and the clamp decision, 8 bytes per token and head) for
+the backward, which then does not recompute them. Kernels: ``vb_keys_fwd`` / ``vb_keys_bwd``.
 """
 
 from __future__ import annotations
@@ -50,7 +50,7 @@ def keys_forward(
     z: Tensor, hist: Tensor, taps: Tensor, heads: int, floor: float, stats: Tensor | None = None
 ) -> Tensor:
     """Keys ``[b, n, heads, d/heads]``; ``stats`` (float32 ``[b, heads, n, 2]``) receives each
-    token's 1/scale and 1/den (the second negated where the clamp passes gradient)."""
+    token's ``r = 1 / max(||u||, floor)`` and -1 where the clamp passes gradient (else +1)."""
     b, n, width = z.shape
     out = torch.empty(b, n, heads, width // heads, dtype=z.dtype, device=z.device)
     _lib.call(
