@@ -51,6 +51,15 @@ VB_API unsigned long long vb_launch_count(void);
 VB_API int vb_rms_norm_fwd(const void *x, const float *weight, void *y, float *inv, int64_t rows,
                     int width, float floor_, float eps, int dtype, void *stream);
 
+/* The forward with the output in another element type: a float32 x normalised in float32 and y
+ * rounded once to bf16 or f16 (y_dtype), as the norm's float32 output cast to the autocast dtype
+ * rounds it; equal dtypes are vb_rms_norm_fwd. Replaces the norm followed by the cast that every
+ * consumer of a float32 norm output makes under autocast (vesper/column.py:159-188 RMSNorm, its
+ * output fed to F.linear). */
+VB_API int vb_rms_norm_fwd_cast(const void *x, const float *weight, void *y, float *inv, int64_t rows,
+                                int width, float floor_, float eps, int x_dtype, int y_dtype,
+                                void *stream);
+
 /* Bytes of workspace vb_rms_norm_bwd needs (the gain gradient's fixed-order partial sums). */
 VB_API size_t vb_rms_norm_bwd_workspace(int64_t rows, int width);
 
@@ -59,6 +68,13 @@ VB_API size_t vb_rms_norm_bwd_workspace(int64_t rows, int width);
 VB_API int vb_rms_norm_bwd(const void *x, const float *weight, const void *dy, const float *inv,
                     void *dx, float *dweight, void *workspace, int64_t rows, int width,
                     int dtype, void *stream);
+
+/* The backward of vb_rms_norm_fwd_cast: dy in y's dtype (bf16 or f16, read as float32 exactly),
+ * x and dx float32; equal dtypes are vb_rms_norm_bwd. Replaces the cast's backward followed by
+ * vesper/kernels/norm_triton.py:96-109 (rms_backward). */
+VB_API int vb_rms_norm_bwd_cast(const void *x, const float *weight, const void *dy, const float *inv,
+                                void *dx, float *dweight, void *workspace, int64_t rows, int width,
+                                int x_dtype, int dy_dtype, void *stream);
 
 /* The same backward as vb_rms_norm_bwd for callers that cannot allocate device memory (a plugin
  * host with a pre-planned memory budget, a loop that must not allocate, a capture or memory plan

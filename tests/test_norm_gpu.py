@@ -89,3 +89,24 @@ def test_captured_equals_eager_bitwise_and_repeats() -> None:
         graph.replay()
         torch.cuda.synchronize()
         assert all(torch.equal(a, b) for a, b in zip(out, eager[0], strict=True))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("width", [512, 1024, 36])
+def test_float32_input_rounded_in_the_kernel_equals_the_norm_then_a_cast(dtype: torch.dtype, width: int) -> None:
+    """``out_dtype`` rounds the float32 result inside the kernel: the same bits as the float32 norm
+    followed by ``.to(dtype)``, forward and both gradients (the incoming gradient in ``dtype``), on
+    the vector path (widths 512, 1024) and the scalar one (36)."""
+    g = torch.Generator(device=CUDA).manual_seed(5)
+    x = 3 * torch.randn(777, width, device=CUDA, generator=g)
+    gain = 1 + 0.1 * torch.randn(width, device=CUDA, generator=g)
+    up = torch.randn(777, width, device=CUDA, generator=g).to(dtype)
+    outs = []
+    for fused in (True, False):
+        xs, w = x.clone().requires_grad_(), gain.clone().requires_grad_()
+        y = fused_rms_norm(xs, w, FLOOR, EPS, dtype) if fused else fused_rms_norm(xs, w, FLOOR, EPS).to(dtype)
+        assert y.dtype == dtype
+        y.backward(up)
+        outs.append((y.detach(), xs.grad, w.grad))
+    for got, want in zip(*outs, strict=True):
+        assert torch.equal(got, want)

@@ -164,8 +164,9 @@ class RMSNorm(nn.Module):
 
     Every consumer of a norm's output in the column, the halting head and the output head is a
     matrix product, which autocast runs in its lower dtype, casting its float32 input each time.
-    Under CUDA autocast the output is therefore cast once here instead: the same cast, so the
-    same values and gradients, made once per norm instead of once per product.
+    Under CUDA autocast the kernel therefore rounds its float32 result to the autocast dtype as it
+    stores it (and its backward reads that dtype's gradient): the same rounding as a cast, so the
+    same values and gradients, with no float32 output and no cast kernels either way.
     """
 
     def __init__(self, d: int) -> None:
@@ -177,10 +178,10 @@ class RMSNorm(nn.Module):
         if x.shape[-1] != d:
             msg = f"RMSNorm: last axis must be {d}, got {x.shape[-1]} (shape {tuple(x.shape)})"
             raise ContractError(msg)
-        y = fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS)
-        if y.dtype == torch.float32 and y.is_cuda and torch.is_autocast_enabled("cuda"):
-            y = y.to(torch.get_autocast_dtype("cuda"))
-        return y
+        out = None
+        if x.dtype == torch.float32 and x.is_cuda and torch.is_autocast_enabled("cuda"):
+            out = torch.get_autocast_dtype("cuda")  # rounded inside the kernel, no cast kernels
+        return fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS, out)
 
 
 class RecurrentSublayer(nn.Module):

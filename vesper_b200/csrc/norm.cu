@@ -7,6 +7,7 @@
 // warp in registers, per CTA in warp order, then across CTAs in CTA order by a second kernel: no
 // atomics, the same bits on every run.
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -43,6 +44,23 @@ __device__ __forceinline__ void load_raw(const void* __restrict__ row, int nv, i
     r[i] = vi < nv ? __ldg(reinterpret_cast<const uint4*>(row) + vi) : make_uint4(0u, 0u, 0u, 0u);
   }
 }
+// the raw 8-byte words of a row of 8-byte element groups (zero past the width)
+template <int VPL>
+__device__ __forceinline__ void load_raw(const void* __restrict__ row, int nv, int lane, uint2 (&r)[VPL]) {
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int vi = lane + 32 * i;
+    r[i] = vi < nv ? __ldg(reinterpret_cast<const uint2*>(row) + vi) : make_uint2(0u, 0u);
+  }
+}
+// E elements of T from a raw word group (16 or 8 bytes)
+template <typename T, int E, typename W>
+__device__ __forceinline__ void unpack_e(const W& raw, float (&f)[E]) {
+  static_assert(sizeof(W) == E * sizeof(T), "the raw group holds E elements");
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < E; ++i) f[i] = to_f32<T>(e[i]);
+}
 template <typename T>
 __device__ __forceinline__ void unpack(const uint4& raw, float (&f)[16 / sizeof(T)]) {
   const T* e = reinterpret_cast<const T*>(&raw);
@@ -60,20 +78,49 @@ __device__ __forceinline__ void load_gain(const float* __restrict__ w, int vi, f
   }
 }
 
-template <typename T, int VPL>
-__global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const T* __restrict__ x,
+// E consecutive elements of T (E * sizeof(T) = 16 or 8 bytes, aligned to that) as floats, and back
+template <typename T, int E>
+__device__ __forceinline__ void ld_e(const T* __restrict__ p, float (&out)[E]) {
+  if constexpr (E * sizeof(T) == 16) {
+    load_vec<T, E>(p, out);
+  } else {
+    static_assert(E * sizeof(T) == 8, "8- or 16-byte element groups");
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < E; ++i) out[i] = to_f32<T>(e[i]);
+  }
+}
+template <typename T, int E>
+__device__ __forceinline__ void st_e(T* __restrict__ p, const float (&in)[E]) {
+  if constexpr (E * sizeof(T) == 16) {
+    store_vec<T, E>(p, in);
+  } else {
+    static_assert(E * sizeof(T) == 8, "8- or 16-byte element groups");
+    uint2 raw;
+    T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < E; ++i) e[i] = from_f32<T>(in[i]);
+    *reinterpret_cast<uint2*>(p) = raw;
+  }
+}
+
+// TX: the input's element type, TY: the output's (TX itself, or a 16-bit type for a float32 input,
+// the output then rounded once from the float32 result, as a cast of it would round it)
+template <typename TX, typename TY, int VPL>
+__global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const TX* __restrict__ x,
                                                                  const float* __restrict__ w,
-                                                                 T* __restrict__ y, float* __restrict__ inv,
+                                                                 TY* __restrict__ y, float* __restrict__ inv,
                                                                  int64_t rows, int width, float floor_,
                                                                  float eps) {
-  constexpr int E = 16 / sizeof(T);
+  constexpr int E = 16 / sizeof(TX);
   const int lane = threadIdx.x & 31;
   const int64_t row0 = ((int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5)) * FWD_ROWS_PER_WARP;
   const int nv = width / E;
   float v[FWD_ROWS_PER_WARP][VPL][E];
 #pragma unroll
   for (int r = 0; r < FWD_ROWS_PER_WARP; ++r)
-    if (row0 + r < rows) load_row<T, VPL>(x + (row0 + r) * width, nv, lane, v[r]);
+    if (row0 + r < rows) load_row<TX, VPL>(x + (row0 + r) * width, nv, lane, v[r]);
 #pragma unroll
   for (int r = 0; r < FWD_ROWS_PER_WARP; ++r) {
     const int64_t row = row0 + r;
@@ -111,24 +158,24 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_vec_kernel(const T* __rest
         }
 #pragma unroll
         for (int e = 0; e < E; ++e) o[e] = v[r][i][e] * (rrms * g[e]);
-        store_vec<T, E>(y + row * width + vi * E, o);
+        st_e<TY, E>(y + row * width + vi * E, o);
       }
     }
     if (lane == 0) inv[row] = 1.0f / (scale * rms);
   }
 }
 
-template <typename T>
+template <typename T, typename TY>
 __global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict__ x,
                                                              const float* __restrict__ w,
-                                                             T* __restrict__ y, float* __restrict__ inv,
+                                                             TY* __restrict__ y, float* __restrict__ inv,
                                                              int64_t rows, int width, float floor_,
                                                              float eps) {
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
   const T* xr = x + row * width;
-  T* yr = y + row * width;
+  TY* yr = y + row * width;
   float amax = 0.f;
   for (int j = lane; j < width; j += 32) amax = fmaxf(amax, fabsf(to_f32<T>(xr[j])));
   const float scale = fmaxf(warp_max(amax), floor_);
@@ -140,17 +187,19 @@ __global__ void __launch_bounds__(WARPS * 32) rms_fwd_kernel(const T* __restrict
   }
   const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
   const float rrms = 1.0f / rms;
-  for (int j = lane; j < width; j += 32) yr[j] = from_f32<T>(to_f32<T>(xr[j]) * rscale * (rrms * __ldg(w + j)));
+  for (int j = lane; j < width; j += 32) yr[j] = from_f32<TY>(to_f32<T>(xr[j]) * rscale * (rrms * __ldg(w + j)));
   if (lane == 0) inv[row] = 1.0f / (scale * rms);
 }
 
 // Vector backward: each warp walks BWD_ROWS_PER_WARP rows with the next row's x and dy loaded
 // while the current one is computed; the gain gradient stays in registers per lane, then is
 // summed over the CTA's warps in warp order into partial[blockIdx.x][width].
-template <typename T, int VPL>
+// TD: the incoming gradient's element type (T itself, or a 16-bit type for a float32 input whose
+// output was rounded to it); dx in T.
+template <typename T, typename TD, int VPL>
 __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T* __restrict__ x,
                                                                         const float* __restrict__ w,
-                                                                        const T* __restrict__ dy,
+                                                                        const TD* __restrict__ dy,
                                                                         const float* __restrict__ inv,
                                                                         T* __restrict__ dx,
                                                                         float* __restrict__ partial,
@@ -165,7 +214,9 @@ __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T*
 #pragma unroll
     for (int e = 0; e < E; ++e) acc[i][e] = 0.f;
   const int64_t row0 = (int64_t)blockIdx.x * BWD_ROWS_PER_CTA;
-  uint4 xr[2][VPL], dr[2][VPL];
+  using DRaw = typename std::conditional<E * sizeof(TD) == 16, uint4, uint2>::type;
+  uint4 xr[2][VPL];
+  DRaw dr[2][VPL];
   int64_t row = row0 + warp;
   if (row < rows) {
     load_raw<VPL>(x + row * width, nv, lane, xr[0]);
@@ -189,7 +240,7 @@ __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T*
       if (vi < nv) {
         float xv[E], dv[E], g[E];
         unpack<T>(xr[cur][i], xv);
-        unpack<T>(dr[cur][i], dv);
+        unpack_e<TD, E>(dr[cur][i], dv);
         load_gain<E>(w, vi, g);
 #pragma unroll
         for (int e = 0; e < E; ++e) s += dv[e] * g[e] * (xv[e] * iv);
@@ -202,7 +253,7 @@ __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T*
       if (vi < nv) {
         float xv[E], dv[E], g[E], o[E];
         unpack<T>(xr[cur][i], xv);
-        unpack<T>(dr[cur][i], dv);
+        unpack_e<TD, E>(dr[cur][i], dv);
         load_gain<E>(w, vi, g);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
@@ -232,10 +283,10 @@ __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T*
 }
 
 // Scalar backward for widths without a 16-byte vector path.
-template <typename T>
+template <typename T, typename TD>
 __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_kernel(const T* __restrict__ x,
                                                                  const float* __restrict__ w,
-                                                                 const T* __restrict__ dy,
+                                                                 const TD* __restrict__ dy,
                                                                  const float* __restrict__ inv,
                                                                  T* __restrict__ dx,
                                                                  float* __restrict__ partial,
@@ -249,18 +300,18 @@ __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_kernel(const T* __rest
     const int64_t row = row0 + (int64_t)k * BWD_WARPS + warp;
     if (row >= rows) break;
     const T* xr = x + row * width;
-    const T* dr = dy + row * width;
+    const TD* dr = dy + row * width;
     const float iv = __ldg(inv + row);
     float s = 0.f;
     for (int j = lane; j < width; j += 32) {
       const float xh = to_f32<T>(xr[j]) * iv;
-      s += to_f32<T>(dr[j]) * __ldg(w + j) * xh;
+      s += to_f32<TD>(dr[j]) * __ldg(w + j) * xh;
     }
     const float mean = warp_sum(s) / (float)width;
     T* out = dx + row * width;
     for (int j = lane; j < width; j += 32) {
       const float xh = to_f32<T>(xr[j]) * iv;
-      const float d = to_f32<T>(dr[j]);
+      const float d = to_f32<TD>(dr[j]);
       out[j] = from_f32<T>(iv * (d * __ldg(w + j) - xh * mean));
       mine[j] += d * xh;
     }
@@ -337,26 +388,62 @@ int column_sum(const float* partial, float* out, int parts, int width, cudaStrea
   return VB_OK;
 }
 
-// dx and the per-CTA gain partials (vector path when the width allows), then the fixed-order sum
+// Dispatches (input, other) element types: the same type, or a float32 input with a bf16 or f16
+// other side (the output of the forward, the incoming gradient of the backward).
+#define VB_DISPATCH_PAIR(xcode, ocode, TX, TO, ...)                                                      \
+  [&]() -> int {                                                                                          \
+    if ((xcode) == (ocode)) return VB_DISPATCH_DTYPE(xcode, TX, [&]() -> int { using TO = TX; return __VA_ARGS__(); }); \
+    if ((xcode) == VB_F32 && (ocode) == VB_BF16) { using TX = float; using TO = __nv_bfloat16; return __VA_ARGS__(); } \
+    if ((xcode) == VB_F32 && (ocode) == VB_F16) { using TX = float; using TO = __half; return __VA_ARGS__(); }        \
+    ::vb::set_error("rms_norm: element types %d and %d: the same type, or float32 with bf16 or f16", (int)(xcode), \
+                    (int)(ocode));                                                                       \
+    return VB_ERR_INVALID;                                                                                \
+  }()
+
+// y (in TY) and inv (vector path when the width allows)
+int launch_fwd(const void* x, const float* weight, void* y, float* inv, int64_t rows, int width, float floor_,
+               float eps, int xcode, int ycode, cudaStream_t st) {
+  return VB_DISPATCH_PAIR(xcode, ycode, T, TY, [&]() -> int {
+    const int vpl = vpl_for<T>(width);
+    if (vpl && aligned16(x) && aligned16(y) && aligned16(weight)) {
+      const int64_t per = (int64_t)WARPS * FWD_ROWS_PER_WARP;
+      const int ctas = (int)((rows + per - 1) / per);
+      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
+        rms_fwd_vec_kernel<T, TY, VPL><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (TY*)y, inv, rows,
+                                                                    width, floor_, eps);
+        return 0;
+      });
+    } else {
+      const int ctas = (int)((rows + WARPS - 1) / WARPS);
+      rms_fwd_kernel<T, TY><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (TY*)y, inv, rows, width,
+                                                         floor_, eps);
+    }
+    VB_LAUNCH_CHECK("rms_norm_fwd");
+    return VB_OK;
+  });
+}
+
+// dx (in x's type) and the per-CTA gain partials (vector path when the width allows), then the
+// fixed-order sum
 int launch_bwd(const void* x, const float* weight, const void* dy, const float* inv, void* dx, float* dweight,
-               float* partial, int64_t rows, int width, int dtype, cudaStream_t st) {
+               float* partial, int64_t rows, int width, int xcode, int dycode, cudaStream_t st) {
   const int ctas = bwd_ctas(rows);
   const size_t smem = sizeof(float) * BWD_WARPS * width;
-  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
+  return VB_DISPATCH_PAIR(xcode, dycode, T, TD, [&]() -> int {
     const int vpl = vpl_for<T>(width);
     if (vpl && aligned16(x) && aligned16(dy) && aligned16(dx)) {
       VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
         if (smem > 48 * 1024)
-          cudaFuncSetAttribute(rms_bwd_vec_kernel<T, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        rms_bwd_vec_kernel<T, VPL><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv,
-                                                                       (T*)dx, partial, rows, width);
+          cudaFuncSetAttribute(rms_bwd_vec_kernel<T, TD, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        rms_bwd_vec_kernel<T, TD, VPL><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const TD*)dy,
+                                                                           inv, (T*)dx, partial, rows, width);
         return 0;
       });
     } else {
       if (smem > 48 * 1024)
-        cudaFuncSetAttribute(rms_bwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      rms_bwd_kernel<T><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const T*)dy, inv, (T*)dx,
-                                                            partial, rows, width);
+        cudaFuncSetAttribute(rms_bwd_kernel<T, TD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      rms_bwd_kernel<T, TD><<<ctas, BWD_WARPS * 32, smem, st>>>((const T*)x, weight, (const TD*)dy, inv, (T*)dx,
+                                                                partial, rows, width);
     }
     VB_LAUNCH_CHECK("rms_norm_bwd");
     return column_sum(partial, dweight, ctas, width, st);
@@ -372,25 +459,15 @@ extern "C" int vb_rms_norm_fwd(const void* x, const float* weight, void* y, floa
   VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_fwd: bad shape rows=%lld width=%d", (long long)rows, width);
   if (rows == 0) return VB_OK;
   VB_REQUIRE(x && weight && y && inv, "rms_norm_fwd: null pointer");
-  cudaStream_t st = (cudaStream_t)stream;
-  return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
-    const int vpl = vpl_for<T>(width);
-    if (vpl && aligned16(x) && aligned16(y) && aligned16(weight)) {
-      const int64_t per = (int64_t)WARPS * FWD_ROWS_PER_WARP;
-      const int ctas = (int)((rows + per - 1) / per);
-      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
-        rms_fwd_vec_kernel<T, VPL><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows,
-                                                                width, floor_, eps);
-        return 0;
-      });
-    } else {
-      const int ctas = (int)((rows + WARPS - 1) / WARPS);
-      rms_fwd_kernel<T><<<ctas, WARPS * 32, 0, st>>>((const T*)x, weight, (T*)y, inv, rows, width,
-                                                     floor_, eps);
-    }
-    VB_LAUNCH_CHECK("rms_norm_fwd");
-    return VB_OK;
-  });
+  return launch_fwd(x, weight, y, inv, rows, width, floor_, eps, dtype, dtype, (cudaStream_t)stream);
+}
+
+extern "C" int vb_rms_norm_fwd_cast(const void* x, const float* weight, void* y, float* inv, int64_t rows,
+                                    int width, float floor_, float eps, int x_dtype, int y_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_fwd_cast: bad shape rows=%lld width=%d", (long long)rows, width);
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(x && weight && y && inv, "rms_norm_fwd_cast: null pointer");
+  return launch_fwd(x, weight, y, inv, rows, width, floor_, eps, x_dtype, y_dtype, (cudaStream_t)stream);
 }
 
 extern "C" size_t vb_rms_norm_bwd_workspace(int64_t rows, int width) {
@@ -408,7 +485,21 @@ extern "C" int vb_rms_norm_bwd(const void* x, const float* weight, const void* d
     return VB_OK;
   }
   VB_REQUIRE(x && weight && dy && inv && dx && dweight && workspace, "rms_norm_bwd: null pointer");
-  return launch_bwd(x, weight, dy, inv, dx, dweight, (float*)workspace, rows, width, dtype, st);
+  return launch_bwd(x, weight, dy, inv, dx, dweight, (float*)workspace, rows, width, dtype, dtype, st);
+}
+
+extern "C" int vb_rms_norm_bwd_cast(const void* x, const float* weight, const void* dy, const float* inv,
+                                    void* dx, float* dweight, void* workspace, int64_t rows, int width,
+                                    int x_dtype, int dy_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "rms_norm_bwd_cast: bad shape rows=%lld width=%d", (long long)rows, width);
+  VB_REQUIRE(width <= 4096, "rms_norm_bwd_cast: width %d exceeds the kernel's 4096", width);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows == 0) {
+    VB_CUDA_CHECK(cudaMemsetAsync(dweight, 0, sizeof(float) * width, st), "rms_norm_bwd_cast");
+    return VB_OK;
+  }
+  VB_REQUIRE(x && weight && dy && inv && dx && dweight && workspace, "rms_norm_bwd_cast: null pointer");
+  return launch_bwd(x, weight, dy, inv, dx, dweight, (float*)workspace, rows, width, x_dtype, dy_dtype, st);
 }
 
 // ---- RMSNorm backward without allocation ------------------------------------------------------
@@ -465,5 +556,5 @@ extern "C" int vb_rms_norm_bwd_noalloc(const void* x, const float* weight, const
   int rc = scratch_on_current_device(&partial);
   if (rc) return rc;
   // every partial row this call reads is written by this call first: nothing needs clearing
-  return launch_bwd(x, weight, dy, inv, dx, dweight, partial, rows, width, dtype, st);
+  return launch_bwd(x, weight, dy, inv, dx, dweight, partial, rows, width, dtype, dtype, st);
 }

@@ -20,8 +20,12 @@ from vesper_b200.contracts import ContractError
 SUPPORTED = (torch.float32, torch.bfloat16, torch.float16)
 
 
-def fused_rms_norm(x: Tensor, weight: Tensor, floor: float, eps: float) -> Tensor:
-    """``[..., d] -> [..., d]`` in ``x``'s dtype; ``x`` on CUDA, ``weight [d]``."""
+def fused_rms_norm(x: Tensor, weight: Tensor, floor: float, eps: float, out_dtype: torch.dtype | None = None) -> Tensor:
+    """``[..., d] -> [..., d]`` in ``x``'s dtype; ``x`` on CUDA, ``weight [d]``.
+
+    ``out_dtype`` (bf16 or f16, for a float32 ``x``) rounds the float32 result once to that dtype
+    inside the kernel: the values and gradients of the norm followed by ``.to(out_dtype)``, with no
+    float32 output tensor and no cast kernels either way."""
     if x.device.type != "cuda":
         msg = f"the fused RMSNorm runs on CUDA only, got x on {x.device}"
         raise ContractError(msg)
@@ -31,49 +35,59 @@ def fused_rms_norm(x: Tensor, weight: Tensor, floor: float, eps: float) -> Tenso
     if weight.shape != (x.shape[-1],):
         msg = f"weight: expected shape ({x.shape[-1]},), got {tuple(weight.shape)}"
         raise ContractError(msg)
+    if out_dtype is not None and out_dtype != x.dtype and not (
+        x.dtype == torch.float32 and out_dtype in (torch.bfloat16, torch.float16)
+    ):
+        msg = f"out_dtype: a float32 input rounds to bf16 or f16, got {x.dtype} -> {out_dtype}"
+        raise ContractError(msg)
     rows = x.reshape(-1, x.shape[-1])
-    out: Tensor = _FusedRMSNorm.apply(rows, weight, floor, eps)
+    out: Tensor = _FusedRMSNorm.apply(rows, weight, floor, eps, out_dtype or x.dtype)
     return out.view(x.shape)
 
 
-def rms_forward(x: Tensor, weight: Tensor, floor: float, eps: float) -> tuple[Tensor, Tensor]:
-    """``(y, inv)`` of row-contiguous ``x [N, d]``: ``y`` in ``x``'s dtype, ``inv`` float32."""
+def rms_forward(x: Tensor, weight: Tensor, floor: float, eps: float,
+                out_dtype: torch.dtype | None = None) -> tuple[Tensor, Tensor]:  # fmt: skip
+    """``(y, inv)`` of row-contiguous ``x [N, d]``: ``y`` in ``out_dtype`` (default ``x``'s),
+    ``inv`` float32."""
     n, width = x.shape
-    y = torch.empty_like(x)
+    dtype = out_dtype or x.dtype
+    y = torch.empty(n, width, dtype=dtype, device=x.device)
     inv = torch.empty(n, dtype=torch.float32, device=x.device)
     w32 = weight.to(torch.float32).contiguous()
     _lib.call(
-        "vb_rms_norm_fwd", x.data_ptr(), w32.data_ptr(), y.data_ptr(), inv.data_ptr(), n, width,
-        floor, eps, _lib.DTYPE_CODE[x.dtype], _lib.stream(x.device),
+        "vb_rms_norm_fwd_cast", x.data_ptr(), w32.data_ptr(), y.data_ptr(), inv.data_ptr(), n, width,
+        floor, eps, _lib.DTYPE_CODE[x.dtype], _lib.DTYPE_CODE[dtype], _lib.stream(x.device),
     )  # fmt: skip
     return y, inv
 
 
 def rms_backward(x: Tensor, weight: Tensor, dy: Tensor, inv: Tensor) -> tuple[Tensor, Tensor]:
-    """``(dx, dg)``: the input's gradient in ``x``'s dtype and the gain's in float32."""
+    """``(dx, dg)``: the input's gradient in ``x``'s dtype and the gain's in float32; ``dy`` in
+    ``x``'s dtype or, for a float32 ``x``, in bf16 or f16."""
     n, width = x.shape
     dx = torch.empty_like(x)
     dg = torch.empty(width, dtype=torch.float32, device=x.device)
     w32 = weight.to(torch.float32).contiguous()
     ws = _lib.workspace(_lib.query("vb_rms_norm_bwd_workspace", n, width), x.device)
     _lib.call(
-        "vb_rms_norm_bwd", x.data_ptr(), w32.data_ptr(), dy.data_ptr(), inv.data_ptr(),
+        "vb_rms_norm_bwd_cast", x.data_ptr(), w32.data_ptr(), dy.data_ptr(), inv.data_ptr(),
         dx.data_ptr(), dg.data_ptr(), ws.data_ptr(), n, width, _lib.DTYPE_CODE[x.dtype],
-        _lib.stream(x.device),
+        _lib.DTYPE_CODE[dy.dtype], _lib.stream(x.device),
     )  # fmt: skip
     return dx, dg
 
 
 class _FusedRMSNorm(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x: Tensor, weight: Tensor, floor: float, eps: float) -> Tensor:  # type: ignore[override]
+    def forward(ctx, x: Tensor, weight: Tensor, floor: float, eps: float, out_dtype: torch.dtype) -> Tensor:  # type: ignore[override]
         rows = x.contiguous()
-        y, inv = rms_forward(rows, weight, floor, eps)
+        y, inv = rms_forward(rows, weight, floor, eps, out_dtype)
         ctx.save_for_backward(rows, weight, inv)
+        ctx.out_dtype = out_dtype
         return y
 
     @staticmethod
     def backward(ctx, dy: Tensor):  # type: ignore[override]
         rows, weight, inv = ctx.saved_tensors
-        dx, dg = rms_backward(rows, weight, dy.contiguous().to(rows.dtype), inv)
-        return dx, dg.to(weight.dtype), None, None
+        dx, dg = rms_backward(rows, weight, dy.contiguous().to(ctx.out_dtype), inv)
+        return dx, dg.to(weight.dtype), None, None, None
