@@ -76,6 +76,25 @@ VB_API int vb_rms_norm_bwd_cast(const void *x, const float *weight, const void *
                                 void *dx, float *dweight, void *workspace, int64_t rows, int width,
                                 int x_dtype, int dy_dtype, void *stream);
 
+/* A residual add fused with the RMSNorm that reads its sum, over a float32 residual stream:
+ * sum = x + r (x, sum float32; r float32, bf16 or f16, added as float32 in one IEEE addition),
+ * y = RMSNorm(sum) in y_dtype (rounded once, as vb_rms_norm_fwd_cast), inv as vb_rms_norm_fwd.
+ * width a multiple of 4 up to 1024, every tensor 16-byte aligned. Replaces the column's
+ * `x = x + r` followed by the next sublayer's norm (vesper/column.py:709-812 Column.step,
+ * :159-188 RMSNorm). */
+VB_API int vb_add_rms_norm_fwd(const float *x, const void *r, const float *weight, float *sum, void *y,
+                               float *inv, int64_t rows, int width, float floor_, float eps, int r_dtype,
+                               int y_dtype, void *stream);
+
+/* Its backward: d = RMSNorm'(sum) dy + dsum (dsum: the sum's gradient from its other readers,
+ * float32, or NULL for none), dx = d (float32), dr = d rounded to r_dtype (skipped when NULL),
+ * dweight as vb_rms_norm_bwd (workspace of vb_rms_norm_bwd_workspace bytes). dy in dy_dtype.
+ * Replaces the norm's backward, the gradient sum autograd forms for the sum, and the add's
+ * backward cast. */
+VB_API int vb_add_rms_norm_bwd(const float *sum, const float *weight, const void *dy, const float *inv,
+                               const float *dsum, float *dx, void *dr, float *dweight, void *workspace,
+                               int64_t rows, int width, int dy_dtype, int r_dtype, void *stream);
+
 /* The same backward as vb_rms_norm_bwd for callers that cannot allocate device memory (a plugin
  * host with a pre-planned memory budget, a loop that must not allocate, a capture or memory plan
  * an allocation would break): no workspace argument, and no cudaMalloc, cudaFree or allocating

@@ -110,3 +110,31 @@ def test_float32_input_rounded_in_the_kernel_equals_the_norm_then_a_cast(dtype: 
         outs.append((y.detach(), xs.grad, w.grad))
     for got, want in zip(*outs, strict=True):
         assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize(("rdtype", "out"), [(torch.bfloat16, torch.bfloat16), (torch.float32, None), (torch.float16, torch.float16)])
+def test_residual_add_fused_with_the_norm_equals_the_add_then_the_norm(rdtype: torch.dtype, out) -> None:
+    """``add_rms_norm`` (one kernel each way) gives the same bits as ``x + r`` followed by the
+    norm: the sum, the norm, and the gradients of x, r and the gain when both the sum and the norm
+    are read downstream (the column's residual stream)."""
+    from vesper_b200.kernels.norm import add_rms_norm
+
+    g = torch.Generator(device=CUDA).manual_seed(6)
+    x = 3 * torch.randn(1000, 512, device=CUDA, generator=g)
+    r = torch.randn(1000, 512, device=CUDA, generator=g).to(rdtype)
+    gain = 1 + 0.1 * torch.randn(512, device=CUDA, generator=g)
+    up_s = torch.randn(1000, 512, device=CUDA, generator=g)
+    up_y = torch.randn(1000, 512, device=CUDA, generator=g).to(out or torch.float32)
+    outs = []
+    for fused in (True, False):
+        xs, rs, w = x.clone().requires_grad_(), r.clone().requires_grad_(), gain.clone().requires_grad_()
+        if fused:
+            s, y = add_rms_norm(xs, rs, w, FLOOR, EPS, out)
+        else:
+            s = xs + rs
+            y = fused_rms_norm(s, w, FLOOR, EPS, out)
+        torch.autograd.backward([s, y], [up_s, up_y])
+        outs.append((s.detach(), y.detach(), xs.grad, rs.grad, w.grad))
+    for got, want in zip(*outs, strict=True):
+        assert got.dtype == want.dtype
+        assert torch.equal(got, want)

@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_rms_norm_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I, _I, _P]),
     "vb_rms_norm_fwd_cast": (_I, [_P, _P, _P, _P, _I64, _I, _F, _F, _I, _I, _P]),
     "vb_rms_norm_bwd_cast": (_I, [_P, _P, _P, _P, _P, _P, _P, _I64, _I, _I, _I, _P]),
+    "vb_add_rms_norm_fwd": (_I, [_P] * 6 + [_I64, _I, _F, _F, _I, _I, _P]),
+    "vb_add_rms_norm_bwd": (_I, [_P] * 9 + [_I64, _I, _I, _I, _P]),
     "vb_keys_fwd": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P]),
     "vb_keys_bwd_workspace": (_SZ, [_I, _I, _I, _I, _I]),
     "vb_keys_bwd": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _I, _P]),

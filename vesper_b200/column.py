@@ -35,7 +35,7 @@ from vesper_b200.kernels.delta_scan import (
     fused_scan_available,
 )
 from vesper_b200.kernels.keys import fused_keys
-from vesper_b200.kernels.norm import fused_rms_norm
+from vesper_b200.kernels.norm import add_rms_norm, fused_rms_norm
 
 ScanImpl = Literal["fused", "fused-fp32"]
 SCAN_IMPLS: tuple[ScanImpl, ...] = ("fused", "fused-fp32")
@@ -178,10 +178,24 @@ class RMSNorm(nn.Module):
         if x.shape[-1] != d:
             msg = f"RMSNorm: last axis must be {d}, got {x.shape[-1]} (shape {tuple(x.shape)})"
             raise ContractError(msg)
-        out = None
+        return fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS, self._out_dtype(x))
+
+    def add_forward(self, x: Tensor, r: Tensor) -> tuple[Tensor, Tensor]:
+        """``(x + r, forward(x + r))``: the residual add and this norm of its sum, one kernel each
+        way over a float32 residual stream (the same values and gradients as the two steps)."""
+        d = self.weight.shape[0]
+        if x.shape[-1] != d:
+            msg = f"RMSNorm: last axis must be {d}, got {x.shape[-1]} (shape {tuple(x.shape)})"
+            raise ContractError(msg)
+        return add_rms_norm(x, r, self.weight, RMS_SCALE_FLOOR, RMS_EPS, self._out_dtype(x))
+
+    @staticmethod
+    def _out_dtype(x: Tensor) -> torch.dtype | None:
+        """The autocast dtype for a float32 input under CUDA autocast (rounded inside the kernel,
+        no cast kernels), else None (the input's dtype)."""
         if x.dtype == torch.float32 and x.is_cuda and torch.is_autocast_enabled("cuda"):
-            out = torch.get_autocast_dtype("cuda")  # rounded inside the kernel, no cast kernels
-        return fused_rms_norm(x, self.weight, RMS_SCALE_FLOOR, RMS_EPS, out)
+            return torch.get_autocast_dtype("cuda")
+        return None
 
 
 class RecurrentSublayer(nn.Module):
@@ -352,9 +366,9 @@ class Column(nn.Module):
             k, v, beta = select_rows(carry.active, [k, v, beta],
                                      [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
         r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index], from_logits=True)
-        x = x + r
+        x, xn = self.norm_attn.add_forward(x, r)  # x + r and norm_attn of it, one kernel
 
-        aq, ak, av = self.attn.project(self.norm_attn.forward(x), pos)
+        aq, ak, av = self.attn.project(xn, pos)
         window = state.kv[pass_index]
         compaction = None
         if carry is not None:
@@ -362,9 +376,9 @@ class Column(nn.Module):
                                  [carry.projections.attn_k.to(ak.dtype), carry.projections.attn_v.to(av.dtype)])  # fmt: skip
             compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
         a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
-        x = x + a
+        x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
 
-        x = x + self.ffn.forward(self.norm_ffn.forward(x))
+        x = x + self.ffn.forward(xn)
         h = tuple(h_new if i == pass_index else s for i, s in enumerate(state.h))
         kv = tuple(kv_new if i == pass_index else c for i, c in enumerate(state.kv))
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))

@@ -6,6 +6,7 @@
 // raw 16-byte words in flight and two CTAs of eight warps per SM; the gain gradient is summed per
 // warp in registers, per CTA in warp order, then across CTAs in CTA order by a second kernel: no
 // atomics, the same bits on every run.
+#include <initializer_list>
 #include <mutex>
 #include <type_traits>
 
@@ -282,6 +283,170 @@ __global__ void __launch_bounds__(BWD_WARPS * 32, 2) rms_bwd_vec_kernel(const T*
   }
 }
 
+// ---- residual add fused with the norm that reads its sum (float32 residual stream) -------------
+// Forward: s = x + r (float32: x + float(r), one IEEE addition as torch's mixed add makes it), the
+// sum stored, then y = RMSNorm(s) in TY. Backward: d = RMSNorm'(s) dy + ds (the sum's gradient
+// from its other reader), dx = d and dr = d rounded to r's dtype (as autograd's add backward
+// casts it). One read of the residual stream less than the add followed by the norm, and no
+// separate gradient add or cast.
+template <typename TR, typename TY, int VPL>
+__global__ void __launch_bounds__(WARPS * 32) add_rms_fwd_kernel(const float* __restrict__ x, const TR* __restrict__ r,
+                                                                 const float* __restrict__ w, float* __restrict__ sum,
+                                                                 TY* __restrict__ y, float* __restrict__ inv,
+                                                                 int64_t rows, int width, float floor_, float eps) {
+  constexpr int E = 4;  // float32 elements per 16-byte vector
+  const int lane = threadIdx.x & 31;
+  const int64_t row0 = ((int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5)) * FWD_ROWS_PER_WARP;
+  const int nv = width / E;
+  float v[FWD_ROWS_PER_WARP][VPL][E];
+#pragma unroll
+  for (int q = 0; q < FWD_ROWS_PER_WARP; ++q) {
+    const int64_t row = row0 + q;
+    if (row >= rows) break;
+    load_row<float, VPL>(x + row * width, nv, lane, v[q]);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float rv[E];
+        ld_e<TR, E>(r + row * width + vi * E, rv);
+#pragma unroll
+        for (int e = 0; e < E; ++e) v[q][i][e] += rv[e];
+        st_e<float, E>(sum + row * width + vi * E, v[q][i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < FWD_ROWS_PER_WARP; ++q) {
+    const int64_t row = row0 + q;
+    if (row >= rows) break;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) amax = fmaxf(amax, fabsf(v[q][i][e]));
+    const float scale = fmaxf(warp_max(amax), floor_);
+    const float rscale = 1.0f / scale;  // as rms_fwd_vec_kernel: the same products, the same bits
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float z = v[q][i][e] * rscale;
+        v[q][i][e] = z;
+        ss += z * z;
+      }
+    const float rms = sqrtf(warp_sum(ss) / (float)width + eps / (scale * scale));
+    const float rrms = 1.0f / rms;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float g[E], o[E];
+        load_gain<E>(w, vi, g);
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[e] = v[q][i][e] * (rrms * g[e]);
+        st_e<TY, E>(y + row * width + vi * E, o);
+      }
+    }
+    if (lane == 0) inv[row] = 1.0f / (scale * rms);
+  }
+}
+
+template <typename TD, typename TR, int VPL>
+__global__ void __launch_bounds__(BWD_WARPS * 32, 2) add_rms_bwd_kernel(const float* __restrict__ x,
+                                                                        const float* __restrict__ w,
+                                                                        const TD* __restrict__ dy,
+                                                                        const float* __restrict__ inv,
+                                                                        const float* __restrict__ dsum,
+                                                                        float* __restrict__ dx, TR* __restrict__ dr,
+                                                                        float* __restrict__ partial, int64_t rows,
+                                                                        int width) {
+  constexpr int E = 4;
+  extern __shared__ float acc_s[];  // [BWD_WARPS][width]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nv = width / E;
+  float acc[VPL][E];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[i][e] = 0.f;
+  const int64_t row0 = (int64_t)blockIdx.x * BWD_ROWS_PER_CTA;
+  using DRaw = typename std::conditional<E * sizeof(TD) == 16, uint4, uint2>::type;
+  uint4 xr[2][VPL];
+  DRaw drw[2][VPL];
+  int64_t row = row0 + warp;
+  if (row < rows) {
+    load_raw<VPL>(x + row * width, nv, lane, xr[0]);
+    load_raw<VPL>(dy + row * width, nv, lane, drw[0]);
+  }
+#pragma unroll 2
+  for (int k = 0; k < BWD_ROWS_PER_WARP; ++k) {
+    const int cur = k & 1;
+    row = row0 + (int64_t)k * BWD_WARPS + warp;
+    if (row >= rows) break;
+    const int64_t nrow = row + BWD_WARPS;
+    if (k + 1 < BWD_ROWS_PER_WARP && nrow < rows) {
+      load_raw<VPL>(x + nrow * width, nv, lane, xr[cur ^ 1]);
+      load_raw<VPL>(dy + nrow * width, nv, lane, drw[cur ^ 1]);
+    }
+    const float iv = __ldg(inv + row);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float xv[E], dv[E], g[E];
+        unpack<float>(xr[cur][i], xv);
+        unpack_e<TD, E>(drw[cur][i], dv);
+        load_gain<E>(w, vi, g);
+#pragma unroll
+        for (int e = 0; e < E; ++e) s += dv[e] * g[e] * (xv[e] * iv);
+      }
+    }
+    const float mean = warp_sum(s) / (float)width;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int vi = lane + 32 * i;
+      if (vi < nv) {
+        float xv[E], dv[E], g[E], o[E];
+        unpack<float>(xr[cur][i], xv);
+        unpack_e<TD, E>(drw[cur][i], dv);
+        load_gain<E>(w, vi, g);
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float xh = xv[e] * iv;
+          o[e] = iv * (dv[e] * g[e] - xh * mean);
+          acc[i][e] += dv[e] * xh;
+        }
+        if (dsum != nullptr) {
+          float ds[E];
+          ld_e<float, E>(dsum + row * width + vi * E, ds);
+#pragma unroll
+          for (int e = 0; e < E; ++e) o[e] += ds[e];
+        }
+        st_e<float, E>(dx + row * width + vi * E, o);
+        if (dr != nullptr) st_e<TR, E>(dr + row * width + vi * E, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int vi = lane + 32 * i;
+    if (vi < nv) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc_s[(size_t)warp * width + vi * E + e] = acc[i][e];
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < width; j += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int q = 0; q < BWD_WARPS; ++q) t += acc_s[(size_t)q * width + j];
+    partial[(size_t)blockIdx.x * width + j] = t;
+  }
+}
+
 // Scalar backward for widths without a 16-byte vector path.
 template <typename T, typename TD>
 __global__ void __launch_bounds__(BWD_WARPS * 32) rms_bwd_kernel(const T* __restrict__ x,
@@ -450,9 +615,84 @@ int launch_bwd(const void* x, const float* weight, const void* dy, const float* 
   });
 }
 
+// the vectors per lane of the fused add + norm (float32 residual stream), 0 where the width or an
+// address does not allow the 16-byte path
+int add_vpl(int width, std::initializer_list<const void*> ptrs) {
+  for (const void* p : ptrs)
+    if (p != nullptr && !aligned16(p)) return 0;
+  return vpl_for<float>(width);
+}
+
+#define VB_DISPATCH_16(code, T, ...)                                                                 \
+  [&]() -> int {                                                                                     \
+    switch (code) {                                                                                  \
+      case VB_F32: { using T = float; return __VA_ARGS__(); }                                        \
+      case VB_BF16: { using T = __nv_bfloat16; return __VA_ARGS__(); }                               \
+      case VB_F16: { using T = __half; return __VA_ARGS__(); }                                       \
+      default: ::vb::set_error("add_rms_norm: unsupported dtype code %d", (int)(code)); return VB_ERR_INVALID; \
+    }                                                                                                \
+  }()
+
 }  // namespace vb
 
 using namespace vb;
+
+extern "C" int vb_add_rms_norm_fwd(const float* x, const void* r, const float* weight, float* sum, void* y,
+                                   float* inv, int64_t rows, int width, float floor_, float eps, int r_dtype,
+                                   int y_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "add_rms_norm_fwd: bad shape rows=%lld width=%d", (long long)rows, width);
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(x && r && weight && sum && y && inv, "add_rms_norm_fwd: null pointer");
+  const int vpl = add_vpl(width, {x, r, weight, sum, y});
+  VB_REQUIRE(vpl != 0, "add_rms_norm_fwd: width %d must be a multiple of 4 up to 1024 and every tensor 16-byte "
+             "aligned", width);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t per = (int64_t)WARPS * FWD_ROWS_PER_WARP;
+  const int ctas = (int)((rows + per - 1) / per);
+  return VB_DISPATCH_16(r_dtype, TR, [&]() -> int {
+    return VB_DISPATCH_16(y_dtype, TY, [&]() -> int {
+      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
+        add_rms_fwd_kernel<TR, TY, VPL><<<ctas, WARPS * 32, 0, st>>>(x, (const TR*)r, weight, sum, (TY*)y, inv,
+                                                                     rows, width, floor_, eps);
+        return 0;
+      });
+      VB_LAUNCH_CHECK("add_rms_norm_fwd");
+      return VB_OK;
+    });
+  });
+}
+
+extern "C" int vb_add_rms_norm_bwd(const float* sum, const float* weight, const void* dy, const float* inv,
+                                   const float* dsum, float* dx, void* dr, float* dweight, void* workspace,
+                                   int64_t rows, int width, int dy_dtype, int r_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0, "add_rms_norm_bwd: bad shape rows=%lld width=%d", (long long)rows, width);
+  VB_REQUIRE(width <= 4096, "add_rms_norm_bwd: width %d exceeds the kernel's 4096", width);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (rows == 0) {
+    VB_CUDA_CHECK(cudaMemsetAsync(dweight, 0, sizeof(float) * width, st), "add_rms_norm_bwd");
+    return VB_OK;
+  }
+  VB_REQUIRE(sum && weight && dy && inv && dx && dweight && workspace, "add_rms_norm_bwd: null pointer");
+  const int vpl = add_vpl(width, {sum, weight, dy, dsum, dx, dr});
+  VB_REQUIRE(vpl != 0, "add_rms_norm_bwd: width %d must be a multiple of 4 up to 1024 and every tensor 16-byte "
+             "aligned", width);
+  const int ctas = bwd_ctas(rows);
+  const size_t smem = sizeof(float) * BWD_WARPS * width;
+  float* partial = (float*)workspace;
+  return VB_DISPATCH_16(dy_dtype, TD, [&]() -> int {
+    return VB_DISPATCH_16(r_dtype, TR, [&]() -> int {
+      VB_VPL_DISPATCH(vpl, VPL, [&]() -> int {
+        if (smem > 48 * 1024)
+          cudaFuncSetAttribute(add_rms_bwd_kernel<TD, TR, VPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        add_rms_bwd_kernel<TD, TR, VPL><<<ctas, BWD_WARPS * 32, smem, st>>>(sum, weight, (const TD*)dy, inv, dsum,
+                                                                            dx, (TR*)dr, partial, rows, width);
+        return 0;
+      });
+      VB_LAUNCH_CHECK("add_rms_norm_bwd");
+      return column_sum(partial, dweight, ctas, width, st);
+    });
+  });
+}
 
 extern "C" int vb_rms_norm_fwd(const void* x, const float* weight, void* y, float* inv, int64_t rows,
                                int width, float floor_, float eps, int dtype, void* stream) {
