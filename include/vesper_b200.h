@@ -110,6 +110,19 @@ VB_API int vb_rms_norm_bwd_noalloc(const void *x, const float *weight, const voi
                                    const float *inv, void *dx, float *dweight, int64_t rows,
                                    int width, int dtype, void *stream);
 
+/* The residual add that ends a column, over the float32 residual stream, with the loop's zeroing
+ * of halted rows fused in: out[row] = keep[row] ? x + f : 0 (x, out float32 [rows, width]; f in
+ * f_dtype, added as float32 in one IEEE addition; keep uint8 [rows] or NULL for every row); width
+ * a multiple of 4, tensors 16-byte aligned. Replaces the column's `x + ffn(...)`
+ * (vesper/column.py:709-812) followed by the loop's zeroing of halted rows. */
+VB_API int vb_residual_add(const float *x, const void *f, const unsigned char *keep, float *out, long long rows,
+                           int width, int f_dtype, void *stream);
+
+/* Its backward: dx = keep ? g : 0 (float32, skipped when NULL) and df the same rounded to f_dtype
+ * (skipped when NULL). */
+VB_API int vb_residual_add_bwd(const float *g, const unsigned char *keep, float *dx, void *df, long long rows,
+                               int width, int f_dtype, void *stream);
+
 /* ---- causal key filter + key normalisation ---------------------------------------------------
  * u[b,t,j] = sum_r taps[r,j] * full[b, t+K-1-r, j] with full = cat(hist, z) along t, then
  * normalize_keys per head (scale-safe L2 norm, floor `floor_`), float32 arithmetic, keys in z's

@@ -63,3 +63,32 @@ def test_rotary_equals_the_reference_sequence(dtype: torch.dtype, heads: int, dk
     yb.backward(up)
     assert torch.equal(ya, yb)
     assert torch.equal(a.grad, b.grad)
+
+
+@pytest.mark.parametrize("fdtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("masked", [False, True])
+def test_residual_add_with_halted_rows_zeroed_equals_the_add_then_the_zeroing(fdtype: torch.dtype, masked: bool) -> None:
+    """``residual_add`` (one kernel each way) gives the same bits as ``x + f`` followed by the
+    loop's zeroing of halted rows (``select_rows`` with nothing carried), values and gradients."""
+    from vesper_b200.kernels.act import residual_add
+    from vesper_b200.kernels.compact import select_rows
+
+    g = torch.Generator().manual_seed(8)
+    x = (3 * torch.randn(4, 300, 512, generator=g)).to(CUDA)
+    f = torch.randn(4, 300, 512, generator=g).to(fdtype).to(CUDA)
+    keep = (torch.rand(4, 300, generator=g) > 0.3).to(CUDA) if masked else None
+    up = torch.randn(4, 300, 512, generator=g).to(CUDA)
+    outs = []
+    for fused in (True, False):
+        xs, fs = x.clone().requires_grad_(), f.clone().requires_grad_()
+        if fused:
+            y = residual_add(xs, fs, keep)
+        else:
+            y = xs + fs
+            if keep is not None:
+                (y,) = select_rows(keep, [y], [None])
+        y.backward(up)
+        outs.append((y.detach(), xs.grad, fs.grad))
+    for got, want in zip(*outs, strict=True):
+        assert got.dtype == want.dtype
+        assert torch.equal(got, want)

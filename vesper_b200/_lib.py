@@ -67,6 +67,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_relu_square_fwd": (_I, [_P, _P, ctypes.c_longlong, _I, _P]),
     "vb_relu_square_bwd": (_I, [_P, _P, _P, ctypes.c_longlong, _I, _P]),
     "vb_rotary": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _I, _I, _I, _P]),
+    "vb_residual_add": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _I, _P]),
+    "vb_residual_add_bwd": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _I, _P]),
 }
 
 

@@ -26,7 +26,7 @@ from torch import Tensor, nn
 
 from vesper_b200.attention import KVCache, RingKVCache, WindowedAttention, kv_cache_empty, kv_ring_empty
 from vesper_b200.contracts import ContractError, Dims, check_shape
-from vesper_b200.kernels.act import relu_square
+from vesper_b200.kernels.act import relu_square, residual_add
 from vesper_b200.kernels.compact import compact_index, select_rows
 from vesper_b200.kernels.delta_scan import (
     delta_scan_fused,
@@ -327,13 +327,15 @@ class Column(nn.Module):
         self.ffn = FFN(shape.d, shape.ffn_mult, generator)
 
     def step(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int, *,
-             carry: Carry | None = None) -> tuple[Tensor, ColumnState, Projections]:  # fmt: skip
+             carry: Carry | None = None, zero_halted: bool = False) -> tuple[Tensor, ColumnState, Projections]:  # fmt: skip
         """One pass over a chunk through the state of pass ``pass_index`` (``vesper/column.py:709-812``).
 
         With a carry, halted tokens write their carried projections: the key input is merged
         before the filter and ``k, v, beta`` after it (one select launch), the attention keys and
         values after their projection (one launch), and the attention runs the active queries
         only. The output at halted positions is not meaningful; the loop discards it.
+        ``zero_halted`` (the loop's own use, with a carry) sets those positions to zero in the
+        column's last residual add, which the loop would otherwise do in a separate pass.
         """
         if not len(state.h) == len(state.kv) == len(state.key_history):
             msg = f"state has {len(state.h)} recurrent states, {len(state.kv)} windows and {len(state.key_history)} key histories"
@@ -378,7 +380,8 @@ class Column(nn.Module):
         a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
         x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
 
-        x = x + self.ffn.forward(xn)
+        keep = carry.active if zero_halted and carry is not None else None
+        x = residual_add(x, self.ffn.forward(xn), keep)  # the halted rows zeroed here when asked
         h = tuple(h_new if i == pass_index else s for i, s in enumerate(state.h))
         kv = tuple(kv_new if i == pass_index else c for i, c in enumerate(state.kv))
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))

@@ -108,6 +108,79 @@ unsigned grid_for(int64_t items) {
   return (unsigned)(blocks < 148 * 32 ? (blocks > 0 ? blocks : 1) : 148 * 32);
 }
 
+// The residual add at the end of a column over the float32 residual stream, with the loop's
+// zeroing of halted rows fused in: out = keep[row] ? x + float(f) : 0 (one IEEE float32 addition,
+// as torch's mixed-dtype add makes it); the backward writes dx = keep ? g : 0 and the same rounded
+// to f's dtype (autograd's add backward casts it). keep NULL keeps every row. W: the row width.
+constexpr int RA_WARPS = 8;  // rows per CTA of the residual kernels: a warp per row
+template <typename TF>
+__device__ __forceinline__ void ld4(const TF* __restrict__ p, float (&v)[4]) {
+  if constexpr (sizeof(TF) == 4) {
+    load_vec<float, 4>(reinterpret_cast<const float*>(p), v);
+  } else {
+    const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p));
+    const TF* e = reinterpret_cast<const TF*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = to_f32<TF>(e[j]);
+  }
+}
+template <typename TF>
+__device__ __forceinline__ void st4(TF* __restrict__ p, const float (&v)[4]) {
+  if constexpr (sizeof(TF) == 4) {
+    store_vec<float, 4>(reinterpret_cast<float*>(p), v);
+  } else {
+    uint2 raw;
+    TF* e = reinterpret_cast<TF*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) e[j] = from_f32<TF>(v[j]);
+    *reinterpret_cast<uint2*>(p) = raw;
+  }
+}
+
+template <typename TF>
+__global__ void __launch_bounds__(RA_WARPS * 32) residual_add_kernel(const float* __restrict__ x,
+                                                                     const TF* __restrict__ f,
+                                                                     const uint8_t* __restrict__ keep,
+                                                                     float* __restrict__ out, int64_t rows, int W) {
+  const int64_t row = (int64_t)blockIdx.x * RA_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool k = keep == nullptr || keep[row] != 0;
+  const int64_t base = row * W;
+  for (int c = (threadIdx.x & 31) * 4; c < W; c += 128) {
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    if (k) {  // a halted row is zero: its inputs are not read
+      float b[4];
+      load_vec<float, 4>(x + base + c, a);
+      ld4<TF>(f + base + c, b);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[j] += b[j];
+    }
+    store_vec<float, 4>(out + base + c, a);
+  }
+}
+
+template <typename TF>
+__global__ void __launch_bounds__(RA_WARPS * 32) residual_add_bwd_kernel(const float* __restrict__ g,
+                                                                         const uint8_t* __restrict__ keep,
+                                                                         float* __restrict__ dx, TF* __restrict__ df,
+                                                                         int64_t rows, int W) {
+  const int64_t row = (int64_t)blockIdx.x * RA_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const bool k = keep == nullptr || keep[row] != 0;
+  const int64_t base = row * W;
+  for (int c = (threadIdx.x & 31) * 4; c < W; c += 128) {
+    float a[4];
+    if (k) {
+      load_vec<float, 4>(g + base + c, a);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[j] = 0.f;
+    }
+    if (dx != nullptr) store_vec<float, 4>(dx + base + c, a);
+    if (df != nullptr) st4<TF>(df + base + c, a);
+  }
+}
+
 }  // namespace
 }  // namespace vb
 
@@ -154,6 +227,35 @@ extern "C" int vb_rotary(const void* x, const long long* pos, const double* inv_
       rotary_kernel<T, false><<<grid_for(items), 256, 0, (cudaStream_t)stream>>>(
           (const T*)x, (const int64_t*)pos, inv_freq, (T*)y, tokens, heads, dk);
     VB_LAUNCH_CHECK("rotary");
+    return VB_OK;
+  });
+}
+
+extern "C" int vb_residual_add(const float* x, const void* f, const unsigned char* keep, float* out, long long rows,
+                               int width, int f_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0 && width % 4 == 0, "residual_add: bad shape rows=%lld width=%d (a multiple of 4)",
+             rows, width);
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(x && f && out && aligned16(x) && aligned16(f) && aligned16(out), "residual_add: null or unaligned tensor");
+  const unsigned ctas = (unsigned)((rows + RA_WARPS - 1) / RA_WARPS);
+  return VB_DISPATCH_DTYPE(f_dtype, T, [&]() -> int {
+    residual_add_kernel<T><<<ctas, RA_WARPS * 32, 0, (cudaStream_t)stream>>>(x, (const T*)f, keep, out, rows, width);
+    VB_LAUNCH_CHECK("residual_add");
+    return VB_OK;
+  });
+}
+
+extern "C" int vb_residual_add_bwd(const float* g, const unsigned char* keep, float* dx, void* df, long long rows,
+                                   int width, int f_dtype, void* stream) {
+  VB_REQUIRE(rows >= 0 && width > 0 && width % 4 == 0,
+             "residual_add_bwd: bad shape rows=%lld width=%d (a multiple of 4)", rows, width);
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(g && aligned16(g) && (!dx || aligned16(dx)) && (!df || aligned16(df)),
+             "residual_add_bwd: null or unaligned tensor");
+  const unsigned ctas = (unsigned)((rows + RA_WARPS - 1) / RA_WARPS);
+  return VB_DISPATCH_DTYPE(f_dtype, T, [&]() -> int {
+    residual_add_bwd_kernel<T><<<ctas, RA_WARPS * 32, 0, (cudaStream_t)stream>>>(g, keep, dx, (T*)df, rows, width);
+    VB_LAUNCH_CHECK("residual_add_bwd");
     return VB_OK;
   });
 }

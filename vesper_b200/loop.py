@@ -249,13 +249,15 @@ class Loop(nn.Module):
             for c, column in enumerate(self.columns):
                 previous = carried[c]
                 carry = None if previous is None or dense else Carry(active, previous)
+                # with a carry the column zeroes the halted rows in its last residual add; without
+                # one (the first pass) no token has halted yet
                 if recompute:
                     h, current[c], written = checkpoint(column.step, h, pos, current[c], t, carry=carry,
-                                                        use_reentrant=False)  # fmt: skip
+                                                        zero_halted=True, use_reentrant=False)  # fmt: skip
                 else:
-                    h, current[c], written = column.step(h, pos, current[c], t, carry=carry)
+                    h, current[c], written = column.step(h, pos, current[c], t, carry=carry, zero_halted=True)
                 fresh.append(written)
-                if not dense:
+                if not dense and carry is None and t > 0:
                     (h,) = select_rows(active, [h], [None])  # halted rows zeroed before anything reads them
             halts, allocation = decide(t, h, active, last=t == runs - 1)
             y = y + allocation[..., None] * h
