@@ -167,7 +167,7 @@ constexpr uint32_t PREP_X = 0, PREP_P = TILE_TT, PREP_T = 2 * TILE_TT, PREP_U = 
                    PREP_Q = PREP_U + TILE_TD, PREP_M = PREP_Q + TILE_TD, PREP_BYTES = PREP_M + TILE_JI;
 struct PrepSmem {
   // KQ [128 rows][128 d]: K in rows 0-63, Q in rows 64-127 of each atom (Q' replaces Q in place);
-  // Vt: V, then U; AF: float32 A [64][65], then atom 0 of M; Ws: the X image, then W, then atom 1
+  // Vt: V, then U; AF: float32 A [64][AS], then atom 0 of M; Ws: the X image, then W, then atom 1
   // of M; TT: [T'; T'] (128 rows x 64); Ps: P. During the solve Ws and TT hold the float32 X
   // [64][68] and the block products (3 x [16][20]).
   static constexpr uint32_t KQ = 0, Vt = TILE_JI, AF = Vt + TILE_TD, Ws = AF + 17 * 1024, TT = Ws + TILE_TD,
@@ -175,7 +175,7 @@ struct PrepSmem {
 };
 constexpr int NP = 256;
 
-// X = (I + A)^-1 for the strictly lower A (float32 [64][65]) into X (float32 [64][68]), 256
+// X = (I + A)^-1 for the strictly lower A (float32 [64][AS]) into X (float32 [64][68]), 256
 // threads, by blocks of 16 in three levels:
 //   1. the four diagonal blocks X_II by forward substitution (a thread per column; the entries
 //      above a block's diagonal come out as zeros);
@@ -186,6 +186,7 @@ constexpr int NP = 256;
 // Five barriers instead of seven, and each product's dependent chain is at most 32 terms with four
 // independent accumulators per thread. Entries above the diagonal blocks are not written.
 constexpr int XS = 68;  // row stride of X (16-byte aligned rows)
+constexpr int AS = 68;  // row stride of A (16-byte aligned rows: written as 16-byte vectors)
 constexpr int TS = 36;  // row stride of the products' scratch
 __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, float* Tm, int tid) {
   if (tid < C) {  // level 1
@@ -196,8 +197,8 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
       for (int s = 0; s < r; ++s) {
-        if (s & 1) s1 = fmaf(A[(o + r) * 65 + o + s], x[s], s1);
-        else s0 = fmaf(A[(o + r) * 65 + o + s], x[s], s0);
+        if (s & 1) s1 = fmaf(A[(o + r) * AS + o + s], x[s], s1);
+        else s0 = fmaf(A[(o + r) * AS + o + s], x[s], s0);
       }
       x[r] = (r == j ? 1.f : 0.f) - (s0 + s1);
       X[(o + r) * XS + o + j] = x[r];
@@ -212,7 +213,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int s = 0; s < 16; ++s) {
-      const float a = A[(ro + r2) * 65 + co + s];
+      const float a = A[(ro + r2) * AS + co + s];
       const float4 x = *reinterpret_cast<const float4*>(X + (co + s) * XS + co + q4);
       t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
     }
@@ -238,7 +239,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
     for (int k = k0; k < 32; ++k) {
-      const float a = A[(32 + i3) * 65 + k];
+      const float a = A[(32 + i3) * AS + k];
       const float4 x = *reinterpret_cast<const float4*>(X + k * XS + j4);
       t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
     }
@@ -316,7 +317,10 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
       const int t = lane128;
       const float bt = bsm[t];  // 0/1 masks and products below, not per-lane selects
 #pragma unroll
-      for (int e = 0; e < 32; ++e) A[t * 65 + c0 + e] = (c0 + e < t ? 1.f : 0.f) * (bt * v[e]);
+      for (int e = 0; e < 32; e += 4)  // rows of AS floats: 16-byte aligned vectors
+        *reinterpret_cast<float4*>(A + t * AS + c0 + e) =
+            make_float4((c0 + e < t ? 1.f : 0.f) * (bt * v[e]), (c0 + e + 1 < t ? 1.f : 0.f) * (bt * v[e + 1]),
+                        (c0 + e + 2 < t ? 1.f : 0.f) * (bt * v[e + 2]), (c0 + e + 3 < t ? 1.f : 0.f) * (bt * v[e + 3]));
     } else {
       const int t = lane128 - C;
 #pragma unroll
@@ -330,22 +334,39 @@ __global__ void __launch_bounds__(NP, 2) scan_prep_kernel(
   {
     float* Xf = reinterpret_cast<float*>(Ws);
     invert_unit_lower(A, Xf, Xf + 64 * XS, tid);
-    float xv[16];
+    // each thread two 8-column chunks (row t, chunk c): 16-byte reads of X, 16-byte swizzled stores
+    float xv[2][8];
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int idx = tid + NP * e, t = idx >> 6, j = idx & 63;
-      const float xf = Xf[t * XS + j];  // loaded unconditionally (entries above the blocks are not written)
-      xv[e] = (j >> 4) > (t >> 4) ? 0.f : xf;
+    for (int u = 0; u < 2; ++u) {
+      const int q = tid + NP * u, t = q >> 3, c = q & 7;
+      const float4 a = *reinterpret_cast<const float4*>(Xf + t * XS + 8 * c);
+      const float4 b = *reinterpret_cast<const float4*>(Xf + t * XS + 8 * c + 4);
+      // loaded unconditionally (entries above the diagonal blocks are not written): a chunk lies
+      // inside one 16-column block, so it is all zero or all kept
+      // (a select, not a product: the unwritten entries may hold any bits)
+      const bool keep = (c >> 1) <= (t >> 4);
+      xv[u][0] = keep ? a.x : 0.f; xv[u][1] = keep ? a.y : 0.f; xv[u][2] = keep ? a.z : 0.f;
+      xv[u][3] = keep ? a.w : 0.f; xv[u][4] = keep ? b.x : 0.f; xv[u][5] = keep ? b.y : 0.f;
+      xv[u][6] = keep ? b.z : 0.f; xv[u][7] = keep ? b.w : 0.f;
     }
     __syncthreads();
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int idx = tid + NP * e, t = idx >> 6, j = idx & 63;
-      const bf16 xb = __float2bfloat16_rn(xv[e]);
-      const bf16 tb = __float2bfloat16_rn(__bfloat162float(xb) * bsm[j]);
-      *reinterpret_cast<bf16*>(Ws + sw_offset(64, t, j)) = xb;
-      *reinterpret_cast<bf16*>(TT + sw_offset(128, t, j)) = tb;
-      *reinterpret_cast<bf16*>(TT + sw_offset(128, t + 64, j)) = tb;
+    for (int u = 0; u < 2; ++u) {
+      const int q = tid + NP * u, t = q >> 3, c = q & 7;
+      float xr[8], tr[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        xr[i] = __bfloat162float(__float2bfloat16_rn(xv[u][i]));  // the bf16 X, and T' = bf16(X beta)
+        tr[i] = xr[i] * bsm[8 * c + i];
+      }
+      uint4 xw, tw;
+      xw.x = pack_bf16(xr[0], xr[1]); xw.y = pack_bf16(xr[2], xr[3]);
+      xw.z = pack_bf16(xr[4], xr[5]); xw.w = pack_bf16(xr[6], xr[7]);
+      tw.x = pack_bf16(tr[0], tr[1]); tw.y = pack_bf16(tr[2], tr[3]);
+      tw.z = pack_bf16(tr[4], tr[5]); tw.w = pack_bf16(tr[6], tr[7]);
+      *reinterpret_cast<uint4*>(Ws + sw_chunk(64, t, c)) = xw;
+      *reinterpret_cast<uint4*>(TT + sw_chunk(128, t, c)) = tw;
+      *reinterpret_cast<uint4*>(TT + sw_chunk(128, t + 64, c)) = tw;
     }
   }
   ok = publish_ok(ok);
