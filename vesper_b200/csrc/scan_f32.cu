@@ -368,6 +368,615 @@ __global__ void scan_f32_finish_kernel(const float* __restrict__ k, const float*
   if (lane == 0) dbeta[row] = logit ? (dotk * (1.0f - bt)) * bt : dotk;
 }
 
+// ---- staged variants (head width a multiple of 4) ---------------------------------------------
+// The same recurrences, arithmetic and orders as the kernels above, with the inputs of TB-token
+// blocks copied into a CTA-shared ring by cp.async NBUF blocks ahead of their use (one barrier
+// pair per block instead of a load on every token's dependent chain), and the backward's
+// reductions over the CTA's warps buffered per block (the per-token CTA barriers of
+// cta_sum_store become two per block): every partial sum is formed in the same order.
+constexpr int TB = 8;    // tokens per staged block
+constexpr int NBUF = 4;  // blocks in flight
+
+__device__ __forceinline__ void cp_async16(float* dst, const float* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// the write strength of a staged token: the raw value, or with `logit` the sigmoid of it plus the
+// shift, as beta_at forms it
+__device__ __forceinline__ float staged_beta(const float* rec_b, int logit, bool has_shift) {
+  const float raw = rec_b[0];
+  if (!logit) return raw;
+  const float x = raw + (has_shift ? rec_b[1] : 0.f);
+  return 1.0f / (1.0f + expf(-x));
+}
+
+// Copies the rows of tokens [t0, t0 + TB) named by `vecs` (each a float row pointer, an offset into
+// the record and a count of 16-byte chunks) plus beta and the shift into one ring slot.
+struct StageRow {
+  const float* src;  // row of token t0 (advanced by `stride` floats per token)
+  int64_t stride;
+  int at;            // float offset in a token's record
+  int chunks;        // 16-byte chunks per token
+};
+
+template <int NROWS>
+__device__ __forceinline__ void stage_block(float* slot, int REC, int t0, int T, const StageRow (&rows)[NROWS],
+                                            const float* beta_p, const float* shift_p, int64_t beta_stride,
+                                            int BOFF) {
+  int per = 0;
+#pragma unroll
+  for (int r = 0; r < NROWS; ++r) per += rows[r].chunks;
+  for (int c = threadIdx.x; c < TB * per; c += NWARP * 32) {
+    const int tt = c / per, t = t0 + tt;
+    if (t >= T) continue;
+    int w = c - tt * per;
+#pragma unroll
+    for (int r = 0; r < NROWS; ++r) {
+      if (w >= 0 && w < rows[r].chunks) cp_async16(slot + tt * REC + rows[r].at + 4 * w, rows[r].src + (int64_t)t * rows[r].stride + 4 * w);
+      w -= rows[r].chunks;
+    }
+  }
+  for (int tt = threadIdx.x; tt < TB; tt += NWARP * 32) {
+    const int t = t0 + tt;
+    if (t >= T) continue;
+    cp_async4(slot + tt * REC + BOFF, beta_p + (int64_t)t * beta_stride);
+    if (shift_p != nullptr) cp_async4(slot + tt * REC + BOFF + 1, shift_p + t);
+  }
+}
+
+template <int NI>
+__global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_staged_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ beta, const float* __restrict__ shift, int logit, const float* s0,
+    float* __restrict__ o, float* sn, float* __restrict__ resid, int T, int H, int D) {
+  extern __shared__ __align__(16) float ring[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int jb = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int j0 = jb * BV + warp * CPW;
+  const int ncol = min(BV, D - jb * BV);
+  const int REC = 2 * D + BV + 4;  // k, q, this CTA's v columns, beta and shift
+  float S[NI][CPW];
+  const float* s0p = s0 + (int64_t)bh * D * D;
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      S[m][c] = (i < D && j < D) ? s0p[(int64_t)i * D + j] : 0.f;
+    }
+  }
+  const int64_t row0 = (int64_t)b * T * H + h;  // token t's row is row0 + t * H
+  const int64_t rs = (int64_t)H * D;
+  const StageRow rows[3] = {{k + row0 * D, rs, 0, D / 4}, {q + row0 * D, rs, D, D / 4},
+                            {v + row0 * D + jb * BV, rs, 2 * D, ncol / 4}};
+  const float* shift_p = (logit && shift != nullptr) ? shift + (int64_t)b * T : nullptr;
+  const int NBLK = (T + TB - 1) / TB;
+  auto slot = [&](int blk) { return ring + (blk % NBUF) * TB * REC; };
+#pragma unroll 1
+  for (int i = 0; i < NBUF; ++i) {
+    if (i < NBLK) stage_block<3>(slot(i), REC, i * TB, T, rows, beta + row0, shift_p, H, 2 * D + BV);
+    cp_commit();
+  }
+  for (int blk = 0; blk < NBLK; ++blk) {
+    cp_wait<NBUF - 1>();
+    __syncthreads();  // every thread's copies of this block are visible
+    const float* sl = slot(blk);
+    const int tn = min(TB, T - blk * TB);
+    for (int tt = 0; tt < tn; ++tt) {
+      const int t = blk * TB + tt;
+      const float* rec = sl + tt * REC;
+      float kk[NI], qq[NI], vv[CPW];
+#pragma unroll
+      for (int m = 0; m < NI; ++m) {
+        const int i = lane + 32 * m;
+        kk[m] = i < D ? rec[i] : 0.f;
+        qq[m] = i < D ? rec[D + i] : 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) vv[c] = (j0 + c < D) ? rec[2 * D + warp * CPW + c] : 0.f;
+      const float bt = staged_beta(rec + 2 * D + BV, logit, shift_p != nullptr);
+      const int64_t row = row0 + (int64_t)t * H;
+      float red[CPW];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        float a = 0.f;
+#pragma unroll
+        for (int m = 0; m < NI; ++m) a = fmaf(S[m][c], kk[m], a);
+        red[c] = a;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) red[c] += __shfl_xor_sync(0xffffffffu, red[c], off);
+      float r[CPW];
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) r[c] = vv[c] - red[c];
+#pragma unroll
+      for (int m = 0; m < NI; ++m) {
+        const float bk = bt * kk[m];
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) S[m][c] = fmaf(bk, r[c], S[m][c]);
+      }
+#pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        float a = 0.f;
+#pragma unroll
+        for (int m = 0; m < NI; ++m) a = fmaf(S[m][c], qq[m], a);
+        red[c] = a;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) red[c] += __shfl_xor_sync(0xffffffffu, red[c], off);
+      if (lane < CPW) {
+        float ov = red[0], rv = r[0];
+#pragma unroll
+        for (int c = 1; c < CPW; ++c)
+          if (lane == c) { ov = red[c]; rv = r[c]; }
+        const int j = j0 + lane;
+        if (j < D) {
+          o[row * D + j] = ov;
+          if (resid) resid[row * D + j] = rv;
+        }
+      }
+    }
+    __syncthreads();  // every warp has read the slot: it takes block blk + NBUF
+    if (blk + NBUF < NBLK) stage_block<3>(slot(blk), REC, (blk + NBUF) * TB, T, rows, beta + row0, shift_p, H, 2 * D + BV);
+    cp_commit();
+  }
+  cp_wait<0>();
+  float* snp = sn + (int64_t)bh * D * D;
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      if (i < D && j < D) snp[(int64_t)i * D + j] = S[m][c];
+    }
+  }
+}
+
+// Forward, lanes split over (row group, column): lane l = 4 g + c holds rows [g R, g R + R) (R = D/8)
+// of column j0 + c of the state, so each token's two reductions over the key index are R local
+// products and three shuffle levels (xor 4, 8, 16) instead of five levels over four columns: the
+// shuffle unit, not the chain, had bounded the row layout above. Every sum is a different order of
+// the same float32 products (within float32 rounding of the row layout's).
+template <int R>
+__global__ void __launch_bounds__(NWARP * 32) scan_f32_fwd_group_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ beta, const float* __restrict__ shift, int logit, const float* s0,
+    float* __restrict__ o, float* sn, float* __restrict__ resid, int T, int H, int D) {
+  extern __shared__ __align__(16) float ring[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, c = lane & 3;
+  const int jb = blockIdx.x, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int j = jb * BV + warp * CPW + c;  // this lane's column
+  const bool jlive = j < D;
+  const int ncol = min(BV, D - jb * BV);
+  const int REC = 2 * D + BV + 4;  // k, q, this CTA's v columns, beta and shift
+  float S[R];
+  const float* s0p = s0 + (int64_t)bh * D * D;
+#pragma unroll
+  for (int r = 0; r < R; ++r) S[r] = jlive ? s0p[(int64_t)(g * R + r) * D + j] : 0.f;
+  const int64_t row0 = (int64_t)b * T * H + h;
+  const int64_t rs = (int64_t)H * D;
+  const StageRow rows[3] = {{k + row0 * D, rs, 0, D / 4}, {q + row0 * D, rs, D, D / 4},
+                            {v + row0 * D + jb * BV, rs, 2 * D, ncol / 4}};
+  const float* shift_p = (logit && shift != nullptr) ? shift + (int64_t)b * T : nullptr;
+  const int NBLK = (T + TB - 1) / TB;
+  auto slot = [&](int blk) { return ring + (blk % NBUF) * TB * REC; };
+#pragma unroll 1
+  for (int i = 0; i < NBUF; ++i) {
+    if (i < NBLK) stage_block<3>(slot(i), REC, i * TB, T, rows, beta + row0, shift_p, H, 2 * D + BV);
+    cp_commit();
+  }
+  float pq[R];  // the previous token's query: its output is reduced with this token's read
+#pragma unroll
+  for (int r = 0; r < R; ++r) pq[r] = 0.f;
+  int64_t prow = -1;  // the previous token's row (none yet)
+  float prv = 0.f;
+  for (int blk = 0; blk < NBLK; ++blk) {
+    cp_wait<NBUF - 1>();
+    __syncthreads();
+    const float* sl = slot(blk);
+    const int tn = min(TB, T - blk * TB);
+    for (int tt = 0; tt < tn; ++tt) {
+      const int t = blk * TB + tt;
+      const float* rec = sl + tt * REC;
+      float kk[R], qq[R];
+#pragma unroll
+      for (int r = 0; r < R; r += (R % 4 == 0 ? 4 : 1)) {
+        if constexpr (R % 4 == 0) {
+          const float4 a = *reinterpret_cast<const float4*>(rec + g * R + r);
+          const float4 e = *reinterpret_cast<const float4*>(rec + D + g * R + r);
+          kk[r] = a.x; kk[r + 1] = a.y; kk[r + 2] = a.z; kk[r + 3] = a.w;
+          qq[r] = e.x; qq[r + 1] = e.y; qq[r + 2] = e.z; qq[r + 3] = e.w;
+        } else {
+          kk[r] = rec[g * R + r];
+          qq[r] = rec[D + g * R + r];
+        }
+      }
+      const float vv = jlive ? rec[2 * D + warp * CPW + c] : 0.f;
+      const float bt = staged_beta(rec + 2 * D + BV, logit, shift_p != nullptr);
+      // token t's read H^T k and token t-1's output H^T q use the same state (after t-1's write):
+      // one pass of three shuffle levels reduces both (two partial sums each: half the chain)
+      float a0 = 0.f, a1 = 0.f, o0 = 0.f, o1 = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (r & 1) { a1 = fmaf(S[r], kk[r], a1); o1 = fmaf(S[r], pq[r], o1); }
+        else { a0 = fmaf(S[r], kk[r], a0); o0 = fmaf(S[r], pq[r], o0); }
+      }
+      float red = a0 + a1, ov = o0 + o1;
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        red += __shfl_xor_sync(0xffffffffu, red, off);
+        ov += __shfl_xor_sync(0xffffffffu, ov, off);
+      }
+      if (prow >= 0 && g == 0 && jlive) {
+        o[prow * D + j] = ov;
+        if (resid) resid[prow * D + j] = prv;
+      }
+      const float rv = vv - red;
+      const float br = bt * rv;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        S[r] = fmaf(kk[r], br, S[r]);
+        pq[r] = qq[r];
+      }
+      prow = row0 + (int64_t)t * H;
+      prv = rv;
+    }
+    __syncthreads();
+    if (blk + NBUF < NBLK) stage_block<3>(slot(blk), REC, (blk + NBUF) * TB, T, rows, beta + row0, shift_p, H, 2 * D + BV);
+    cp_commit();
+  }
+  cp_wait<0>();
+  if (prow >= 0) {  // the last token's output
+    float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r & 1) o1 = fmaf(S[r], pq[r], o1);
+      else o0 = fmaf(S[r], pq[r], o0);
+    }
+    float ov = o0 + o1;
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) ov += __shfl_xor_sync(0xffffffffu, ov, off);
+    if (g == 0 && jlive) {
+      o[prow * D + j] = ov;
+      if (resid) resid[prow * D + j] = prv;
+    }
+  }
+  if (jlive) {
+    float* snp = sn + (int64_t)bh * D * D;
+#pragma unroll
+    for (int r = 0; r < R; ++r) snp[(int64_t)(g * R + r) * D + j] = S[r];
+  }
+}
+
+// Adds one token's per-warp partials (NI per lane over i) of the CTA's buffered block into
+// part[row][i] in warp order, for the block's tn tokens; buf: [TB][NWARP][D].
+__device__ __forceinline__ void flush_partials(const float* buf, float* part, int64_t row0, int64_t H, int t0,
+                                               int tn, int D) {
+  for (int e = threadIdx.x; e < tn * D; e += NWARP * 32) {
+    const int tt = e / D, i = e - tt * D;
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < NWARP; ++w) a += buf[(tt * NWARP + w) * D + i];
+    part[(row0 + (int64_t)(t0 + tt) * H) * D + i] = a;
+  }
+}
+
+// GA: phase A in the (row group, column) lane layout of scan_f32_fwd_group_kernel (D = 32 NI):
+// the reduction over the key index takes three shuffle levels, the one over the CTA's columns two
+// recursive-halving levels and the warp buffer; phase B keeps the row layout, whose reductions
+// over columns are local.
+template <int NI, bool GA>
+__global__ void __launch_bounds__(NWARP * 32) scan_f32_bwd_staged_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ beta,
+    const float* __restrict__ shift, int logit,
+    const float* __restrict__ s0, const float* __restrict__ resid, const float* __restrict__ dout,
+    const float* __restrict__ dsn, float* __restrict__ dv, float* __restrict__ ds0,
+    float* __restrict__ part, int B, int T, int H, int D) {
+  extern __shared__ __align__(16) float smem[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int jb = blockIdx.x, NJB = gridDim.x, bh = blockIdx.y, b = bh / H, h = bh % H;
+  const int j0 = jb * BV + warp * CPW;
+  const int ncol = min(BV, D - jb * BV);
+  const int64_t rows = (int64_t)B * T * H;
+  float* part_gr = part + ((int64_t)0 * NJB + jb) * rows * D;
+  float* part_hd = part + ((int64_t)1 * NJB + jb) * rows * D;
+  float* part_dq = part + ((int64_t)2 * NJB + jb) * rows * D;
+  const int REC = 2 * D + 3 * BV + 4;  // k, q, g, r, dv (this CTA's columns), beta and shift
+  float* ring = smem;
+  float* buf = smem + NBUF * TB * REC;  // [2][TB][NWARP][D] partials of a block
+  float* buf1 = buf + TB * NWARP * D;
+  const int64_t row0 = (int64_t)b * T * H + h;
+  const int64_t rs = (int64_t)H * D;
+  const float* shift_p = (logit && shift != nullptr) ? shift + (int64_t)b * T : nullptr;
+  const int NBLK = (T + TB - 1) / TB;
+  auto slot = [&](int i) { return ring + (i % NBUF) * TB * REC; };
+  if constexpr (GA) {
+    // ---- phase A, (row group, column) layout: lane = 4 g + c holds rows [g R, g R + R) of column jc
+    constexpr int R = 4 * NI;
+    const int g = lane >> 2, c = lane & 3;
+    const int jc = jb * BV + warp * CPW + c;
+    const bool jlive = jc < D;
+    float G[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) G[r] = (dsn && jlive) ? dsn[(int64_t)bh * D * D + (int64_t)(g * R + r) * D + jc] : 0.f;
+    const StageRow rows_a[4] = {{k + row0 * D, rs, 0, D / 4}, {q + row0 * D, rs, D, D / 4},
+                                {dout + row0 * D + jb * BV, rs, 2 * D, ncol / 4},
+                                {resid + row0 * D + jb * BV, rs, 2 * D + BV, ncol / 4}};
+#pragma unroll 1
+    for (int i = 0; i < NBUF; ++i) {
+      if (i < NBLK) stage_block<4>(slot(i), REC, (NBLK - 1 - i) * TB, T, rows_a, beta + row0, shift_p, H, 2 * D + 3 * BV);
+      cp_commit();
+    }
+    // this lane's rows of the CTA-column sums after two halving levels (xor 1, then xor 2)
+    const int rbase = g * R + (c & 1) * (R / 2) + ((c >> 1) & 1) * (R / 4);
+    for (int i = 0; i < NBLK; ++i) {
+      const int blk = NBLK - 1 - i, t0 = blk * TB, tn = min(TB, T - t0);
+      cp_wait<NBUF - 1>();
+      __syncthreads();
+      const float* sl = slot(i);
+      for (int tt = tn - 1; tt >= 0; --tt) {
+        const int t = t0 + tt;
+        const float* rec = sl + tt * REC;
+        float kk[R], qq[R];
+#pragma unroll
+        for (int r = 0; r < R; r += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(rec + g * R + r);
+          const float4 e = *reinterpret_cast<const float4*>(rec + D + g * R + r);
+          kk[r] = a.x; kk[r + 1] = a.y; kk[r + 2] = a.z; kk[r + 3] = a.w;
+          qq[r] = e.x; qq[r + 1] = e.y; qq[r + 2] = e.z; qq[r + 3] = e.w;
+        }
+        const float gg = jlive ? rec[2 * D + warp * CPW + c] : 0.f;
+        const float rr = jlive ? rec[2 * D + BV + warp * CPW + c] : 0.f;
+        const float bt = staged_beta(rec + 2 * D + 3 * BV, logit, shift_p != nullptr);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          G[r] = fmaf(qq[r], gg, G[r]);
+          if (r & 1) a1 = fmaf(G[r], kk[r], a1);
+          else a0 = fmaf(G[r], kk[r], a0);
+        }
+        // the read H^T k (three levels over the row groups) and gr = G r over the warp's four
+        // columns (recursive halving, xor 1 then xor 2) are independent: their shuffles interleave
+        float red = a0 + a1;
+        float p[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) p[r] = G[r] * rr;
+        red += __shfl_xor_sync(0xffffffffu, red, 4);
+        {
+          const bool up = (lane & 1) != 0;
+#pragma unroll
+          for (int r = 0; r < R / 2; ++r) {
+            const float send = up ? p[r] : p[r + R / 2];
+            const float keep = up ? p[r + R / 2] : p[r];
+            p[r] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+          }
+        }
+        red += __shfl_xor_sync(0xffffffffu, red, 8);
+        {
+          const bool up = (lane & 2) != 0;
+#pragma unroll
+          for (int r = 0; r < R / 4; ++r) {
+            const float send = up ? p[r] : p[r + R / 4];
+            const float keep = up ? p[r + R / 4] : p[r];
+            p[r] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+          }
+        }
+        red += __shfl_xor_sync(0xffffffffu, red, 16);
+        const float dr = bt * red;
+        if (g == 0 && jlive) dv[(row0 + (int64_t)t * H) * D + jc] = dr;
+#pragma unroll
+        for (int r = 0; r < R / 4; ++r) buf[(tt * NWARP + warp) * D + rbase + r] = p[r];
+#pragma unroll
+        for (int r = 0; r < R; ++r) G[r] = fmaf(-kk[r], dr, G[r]);
+      }
+      __syncthreads();  // the slot is read and the block's partials are in buf
+      flush_partials(buf, part_gr, row0, H, t0, tn, D);
+      if (i + NBUF < NBLK) stage_block<4>(slot(i), REC, (NBLK - 1 - (i + NBUF)) * TB, T, rows_a, beta + row0, shift_p, H, 2 * D + 3 * BV);
+      cp_commit();
+      __syncthreads();  // buf is free again
+    }
+    cp_wait<0>();
+    if (jlive) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) ds0[(int64_t)bh * D * D + (int64_t)(g * R + r) * D + jc] = G[r];
+    }
+  } else {
+    float G[NI][CPW];
+  #pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const int i = lane + 32 * m;
+  #pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        const int j = j0 + c;
+        G[m][c] = (dsn && i < D && j < D) ? dsn[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
+      }
+    }
+    // phase A, blocks in reverse: block i of the walk is block NBLK - 1 - i of the sequence
+    {
+      const StageRow rows_a[4] = {{k + row0 * D, rs, 0, D / 4}, {q + row0 * D, rs, D, D / 4},
+                                  {dout + row0 * D + jb * BV, rs, 2 * D, ncol / 4},
+                                  {resid + row0 * D + jb * BV, rs, 2 * D + BV, ncol / 4}};
+  #pragma unroll 1
+      for (int i = 0; i < NBUF; ++i) {
+        if (i < NBLK) stage_block<4>(slot(i), REC, (NBLK - 1 - i) * TB, T, rows_a, beta + row0, shift_p, H, 2 * D + 3 * BV);
+        cp_commit();
+      }
+      for (int i = 0; i < NBLK; ++i) {
+        const int blk = NBLK - 1 - i, t0 = blk * TB, tn = min(TB, T - t0);
+        cp_wait<NBUF - 1>();
+        __syncthreads();
+        const float* sl = slot(i);
+        for (int tt = tn - 1; tt >= 0; --tt) {
+          const int t = t0 + tt;
+          const float* rec = sl + tt * REC;
+          float kk[NI], qq[NI], gg[CPW], rr[CPW];
+  #pragma unroll
+          for (int m = 0; m < NI; ++m) {
+            const int ii = lane + 32 * m;
+            kk[m] = ii < D ? rec[ii] : 0.f;
+            qq[m] = ii < D ? rec[D + ii] : 0.f;
+          }
+  #pragma unroll
+          for (int c = 0; c < CPW; ++c) {
+            const bool ok = j0 + c < D;
+            gg[c] = ok ? rec[2 * D + warp * CPW + c] : 0.f;
+            rr[c] = ok ? rec[2 * D + BV + warp * CPW + c] : 0.f;
+          }
+          const float bt = staged_beta(rec + 2 * D + 3 * BV, logit, shift_p != nullptr);
+          const int64_t row = row0 + (int64_t)t * H;
+  #pragma unroll
+          for (int m = 0; m < NI; ++m)
+  #pragma unroll
+            for (int c = 0; c < CPW; ++c) G[m][c] = fmaf(qq[m], gg[c], G[m][c]);
+          float red_c[CPW];
+  #pragma unroll
+          for (int c = 0; c < CPW; ++c) {
+            float a = 0.f;
+  #pragma unroll
+            for (int m = 0; m < NI; ++m) a = fmaf(G[m][c], kk[m], a);
+            red_c[c] = a;
+          }
+  #pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+  #pragma unroll
+            for (int c = 0; c < CPW; ++c) red_c[c] += __shfl_xor_sync(0xffffffffu, red_c[c], off);
+          float dr[CPW];
+  #pragma unroll
+          for (int c = 0; c < CPW; ++c) dr[c] = bt * red_c[c];
+          if (lane < CPW) {
+            float x = dr[0];
+  #pragma unroll
+            for (int c = 1; c < CPW; ++c)
+              if (lane == c) x = dr[c];
+            if (j0 + lane < D) dv[row * D + j0 + lane] = x;
+          }
+  #pragma unroll
+          for (int m = 0; m < NI; ++m) {
+            float a = 0.f;
+  #pragma unroll
+            for (int c = 0; c < CPW; ++c) a = fmaf(G[m][c], rr[c], a);
+            const int ii = lane + 32 * m;
+            if (ii < D) buf[(tt * NWARP + warp) * D + ii] = a;
+          }
+  #pragma unroll
+          for (int m = 0; m < NI; ++m)
+  #pragma unroll
+            for (int c = 0; c < CPW; ++c) G[m][c] = fmaf(-kk[m], dr[c], G[m][c]);
+        }
+        __syncthreads();  // the slot is read and the block's partials are in buf
+        flush_partials(buf, part_gr, row0, H, t0, tn, D);
+        if (i + NBUF < NBLK) stage_block<4>(slot(i), REC, (NBLK - 1 - (i + NBUF)) * TB, T, rows_a, beta + row0, shift_p, H, 2 * D + 3 * BV);
+        cp_commit();
+        __syncthreads();  // buf is free again
+      }
+      cp_wait<0>();
+    }
+  #pragma unroll
+    for (int m = 0; m < NI; ++m) {
+      const int i = lane + 32 * m;
+  #pragma unroll
+      for (int c = 0; c < CPW; ++c) {
+        const int j = j0 + c;
+        if (i < D && j < D) ds0[(int64_t)bh * D * D + (int64_t)i * D + j] = G[m][c];
+      }
+    }
+  }
+  __syncthreads();  // dv of this CTA's columns is complete before phase B copies it back
+  float S[NI][CPW];
+#pragma unroll
+  for (int m = 0; m < NI; ++m) {
+    const int i = lane + 32 * m;
+#pragma unroll
+    for (int c = 0; c < CPW; ++c) {
+      const int j = j0 + c;
+      S[m][c] = (i < D && j < D) ? s0[(int64_t)bh * D * D + (int64_t)i * D + j] : 0.f;
+    }
+  }
+  // phase B, blocks forward: k, g, r, dv
+  {
+    const StageRow rows_b[4] = {{k + row0 * D, rs, 0, D / 4}, {dout + row0 * D + jb * BV, rs, 2 * D, ncol / 4},
+                                {resid + row0 * D + jb * BV, rs, 2 * D + BV, ncol / 4},
+                                {dv + row0 * D + jb * BV, rs, 2 * D + 2 * BV, ncol / 4}};
+#pragma unroll 1
+    for (int i = 0; i < NBUF; ++i) {
+      if (i < NBLK) stage_block<4>(slot(i), REC, i * TB, T, rows_b, beta + row0, shift_p, H, 2 * D + 3 * BV);
+      cp_commit();
+    }
+    for (int blk = 0; blk < NBLK; ++blk) {
+      const int t0 = blk * TB, tn = min(TB, T - t0);
+      cp_wait<NBUF - 1>();
+      __syncthreads();
+      const float* sl = slot(blk);
+      for (int tt = 0; tt < tn; ++tt) {
+        const float* rec = sl + tt * REC;
+        float kk[NI], gg[CPW], rr[CPW], dr[CPW];
+#pragma unroll
+        for (int m = 0; m < NI; ++m) {
+          const int ii = lane + 32 * m;
+          kk[m] = ii < D ? rec[ii] : 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < CPW; ++c) {
+          const bool ok = j0 + c < D;
+          gg[c] = ok ? rec[2 * D + warp * CPW + c] : 0.f;
+          rr[c] = ok ? rec[2 * D + BV + warp * CPW + c] : 0.f;
+          dr[c] = ok ? rec[2 * D + 2 * BV + warp * CPW + c] : 0.f;
+        }
+        const float bt = staged_beta(rec + 2 * D + 3 * BV, logit, shift_p != nullptr);
+#pragma unroll
+        for (int m = 0; m < NI; ++m) {
+          float a = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPW; ++c) a = fmaf(S[m][c], dr[c], a);
+          const int ii = lane + 32 * m;
+          if (ii < D) buf[(tt * NWARP + warp) * D + ii] = a;
+        }
+#pragma unroll
+        for (int m = 0; m < NI; ++m) {
+          const float bk = bt * kk[m];
+#pragma unroll
+          for (int c = 0; c < CPW; ++c) S[m][c] = fmaf(bk, rr[c], S[m][c]);
+        }
+#pragma unroll
+        for (int m = 0; m < NI; ++m) {
+          float a = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPW; ++c) a = fmaf(S[m][c], gg[c], a);
+          const int ii = lane + 32 * m;
+          if (ii < D) buf1[(tt * NWARP + warp) * D + ii] = a;
+        }
+      }
+      __syncthreads();
+      flush_partials(buf, part_hd, row0, H, t0, tn, D);
+      flush_partials(buf1, part_dq, row0, H, t0, tn, D);
+      if (blk + NBUF < NBLK) stage_block<4>(slot(blk), REC, (blk + NBUF) * TB, T, rows_b, beta + row0, shift_p, H, 2 * D + 3 * BV);
+      cp_commit();
+      __syncthreads();
+    }
+    cp_wait<0>();
+  }
+}
+
+size_t fwd_staged_smem(int D) { return sizeof(float) * (size_t)NBUF * TB * (2 * D + BV + 4); }
+size_t bwd_staged_smem(int D) {
+  return sizeof(float) * ((size_t)NBUF * TB * (2 * D + 3 * BV + 4) + 2 * (size_t)TB * NWARP * D);
+}
+
 // ---- the one-token step (decode) -------------------------------------------------------------
 // One CTA of 256 threads per (batch, head): thread t owns the 4-column group j4 = t % (D/4) of
 // rows i = t / (D/4) + s * NS (NS = 256 / (D/4) row slices), so every state access is a coalesced
@@ -465,9 +1074,25 @@ int scan_f32_fwd(const float* q, const float* k, const float* v, const float* be
   VB_REQUIRE(q && k && v && beta && state0 && o && state_n, "delta_scan_f32_fwd: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   dim3 grid(njb(D), B * H);
+  const bool staged = D % 4 == 0 && aligned16(q) && aligned16(k) && aligned16(v);
   return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    scan_f32_fwd_kernel<NI, float><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, shift, logit, state0, o, state_n,
-                                                                resid, T, H, D);
+    if (staged && D == 32 * NI) {  // rows in 8 groups of D / 8 (D a power of two from 32 to 256)
+      const size_t smem = fwd_staged_smem(D);
+      constexpr int R = 4 * NI;
+      VB_CUDA_CHECK(cudaFuncSetAttribute(scan_f32_fwd_group_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem), "delta_scan_f32_fwd attr");
+      scan_f32_fwd_group_kernel<R><<<grid, NWARP * 32, smem, st>>>(q, k, v, beta, shift, logit, state0, o, state_n,
+                                                                   resid, T, H, D);
+    } else if (staged) {
+      const size_t smem = fwd_staged_smem(D);
+      VB_CUDA_CHECK(cudaFuncSetAttribute(scan_f32_fwd_staged_kernel<NI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem), "delta_scan_f32_fwd attr");
+      scan_f32_fwd_staged_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, v, beta, shift, logit, state0, o, state_n,
+                                                                     resid, T, H, D);
+    } else {
+      scan_f32_fwd_kernel<NI, float><<<grid, NWARP * 32, 0, st>>>(q, k, v, beta, shift, logit, state0, o, state_n,
+                                                                  resid, T, H, D);
+    }
     VB_LAUNCH_CHECK("delta_scan_f32_fwd");
     return VB_OK;
   });
@@ -532,9 +1157,26 @@ int scan_f32_bwd(const float* q, const float* k, const float* beta, const float*
   dim3 grid(njb(D), B * H);
   const size_t smem = sizeof(float) * NWARP * D;
   float* part = (float*)workspace;
+  const bool staged = D % 4 == 0 && aligned16(q) && aligned16(k) && aligned16(resid) && aligned16(dout) &&
+                      aligned16(dv);
   return VB_NI_DISPATCH(D, NI, [&]() -> int {
-    scan_f32_bwd_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, beta, shift, logit, state0, resid, dout,
-                                                            dstate_n, dv, dstate0, part, B, T, H, D);
+    if (staged) {
+      const size_t sm = bwd_staged_smem(D);
+      if (D == 32 * NI) {
+        VB_CUDA_CHECK(cudaFuncSetAttribute(scan_f32_bwd_staged_kernel<NI, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm), "delta_scan_f32_bwd attr");
+        scan_f32_bwd_staged_kernel<NI, true><<<grid, NWARP * 32, sm, st>>>(q, k, beta, shift, logit, state0, resid,
+                                                                           dout, dstate_n, dv, dstate0, part, B, T, H, D);
+      } else {
+        VB_CUDA_CHECK(cudaFuncSetAttribute(scan_f32_bwd_staged_kernel<NI, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm), "delta_scan_f32_bwd attr");
+        scan_f32_bwd_staged_kernel<NI, false><<<grid, NWARP * 32, sm, st>>>(q, k, beta, shift, logit, state0, resid,
+                                                                            dout, dstate_n, dv, dstate0, part, B, T, H, D);
+      }
+    } else {
+      scan_f32_bwd_kernel<NI><<<grid, NWARP * 32, smem, st>>>(q, k, beta, shift, logit, state0, resid, dout,
+                                                              dstate_n, dv, dstate0, part, B, T, H, D);
+    }
     VB_LAUNCH_CHECK("delta_scan_f32_bwd");
     const int64_t rows = (int64_t)B * T * H;
     if (rows > 0) {
