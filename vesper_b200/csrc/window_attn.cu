@@ -155,11 +155,14 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   constexpr bool BF = std::is_same<E, __nv_bfloat16>::value;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024(smem_raw);
+  // Q, K double-buffered, V single-buffered (V_i is read only by tile i's second product, which
+  // runs after the tile's softmax: its copy is issued once the previous tile's product is done),
+  // P: 96 KB at DK 64, so two CTAs share an SM and one's products overlap the other's softmax
   uint8_t* Qt = sm;
-  auto Kt = [&](int i) { return sm + (1 + 2 * (i & 1)) * TQ; };  // K, V tiles double-buffered
-  auto Vt = [&](int i) { return sm + (2 + 2 * (i & 1)) * TQ; };
-  uint8_t* Pt = sm + 5 * TQ;  // P [128 q][128 keys]
-  __shared__ uint64_t barS, barO, lbarQ, lbar[2];
+  auto Kt = [&](int i) { return sm + (1 + (i & 1)) * TQ; };
+  uint8_t* Vt = sm + 3 * TQ;
+  uint8_t* Pt = sm + 4 * TQ;  // P [128 q][128 keys]
+  __shared__ uint64_t barS, barO, lbarQ, lbar[2], lbarV;
   __shared__ uint32_t tbase;
   __shared__ float xch[2][BQ];  // the two half-row threads' partial maxima, then sums
   const int NQ = qpos.NQ;
@@ -181,6 +184,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   const int g = h / (H / HKV);
   if (tid == 0) {
     mbar_init(&barS, 1); mbar_init(&barO, 1); mbar_init(&lbarQ, 1); mbar_init(&lbar[0], 1); mbar_init(&lbar[1], 1);
+    mbar_init(&lbarV, 1);
     mbar_fence_init();
   }
   if (warp == 0) { tmem_alloc(&tbase, 256); tmem_relinquish(); }
@@ -195,18 +199,21 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
   const int klo = max(0, qp_first - window + 1), khi = min(L - 1, qp_last);
   const int kt_lo = klo / BK;
   const int ntiles = khi >= klo ? khi / BK - kt_lo + 1 : 0;
-  auto load_kv = [&](int i) {
+  auto load_k = [&](int i) {
     uint64_t* lb = &lbar[i & 1];
-    mbar_arrive_expect_tx(lb, 2 * TQ);
+    mbar_arrive_expect_tx(lb, TQ);
     tma_rows<ATOMS>(Kt(i), &kmap, lb, g, (kt_lo + i) * BK, b);
-    tma_rows<ATOMS>(Vt(i), &vmap, lb, g, (kt_lo + i) * BK, b);
+  };
+  auto load_v = [&](int i) {
+    mbar_arrive_expect_tx(&lbarV, TQ);
+    tma_rows<ATOMS>(Vt, &vmap, &lbarV, g, (kt_lo + i) * BK, b);
   };
   if (tid == 0) {
     mbar_arrive_expect_tx(&lbarQ, TQ);
     tma_rows<ATOMS>(Qt, &qmap, &lbarQ, h, r0, b);
-    if (ntiles > 0) load_kv(0);
+    if (ntiles > 0) { load_k(0); load_v(0); }
   }
-  uint32_t lph[2] = {0u, 0u}, pS = 0, pO = 0, pQ = 0;
+  uint32_t lph[2] = {0u, 0u}, pS = 0, pO = 0, pQ = 0, pV = 0;
   bool ok = wait_flag(&lbarQ, pQ, status);
   const uint32_t id_s = idesc_16(BQ, BK, 0, 0, BF);
   const uint32_t id_o = idesc_16(BQ, DK, 0, 1, BF);
@@ -219,9 +226,12 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
       umma_commit(&barS);
     }
     ok = wait_flag(&barS, pS, status) && ok;
-    // every earlier product is complete: the other buffer and P are free
+    // every earlier product is complete: the other K buffer, V and P are free
     if (i > 0) ok = wait_flag(&barO, pO, status) && ok;
-    if (tid == 0 && i + 1 < ntiles) load_kv(i + 1);
+    if (tid == 0) {
+      if (i > 0) load_v(i);  // V_0 was copied with K_0
+      if (i + 1 < ntiles) load_k(i + 1);
+    }
     const int k0 = (kt_lo + i) * BK;
     // a tile inside every row's window needs no mask (rows ascend in position)
     const bool interior = k0 + BK - 1 <= qp_first && k0 > qp_last - window && k0 + BK <= L && r0 + BQ <= nb;
@@ -277,8 +287,12 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
     }
     ok = publish(ok);
     if (tid == 0 && ok) {
-      mma_seq<BK / 16, 0, BQ, 1, BK>(tm + C_O, smem_u32(Pt), smem_u32(Vt(i)), id_o, i > 0 ? 1u : 0u);
-      umma_commit(&barO);
+      if (wait_flag(&lbarV, pV, status)) {  // V_i has landed
+        mma_seq<BK / 16, 0, BQ, 1, BK>(tm + C_O, smem_u32(Pt), smem_u32(Vt), id_o, i > 0 ? 1u : 0u);
+        umma_commit(&barO);
+      } else {
+        ok = false;
+      }
     }
   }
   if (ntiles > 0 && ok) ok = wait_flag(&barO, pO, status);
@@ -622,7 +636,7 @@ __global__ void __launch_bounds__(NT) attn_dkv_kernel(
 }
 
 template <int DK> constexpr int dkv_nbuf() { return DK > 64 ? 1 : 2; }
-template <int DK> constexpr size_t fwd_smem() { return (size_t)5 * BQ * 128 * ((DK + 63) / 64) + BQ * 256 + 1024; }
+template <int DK> constexpr size_t fwd_smem() { return (size_t)4 * BQ * 128 * ((DK + 63) / 64) + BQ * 256 + 1024; }
 template <int DK> constexpr size_t dq_smem() { return (size_t)6 * BQ * 128 * ((DK + 63) / 64) + BQ * 256 + 1024; }
 template <int DK> constexpr size_t dkv_smem() {
   return (size_t)(2 + 2 * dkv_nbuf<DK>()) * BQ * 128 * ((DK + 63) / 64) + 2 * BK * 256 + 1024;
