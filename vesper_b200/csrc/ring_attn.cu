@@ -11,7 +11,10 @@
 // row never read what another is writing.
 //
 // A row's window is split into ranges of 128 slots, one CTA of eight warps per (row, key head,
-// range) so that enough warps keep loads in flight: (1) the warps share the range's candidates
+// range). Rows of a multiple of 16 bytes take the staged kernel (every key and value row of the
+// range copied into shared memory at once, one thread per candidate for the scores and one per
+// head and channel for the weighted values); other rows the kernel below, in which (1) the warps
+// share the range's candidates
 // and form the group's scores for each (lane l holding channels l, l + 32, ... of the queries and
 // the key row; the scores are warp sums), -inf for a slot that is not visible; (2) warp g reduces
 // head g's scores to the range's max and the unnormalised weights and their sum; (3) the warps
@@ -174,6 +177,116 @@ __global__ void __launch_bounds__(NT) ring_attn_part_kernel(
   }
 }
 
+// The same partials from rows staged in shared memory (rows of a multiple of 16 bytes): every key
+// and value row of the range (and, in the last range, the new token's) is copied at once by
+// cp.async into an XOR-swizzled tile (16-byte chunk c of row r at c ^ (r mod 8)), the visibility
+// pass runs while they land, then one thread per candidate forms the group's scores over the whole
+// row and one thread per (head, channel) sums weight x value over the candidates: no shuffles and
+// no cross-warp reduction, and only one round trip to memory per CTA.
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+template <typename E, int GC>
+__global__ void __launch_bounds__(NT) ring_attn_part_staged_kernel(
+    const E* __restrict__ q, const E* __restrict__ k_new, const E* __restrict__ v_new, const E* __restrict__ ring_k,
+    const E* __restrict__ ring_v, const int64_t* __restrict__ ring_pos, const uint8_t* __restrict__ ring_valid,
+    const int64_t* __restrict__ pos, float* __restrict__ part, int W, int H, int HKV, int DK, int window,
+    float scale) {
+  extern __shared__ __align__(16) uint8_t sraw[];
+  constexpr int G = GC;
+  const int nsplit = gridDim.z;
+  const int b = blockIdx.x, kh = blockIdx.y, z = blockIdx.z, tid = threadIdx.x;
+  const int lo = z * SPLIT_SLOTS, hi = min(W, lo + SPLIT_SLOTS);
+  const bool last = z == nsplit - 1;
+  const int L = hi - lo + (last ? 1 : 0);  // candidates: local index i is slot lo + i, or the new token
+  const int RB = DK * (int)sizeof(E), NCH = RB / 16, SWM = (NCH < 8 ? NCH : 8) - 1;
+  constexpr int EPC = 16 / (int)sizeof(E);
+  uint8_t* ks = sraw;                                                      // [L][RB]
+  uint8_t* vs = ks + (size_t)(SPLIT_SLOTS + 1) * RB;                       // [L][RB]
+  float* qs = reinterpret_cast<float*>(vs + (size_t)(SPLIT_SLOTS + 1) * RB);  // [G][DK]
+  float* ps = qs + G * DK;                                                 // [G][L]
+  uint8_t* vis = reinterpret_cast<uint8_t*>(ps + G * (SPLIT_SLOTS + 1));   // [L]
+  auto row_k = [&](int i) -> const E* {
+    return i < hi - lo ? ring_k + (((int64_t)b * W + lo + i) * HKV + kh) * DK : k_new + ((int64_t)b * HKV + kh) * DK;
+  };
+  auto row_v = [&](int i) -> const E* {
+    return i < hi - lo ? ring_v + (((int64_t)b * W + lo + i) * HKV + kh) * DK : v_new + ((int64_t)b * HKV + kh) * DK;
+  };
+  for (int c = tid; c < L * NCH; c += NT) {
+    const int i = c / NCH, ch = c - i * NCH, at = (i * NCH + (ch ^ (i & SWM))) * 16;
+    cp16(ks + at, reinterpret_cast<const uint8_t*>(row_k(i)) + ch * 16);
+    cp16(vs + at, reinterpret_cast<const uint8_t*>(row_v(i)) + ch * 16);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int64_t p = pos[b];
+  const int own = (int)(p % W);
+  for (int e = tid; e < G * DK; e += NT) qs[e] = to_f32<E>(q[((int64_t)b * H + kh * G) * DK + e]);
+  for (int i = tid; i < L; i += NT) {
+    const int s = i < hi - lo ? lo + i : W;
+    bool v = s == W;
+    if (!v && s != own && ring_valid[(int64_t)b * W + s]) {
+      const int64_t kp = ring_pos[(int64_t)b * W + s];
+      v = kp <= p && kp > p - window;
+    }
+    vis[i] = v ? 1 : 0;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  // scores: one thread per candidate, the whole row against each head's query
+  for (int i = tid; i < L; i += NT) {
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    for (int ch = 0; ch < NCH; ++ch) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(ks + (i * NCH + (ch ^ (i & SWM))) * 16);
+      const E* e = reinterpret_cast<const E*>(&raw);
+#pragma unroll
+      for (int u = 0; u < EPC; ++u) {
+        const float kv = to_f32<E>(e[u]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc[g] = fmaf(qs[g * DK + ch * EPC + u], kv, acc[g]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) ps[g * L + i] = vis[i] ? acc[g] * scale : -INFINITY;
+  }
+  __syncthreads();
+  // head g (warp g): the local max and the unnormalised weights exp(score - max), their sum
+  float* stats = part + ((((int64_t)b * HKV + kh) * nsplit + z) * G) * (DK + 2);
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int g = warp; g < G; g += NT / 32) {
+    float* row = ps + g * L;
+    float m = -INFINITY;
+    for (int i = lane; i < L; i += 32) m = fmaxf(m, row[i]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int i = lane; i < L; i += 32) {
+      const float e = row[i] == -INFINITY ? 0.f : expf(row[i] - m);
+      row[i] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stats[g * (DK + 2) + DK] = m;
+      stats[g * (DK + 2) + DK + 1] = l;
+    }
+  }
+  __syncthreads();
+  // weight x value: one thread per (head, channel), the candidates in order
+  for (int e = tid; e < G * DK; e += NT) {
+    const int g = e / DK, d = e - g * DK, ch = d / EPC, u = d - ch * EPC;
+    const float* w = ps + g * L;
+    float a = 0.f;
+    for (int i = 0; i < L; ++i) {
+      const E* vr = reinterpret_cast<const E*>(vs + (i * NCH + (ch ^ (i & SWM))) * 16);
+      a = fmaf(w[i], to_f32<E>(vr[u]), a);
+    }
+    stats[g * (DK + 2) + d] = a;
+  }
+}
+
 // Merges a (row, key head)'s range partials in range order into the output, then writes the new
 // token into its slot: the partial kernel has finished every read of the ring.
 template <typename E>
@@ -242,6 +355,18 @@ extern "C" int vb_ring_attend(const void* q, const void* k_new, const void* v_ne
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
     auto part_launch = [&](auto gc, auto nec) -> int {
       constexpr int GG = decltype(gc)::value, NN = decltype(nec)::value;
+      if ((DK * (int)sizeof(T)) % 16 == 0 && aligned16(ring_k) && aligned16(ring_v) && aligned16(k_new) &&
+          aligned16(v_new)) {
+        const size_t sm2 = 2 * (size_t)L * DK * sizeof(T) + sizeof(float) * ((size_t)GG * DK + (size_t)GG * L) + L;
+        VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_part_staged_kernel<T, GG>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm2),
+                      "ring_attend: smem attribute");
+        ring_attn_part_staged_kernel<T, GG><<<dim3(B, HKV, nsplit), NT, sm2, st>>>(
+            (const T*)q, (const T*)k_new, (const T*)v_new, (const T*)ring_k, (const T*)ring_v, ring_pos, ring_valid,
+            pos, part, W, H, HKV, DK, window, scale);
+        VB_LAUNCH_CHECK("ring_attend part");
+        return VB_OK;
+      }
       VB_CUDA_CHECK(cudaFuncSetAttribute(ring_attn_part_kernel<T, GG, NN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                     "ring_attend: smem attribute");
