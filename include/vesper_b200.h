@@ -296,6 +296,35 @@ VB_API int vb_expand_rows(const int *rank, int B, int N, int NC, int ntensors,
                           const void *const *src, const void *const *fallback, void *const *dst,
                           const long long *row_bytes, void *stream);
 
+/* gather for bucketed work: as vb_gather_rows with counts required, except that the rows from
+ * counts[b] up to the end of its bucket (the smallest first * 2^k >= counts[b], clamped to NC) are
+ * zeroed and the rows past it are left untouched, so the copy's cost follows the active rows. */
+VB_API int vb_gather_rows_slabs(const int *idx, const int *counts, int B, int N, int NC, int first,
+                                int ntensors, const void *const *src, void *const *dst,
+                                const long long *row_bytes, void *stream);
+
+/* flatten: the compaction of all B x N tokens as one row from the per-row one (vb_compact_index):
+ * flat_idx[base_b + r] = b N + idx[b][r] for r < counts[b], flat_rank[b N + t] = base_b +
+ * rank[b][t] (-1 halted), *flat_count = the active total; base_b = counts[0] + ... + counts[b-1].
+ * The loop's per-token work after compaction (vesper/loop.py:24-26: "a kernel skips them"). */
+VB_API int vb_flatten_compaction(const int *idx, const int *rank, const int *counts, int B, int N,
+                                 int *flat_idx, int *flat_rank, int *flat_count, void *stream);
+
+/* ---- buckets: work over a device-side row count inside one captured graph ----
+ * The prefixes [0, end_k) of a buffer of `cap` rows, end_0 = first, end_k = 2 end_{k-1} (the last
+ * clamped to cap), are the buckets; vb_slab_count gives their number n (at most 24). While
+ * `stream` is being captured, vb_slab_switch captures a kernel that reads *count when the graph
+ * runs, then adds a SWITCH conditional node with n bodies (returned in bodies[0..n)): the node
+ * runs body k for the smallest k with end_k >= *count, and none for a count of zero.
+ * vb_slab_begin starts capturing one body on `body_stream` (launches made there until
+ * vb_slab_close form it). A replay then does the work of at most twice the active rows. The
+ * loop's dense compute of halted tokens is what this removes (vesper/loop.py:24-26); the graph it
+ * lives in is the captured train step (vesper/graphs.py:49-289). */
+VB_API int vb_slab_count(int cap, int first);
+VB_API int vb_slab_switch(const int *count, int cap, int first, void *stream, void **bodies);
+VB_API int vb_slab_begin(void *body, void *body_stream);
+VB_API int vb_slab_close(void *body_stream);
+
 /* ---- fused elementwise ops of the column (bf16, f16 or f32 by `dtype`, 16-byte aligned) ----
  * relu_square: y = relu(z)^2 and dz from dy, n elements, bit-identical to the reference's
  * separate relu and product ops in the same dtype. Replaces vesper/kernels/act.py:21

@@ -64,6 +64,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_select_rows": (_I, [_P, _I, _I, _P, _P, _P, _P, ctypes.c_longlong, _P]),
     "vb_gather_rows": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "vb_expand_rows": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
+    "vb_gather_rows_slabs": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "vb_flatten_compaction": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "vb_slab_count": (_I, [_I, _I]),
+    "vb_slab_switch": (_I, [_P, _I, _I, _P, _P]),
+    "vb_slab_begin": (_I, [_P, _P]),
+    "vb_slab_close": (_I, [_P]),
     "vb_relu_square_fwd": (_I, [_P, _P, ctypes.c_longlong, _I, _P]),
     "vb_relu_square_bwd": (_I, [_P, _P, _P, ctypes.c_longlong, _I, _P]),
     "vb_rotary": (_I, [_P, _P, _P, _P, ctypes.c_longlong, _I, _I, _I, _I, _P]),

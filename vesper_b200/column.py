@@ -27,7 +27,7 @@ from torch import Tensor, nn
 from vesper_b200.attention import KVCache, RingKVCache, WindowedAttention, kv_cache_empty, kv_ring_empty
 from vesper_b200.contracts import ContractError, Dims, check_shape
 from vesper_b200.kernels.act import relu_square, residual_add
-from vesper_b200.kernels.compact import compact_index, select_rows
+from vesper_b200.kernels.compact import Compaction, compact_index, expand_rows, gather_rows, select_rows
 from vesper_b200.kernels.delta_scan import (
     delta_scan_fused,
     delta_scan_fused_fp32,
@@ -36,6 +36,7 @@ from vesper_b200.kernels.delta_scan import (
 )
 from vesper_b200.kernels.keys import fused_keys
 from vesper_b200.kernels.norm import add_rms_norm, fused_rms_norm
+from vesper_b200.kernels.slabs import slab_ffn
 
 ScanImpl = Literal["fused", "fused-fp32"]
 SCAN_IMPLS: tuple[ScanImpl, ...] = ("fused", "fused-fp32")
@@ -87,10 +88,13 @@ class Projections:
 
 @dataclass(frozen=True)
 class Carry:
-    """Which tokens are active (``bool[b, n]``) and what the halted ones write instead."""
+    """Which tokens are active (``bool[b, n]``) and what the halted ones write instead; ``rows``
+    (optional, ``compact_flat(active, ...)``) lets the feed-forward block run on the active rows
+    only."""
 
     active: Tensor
     projections: Projections
+    rows: Compaction | None = None
 
 
 @dataclass(frozen=True)
@@ -291,6 +295,17 @@ class FFN(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         return F.linear(relu_square(F.linear(x, self.w1)), self.w2)
 
+    def forward_rows(self, x: Tensor, rows: Compaction) -> Tensor:
+        """``forward(x)`` at the active tokens of ``rows`` (a ``compact_flat`` compaction of
+        ``x [b, n, d]``'s tokens) and zero at the others: the active rows are gathered, the block
+        runs as slab-sized work over their live count (``slab_ffn``), the result is expanded."""
+        b, n, d = x.shape
+        (xc,) = gather_rows(rows, [x.reshape(1, b * n, d)])
+        w1, w2 = self.w1.to(xc.dtype), self.w2.to(xc.dtype)  # the casts autocast's linear makes
+        yc = slab_ffn(xc[0], w1, w2, rows.counts, rows.slab_first)
+        (y,) = expand_rows(rows, [yc.view(1, b * n, -1)])
+        return y.view(b, n, -1)
+
 
 def set_scan(model: nn.Module, impl: str) -> int:
     """Choose the scan of every ``RecurrentSublayer`` (``vesper/column.py:353-384``); the
@@ -381,7 +396,11 @@ class Column(nn.Module):
         x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
 
         keep = carry.active if zero_halted and carry is not None else None
-        x = residual_add(x, self.ffn.forward(xn), keep)  # the halted rows zeroed here when asked
+        if carry is not None and carry.rows is not None:  # the active rows only, zero at the others
+            f = self.ffn.forward_rows(xn, carry.rows)
+        else:
+            f = self.ffn.forward(xn)
+        x = residual_add(x, f, keep)  # the halted rows zeroed here when asked
         h = tuple(h_new if i == pass_index else s for i, s in enumerate(state.h))
         kv = tuple(kv_new if i == pass_index else c for i, c in enumerate(state.kv))
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))

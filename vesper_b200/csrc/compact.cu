@@ -101,6 +101,78 @@ __global__ void expand_rows_kernel(const int* __restrict__ rank, RowSets s, int 
   }
 }
 
+// The end of the bucket that runs for `c` active rows: the smallest first * 2^k >= c, clamped to
+// the buffer's NC rows (0 when no row is active).
+__device__ __forceinline__ int slab_end(int c, int first, int NC) {
+  if (c <= 0) return 0;
+  long long end = first;
+  while (end < c) end *= 2;
+  return (int)(end < NC ? end : NC);
+}
+
+// As gather_rows_kernel, for compact buffers that bucketed work reads: rows from counts[b] to the
+// end of the bucket are zeroed, the rows past it are left as they are (never read).
+__global__ void gather_slabs_kernel(const int* __restrict__ idx, const int* __restrict__ counts, RowSets s, int B,
+                                    int N, int NC, int first) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)B * NC;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows * s.n; w += warps) {
+    const int i = (int)(w / rows);
+    const int64_t br = w % rows;
+    const int b = (int)(br / NC), r = (int)(br % NC);
+    const int c = counts[b];
+    if (r >= slab_end(c, first, NC)) continue;
+    const int t = r < c ? idx[br] : -1;
+    const bool ok = t >= 0 && t < N;
+    copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, lane);
+  }
+}
+
+// One compaction of all B x N tokens from the per-row one: base = the active tokens of the rows
+// before b; flat_idx[base + r] = b N + idx[b][r] (r < counts[b]), flat_rank[b N + t] = base +
+// rank[b][t] (or -1), *flat_count = the total. One CTA per row; the base is a sum over counts.
+constexpr int FLAT_T = 256;
+__global__ void __launch_bounds__(FLAT_T) flatten_compaction_kernel(const int* __restrict__ idx,
+                                                                    const int* __restrict__ rank,
+                                                                    const int* __restrict__ counts, int B, int N,
+                                                                    int* __restrict__ flat_idx,
+                                                                    int* __restrict__ flat_rank,
+                                                                    int* __restrict__ flat_count) {
+  __shared__ int part[FLAT_T / 32];
+  const int b = blockIdx.x, tid = threadIdx.x;
+  int before = 0, all = 0;
+  for (int j = tid; j < B; j += FLAT_T) {
+    const int c = counts[j];
+    all += c;
+    if (j < b) before += c;
+  }
+  before = __reduce_add_sync(0xffffffffu, before);
+  if ((tid & 31) == 0) part[tid >> 5] = before;
+  __syncthreads();
+  int base = 0;
+#pragma unroll
+  for (int w = 0; w < FLAT_T / 32; ++w) base += part[w];
+  if (b == 0) {
+    __syncthreads();
+    all = __reduce_add_sync(0xffffffffu, all);
+    if ((tid & 31) == 0) part[tid >> 5] = all;
+    __syncthreads();
+    if (tid == 0) {
+      int total = 0;
+      for (int w = 0; w < FLAT_T / 32; ++w) total += part[w];
+      *flat_count = total;
+    }
+  }
+  const int c = counts[b];
+  const int64_t row = (int64_t)b * N;
+  for (int r = tid; r < c; r += FLAT_T) flat_idx[base + r] = (int)(row + idx[row + r]);
+  for (int t = tid; t < N; t += FLAT_T) {
+    const int k = rank[row + t];
+    flat_rank[row + t] = k >= 0 ? base + k : -1;
+  }
+}
+
 constexpr int SCAN_T = 1024;
 
 __global__ void __launch_bounds__(SCAN_T) compact_index_kernel(const uint8_t* __restrict__ active, int* __restrict__ idx,
@@ -215,6 +287,34 @@ extern "C" int vb_gather_rows(const int* idx, const int* counts, int B, int N, i
   if (rc) return rc;
   gather_rows_kernel<<<grid_for((int64_t)B * NC * ntensors), 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N, NC);
   VB_LAUNCH_CHECK("gather_rows");
+  return VB_OK;
+}
+
+extern "C" int vb_gather_rows_slabs(const int* idx, const int* counts, int B, int N, int NC, int first, int ntensors,
+                                    const void* const* src, void* const* dst, const long long* row_bytes,
+                                    void* stream) {
+  VB_REQUIRE(B >= 0 && N >= 0 && NC >= 0 && first > 0, "gather_rows_slabs: bad shape B=%d N=%d NC=%d first=%d", B, N,
+             NC, first);
+  if ((int64_t)B * NC == 0) return VB_OK;
+  VB_REQUIRE(idx != nullptr && counts != nullptr, "gather_rows_slabs: null index or counts");
+  RowSets s;
+  int rc = fill_sets(s, ntensors, src, nullptr, dst, row_bytes, "gather_rows_slabs");
+  if (rc) return rc;
+  gather_slabs_kernel<<<grid_for((int64_t)B * NC * ntensors), 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N,
+                                                                                                NC, first);
+  VB_LAUNCH_CHECK("gather_rows_slabs");
+  return VB_OK;
+}
+
+extern "C" int vb_flatten_compaction(const int* idx, const int* rank, const int* counts, int B, int N, int* flat_idx,
+                                     int* flat_rank, int* flat_count, void* stream) {
+  VB_REQUIRE(B >= 0 && N >= 0, "flatten_compaction: bad shape B=%d N=%d", B, N);
+  VB_REQUIRE((int64_t)B * N <= 0x7fffffff, "flatten_compaction: %lld tokens exceed int32 indices", (long long)B * N);
+  if (B == 0) return VB_OK;
+  VB_REQUIRE(idx && rank && counts && flat_idx && flat_rank && flat_count, "flatten_compaction: null pointer");
+  flatten_compaction_kernel<<<B, FLAT_T, 0, (cudaStream_t)stream>>>(idx, rank, counts, B, N, flat_idx, flat_rank,
+                                                                    flat_count);
+  VB_LAUNCH_CHECK("flatten_compaction");
   return VB_OK;
 }
 

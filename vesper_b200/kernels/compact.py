@@ -35,6 +35,7 @@ class Compaction:
     rank: Tensor
     counts: Tensor
     qpos: Tensor
+    slab_first: int = 0  # > 0: compact buffers feed slab-sized work (``compact_flat``)
 
 
 def compact_index(active: Tensor, qpos_offset: int = 0) -> Compaction:
@@ -55,6 +56,28 @@ def compact_index(active: Tensor, qpos_offset: int = 0) -> Compaction:
         qpos.data_ptr(), b, n, int(qpos_offset), _lib.stream(active.device),
     )  # fmt: skip
     return Compaction(active, idx, rank, counts, qpos)
+
+
+def compact_flat(active: Tensor, slab_first: int) -> Compaction:
+    """All ``b x n`` tokens of ``active bool[b, n]`` as ONE compact row: ``idx``, ``rank``
+    ``[1, b n]`` over the flattened tokens, ``counts [1]`` the active total (on the device, no
+    synchronisation). Its compact buffers feed work cut into slabs of ``slab_first``, ``slab_first``,
+    ``2 slab_first``, ... rows (``vesper_b200.kernels.slabs``): a gather zeroes its rows from the
+    count to the end of the last running slab and leaves the rest, so copies follow the active
+    rows, not the buffer's size."""
+    if slab_first < 1:
+        msg = f"slab_first must be at least 1, got {slab_first}"
+        raise ContractError(msg)
+    per_row = compact_index(active)
+    b, n = per_row.idx.shape
+    idx = torch.empty(1, b * n, dtype=torch.int32, device=active.device)
+    rank = torch.empty_like(idx)
+    counts = torch.empty(1, dtype=torch.int32, device=active.device)
+    _lib.call(
+        "vb_flatten_compaction", per_row.idx.data_ptr(), per_row.rank.data_ptr(), per_row.counts.data_ptr(), b, n,
+        idx.data_ptr(), rank.data_ptr(), counts.data_ptr(), _lib.stream(active.device),
+    )  # fmt: skip
+    return Compaction(per_row.active.view(1, b * n), idx, rank, counts, idx, slab_first)
 
 
 def _row_bytes(t: Tensor, rows: int) -> int:
@@ -138,6 +161,13 @@ def _gather(comp: Compaction, src: Sequence[Tensor]) -> list[Tensor]:
     out = [torch.empty_like(t) for t in src]  # compact buffers sized for the worst case (n rows)
     if b * n == 0:
         return out
+    if comp.slab_first > 0:  # zero padding up to the last running slab only
+        _lib.call(
+            "vb_gather_rows_slabs", comp.idx.data_ptr(), comp.counts.data_ptr(), b, n, n, comp.slab_first,
+            len(src), _ptrs(src), _ptrs(out), _sizes([_row_bytes(t, b * n) for t in src]),
+            _lib.stream(comp.idx.device),
+        )  # fmt: skip
+        return out
     _lib.call(
         "vb_gather_rows", comp.idx.data_ptr(), comp.counts.data_ptr(), b, n, n, len(src), _ptrs(src),
         _ptrs(out), _sizes([_row_bytes(t, b * n) for t in src]), _lib.stream(comp.idx.device),
@@ -181,13 +211,16 @@ class _Expand(torch.autograd.Function):
     def backward(ctx, *grads):  # type: ignore[override]
         g = [x.contiguous() for x in grads]
         d_src = _gather(ctx.comp, g)
-        d_fb = _select(ctx.comp.active, True, g, [None] * len(g), g)
-        d_fb = [d if has else None for d, has in zip(d_fb, ctx.has_fallback, strict=True)]
+        d_fb: list[Tensor | None] = [None] * len(g)
+        if any(ctx.has_fallback):  # the halted rows' gradients go to the fallbacks
+            d_fb = list(_select(ctx.comp.active, True, g, [None] * len(g), g))
+            d_fb = [d if has else None for d, has in zip(d_fb, ctx.has_fallback, strict=True)]
         return (None, None, *d_src, *d_fb)
 
 
 def gather_rows(comp: Compaction, dense: Sequence[Tensor]) -> list[Tensor]:
-    """Each ``[b, n, ...]`` tensor's active rows packed at the front (zero padding rows)."""
+    """Each ``[b, n, ...]`` tensor's active rows packed at the front (zero padding rows; for a
+    ``compact_flat`` compaction only up to the end of the last running slab)."""
     _check_rows("dense", dense, tuple(comp.idx.shape), comp.idx.device)
     return list(_Gather.apply(comp, *[t.contiguous() for t in dense]))
 

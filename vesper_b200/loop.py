@@ -11,7 +11,11 @@ for operation, in torch (so pass counts agree to the bit on the same inputs); wh
 per-token bookkeeping around it: the copy-forward merge of all six carried projections, the
 zeroing of halted rows and the selection of the next input are each one multi-tensor select
 launch (``vb_select_rows``) instead of a ``torch.where`` per tensor, and the columns compute the
-attention queries of active tokens only.
+attention queries of active tokens only. With ``compact_rows`` (the default) every pass after the
+first compacts the active tokens once (``compact_flat``) and the columns run their feed-forward
+blocks on those rows only, as slab-sized work that follows the live count on the device
+(``vesper_b200.kernels.slabs``): the reference computes them densely and discards the halted
+rows' outputs (``vesper/loop.py:24-26``).
 """
 
 from __future__ import annotations
@@ -28,7 +32,8 @@ from torch.utils.checkpoint import checkpoint
 
 from vesper_b200.column import Carry, Column, ColumnState, Projections, RMSNorm
 from vesper_b200.contracts import ContractError, Dims, check_shape, require
-from vesper_b200.kernels.compact import select_rows
+from vesper_b200.kernels.compact import compact_flat, select_rows
+from vesper_b200.kernels.slabs import SLAB_FIRST
 
 CDF_SLACK = 1e-9  # vesper/exits.py:164
 HAZARD_LIMIT = 1e4  # vesper/exits.py:234
@@ -203,6 +208,7 @@ class Loop(nn.Module):
         self.halting_module = halting
         self.t_max, self.halt_epsilon = t_max, halt_epsilon
         self.u = nn.Parameter(torch.zeros(t_max, d))
+        self.compact_rows = True  # feed-forward blocks of passes after the first on active rows only
 
     def forward(self, x0: Tensor, pos: Tensor, states: Sequence[ColumnState], passes: int | None = None, *,
                 recompute: bool = False, exit_rule: ExitRule | None = None,
@@ -246,9 +252,10 @@ class Loop(nn.Module):
         for t in range(steps):
             h = x + self.u[t]
             fresh: list[Projections] = []
+            rows = compact_flat(active, SLAB_FIRST) if self.compact_rows and t > 0 and not dense else None
             for c, column in enumerate(self.columns):
                 previous = carried[c]
-                carry = None if previous is None or dense else Carry(active, previous)
+                carry = None if previous is None or dense else Carry(active, previous, rows)
                 # with a carry the column zeroes the halted rows in its last residual add; without
                 # one (the first pass) no token has halted yet
                 if recompute:
