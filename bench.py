@@ -513,7 +513,8 @@ def _kernel_group(name: str) -> str:
                        ("nll_", "head loss"), ("keys_", "key filter"),
                        ("rms_", "rmsnorm"), ("column_sum", "rmsnorm"), ("select_rows", "copy-forward/compaction"),
                        ("gather_rows", "copy-forward/compaction"), ("expand_rows", "copy-forward/compaction"),
-                       ("compact_", "copy-forward/compaction"), ("relu", "relu^2"), ("rotary", "rotary"),
+                       ("compact_", "copy-forward/compaction"), ("gather_slabs", "copy-forward/compaction"),
+                       ("flatten_compaction", "copy-forward/compaction"), ("bucket_select", "copy-forward/compaction"), ("relu", "relu^2"), ("rotary", "rotary"),
                        ("gemm", "gemm (cuBLAS)"), ("cutlass", "gemm (cuBLAS)"), ("nvjet", "gemm (cuBLAS)"),
                        ("xmma", "gemm (cuBLAS)"), ("cublas", "gemm (cuBLAS)")):  # fmt: skip
         if key in n:

@@ -306,9 +306,13 @@ VB_API int vb_gather_rows_slabs(const int *idx, const int *counts, int B, int N,
 /* flatten: the compaction of all B x N tokens as one row from the per-row one (vb_compact_index):
  * flat_idx[base_b + r] = b N + idx[b][r] for r < counts[b], flat_rank[b N + t] = base_b +
  * rank[b][t] (-1 halted), *flat_count = the active total; base_b = counts[0] + ... + counts[b-1].
- * The loop's per-token work after compaction (vesper/loop.py:24-26: "a kernel skips them"). */
+ * With flat_pb and pb_flat (both or neither), the map between flat compact rows and per-row
+ * compact rows (b, r) stored at b N + r: flat_pb[base_b + r] = b N + r, pb_flat[b N + r] =
+ * base_b + r for r < counts[b], else -1. The loop's per-token work after compaction
+ * (vesper/loop.py:24-26: "a kernel skips them"). */
 VB_API int vb_flatten_compaction(const int *idx, const int *rank, const int *counts, int B, int N,
-                                 int *flat_idx, int *flat_rank, int *flat_count, void *stream);
+                                 int *flat_idx, int *flat_rank, int *flat_count, int *flat_pb,
+                                 int *pb_flat, void *stream);
 
 /* ---- buckets: work over a device-side row count inside one captured graph ----
  * The prefixes [0, end_k) of a buffer of `cap` rows, end_0 = first, end_k = 2 end_{k-1} (the last

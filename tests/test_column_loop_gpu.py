@@ -21,6 +21,7 @@ from conftest import elem_rel, golden, max_rel, rel
 from vesper_b200 import _lib
 from vesper_b200.attention import KVCache
 from vesper_b200.column import Carry, Column, ColumnShape, ColumnState, Projections, init_column_state, set_scan
+from vesper_b200.kernels.compact import compact_flat
 from vesper_b200.loop import CdfRule, HaltingHead, Loop
 
 pytestmark = pytest.mark.gpu
@@ -74,7 +75,10 @@ def _logit(beta: np.ndarray) -> np.ndarray:
     return np.log(b) - np.log1p(-b)
 
 
-def _column_run(f: dict[str, np.ndarray], bf16: bool):
+def _column_run(f: dict[str, np.ndarray], bf16: bool, rows_first: int | None = None, active_loss: bool = False):
+    """One carried column step on the fixture's inputs, then the backward. ``rows_first``: the
+    compacted form (``Carry.rows``, buckets from that many rows), whose halted outputs are not the
+    dense ones (the loop zeroes them); ``active_loss``: the loss over the active rows only."""
     col = Column(SHAPE, torch.Generator().manual_seed(SEED))
     _check_sums(col, f)
     col = col.to(CUDA)
@@ -92,9 +96,11 @@ def _column_run(f: dict[str, np.ndarray], bf16: bool):
     )
     active = _t(f["active"], None)
     proj = Projections(*(leaves[k] for k in ("rec_z", "rec_k", "rec_v", "rec_beta", "attn_k", "attn_v")))
+    rows = None if rows_first is None else compact_flat(active, rows_first)
     with torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
-        y, new, written = col.step(leaves["x"], _t(f["pos"], None), state, 1, carry=Carry(active, proj))
-    ((y.float() * _t(f["up"])).sum() + (new.h[1] * _t(f["up_h"])).sum()).backward()
+        y, new, written = col.step(leaves["x"], _t(f["pos"], None), state, 1, carry=Carry(active, proj, rows))
+    up = torch.where(active[..., None], _t(f["up"]), 0.0) if active_loss else _t(f["up"])
+    ((y.float() * up).sum() + (new.h[1] * _t(f["up_h"])).sum()).backward()
     _lib.check_status(CUDA)
     return col, leaves, active, y, new, written
 
@@ -124,6 +130,34 @@ def test_column_step_with_a_carry_matches_the_reference(bf16: bool) -> None:
         _close(t.grad, want, f"grad {k}")
     for k, p in col.named_parameters():
         _close(p.grad, f[f"grad.{k}"], f"grad {k}")
+    _close.check()
+
+
+@pytest.mark.parametrize("bf16", [False, True], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("first", [4, 64])
+def test_the_compacted_column_step_matches_the_dense_one(bf16: bool, first: int) -> None:
+    """``Carry.rows`` (norms, projections, attention queries and the feed-forward block of the
+    active tokens only, bucketed) against the dense step, with the loss over the active rows:
+    outputs there, the state, the window, the written projections and every gradient agree."""
+    f = golden("column_step")
+    _close = _Report(2e-2, 2e-2, 1e-1) if bf16 else _Report(1e-5, 1e-4, 1e-4)
+    col_r, leaves_r, active, y_r, new_r, written_r = _column_run(f, bf16, rows_first=first, active_loss=True)
+    col_d, leaves_d, _, y_d, new_d, written_d = _column_run(f, bf16, active_loss=True)
+
+    def want(t: torch.Tensor) -> np.ndarray:
+        return t.detach().double().cpu().numpy()
+
+    _close(y_r[active], want(y_d[active]), "y (active rows)")
+    _close(new_r.h[1], want(new_d.h[1]), "state")
+    _close(new_r.key_history[1], want(new_d.key_history[1]), "key history")
+    _close(new_r.kv[1].k, want(new_d.kv[1].k), "cache k")
+    _close(new_r.kv[1].v, want(new_d.kv[1].v), "cache v")
+    for k in ("rec_z", "rec_k", "rec_v", "rec_beta", "attn_k", "attn_v"):
+        _close(getattr(written_r, k), want(getattr(written_d, k)), f"written {k}")
+    for k, t in leaves_r.items():
+        _close(t.grad, want(leaves_d[k].grad), f"grad {k}")
+    for (k, p), (_, q) in zip(col_r.named_parameters(), col_d.named_parameters(), strict=True):
+        _close(p.grad, want(q.grad), f"grad {k}")
     _close.check()
 
 

@@ -15,7 +15,7 @@ import torch
 from conftest import elem_rel, max_rel, rel
 from vesper_b200 import _lib
 from vesper_b200.kernels.compact import compact_flat, expand_rows, gather_rows
-from vesper_b200.kernels.slabs import bucket_end, bucket_ends, slab_ffn
+from vesper_b200.kernels.slabs import bucket_end, bucket_ends, slab_ffn, slab_linears
 
 FIRST = 512
 
@@ -69,6 +69,44 @@ def test_the_compact_block_matches_the_dense_one_at_the_active_rows(dtype: torch
         assert rel(got_np, want_np) < tol
         if dtype == torch.float32:
             assert elem_rel(got_np, want_np) < 1e-4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("frac", [0.0, 0.003, 0.3, 1.0])
+def test_the_compact_norm_and_projections_match_the_dense_ones(dtype: torch.dtype, frac: float) -> None:
+    """``slab_linears`` with the norm (float32 rows, the RMSNorm rounded to ``dtype``, four
+    projections) against the reference's norm and linears at the active rows."""
+    g = torch.Generator(device="cuda").manual_seed(5)
+    b, n, d, heads = 2, 1536, 64, 4
+    x = torch.randn(b, n, d, device="cuda", generator=g) * 3
+    gain = 1 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    ws = [torch.randn(o, d, device="cuda", generator=g) / d**0.5 for o in (d, d, d, heads)]
+    active = torch.rand(b, n, device="cuda", generator=g) < frac
+    ups = [torch.randn(b, n, w.shape[0], device="cuda", generator=g) for w in ws]
+    leaves = [t.detach().requires_grad_() for t in (x, gain, *ws)]
+    rows = compact_flat(active, FIRST)
+    (xc,) = gather_rows(rows, [leaves[0].reshape(1, b * n, d)])
+    outs = slab_linears(xc[0], [w.to(dtype) for w in leaves[2:]], rows.counts, FIRST, norm=(leaves[1], 1e-3, 1e-6))
+    dense = expand_rows(rows, [o.view(1, b * n, -1) for o in outs])
+    loss = sum((y.float().view(b, n, -1) * u).sum() for y, u in zip(dense, ups, strict=True))
+    grads = torch.autograd.grad([loss], leaves)
+
+    ref = [t.detach().double().requires_grad_() for t in (x, gain, *ws)]
+    xr, gr = ref[0], ref[1]
+    xn = xr * torch.rsqrt(xr.square().mean(-1, keepdim=True) + 1e-6) * gr  # vesper/column.py:159-188, exact
+    ref_outs = [torch.where(active[..., None], xn @ w.t(), 0.0) for w in ref[2:]]
+    ref_loss = sum((y * u.double()).sum() for y, u in zip(ref_outs, ups, strict=True))
+    ref_grads = torch.autograd.grad([ref_loss], ref)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    pairs = [(y.view(b, n, -1), r) for y, r in zip(dense, ref_outs, strict=True)]
+    for got, want in [*pairs, *zip(grads, ref_grads, strict=True)]:
+        got_np, want_np = got.detach().double().cpu().numpy(), want.detach().cpu().numpy()
+        if not want_np.any():
+            assert not got_np.any()
+            continue
+        assert max_rel(got_np, want_np) < tol
+        assert rel(got_np, want_np) < tol
 
 
 @pytest.mark.gpu

@@ -65,7 +65,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vb_gather_rows": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "vb_expand_rows": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P, _P]),
     "vb_gather_rows_slabs": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P]),
-    "vb_flatten_compaction": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "vb_flatten_compaction": (_I, [_P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _P]),
     "vb_slab_count": (_I, [_I, _I]),
     "vb_slab_switch": (_I, [_P, _I, _I, _P, _P]),
     "vb_slab_begin": (_I, [_P, _P]),

@@ -170,6 +170,36 @@ class WindowedAttention(nn.Module):
         """
         dims: Dims = {"hkv": self.kv_heads, "dk": self.head_dim, "h": self.heads}
         check_shape("q", q, ("b", "n", "h", "dk"), dims)
+        keys, vals = self._keys_values(q.dtype, k, v, pos, cache, dims)
+        if dims["n"] == 0:
+            return q.new_zeros(dims["b"], 0, self.w_o.shape[0]), cache
+        w = self.window
+        if compaction is None:
+            o = window_attention(q, keys, vals, w)
+        else:
+            (qc,) = gather_rows(compaction, [q])
+            oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
+            (o,) = expand_rows(compaction, [oc])
+        return self.output(o), kv_cache_push(cache, k, v, pos)
+
+    def attend_packed(self, qc: Tensor, k: Tensor, v: Tensor, pos: Tensor, cache: KVCache,
+                      compaction: Compaction) -> tuple[Tensor, KVCache]:  # fmt: skip
+        """``attend`` with the queries of the active tokens only, packed at the front of each batch
+        row as ``compaction`` packs them (``qc [b, n, h, dk]``, padding rows ignored), returning
+        their outputs packed the same way (zero padding) BEFORE the output projection, and the new
+        cache. The loop's compacted passes project those rows themselves."""
+        dims: Dims = {"hkv": self.kv_heads, "dk": self.head_dim, "h": self.heads}
+        check_shape("qc", qc, ("b", "n", "h", "dk"), dims)
+        keys, vals = self._keys_values(qc.dtype, k, v, pos, cache, dims)
+        if dims["n"] == 0:
+            return qc.new_zeros(qc.shape), cache
+        oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, self.window)
+        return oc, kv_cache_push(cache, k, v, pos)
+
+    def _keys_values(self, dtype: torch.dtype, k: Tensor, v: Tensor, pos: Tensor, cache: KVCache,
+                     dims: Dims) -> tuple[Tensor, Tensor]:  # fmt: skip
+        """The checks of the chunk and the cache, and every position's keys and values (cache
+        rows, then the chunk's) in ``dtype``."""
         check_shape("k", k, ("b", "n", "hkv", "dk"), dims)
         check_shape("v", v, ("b", "n", "hkv", "dk"), dims)
         check_shape("pos", pos, ("b", "n"), dims, dtype=torch.long)
@@ -179,26 +209,19 @@ class WindowedAttention(nn.Module):
         if cache.window != self.window:
             msg = f"cache window {cache.window} does not match the layer's {self.window}"
             raise ContractError(msg)
-        n, w = dims["n"], self.window
-        if n == 0:
-            return q.new_zeros(dims["b"], 0, self.w_o.shape[0]), cache
-        if q.device.type != "cuda":
-            msg = f"the windowed attention runs on CUDA only, got {q.device}"
+        if dims["n"] == 0:
+            return k, v
+        if k.device.type != "cuda":
+            msg = f"the windowed attention runs on CUDA only, got {k.device}"
             raise ContractError(msg)
-        if q.dtype not in WINDOW_KERNEL_DTYPES:
-            msg = f"q: dtype must be one of {WINDOW_KERNEL_DTYPES}, got {q.dtype}"
+        if dtype not in WINDOW_KERNEL_DTYPES:
+            msg = f"q: dtype must be one of {WINDOW_KERNEL_DTYPES}, got {dtype}"
             raise ContractError(msg)
         kpos = torch.cat([cache.pos, pos], dim=1)
         require((kpos[:, 1:] - kpos[:, :-1] == 1).all(), "attend: cache and chunk positions must be consecutive")
-        keys = torch.cat([cache.k.to(q.dtype), k.to(q.dtype)], dim=1)
-        vals = torch.cat([cache.v.to(q.dtype), v.to(q.dtype)], dim=1)
-        if compaction is None:
-            o = window_attention(q, keys, vals, w)
-        else:
-            (qc,) = gather_rows(compaction, [q])
-            oc = window_attention_active(qc, compaction.qpos, compaction.counts, keys, vals, w)
-            (o,) = expand_rows(compaction, [oc])
-        return self.output(o), kv_cache_push(cache, k, v, pos)
+        keys = torch.cat([cache.k.to(dtype), k.to(dtype)], dim=1)
+        vals = torch.cat([cache.v.to(dtype), v.to(dtype)], dim=1)
+        return keys, vals
 
     def attend_ring(self, q: Tensor, k: Tensor, v: Tensor, pos: Tensor, ring: RingKVCache) -> tuple[Tensor, RingKVCache]:
         """One decoding token per row over its ring and itself (``vesper/attention.py:298-338``):

@@ -36,7 +36,8 @@ from vesper_b200.kernels.delta_scan import (
 )
 from vesper_b200.kernels.keys import fused_keys
 from vesper_b200.kernels.norm import add_rms_norm, fused_rms_norm
-from vesper_b200.kernels.slabs import slab_ffn
+from vesper_b200.kernels.rotary import inv_freq
+from vesper_b200.kernels.slabs import slab_ffn, slab_linears
 
 ScanImpl = Literal["fused", "fused-fp32"]
 SCAN_IMPLS: tuple[ScanImpl, ...] = ("fused", "fused-fp32")
@@ -374,25 +375,36 @@ class Column(nn.Module):
             check_shape("carry.attn_k", p.attn_k, ("b", "n", "hkv", "dk"), dims)
             check_shape("carry.attn_v", p.attn_v, ("b", "n", "hkv", "dk"), dims)
 
-        q, z, v, beta = self.rec.project_logits(self.norm_rec.forward(x))  # beta: the logits
-        if carry is not None:
-            (z,) = select_rows(carry.active, [z], [carry.projections.rec_z.to(z.dtype)])
-        k, history_next = self.rec.keys(z, history)
-        if carry is not None:
-            p = carry.projections
-            k, v, beta = select_rows(carry.active, [k, v, beta],
-                                     [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
+        if carry is not None and carry.rows is not None:  # norm and projections of the active rows only
+            q, z, v, beta = self._rec_inputs_rows(x, carry)
+            k, history_next = self.rec.keys(z, history)
+            (k,) = select_rows(carry.active, [k], [carry.projections.rec_k.to(k.dtype)])
+        else:
+            q, z, v, beta = self.rec.project_logits(self.norm_rec.forward(x))  # beta: the logits
+            if carry is not None:
+                (z,) = select_rows(carry.active, [z], [carry.projections.rec_z.to(z.dtype)])
+            k, history_next = self.rec.keys(z, history)
+            if carry is not None:
+                p = carry.projections
+                k, v, beta = select_rows(carry.active, [k, v, beta],
+                                         [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
         r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index], from_logits=True)
         x, xn = self.norm_attn.add_forward(x, r)  # x + r and norm_attn of it, one kernel
 
-        aq, ak, av = self.attn.project(xn, pos)
         window = state.kv[pass_index]
-        compaction = None
-        if carry is not None:
-            ak, av = select_rows(carry.active, [ak, av],
-                                 [carry.projections.attn_k.to(ak.dtype), carry.projections.attn_v.to(av.dtype)])  # fmt: skip
+        if carry is not None and carry.rows is not None:  # projections of the active rows only
             compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
-        a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
+            aq, ak, av = self._attn_inputs_rows(xn, pos, carry)  # aq packed per batch row
+            oc, kv_new = self.attn.attend_packed(aq, ak, av, pos, window, compaction)
+            a = self._attn_output_rows(oc, carry)
+        else:
+            aq, ak, av = self.attn.project(xn, pos)
+            compaction = None
+            if carry is not None:
+                ak, av = select_rows(carry.active, [ak, av],
+                                     [carry.projections.attn_k.to(ak.dtype), carry.projections.attn_v.to(av.dtype)])  # fmt: skip
+                compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
+            a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
         x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
 
         keep = carry.active if zero_halted and carry is not None else None
@@ -406,6 +418,61 @@ class Column(nn.Module):
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))
         written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
         return x, ColumnState(h=h, kv=kv, key_history=hist), written
+
+    def _rec_inputs_rows(self, x: Tensor, carry: Carry) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+        """The scan's inputs ``q, z, v`` and the write-strength logits with the halted tokens'
+        carried projections in place (``q`` zero there: the halted outputs are discarded), the
+        norm and the four projections computed for the active rows only (``slab_linears``)."""
+        rows, p = carry.rows, carry.projections
+        assert rows is not None
+        b, n, d = x.shape
+        heads, dk = self.rec.heads, self.rec.head_dim
+        (xc,) = gather_rows(rows, [x.reshape(1, b * n, d)])
+        dtype = RMSNorm._out_dtype(x) or x.dtype  # the autocast dtype, as F.linear would cast
+        weights = [w.to(dtype) for w in (self.rec.w_q, self.rec.w_k, self.rec.w_v, self.rec.w_beta)]
+        qc, zc, vc, bc = slab_linears(xc[0], weights, rows.counts, rows.slab_first,
+                                      norm=(self.norm_rec.weight, RMS_SCALE_FLOOR, RMS_EPS))  # fmt: skip
+        flat = (1, b * n)
+        q, z, v, beta = expand_rows(
+            rows, [qc.view(*flat, d), zc.view(*flat, d), vc.view(*flat, d), bc.view(*flat, heads)],
+            [None, p.rec_z.to(dtype).reshape(*flat, d), p.rec_v.to(dtype).reshape(*flat, d),
+             p.rec_beta.to(dtype).reshape(*flat, heads)],
+        )  # fmt: skip
+        return q.view(b, n, heads, dk), z.view(b, n, d), v.view(b, n, heads, dk), beta.view(b, n, heads)
+
+    def _attn_inputs_rows(self, xn: Tensor, pos: Tensor, carry: Carry) -> tuple[Tensor, Tensor, Tensor]:
+        """The attention's queries of the active tokens packed per batch row (the layout of
+        ``compact_index(carry.active)``) and every token's keys and values with the halted
+        tokens' carried ones in place; the three projections and the rotary turns of the active
+        rows only (``slab_linears`` over the flat compaction, then one relayout of the queries)."""
+        rows, p = carry.rows, carry.projections
+        assert rows is not None and rows.relayout is not None
+        b, n, d = xn.shape
+        heads, kv_heads, dk = self.attn.heads, self.attn.kv_heads, self.attn.head_dim
+        flat = (1, b * n)
+        (xc,) = gather_rows(rows, [xn.reshape(*flat, d)])
+        with torch.no_grad():
+            (pc,) = gather_rows(rows, [pos.reshape(*flat, 1)])  # positions of the compact rows
+        weights = [w.to(xn.dtype) for w in (self.attn.w_q, self.attn.w_k, self.attn.w_v)]
+        turn = (pc.view(-1), inv_freq(dk, self.attn.rotary_base, xn.device), (heads, kv_heads, 0))
+        qc, kc, vc = slab_linears(xc[0], weights, rows.counts, rows.slab_first, rotary=turn)
+        ak, av = expand_rows(rows, [kc.view(*flat, kv_heads * dk), vc.view(*flat, kv_heads * dk)],
+                             [p.attn_k.to(xn.dtype).reshape(*flat, kv_heads * dk),
+                              p.attn_v.to(xn.dtype).reshape(*flat, kv_heads * dk)])  # fmt: skip
+        (aq,) = expand_rows(rows.relayout, [qc.view(*flat, heads * dk)])
+        return aq.view(b, n, heads, dk), ak.view(b, n, kv_heads, dk), av.view(b, n, kv_heads, dk)
+
+    def _attn_output_rows(self, oc: Tensor, carry: Carry) -> Tensor:
+        """The output projection of the active tokens' attention outputs (``oc`` packed per batch
+        row), dense with zero at the halted tokens."""
+        rows = carry.rows
+        assert rows is not None and rows.relayout is not None
+        b, n, heads, dk = oc.shape
+        flat = (1, b * n)
+        (o,) = gather_rows(rows.relayout, [oc.reshape(*flat, heads * dk)])  # per-row packed -> flat
+        (ac,) = slab_linears(o[0], [self.attn.w_o.to(oc.dtype)], rows.counts, rows.slab_first)
+        (a,) = expand_rows(rows, [ac.view(*flat, -1)])
+        return a.view(b, n, -1)
 
     def step_decode(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int) -> Tensor:
         """One decoding token per row through pass ``pass_index``'s state, updated IN PLACE.

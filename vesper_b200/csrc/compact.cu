@@ -111,34 +111,40 @@ __device__ __forceinline__ int slab_end(int c, int first, int NC) {
 }
 
 // As gather_rows_kernel, for compact buffers that bucketed work reads: rows from counts[b] to the
-// end of the bucket are zeroed, the rows past it are left as they are (never read).
+// end of the bucket are zeroed, the rows past it are left as they are (never read). Tensor i is
+// blockIdx.y; the warps stride over the rows that are written only (no per-row index division).
 __global__ void gather_slabs_kernel(const int* __restrict__ idx, const int* __restrict__ counts, RowSets s, int B,
                                     int N, int NC, int first) {
   const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)B * NC;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows * s.n; w += warps) {
-    const int i = (int)(w / rows);
-    const int64_t br = w % rows;
-    const int b = (int)(br / NC), r = (int)(br % NC);
+  const int i = blockIdx.y;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int w0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (int b = 0; b < B; ++b) {
     const int c = counts[b];
-    if (r >= slab_end(c, first, NC)) continue;
-    const int t = r < c ? idx[br] : -1;
-    const bool ok = t >= 0 && t < N;
-    copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, lane);
+    const int end = slab_end(c, first, NC);
+    for (int r = w0; r < end; r += warps) {
+      const int64_t br = (int64_t)b * NC + r;
+      const int t = r < c ? idx[br] : -1;
+      const bool ok = t >= 0 && t < N;
+      copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, lane);
+    }
   }
 }
 
 // One compaction of all B x N tokens from the per-row one: base = the active tokens of the rows
 // before b; flat_idx[base + r] = b N + idx[b][r] (r < counts[b]), flat_rank[b N + t] = base +
-// rank[b][t] (or -1), *flat_count = the total. One CTA per row; the base is a sum over counts.
+// rank[b][t] (or -1), *flat_count = the total. Optionally the map between the flat compact rows and
+// the per-row compact rows (b, r) at b N + r: flat_pb[base + r] = b N + r, pb_flat[b N + r] = base + r
+// (r < counts[b], else -1). One CTA per row; the base is a sum over counts.
 constexpr int FLAT_T = 256;
 __global__ void __launch_bounds__(FLAT_T) flatten_compaction_kernel(const int* __restrict__ idx,
                                                                     const int* __restrict__ rank,
                                                                     const int* __restrict__ counts, int B, int N,
                                                                     int* __restrict__ flat_idx,
                                                                     int* __restrict__ flat_rank,
-                                                                    int* __restrict__ flat_count) {
+                                                                    int* __restrict__ flat_count,
+                                                                    int* __restrict__ flat_pb,
+                                                                    int* __restrict__ pb_flat) {
   __shared__ int part[FLAT_T / 32];
   const int b = blockIdx.x, tid = threadIdx.x;
   int before = 0, all = 0;
@@ -170,6 +176,10 @@ __global__ void __launch_bounds__(FLAT_T) flatten_compaction_kernel(const int* _
   for (int t = tid; t < N; t += FLAT_T) {
     const int k = rank[row + t];
     flat_rank[row + t] = k >= 0 ? base + k : -1;
+  }
+  if (flat_pb != nullptr && pb_flat != nullptr) {
+    for (int r = tid; r < c; r += FLAT_T) flat_pb[base + r] = (int)(row + r);
+    for (int r = tid; r < N; r += FLAT_T) pb_flat[row + r] = r < c ? base + r : -1;
   }
 }
 
@@ -300,20 +310,21 @@ extern "C" int vb_gather_rows_slabs(const int* idx, const int* counts, int B, in
   RowSets s;
   int rc = fill_sets(s, ntensors, src, nullptr, dst, row_bytes, "gather_rows_slabs");
   if (rc) return rc;
-  gather_slabs_kernel<<<grid_for((int64_t)B * NC * ntensors), 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N,
-                                                                                                NC, first);
+  const unsigned blocks = grid_for((int64_t)NC);  // at most 4 CTAs per SM: most return at once
+  const dim3 grid(blocks < 148 * 4 ? blocks : 148 * 4, (unsigned)ntensors);
+  gather_slabs_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N, NC, first);
   VB_LAUNCH_CHECK("gather_rows_slabs");
   return VB_OK;
 }
 
 extern "C" int vb_flatten_compaction(const int* idx, const int* rank, const int* counts, int B, int N, int* flat_idx,
-                                     int* flat_rank, int* flat_count, void* stream) {
+                                     int* flat_rank, int* flat_count, int* flat_pb, int* pb_flat, void* stream) {
   VB_REQUIRE(B >= 0 && N >= 0, "flatten_compaction: bad shape B=%d N=%d", B, N);
   VB_REQUIRE((int64_t)B * N <= 0x7fffffff, "flatten_compaction: %lld tokens exceed int32 indices", (long long)B * N);
   if (B == 0) return VB_OK;
   VB_REQUIRE(idx && rank && counts && flat_idx && flat_rank && flat_count, "flatten_compaction: null pointer");
   flatten_compaction_kernel<<<B, FLAT_T, 0, (cudaStream_t)stream>>>(idx, rank, counts, B, N, flat_idx, flat_rank,
-                                                                    flat_count);
+                                                                    flat_count, flat_pb, pb_flat);
   VB_LAUNCH_CHECK("flatten_compaction");
   return VB_OK;
 }

@@ -35,7 +35,8 @@ class Compaction:
     rank: Tensor
     counts: Tensor
     qpos: Tensor
-    slab_first: int = 0  # > 0: compact buffers feed slab-sized work (``compact_flat``)
+    slab_first: int = 0  # > 0: compact buffers feed bucketed work (``compact_flat``)
+    relayout: Compaction | None = None  # ``compact_flat``: flat compact rows <-> per-row compact rows
 
 
 def compact_index(active: Tensor, qpos_offset: int = 0) -> Compaction:
@@ -61,7 +62,8 @@ def compact_index(active: Tensor, qpos_offset: int = 0) -> Compaction:
 def compact_flat(active: Tensor, slab_first: int) -> Compaction:
     """All ``b x n`` tokens of ``active bool[b, n]`` as ONE compact row: ``idx``, ``rank``
     ``[1, b n]`` over the flattened tokens, ``counts [1]`` the active total (on the device, no
-    synchronisation). Its compact buffers feed work cut into slabs of ``slab_first``, ``slab_first``,
+    synchronisation); ``relayout`` moves rows between this flat compact layout and the per-row
+    one of ``compact_index(active)`` (its rows ``(b, r)`` at ``b n + r``). Its compact buffers feed work cut into slabs of ``slab_first``, ``slab_first``,
     ``2 slab_first``, ... rows (``vesper_b200.kernels.slabs``): a gather zeroes its rows from the
     count to the end of the last running slab and leaves the rest, so copies follow the active
     rows, not the buffer's size."""
@@ -71,13 +73,18 @@ def compact_flat(active: Tensor, slab_first: int) -> Compaction:
     per_row = compact_index(active)
     b, n = per_row.idx.shape
     idx = torch.empty(1, b * n, dtype=torch.int32, device=active.device)
-    rank = torch.empty_like(idx)
+    rank, flat_pb, pb_flat = torch.empty_like(idx), torch.empty_like(idx), torch.empty_like(idx)
     counts = torch.empty(1, dtype=torch.int32, device=active.device)
     _lib.call(
         "vb_flatten_compaction", per_row.idx.data_ptr(), per_row.rank.data_ptr(), per_row.counts.data_ptr(), b, n,
-        idx.data_ptr(), rank.data_ptr(), counts.data_ptr(), _lib.stream(active.device),
+        idx.data_ptr(), rank.data_ptr(), counts.data_ptr(), flat_pb.data_ptr(), pb_flat.data_ptr(),
+        _lib.stream(active.device),
     )  # fmt: skip
-    return Compaction(per_row.active.view(1, b * n), idx, rank, counts, idx, slab_first)
+    flat_active = per_row.active.view(1, b * n)
+    # gather through it: per-row compact rows ([1, b n] = [b, n] packed per row) -> flat compact rows;
+    # expand through it: the inverse (padding rows of each batch row zero)
+    relayout = Compaction(flat_active, flat_pb, pb_flat, counts, flat_pb, slab_first)
+    return Compaction(flat_active, idx, rank, counts, idx, slab_first, relayout)
 
 
 def _row_bytes(t: Tensor, rows: int) -> int:

@@ -136,3 +136,109 @@ def slab_ffn(x: Tensor, w1: Tensor, w2: Tensor, count: Tensor, first: int = SLAB
     ``w2 [d, hidden]`` in ``x``'s dtype. Rows past the bucket of the result are undefined; the
     weights' gradients are zero when no row is active."""
     return _SlabFFN.apply(x.contiguous(), w1.contiguous(), w2.contiguous(), count, first)
+
+
+class _SlabLinears(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, gain: Tensor | None, count: Tensor, first: int, floor: float, eps: float,  # type: ignore[override]
+                pos: Tensor | None, freq: Tensor | None, turns: tuple[int, ...], *weights: Tensor) -> tuple[Tensor, ...]:  # fmt: skip
+        cap, d = x.shape
+        dtype = weights[0].dtype
+        norm = gain is not None
+        xn = x.new_empty(cap, d, dtype=dtype) if norm else x
+        inv = x.new_empty(cap, dtype=torch.float32) if norm else None
+        g32 = gain.to(torch.float32).contiguous() if gain is not None else None
+        outs = [x.new_empty(cap, w.shape[0], dtype=dtype) for w in weights]
+        raws = [x.new_empty(cap, w.shape[0], dtype=dtype) if h else None for w, h in zip(weights, turns, strict=True)]
+
+        def body(e: int) -> None:
+            if norm:
+                _lib.call(
+                    "vb_rms_norm_fwd_cast", x.data_ptr(), g32.data_ptr(), xn.data_ptr(), inv.data_ptr(), e, d,
+                    floor, eps, _lib.DTYPE_CODE[x.dtype], _lib.DTYPE_CODE[dtype], _lib.stream(x.device),
+                )  # fmt: skip
+            for w, o, raw, heads in zip(weights, outs, raws, turns, strict=True):
+                if raw is None:
+                    torch.mm(xn[:e], w.t(), out=o[:e])
+                    continue
+                torch.mm(xn[:e], w.t(), out=raw[:e])
+                _rotate(raw, pos, freq, o, e, heads, backward=False)
+
+        run_slabs(count, cap, body, first)
+        ctx.save_for_backward(x, g32, xn, inv, count, pos, freq, *weights)
+        ctx.first, ctx.norm, ctx.turns = first, norm, turns
+        ctx.gain_dtype = None if gain is None else gain.dtype
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, *douts: Tensor | None):  # type: ignore[override]
+        x, g32, xn, inv, count, pos, freq, *weights = ctx.saved_tensors
+        cap, d = x.shape
+        grads = [None if g is None else g.contiguous().to(xn.dtype) for g in douts]
+        unturned = [torch.empty_like(g) if g is not None and h else None for g, h in zip(grads, ctx.turns, strict=True)]
+        dxn = torch.empty_like(xn)
+        dws = [torch.zeros_like(w) for w in weights]  # what no bucket writes: no active row
+        dx = torch.empty_like(x) if ctx.norm else dxn
+        dg = torch.zeros(d, dtype=torch.float32, device=x.device) if ctx.norm else None
+        ws = _lib.workspace(_lib.query("vb_rms_norm_bwd_workspace", cap, d), x.device) if ctx.norm else None
+
+        def body(e: int) -> None:
+            started = False
+            for w, g, gu, dw, heads in zip(weights, grads, unturned, dws, ctx.turns, strict=True):
+                if g is None:
+                    continue
+                if gu is not None:  # the rotation's transpose first
+                    _rotate(g, pos, freq, gu, e, heads, backward=True)
+                    g = gu
+                if started:
+                    dxn[:e].addmm_(g[:e], w)  # accumulated in the product's epilogue, no separate add
+                else:
+                    torch.mm(g[:e], w, out=dxn[:e])
+                    started = True
+                torch.mm(g[:e].t(), xn[:e], out=dw)
+            if not started:
+                dxn[:e].zero_()
+            if ctx.norm:
+                _lib.call(
+                    "vb_rms_norm_bwd_cast", x.data_ptr(), g32.data_ptr(), dxn.data_ptr(), inv.data_ptr(),
+                    dx.data_ptr(), dg.data_ptr(), ws.data_ptr(), e, d, _lib.DTYPE_CODE[x.dtype],
+                    _lib.DTYPE_CODE[dxn.dtype], _lib.stream(x.device),
+                )  # fmt: skip
+
+        run_slabs(count, cap, body, ctx.first)
+        dgain = None if dg is None else dg.to(ctx.gain_dtype)
+        return (dx, dgain, None, None, None, None, None, None, None, *dws)
+
+
+def _rotate(src: Tensor, pos: Tensor, freq: Tensor, dst: Tensor, rows: int, heads: int, *, backward: bool) -> None:
+    """The rotary turn of rows ``[0, rows)`` of ``src [cap, heads * dk]`` into ``dst``
+    (``vb_rotary``; ``backward``: the transposed turn of a gradient)."""
+    dk = src.shape[1] // heads
+    _lib.call(
+        "vb_rotary", src.data_ptr(), pos.data_ptr(), freq.data_ptr(), dst.data_ptr(), rows, heads, dk, int(backward),
+        _lib.DTYPE_CODE[src.dtype], _lib.stream(src.device),
+    )  # fmt: skip
+
+
+def slab_linears(x: Tensor, weights: list[Tensor], count: Tensor, first: int = SLAB_FIRST,
+                 norm: tuple[Tensor, float, float] | None = None,
+                 rotary: tuple[Tensor, Tensor, tuple[int, ...]] | None = None) -> tuple[Tensor, ...]:  # fmt: skip
+    """``[x_n W^T for W in weights]`` over the first ``count`` rows of the compact buffer
+    ``x [cap, d]`` (bucketed work, the rows up to the bucket's end finite), ``x_n = x`` or, with
+    ``norm = (gain, floor, eps)``, the RMSNorm of a float32 ``x`` rounded to the weights' dtype
+    (``vb_rms_norm_fwd_cast``: the column's norm followed by its projections). ``rotary = (pos
+    int64 [cap], inv_freq float64 [dk/2], heads per output)`` turns each output with a nonzero
+    head count by the rotary embedding at its row's position (``vb_rotary``; 0: not turned). The
+    backward forms ``x_n``'s gradient as one accumulated product chain (no separate adds). Rows
+    past the bucket of the results are undefined; the weights' and gain's gradients are zero when
+    no row is active."""
+    gain, floor, eps = norm if norm is not None else (None, 0.0, 0.0)
+    if norm is None and x.dtype != weights[0].dtype:
+        msg = f"x ({x.dtype}) and the weights ({weights[0].dtype}) must share a dtype without a norm"
+        raise ValueError(msg)
+    pos, freq, turns = rotary if rotary is not None else (None, None, (0,) * len(weights))
+    if len(turns) != len(weights):
+        msg = f"rotary: {len(turns)} head counts for {len(weights)} weights"
+        raise ValueError(msg)
+    return _SlabLinears.apply(x.contiguous(), gain, count, first, floor, eps, pos, freq, tuple(turns),
+                              *[w.contiguous() for w in weights])  # fmt: skip
