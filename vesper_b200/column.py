@@ -37,7 +37,7 @@ from vesper_b200.kernels.delta_scan import (
 from vesper_b200.kernels.keys import fused_keys
 from vesper_b200.kernels.norm import add_rms_norm, fused_rms_norm
 from vesper_b200.kernels.rotary import inv_freq
-from vesper_b200.kernels.slabs import slab_ffn, slab_linears
+from vesper_b200.kernels.slabs import slab_ffn, slab_linears, slab_residual_norm
 
 ScanImpl = Literal["fused", "fused-fp32"]
 SCAN_IMPLS: tuple[ScanImpl, ...] = ("fused", "fused-fp32")
@@ -266,12 +266,18 @@ class RecurrentSublayer(nn.Module):
              from_logits: bool = False) -> tuple[Tensor, Tensor]:  # fmt: skip
         """The scan (``scan_impl``) with autocast off, then ``W_o`` in the activation dtype;
         ``from_logits``: ``beta`` holds the write-strength logits (the kernels form the sigmoid)."""
+        o, new_state = self.scan_outputs(q, k, v, beta, state, from_logits=from_logits)
+        return F.linear(o.flatten(2), self.w_o), new_state
+
+    def scan_outputs(self, q: Tensor, k: Tensor, v: Tensor, beta: Tensor, state: Tensor, *,
+                     from_logits: bool = False) -> tuple[Tensor, Tensor]:  # fmt: skip
+        """The scan's outputs ``o [b,n,h,dk]`` in ``q``'s dtype (before ``W_o``) and new state."""
         kernel = delta_scan_fused if self.scan_impl == "fused" else delta_scan_fused_fp32
         dtype = FUSED_INPUT_DTYPES[self.scan_impl]
         with torch.autocast(device_type=q.device.type, enabled=False):
             o, new_state = kernel(q.to(dtype), k.to(dtype), v.to(dtype), beta.to(dtype), state.to(STATE_DTYPE),
                                   from_logits=from_logits)  # fmt: skip
-        return F.linear(o.to(q.dtype).flatten(2), self.w_o), new_state
+        return o.to(q.dtype), new_state
 
     def forward(self, x: Tensor, state: Tensor, history: Tensor) -> tuple[Tensor, Tensor, Tensor]:
         q, z, v, logits = self.project_logits(x)
@@ -295,17 +301,6 @@ class FFN(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         return F.linear(relu_square(F.linear(x, self.w1)), self.w2)
-
-    def forward_rows(self, x: Tensor, rows: Compaction) -> Tensor:
-        """``forward(x)`` at the active tokens of ``rows`` (a ``compact_flat`` compaction of
-        ``x [b, n, d]``'s tokens) and zero at the others: the active rows are gathered, the block
-        runs as slab-sized work over their live count (``slab_ffn``), the result is expanded."""
-        b, n, d = x.shape
-        (xc,) = gather_rows(rows, [x.reshape(1, b * n, d)])
-        w1, w2 = self.w1.to(xc.dtype), self.w2.to(xc.dtype)  # the casts autocast's linear makes
-        yc = slab_ffn(xc[0], w1, w2, rows.counts, rows.slab_first)
-        (y,) = expand_rows(rows, [yc.view(1, b * n, -1)])
-        return y.view(b, n, -1)
 
 
 def set_scan(model: nn.Module, impl: str) -> int:
@@ -375,10 +370,10 @@ class Column(nn.Module):
             check_shape("carry.attn_k", p.attn_k, ("b", "n", "hkv", "dk"), dims)
             check_shape("carry.attn_v", p.attn_v, ("b", "n", "hkv", "dk"), dims)
 
-        if carry is not None and carry.rows is not None:  # norm and projections of the active rows only
-            q, z, v, beta = self._rec_inputs_rows(x, carry)
-            k, history_next = self.rec.keys(z, history)
-            (k,) = select_rows(carry.active, [k], [carry.projections.rec_k.to(k.dtype)])
+        window = state.kv[pass_index]
+        if carry is not None and carry.rows is not None:  # every per-token step on the active rows only
+            x, h_new, history_next, kv_new, written = self._step_rows(x, pos, state.h[pass_index], history,
+                                                                      window, carry)  # fmt: skip
         else:
             q, z, v, beta = self.rec.project_logits(self.norm_rec.forward(x))  # beta: the logits
             if carry is not None:
@@ -388,16 +383,9 @@ class Column(nn.Module):
                 p = carry.projections
                 k, v, beta = select_rows(carry.active, [k, v, beta],
                                          [p.rec_k.to(k.dtype), p.rec_v.to(v.dtype), p.rec_beta.to(beta.dtype)])  # fmt: skip
-        r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index], from_logits=True)
-        x, xn = self.norm_attn.add_forward(x, r)  # x + r and norm_attn of it, one kernel
+            r, h_new = self.rec.scan(q, k, v, beta, state.h[pass_index], from_logits=True)
+            x, xn = self.norm_attn.add_forward(x, r)  # x + r and norm_attn of it, one kernel
 
-        window = state.kv[pass_index]
-        if carry is not None and carry.rows is not None:  # projections of the active rows only
-            compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
-            aq, ak, av = self._attn_inputs_rows(xn, pos, carry)  # aq packed per batch row
-            oc, kv_new = self.attn.attend_packed(aq, ak, av, pos, window, compaction)
-            a = self._attn_output_rows(oc, carry)
-        else:
             aq, ak, av = self.attn.project(xn, pos)
             compaction = None
             if carry is not None:
@@ -405,74 +393,69 @@ class Column(nn.Module):
                                      [carry.projections.attn_k.to(ak.dtype), carry.projections.attn_v.to(av.dtype)])  # fmt: skip
                 compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
             a, kv_new = self.attn.attend(aq, ak, av, pos, window, compaction)
-        x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
-
-        keep = carry.active if zero_halted and carry is not None else None
-        if carry is not None and carry.rows is not None:  # the active rows only, zero at the others
-            f = self.ffn.forward_rows(xn, carry.rows)
-        else:
-            f = self.ffn.forward(xn)
-        x = residual_add(x, f, keep)  # the halted rows zeroed here when asked
+            x, xn = self.norm_ffn.add_forward(x, a)  # x + a and norm_ffn of it, one kernel
+            keep = carry.active if zero_halted and carry is not None else None
+            x = residual_add(x, self.ffn.forward(xn), keep)  # the halted rows zeroed here when asked
+            written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
         h = tuple(h_new if i == pass_index else s for i, s in enumerate(state.h))
         kv = tuple(kv_new if i == pass_index else c for i, c in enumerate(state.kv))
         hist = tuple(history_next if i == pass_index else o for i, o in enumerate(state.key_history))
-        written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
         return x, ColumnState(h=h, kv=kv, key_history=hist), written
 
-    def _rec_inputs_rows(self, x: Tensor, carry: Carry) -> tuple[Tensor, Tensor, Tensor, Tensor]:
-        """The scan's inputs ``q, z, v`` and the write-strength logits with the halted tokens'
-        carried projections in place (``q`` zero there: the halted outputs are discarded), the
-        norm and the four projections computed for the active rows only (``slab_linears``)."""
-        rows, p = carry.rows, carry.projections
-        assert rows is not None
-        b, n, d = x.shape
-        heads, dk = self.rec.heads, self.rec.head_dim
-        (xc,) = gather_rows(rows, [x.reshape(1, b * n, d)])
-        dtype = RMSNorm._out_dtype(x) or x.dtype  # the autocast dtype, as F.linear would cast
-        weights = [w.to(dtype) for w in (self.rec.w_q, self.rec.w_k, self.rec.w_v, self.rec.w_beta)]
-        qc, zc, vc, bc = slab_linears(xc[0], weights, rows.counts, rows.slab_first,
-                                      norm=(self.norm_rec.weight, RMS_SCALE_FLOOR, RMS_EPS))  # fmt: skip
-        flat = (1, b * n)
-        q, z, v, beta = expand_rows(
-            rows, [qc.view(*flat, d), zc.view(*flat, d), vc.view(*flat, d), bc.view(*flat, heads)],
-            [None, p.rec_z.to(dtype).reshape(*flat, d), p.rec_v.to(dtype).reshape(*flat, d),
-             p.rec_beta.to(dtype).reshape(*flat, heads)],
-        )  # fmt: skip
-        return q.view(b, n, heads, dk), z.view(b, n, d), v.view(b, n, heads, dk), beta.view(b, n, heads)
-
-    def _attn_inputs_rows(self, xn: Tensor, pos: Tensor, carry: Carry) -> tuple[Tensor, Tensor, Tensor]:
-        """The attention's queries of the active tokens packed per batch row (the layout of
-        ``compact_index(carry.active)``) and every token's keys and values with the halted
-        tokens' carried ones in place; the three projections and the rotary turns of the active
-        rows only (``slab_linears`` over the flat compaction, then one relayout of the queries)."""
+    def _step_rows(self, x: Tensor, pos: Tensor, h: Tensor, history: Tensor, window: KVCache,
+                   carry: Carry) -> tuple[Tensor, Tensor, Tensor, KVCache, Projections]:  # fmt: skip
+        """``step`` with a carry whose ``rows`` compact the active tokens: every per-token step runs
+        on those rows only (bucketed on their live count, ``vesper_b200.kernels.slabs``), the
+        residual stream stays compact from the input to the output, and only the key filter, the
+        scan and the attention's keys and values see every token (the halted ones' carried
+        projections in place). The output is zero at the halted tokens, as the loop leaves them.
+        Returns the output, the new state, key history and window, and the written projections."""
         rows, p = carry.rows, carry.projections
         assert rows is not None and rows.relayout is not None
-        b, n, d = xn.shape
+        b, n, d = x.shape
         heads, kv_heads, dk = self.attn.heads, self.attn.kv_heads, self.attn.head_dim
-        flat = (1, b * n)
-        (xc,) = gather_rows(rows, [xn.reshape(*flat, d)])
+        flat, first, count = (1, b * n), rows.slab_first, rows.counts
+        dtype = RMSNorm._out_dtype(x) or x.dtype  # the autocast dtype, as F.linear would cast
+
+        (xc,) = gather_rows(rows, [x.reshape(*flat, d)])  # the active rows of the residual stream
+        weights = [w.to(dtype) for w in (self.rec.w_q, self.rec.w_k, self.rec.w_v, self.rec.w_beta)]
+        qc, zc, vc, bc = slab_linears(xc[0], weights, count, first,
+                                      norm=(self.norm_rec.weight, RMS_SCALE_FLOOR, RMS_EPS))  # fmt: skip
+        q, z, v, beta = expand_rows(
+            rows, [qc.view(*flat, d), zc.view(*flat, d), vc.view(*flat, d), bc.view(*flat, self.rec.heads)],
+            [None, p.rec_z.to(dtype).reshape(*flat, d), p.rec_v.to(dtype).reshape(*flat, d),
+             p.rec_beta.to(dtype).reshape(*flat, self.rec.heads)],
+        )  # fmt: skip
+        q, z = q.view(b, n, self.rec.heads, self.rec.head_dim), z.view(b, n, d)
+        v, beta = v.view(b, n, self.rec.heads, self.rec.head_dim), beta.view(b, n, self.rec.heads)
+        k, history_next = self.rec.keys(z, history)
+        (k,) = select_rows(carry.active, [k], [p.rec_k.to(k.dtype)])
+        o, h_new = self.rec.scan_outputs(q, k, v, beta, h, from_logits=True)
+
+        (oc,) = gather_rows(rows, [o.reshape(*flat, d)])
+        sc, xnc = slab_residual_norm(xc[0], oc[0], self.rec.w_o.to(dtype), self.norm_attn.weight, count, first,
+                                     RMS_SCALE_FLOOR, RMS_EPS)  # fmt: skip
+
         with torch.no_grad():
             (pc,) = gather_rows(rows, [pos.reshape(*flat, 1)])  # positions of the compact rows
-        weights = [w.to(xn.dtype) for w in (self.attn.w_q, self.attn.w_k, self.attn.w_v)]
-        turn = (pc.view(-1), inv_freq(dk, self.attn.rotary_base, xn.device), (heads, kv_heads, 0))
-        qc, kc, vc = slab_linears(xc[0], weights, rows.counts, rows.slab_first, rotary=turn)
-        ak, av = expand_rows(rows, [kc.view(*flat, kv_heads * dk), vc.view(*flat, kv_heads * dk)],
-                             [p.attn_k.to(xn.dtype).reshape(*flat, kv_heads * dk),
-                              p.attn_v.to(xn.dtype).reshape(*flat, kv_heads * dk)])  # fmt: skip
-        (aq,) = expand_rows(rows.relayout, [qc.view(*flat, heads * dk)])
-        return aq.view(b, n, heads, dk), ak.view(b, n, kv_heads, dk), av.view(b, n, kv_heads, dk)
+        weights = [w.to(dtype) for w in (self.attn.w_q, self.attn.w_k, self.attn.w_v)]
+        turn = (pc.view(-1), inv_freq(dk, self.attn.rotary_base, x.device), (heads, kv_heads, 0))
+        aqc, akc, avc = slab_linears(xnc, weights, count, first, rotary=turn)
+        ak, av = expand_rows(rows, [akc.view(*flat, kv_heads * dk), avc.view(*flat, kv_heads * dk)],
+                             [p.attn_k.to(dtype).reshape(*flat, kv_heads * dk),
+                              p.attn_v.to(dtype).reshape(*flat, kv_heads * dk)])  # fmt: skip
+        ak, av = ak.view(b, n, kv_heads, dk), av.view(b, n, kv_heads, dk)
+        (aq,) = expand_rows(rows.relayout, [aqc.view(*flat, heads * dk)])  # packed per batch row
+        compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
+        oa, kv_new = self.attn.attend_packed(aq.view(b, n, heads, dk), ak, av, pos, window, compaction)
+        (oac,) = gather_rows(rows.relayout, [oa.reshape(*flat, heads * dk)])  # per-row packed -> flat
+        sc, xnc = slab_residual_norm(sc, oac[0], self.attn.w_o.to(dtype), self.norm_ffn.weight, count, first,
+                                     RMS_SCALE_FLOOR, RMS_EPS)  # fmt: skip
 
-    def _attn_output_rows(self, oc: Tensor, carry: Carry) -> Tensor:
-        """The output projection of the active tokens' attention outputs (``oc`` packed per batch
-        row), dense with zero at the halted tokens."""
-        rows = carry.rows
-        assert rows is not None and rows.relayout is not None
-        b, n, heads, dk = oc.shape
-        flat = (1, b * n)
-        (o,) = gather_rows(rows.relayout, [oc.reshape(*flat, heads * dk)])  # per-row packed -> flat
-        (ac,) = slab_linears(o[0], [self.attn.w_o.to(oc.dtype)], rows.counts, rows.slab_first)
-        (a,) = expand_rows(rows, [ac.view(*flat, -1)])
-        return a.view(b, n, -1)
+        outc = slab_ffn(xnc, self.ffn.w1.to(dtype), self.ffn.w2.to(dtype), count, first, residual=sc)
+        (out,) = expand_rows(rows, [outc.view(*flat, d)])  # zero at the halted tokens
+        written = Projections(rec_z=z, rec_k=k, rec_v=v, rec_beta=beta, attn_k=ak, attn_v=av)
+        return out.view(b, n, d), h_new, history_next, kv_new, written
 
     def step_decode(self, x: Tensor, pos: Tensor, state: ColumnState, pass_index: int) -> Tensor:
         """One decoding token per row through pass ``pass_index``'s state, updated IN PLACE.

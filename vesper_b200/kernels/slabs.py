@@ -91,33 +91,42 @@ def run_slabs(count: Tensor, cap: int, body: Callable[[int], None], first: int =
 
 class _SlabFFN(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x: Tensor, w1: Tensor, w2: Tensor, count: Tensor, first: int) -> Tensor:  # type: ignore[override]
+    def forward(ctx, x: Tensor, w1: Tensor, w2: Tensor, count: Tensor, first: int,  # type: ignore[override]
+                base: Tensor | None) -> Tensor:  # fmt: skip
         cap, hidden = x.shape[0], w1.shape[0]
         h = x.new_empty(cap, hidden)
         g = x.new_empty(cap, hidden)
         y = x.new_empty(cap, w2.shape[0])
+        out = torch.empty_like(base) if base is not None else y
         code = _lib.DTYPE_CODE[x.dtype]
 
         def body(e: int) -> None:
             torch.mm(x[:e], w1.t(), out=h[:e])
             _lib.call("vb_relu_square_fwd", h.data_ptr(), g.data_ptr(), e * hidden, code, _lib.stream(x.device))
             torch.mm(g[:e], w2.t(), out=y[:e])
+            if base is not None:  # the residual: base + y in float32, one rounding-free add
+                _lib.call("vb_residual_add", base.data_ptr(), y.data_ptr(), None, out.data_ptr(), e, base.shape[1],
+                          code, _lib.stream(x.device))  # fmt: skip
 
         run_slabs(count, cap, body, first)
         ctx.save_for_backward(x, w1, w2, h, g, count)
-        ctx.first = first
-        return y
+        ctx.first, ctx.residual = first, base is not None
+        return out
 
     @staticmethod
-    def backward(ctx, dy: Tensor):  # type: ignore[override]
+    def backward(ctx, dout: Tensor):  # type: ignore[override]
         x, w1, w2, h, g, count = ctx.saved_tensors
-        dy = dy.contiguous().to(x.dtype)
+        dout = dout.contiguous()
         cap, hidden = x.shape[0], w1.shape[0]
+        dy = torch.empty(cap, w2.shape[0], dtype=x.dtype, device=x.device) if ctx.residual else dout.to(x.dtype)
         dg, dh, dx = torch.empty_like(g), torch.empty_like(h), torch.empty_like(x)
         dw1, dw2 = torch.zeros_like(w1), torch.zeros_like(w2)  # what no bucket writes: no active row
         code = _lib.DTYPE_CODE[x.dtype]
 
         def body(e: int) -> None:
+            if ctx.residual:  # y's gradient: the output's, rounded to y's dtype
+                _lib.call("vb_residual_add_bwd", dout.data_ptr(), None, None, dy.data_ptr(), e, dout.shape[1], code,
+                          _lib.stream(x.device))  # fmt: skip
             torch.mm(dy[:e], w2, out=dg[:e])
             torch.mm(dy[:e].t(), g[:e], out=dw2)
             _lib.call("vb_relu_square_bwd", h.data_ptr(), dg.data_ptr(), dh.data_ptr(), e * hidden, code,
@@ -126,16 +135,80 @@ class _SlabFFN(torch.autograd.Function):
             torch.mm(dh[:e], w1, out=dx[:e])
 
         run_slabs(count, cap, body, ctx.first)
-        return dx, dw1, dw2, None, None
+        return dx, dw1, dw2, None, None, (dout if ctx.residual else None)
 
 
-def slab_ffn(x: Tensor, w1: Tensor, w2: Tensor, count: Tensor, first: int = SLAB_FIRST) -> Tensor:
+def slab_ffn(x: Tensor, w1: Tensor, w2: Tensor, count: Tensor, first: int = SLAB_FIRST,
+             residual: Tensor | None = None) -> Tensor:  # fmt: skip
     """``W_2 relu(W_1 x)^2`` over the first ``count`` rows of the compact buffer ``x [cap, d]``
     (bucketed work; the rows from the count to the end of its bucket must be finite, as
     ``gather_rows`` over a ``compact_flat`` compaction leaves them). ``w1 [hidden, d]``,
-    ``w2 [d, hidden]`` in ``x``'s dtype. Rows past the bucket of the result are undefined; the
-    weights' gradients are zero when no row is active."""
-    return _SlabFFN.apply(x.contiguous(), w1.contiguous(), w2.contiguous(), count, first)
+    ``w2 [d, hidden]`` in ``x``'s dtype. With ``residual`` (float32 ``[cap, d]``) the result is
+    ``residual + W_2 relu(W_1 x)^2`` in float32 (the column's last residual add). Rows past the
+    bucket of the result are undefined; the weights' gradients are zero when no row is active."""
+    base = None if residual is None else residual.contiguous()
+    return _SlabFFN.apply(x.contiguous(), w1.contiguous(), w2.contiguous(), count, first, base)
+
+
+class _SlabResidualNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, o: Tensor, gain: Tensor, count: Tensor, first: int, floor: float, eps: float,  # type: ignore[override]
+                w: Tensor) -> tuple[Tensor, Tensor]:  # fmt: skip
+        cap, d = x.shape
+        r = o.new_empty(cap, d, dtype=w.dtype)
+        s = torch.empty_like(x)
+        y = x.new_empty(cap, d, dtype=w.dtype)
+        inv = x.new_empty(cap, dtype=torch.float32)
+        g32 = gain.to(torch.float32).contiguous()
+
+        def body(e: int) -> None:
+            torch.mm(o[:e], w.t(), out=r[:e])
+            _lib.call(
+                "vb_add_rms_norm_fwd", x.data_ptr(), r.data_ptr(), g32.data_ptr(), s.data_ptr(), y.data_ptr(),
+                inv.data_ptr(), e, d, floor, eps, _lib.DTYPE_CODE[r.dtype], _lib.DTYPE_CODE[y.dtype],
+                _lib.stream(x.device),
+            )  # fmt: skip
+
+        run_slabs(count, cap, body, first)
+        ctx.save_for_backward(o, w, s, g32, inv, count)
+        ctx.first, ctx.gain_dtype = first, gain.dtype
+        return s, y
+
+    @staticmethod
+    def backward(ctx, ds: Tensor | None, dy: Tensor | None):  # type: ignore[override]
+        o, w, s, g32, inv, count = ctx.saved_tensors
+        cap, d = s.shape
+        dy = torch.zeros(cap, d, dtype=w.dtype, device=s.device) if dy is None else dy.contiguous().to(w.dtype)
+        ds = None if ds is None else ds.contiguous().to(torch.float32)
+        dx = torch.empty_like(s)
+        dr = torch.empty(cap, d, dtype=w.dtype, device=s.device)
+        do = torch.empty_like(o)
+        dw = torch.zeros_like(w)  # what no bucket writes: no active row
+        dg = torch.zeros(d, dtype=torch.float32, device=s.device)
+        ws = _lib.workspace(_lib.query("vb_rms_norm_bwd_workspace", cap, d), s.device)
+
+        def body(e: int) -> None:
+            _lib.call(
+                "vb_add_rms_norm_bwd", s.data_ptr(), g32.data_ptr(), dy.data_ptr(), inv.data_ptr(), _lib.ptr(ds),
+                dx.data_ptr(), dr.data_ptr(), dg.data_ptr(), ws.data_ptr(), e, d, _lib.DTYPE_CODE[dy.dtype],
+                _lib.DTYPE_CODE[dr.dtype], _lib.stream(s.device),
+            )  # fmt: skip
+            torch.mm(dr[:e], w, out=do[:e])
+            torch.mm(dr[:e].t(), o[:e], out=dw)
+
+        run_slabs(count, cap, body, ctx.first)
+        return dx, do, dg.to(ctx.gain_dtype), None, None, None, None, dw
+
+
+def slab_residual_norm(x: Tensor, o: Tensor, w: Tensor, gain: Tensor, count: Tensor, first: int = SLAB_FIRST,
+                       floor: float = 1e-3, eps: float = 1e-6) -> tuple[Tensor, Tensor]:  # fmt: skip
+    """``(s, y)`` over the first ``count`` rows of compact buffers: the residual add
+    ``s = x + o W^T`` (float32 ``x``; the product in ``w``'s dtype, added as one float32 addition)
+    and the RMSNorm of the sum rounded to ``w``'s dtype (``vb_add_rms_norm_fwd``: a sublayer's
+    output projection, its residual add and the next sublayer's norm). Width a multiple of 4 up to
+    1024. Rows past the bucket are undefined; ``w``'s and the gain's gradients are zero when no
+    row is active."""
+    return _SlabResidualNorm.apply(x.contiguous(), o.contiguous(), gain, count, first, floor, eps, w.contiguous())
 
 
 class _SlabLinears(torch.autograd.Function):
