@@ -890,8 +890,9 @@ def profile_column(args) -> None:
 
 def breakdown(args) -> None:
     """Device time per kernel of one leg under torch's profiler (CUPTI activity, no ncu):
-    ``step`` one config-2 step, ``train`` one config-4 training step (eager), ``decode`` one
-    config-5 decode step (a graph replay) after a 1024-token prefill. Prints a table by kernel
+    ``step`` one config-2 step, ``train`` one config-4 training step (a replay of the captured
+    step, as the bench times it), ``decode`` one config-5 decode step (a graph replay) after a
+    1024-token prefill. Prints a table by kernel
     group and the top kernels. Times under the profiler are not bench values."""
     import collections
 
@@ -915,11 +916,12 @@ def breakdown(args) -> None:
         cfg = VESPER_S
         model = Vesper(cfg.shape, cfg.vocab, cfg.columns, cfg.t_max, cfg.halt_epsilon,
                        torch.Generator().manual_seed(0)).to(device)  # fmt: skip
-        trainer = TrainStep(model, cfg, b=TRAIN_B, n=TRAIN_T, warm=10**6)  # eager: kernel names
+        model.loop.compact_rows = not args.no_compact
+        trainer = TrainStep(model, cfg, b=TRAIN_B, n=TRAIN_T, warm=3)  # captured after 3 eager steps
         g = torch.Generator(device=device).manual_seed(99)
         batch = torch.randint(0, cfg.vocab, (TRAIN_B, TRAIN_T + 1), device=device, generator=g)
         trainer.load(batch[:, :-1], batch[:, 1:])
-        for _ in range(3):
+        for _ in range(5):  # three eager steps, the capture, one replay
             trainer.run()
 
         def run() -> None:
@@ -981,6 +983,8 @@ def main() -> None:
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")
     p.add_argument("--profile-column", action="store_true",
                    help="warm up, run one eager config-3 column fwd+bwd of --batch rows, exit (for ncu)")
+    p.add_argument("--no-compact", action="store_true",
+                   help="--breakdown train: every pass dense (the loop's compact_rows off), for comparison")
     p.add_argument("--breakdown", choices=("step", "train", "decode"), default=None,
                    help="print one leg's device time per kernel group under torch's profiler, then exit")
     p.add_argument("--steps-ref", type=int, default=0, help="reference samples (default: min(steps, 10))")
