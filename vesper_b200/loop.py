@@ -8,12 +8,14 @@ projections of its exit pass are copied forward into every later pass's states (
 
 The arithmetic of the decision, the output weights and the counts is the reference's, operation
 for operation, in torch (so pass counts agree to the bit on the same inputs); what changes is the
-per-token bookkeeping around it: the copy-forward merge of all six carried projections, the
-zeroing of halted rows and the selection of the next input are each one multi-tensor select
-launch (``vb_select_rows``) instead of a ``torch.where`` per tensor, and the columns compute the
-attention queries of active tokens only. With ``compact_rows`` (the default) every pass after the
-first compacts the active tokens once (``compact_flat``) and the columns run their feed-forward
-blocks on those rows only, as slab-sized work that follows the live count on the device
+per-token bookkeeping around it. The reference's copy-forward merge (``vesper/loop.py:523-537``:
+tokens halting now take their fresh projections, every other token keeps the previous ones) is
+the column's written projections themselves: a column with a carry writes a halted token's
+carried projections, so the merge changes only tokens still active, whose carried values no later
+pass reads. The zeroing of halted rows and the selection of the next input are each one
+multi-tensor select launch (``vb_select_rows``). With ``compact_rows`` (the default) every pass
+after the first compacts the active tokens once (``compact_flat``) and the columns run every
+per-token step on those rows only, as bucketed work that follows the live count on the device
 (``vesper_b200.kernels.slabs``): the reference computes them densely and discards the halted
 rows' outputs (``vesper/loop.py:24-26``).
 """
@@ -177,17 +179,6 @@ class LoopResult:
     per_pass: Tensor
 
 
-def _proj_list(p: Projections) -> list[Tensor]:
-    return [p.rec_z, p.rec_k, p.rec_v, p.rec_beta, p.attn_k, p.attn_v]
-
-
-def _merge(halts: Tensor, fresh: Projections, previous: Projections) -> Projections:
-    """Tokens halting now freeze their fresh projections, the others keep the previous ones:
-    ``vesper/loop.py:523-537`` as one launch over the six tensors."""
-    prev = [q.to(f.dtype) for f, q in zip(_proj_list(fresh), _proj_list(previous), strict=True)]
-    return Projections(*select_rows(halts, _proj_list(fresh), prev))
-
-
 class Loop(nn.Module):
     """``T_max`` passes of ``C`` columns with halting and copy-forward (``vesper/loop.py:300-465``)."""
 
@@ -272,9 +263,8 @@ class Loop(nn.Module):
             n_iters = n_iters + active.to(torch.int32)
             per_pass.append(h)
             if not dense:
-                for c, written in enumerate(fresh):
-                    previous = carried[c]
-                    carried[c] = written if previous is None else _merge(halts, written, previous)
+                # the copy-forward merge: a halted token's written projections are its carried ones
+                carried[:] = fresh
                 (x,) = select_rows(active, [h], [x])
             else:
                 x = h
