@@ -417,9 +417,12 @@ class Column(nn.Module):
         flat, first, count = (1, b * n), rows.slab_first, rows.counts
         dtype = RMSNorm._out_dtype(x) or x.dtype  # the autocast dtype, as F.linear would cast
 
-        (xc,) = gather_rows(rows, [x.reshape(*flat, d)])  # the active rows of the residual stream
+        # the active rows of the residual stream; compact buffers are used as views [cap, width]
+        # (a view's backward is a view; indexing's would zero-fill and copy the whole buffer)
+        (xc,) = gather_rows(rows, [x.reshape(*flat, d)])
+        xc = xc.view(b * n, d)
         weights = [w.to(dtype) for w in (self.rec.w_q, self.rec.w_k, self.rec.w_v, self.rec.w_beta)]
-        qc, zc, vc, bc = slab_linears(xc[0], weights, count, first,
+        qc, zc, vc, bc = slab_linears(xc, weights, count, first,
                                       norm=(self.norm_rec.weight, RMS_SCALE_FLOOR, RMS_EPS))  # fmt: skip
         q, z, v, beta = expand_rows(
             rows, [qc.view(*flat, d), zc.view(*flat, d), vc.view(*flat, d), bc.view(*flat, self.rec.heads)],
@@ -433,7 +436,7 @@ class Column(nn.Module):
         o, h_new = self.rec.scan_outputs(q, k, v, beta, h, from_logits=True)
 
         (oc,) = gather_rows(rows, [o.reshape(*flat, d)])
-        sc, xnc = slab_residual_norm(xc[0], oc[0], self.rec.w_o.to(dtype), self.norm_attn.weight, count, first,
+        sc, xnc = slab_residual_norm(xc, oc.view(b * n, d), self.rec.w_o.to(dtype), self.norm_attn.weight, count, first,
                                      RMS_SCALE_FLOOR, RMS_EPS)  # fmt: skip
 
         with torch.no_grad():
@@ -449,8 +452,8 @@ class Column(nn.Module):
         compaction = compact_index(carry.active, qpos_offset=window.k.shape[1])
         oa, kv_new = self.attn.attend_packed(aq.view(b, n, heads, dk), ak, av, pos, window, compaction)
         (oac,) = gather_rows(rows.relayout, [oa.reshape(*flat, heads * dk)])  # per-row packed -> flat
-        sc, xnc = slab_residual_norm(sc, oac[0], self.attn.w_o.to(dtype), self.norm_ffn.weight, count, first,
-                                     RMS_SCALE_FLOOR, RMS_EPS)  # fmt: skip
+        sc, xnc = slab_residual_norm(sc, oac.view(b * n, heads * dk), self.attn.w_o.to(dtype), self.norm_ffn.weight,
+                                     count, first, RMS_SCALE_FLOOR, RMS_EPS)  # fmt: skip
 
         outc = slab_ffn(xnc, self.ffn.w1.to(dtype), self.ffn.w2.to(dtype), count, first, residual=sc)
         (out,) = expand_rows(rows, [outc.view(*flat, d)])  # zero at the halted tokens
