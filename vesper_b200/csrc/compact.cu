@@ -25,9 +25,23 @@ struct RowSets {
   const uint8_t* b[MAXT];  // second source (carried / fallback) or null = zeros
   uint8_t* out[MAXT];
   int64_t row_bytes[MAXT];
-  int vec[MAXT];  // copy unit in bytes: 16, 4 or 1 (every pointer and row_bytes a multiple)
+  int vec[MAXT];    // copy unit in bytes: 16, 4 or 1 (every pointer and row_bytes a multiple)
+  int lshift[MAXT];  // log2 of the lanes that copy one row: enough for its units, at most 32
   int n;
 };
+
+// Tensor i of a launch is blockIdx.y; its rows go to teams of 2^lshift lanes (a row of 16 bytes
+// takes one lane, a row of 512 bytes or more a warp), the teams striding over the rows.
+struct Team {
+  int64_t first, stride;  // this team's first row, the number of teams
+  int lane, size;         // lane within the team, lanes per team
+};
+
+__device__ __forceinline__ Team team_of(const RowSets& s, int i) {
+  const int sh = s.lshift[i];
+  const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> sh;
+  return Team{t, ((int64_t)gridDim.x * blockDim.x) >> sh, (int)(threadIdx.x & ((1u << sh) - 1u)), 1 << sh};
+}
 
 template <int U>
 __device__ __forceinline__ void copy_unit(uint8_t* dst, const uint8_t* src, int64_t off) {
@@ -40,64 +54,58 @@ __device__ __forceinline__ void copy_unit(uint8_t* dst, const uint8_t* src, int6
   }
 }
 
-// Copies row `row_out` of tensor i from `src_row` of `src` (null = zeros); one warp per row and
-// tensor, lanes striding the row in copy units.
+// Copies row `row_out` of tensor i from `src_row` of `src` (null = zeros); the team's lanes stride
+// the row in copy units.
 __device__ __forceinline__ void copy_row(const RowSets& s, int i, const uint8_t* src, int64_t src_row, int64_t row_out,
-                                         int lane) {
+                                         const Team& tm) {
   const int64_t rb = s.row_bytes[i];
   uint8_t* dst = s.out[i] + row_out * rb;
   const uint8_t* sp = src ? src + src_row * rb : nullptr;
   const int u = s.vec[i];
   if (u == 16) {
-    for (int64_t off = (int64_t)lane * 16; off < rb; off += 32 * 16) copy_unit<16>(dst, sp, off);
+    for (int64_t off = (int64_t)tm.lane * 16; off < rb; off += tm.size * 16) copy_unit<16>(dst, sp, off);
   } else if (u == 4) {
-    for (int64_t off = (int64_t)lane * 4; off < rb; off += 32 * 4) copy_unit<4>(dst, sp, off);
+    for (int64_t off = (int64_t)tm.lane * 4; off < rb; off += tm.size * 4) copy_unit<4>(dst, sp, off);
   } else {
-    for (int64_t off = lane; off < rb; off += 32) copy_unit<1>(dst, sp, off);
+    for (int64_t off = tm.lane; off < rb; off += tm.size) copy_unit<1>(dst, sp, off);
   }
 }
 
 // out[t] = (mask[t] != invert) ? a[t] : b[t]
 __global__ void select_rows_kernel(const uint8_t* __restrict__ mask, int invert, RowSets s, int64_t tokens) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < tokens * s.n; w += warps) {
-    const int i = (int)(w / tokens);
-    const int64_t t = w % tokens;
+  const int i = blockIdx.y;
+  const Team tm = team_of(s, i);
+  for (int64_t t = tm.first; t < tokens; t += tm.stride) {
     const bool pick_a = (mask[t] != 0) != (invert != 0);
-    copy_row(s, i, pick_a ? s.a[i] : s.b[i], t, t, lane);
+    copy_row(s, i, pick_a ? s.a[i] : s.b[i], t, t, tm);
   }
 }
 
 // out[b][r] = r < counts[b] and 0 <= idx[b][r] < N ? a[b][idx] : 0       (compact <- dense)
 __global__ void gather_rows_kernel(const int* __restrict__ idx, const int* __restrict__ counts, RowSets s, int B,
                                    int N, int NC) {
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)B * NC;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows * s.n; w += warps) {
-    const int i = (int)(w / rows);
-    const int64_t br = w % rows;
-    const int b = (int)(br / NC), r = (int)(br % NC);
+  const int i = blockIdx.y;
+  const Team tm = team_of(s, i);
+  const int64_t rows = (int64_t)B * NC;  // below 2^31 (checked by the entry point)
+  for (int64_t br = tm.first; br < rows; br += tm.stride) {
+    const int b = (int)br / NC, r = (int)br - b * NC;
     const int c = counts ? counts[b] : NC;
     const int t = r < c ? idx[br] : -1;
     const bool ok = t >= 0 && t < N;
-    copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, lane);
+    copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, tm);
   }
 }
 
 // out[b][t] = 0 <= rank[b][t] < NC ? a[b][rank] : b_src[b][t]             (dense <- compact)
 __global__ void expand_rows_kernel(const int* __restrict__ rank, RowSets s, int B, int N, int NC) {
-  const int lane = threadIdx.x & 31;
-  const int64_t rows = (int64_t)B * N;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < rows * s.n; w += warps) {
-    const int i = (int)(w / rows);
-    const int64_t bt = w % rows;
-    const int b = (int)(bt / N);
+  const int i = blockIdx.y;
+  const Team tm = team_of(s, i);
+  const int64_t rows = (int64_t)B * N;  // below 2^31 (checked by the entry point)
+  for (int64_t bt = tm.first; bt < rows; bt += tm.stride) {
+    const int b = (int)bt / N;
     const int r = rank[bt];
-    if (r >= 0 && r < NC) copy_row(s, i, s.a[i], (int64_t)b * NC + r, bt, lane);
-    else copy_row(s, i, s.b[i], bt, bt, lane);
+    if (r >= 0 && r < NC) copy_row(s, i, s.a[i], (int64_t)b * NC + r, bt, tm);
+    else copy_row(s, i, s.b[i], bt, bt, tm);
   }
 }
 
@@ -115,18 +123,16 @@ __device__ __forceinline__ int slab_end(int c, int first, int NC) {
 // blockIdx.y; the warps stride over the rows that are written only (no per-row index division).
 __global__ void gather_slabs_kernel(const int* __restrict__ idx, const int* __restrict__ counts, RowSets s, int B,
                                     int N, int NC, int first) {
-  const int lane = threadIdx.x & 31;
   const int i = blockIdx.y;
-  const int warps = gridDim.x * (blockDim.x >> 5);
-  const int w0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const Team tm = team_of(s, i);
   for (int b = 0; b < B; ++b) {
     const int c = counts[b];
     const int end = slab_end(c, first, NC);
-    for (int r = w0; r < end; r += warps) {
+    for (int64_t r = tm.first; r < end; r += tm.stride) {
       const int64_t br = (int64_t)b * NC + r;
       const int t = r < c ? idx[br] : -1;
       const bool ok = t >= 0 && t < N;
-      copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, lane);
+      copy_row(s, i, ok ? s.a[i] : nullptr, (int64_t)b * N + (ok ? t : 0), br, tm);
     }
   }
 }
@@ -249,13 +255,23 @@ int fill_sets(RowSets& s, int n, const void* const* a, const void* const* b, voi
              ((uint64_t)row_bytes[i] & m) == 0;
     };
     s.vec[i] = all(15) ? 16 : all(3) ? 4 : 1;
+    const int64_t units = row_bytes[i] / s.vec[i];
+    int sh = 0;
+    while (sh < 5 && ((int64_t)1 << sh) < units) ++sh;
+    s.lshift[i] = sh;
   }
   return VB_OK;
 }
 
-unsigned grid_for(int64_t warps_needed) {
-  const int64_t blocks = (warps_needed + 7) / 8;  // 256 threads = 8 warps
-  return (unsigned)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+// The launch of a row-copy kernel over `rows` rows of each tensor: blocks of 256 threads, enough
+// for every row's team where the widest team decides, at most 8 blocks per SM (the teams then
+// stride), one grid row per tensor.
+dim3 grid_rows(const RowSets& s, int64_t rows) {
+  int sh = 0;
+  for (int i = 0; i < s.n; ++i) sh = s.lshift[i] > sh ? s.lshift[i] : sh;
+  const int64_t blocks = (rows * ((int64_t)1 << sh) + 255) / 256;
+  const int64_t cap = 148 * 8;
+  return dim3((unsigned)(blocks < 1 ? 1 : blocks < cap ? blocks : cap), (unsigned)s.n);
 }
 
 }  // namespace
@@ -282,7 +298,7 @@ extern "C" int vb_select_rows(const unsigned char* mask, int invert, int ntensor
   RowSets s;
   int rc = fill_sets(s, ntensors, a, b, out, row_bytes, "select_rows");
   if (rc) return rc;
-  select_rows_kernel<<<grid_for(tokens * ntensors), 256, 0, (cudaStream_t)stream>>>(mask, invert, s, tokens);
+  select_rows_kernel<<<grid_rows(s, tokens), 256, 0, (cudaStream_t)stream>>>(mask, invert, s, tokens);
   VB_LAUNCH_CHECK("select_rows");
   return VB_OK;
 }
@@ -290,12 +306,13 @@ extern "C" int vb_select_rows(const unsigned char* mask, int invert, int ntensor
 extern "C" int vb_gather_rows(const int* idx, const int* counts, int B, int N, int NC, int ntensors,
                               const void* const* src, void* const* dst, const long long* row_bytes, void* stream) {
   VB_REQUIRE(B >= 0 && N >= 0 && NC >= 0, "gather_rows: bad shape B=%d N=%d NC=%d", B, N, NC);
+  VB_REQUIRE((int64_t)B * NC <= 0x7fffffff && (int64_t)B * N <= 0x7fffffff, "gather_rows: rows exceed int32 indices");
   if ((int64_t)B * NC == 0) return VB_OK;
   VB_REQUIRE(idx != nullptr, "gather_rows: null index");
   RowSets s;
   int rc = fill_sets(s, ntensors, src, nullptr, dst, row_bytes, "gather_rows");
   if (rc) return rc;
-  gather_rows_kernel<<<grid_for((int64_t)B * NC * ntensors), 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N, NC);
+  gather_rows_kernel<<<grid_rows(s, (int64_t)B * NC), 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N, NC);
   VB_LAUNCH_CHECK("gather_rows");
   return VB_OK;
 }
@@ -310,8 +327,8 @@ extern "C" int vb_gather_rows_slabs(const int* idx, const int* counts, int B, in
   RowSets s;
   int rc = fill_sets(s, ntensors, src, nullptr, dst, row_bytes, "gather_rows_slabs");
   if (rc) return rc;
-  const unsigned blocks = grid_for((int64_t)NC);  // at most 4 CTAs per SM: most return at once
-  const dim3 grid(blocks < 148 * 4 ? blocks : 148 * 4, (unsigned)ntensors);
+  dim3 grid = grid_rows(s, (int64_t)NC);  // teams for one batch row's worth: most return at once
+  grid.x = grid.x < 148 * 4 ? grid.x : 148 * 4;
   gather_slabs_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(idx, counts, s, B, N, NC, first);
   VB_LAUNCH_CHECK("gather_rows_slabs");
   return VB_OK;
@@ -333,12 +350,13 @@ extern "C" int vb_expand_rows(const int* rank, int B, int N, int NC, int ntensor
                               const void* const* fallback, void* const* dst, const long long* row_bytes,
                               void* stream) {
   VB_REQUIRE(B >= 0 && N >= 0 && NC >= 0, "expand_rows: bad shape B=%d N=%d NC=%d", B, N, NC);
+  VB_REQUIRE((int64_t)B * N <= 0x7fffffff && (int64_t)B * NC <= 0x7fffffff, "expand_rows: rows exceed int32 indices");
   if ((int64_t)B * N == 0) return VB_OK;
   VB_REQUIRE(rank != nullptr, "expand_rows: null rank");
   RowSets s;
   int rc = fill_sets(s, ntensors, src, fallback, dst, row_bytes, "expand_rows");
   if (rc) return rc;
-  expand_rows_kernel<<<grid_for((int64_t)B * N * ntensors), 256, 0, (cudaStream_t)stream>>>(rank, s, B, N, NC);
+  expand_rows_kernel<<<grid_rows(s, (int64_t)B * N), 256, 0, (cudaStream_t)stream>>>(rank, s, B, N, NC);
   VB_LAUNCH_CHECK("expand_rows");
   return VB_OK;
 }
