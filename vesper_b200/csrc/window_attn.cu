@@ -321,20 +321,33 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
 }
 
 // ------------------------------------------------------------------------------------------
-// backward: delta = rowsum(dO * O) per (b, h, row), float32; one warp per (b, row, h)
+// backward: delta = rowsum(dO * O) per (b, h, row), float32; a team of lanes per (b, row, h), each
+// lane one 16-byte vector of both rows (DK / 8 lanes, rounded up to a power of two), the products
+// summed in the lane and then across the team
 // ------------------------------------------------------------------------------------------
 template <int DK, typename E>
 __global__ void attn_delta_kernel(const E* __restrict__ o, const E* __restrict__ dout, float* __restrict__ delta,
-                                  int64_t rows, int NQ, int H) {
-  const int lane = threadIdx.x & 31;
-  const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (r >= rows) return;
+                                  int rows, int NQ, int H) {
+  constexpr int VEC = 16 / (int)sizeof(E);
+  constexpr int NV = DK / VEC;  // 16-byte vectors per row
+  constexpr int LPR = NV <= 1 ? 1 : NV <= 2 ? 2 : NV <= 4 ? 4 : NV <= 8 ? 8 : NV <= 16 ? 16 : 32;
+  static_assert(DK % VEC == 0 && NV <= 32, "a row is whole 16-byte vectors, at most 32 of them");
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = g / LPR, l = g % LPR;
   float a = 0.f;
-  for (int d = lane; d < DK; d += 32) a += to_f32(o[r * DK + d]) * to_f32(dout[r * DK + d]);
-  a = warp_sum(a);
-  if (lane == 0) {
-    const int64_t h = r % H, bn = r / H;
-    delta[((bn / NQ) * H + h) * NQ + bn % NQ] = a;
+  if (r < rows && l < NV) {
+    const uint4 x = *reinterpret_cast<const uint4*>(o + (size_t)r * DK + l * VEC);
+    const uint4 y = *reinterpret_cast<const uint4*>(dout + (size_t)r * DK + l * VEC);
+    const E* xe = reinterpret_cast<const E*>(&x);
+    const E* ye = reinterpret_cast<const E*>(&y);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) a = fmaf(to_f32(xe[i]), to_f32(ye[i]), a);
+  }
+#pragma unroll
+  for (int off = LPR / 2; off > 0; off >>= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+  if (r < rows && l == 0) {
+    const int h = r % H, bn = r / H;
+    delta[((size_t)(bn / NQ) * H + h) * NQ + bn % NQ] = a;
   }
 }
 
@@ -746,7 +759,7 @@ extern "C" int vb_window_attn_bwd(const void* q, const int* qpos, const int* cou
     return window_attn_f32_bwd((const float*)q, qpos, counts, (const float*)keys, (const float*)values,
                                (const float*)o, lse, (const float*)dout, (float*)dq, (float*)dkeys, (float*)dvalues,
                                (float*)workspace, B, NQ, L, H, HKV, DK, window, st);
-  VB_REQUIRE(aligned16(o) && aligned16(dq) && aligned16(dkeys) && aligned16(dvalues),
+  VB_REQUIRE(aligned16(o) && aligned16(dout) && aligned16(dq) && aligned16(dkeys) && aligned16(dvalues),
              "window_attn_bwd: tensor not 16-byte aligned");
   const bool f16 = dtype == VB_F16;
   CUtensorMap qm, km, vm, gm;
@@ -762,7 +775,11 @@ extern "C" int vb_window_attn_bwd(const void* q, const int* qpos, const int* cou
     constexpr int D = decltype(dkc)::value;
     using E = decltype(e);
     const int64_t rows = (int64_t)B * NQ * H;
-    attn_delta_kernel<D, E><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>((const E*)o, (const E*)dout, delta, rows, NQ, H);
+    constexpr int NV = D * (int)sizeof(E) / 16, LPR = NV <= 1 ? 1 : NV <= 2 ? 2 : NV <= 4 ? 4 : NV <= 8 ? 8 : NV <= 16 ? 16 : 32;
+    VB_REQUIRE(rows * LPR <= 0x7fffffff, "window_attn_bwd: %lld query rows exceed the delta kernel's int32 indices",
+               (long long)rows);
+    attn_delta_kernel<D, E><<<(unsigned)((rows * LPR + 255) / 256), 256, 0, st>>>((const E*)o, (const E*)dout, delta,
+                                                                                  (int)rows, NQ, H);
     VB_LAUNCH_CHECK("window_attn_bwd delta");
     const size_t sq = dq_smem<D>();
     VB_CUDA_CHECK(cudaFuncSetAttribute(attn_dq_kernel<D, E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sq),
