@@ -12,7 +12,8 @@ from __future__ import annotations
 import pytest
 import torch
 
-from vesper_b200.kernels.compact import compact_index, expand_rows, gather_rows, select_rows
+from vesper_b200.kernels.compact import compact_flat, compact_index, expand_rows, gather_rows, select_rows
+from vesper_b200.kernels.slabs import bucket_end
 
 pytestmark = pytest.mark.gpu
 CUDA = torch.device("cuda")
@@ -103,3 +104,44 @@ def test_empty_batches_and_capture() -> None:
         graph.replay()
         torch.cuda.synchronize()
         assert torch.equal(bk, torch.where(act[..., None], x, torch.zeros_like(x)))
+
+
+@pytest.mark.parametrize(("b", "n", "p"), [(3, 700, 0.3), (4, 2048, 0.05), (2, 1000, 0.0), (2, 1500, 1.0)])
+def test_the_flat_compaction_and_its_relayout_match_nonzero(b: int, n: int, p: float) -> None:
+    """``compact_flat``: every active token of the batch in row order, its rank, the total, and
+    the maps between flat compact rows and the per-row compact rows ``(b, r)`` at ``b n + r``."""
+    active = _active(b, n, p, seed=b * n)
+    rows = compact_flat(active, 256)
+    flat = active.reshape(-1).nonzero().flatten().to(torch.int32)
+    c = flat.numel()
+    assert int(rows.counts[0]) == c
+    assert torch.equal(rows.idx[0, :c], flat)
+    rank = torch.full((b * n,), -1, dtype=torch.int32, device=CUDA)
+    rank[flat.long()] = torch.arange(c, dtype=torch.int32, device=CUDA)
+    assert torch.equal(rows.rank[0], rank)
+    counts = active.sum(1).tolist()
+    per_row = [b_ * n + r for b_ in range(b) for r in range(counts[b_])]
+    assert rows.relayout is not None
+    assert rows.relayout.idx[0, :c].tolist() == per_row
+    pb = torch.full((b * n,), -1, dtype=torch.int32)
+    pb[torch.tensor(per_row, dtype=torch.long)] = torch.arange(c, dtype=torch.int32)
+    assert torch.equal(rows.relayout.rank[0].cpu(), pb)
+
+
+def test_the_bucketed_gather_zeroes_to_the_bucket_end_and_leaves_the_rest() -> None:
+    """Rows from the count to the end of the count's bucket are zero; rows past it keep what the
+    buffer held (nothing reads them); the expand back restores the active rows exactly."""
+    b, n, d, first = 2, 3000, 48, 256
+    active = _active(b, n, 0.05, seed=9)
+    rows = compact_flat(active, first)
+    x = torch.randn(1, b * n, d, device=CUDA)
+    (xc,) = gather_rows(rows, [x])
+    c = int(rows.counts[0])
+    end = bucket_end(c, b * n, first)
+    assert end >= c and end < b * n
+    assert torch.equal(xc[0, :c], x[0, rows.idx[0, :c].long()])
+    assert bool((xc[0, c:end] == 0).all())
+    (back,) = expand_rows(rows, [xc])
+    keep = active.reshape(1, -1, 1)
+    assert torch.equal(torch.where(keep, back, 0.0), torch.where(keep, x, 0.0))
+    assert bool((back[~keep.expand_as(back)] == 0).all())
