@@ -69,37 +69,44 @@ __global__ void relu_square_bwd_kernel(const T* __restrict__ z, const T* __restr
     dz[i] = from_f32<T>(relu_square_grad<T>(to_f32<T>(z[i]), to_f32<T>(dy[i])));
 }
 
-// one thread per (token, pair group of 4 pairs = 8 elements) across all heads of the token
+// one thread per (token, pair group of 4 pairs = 8 elements): the group's four phases and their
+// cosines and sines (float64, the costly part) are formed once and turn that group of every head
+// of the token
 template <typename T, bool BWD>
 __global__ void rotary_kernel(const T* __restrict__ x, const int64_t* __restrict__ pos,
                               const double* __restrict__ inv_freq, T* __restrict__ y, int64_t tokens, int heads,
                               int dk) {
   const int groups = dk / 8;  // 8 elements (4 pairs) per group
-  const int64_t per_token = (int64_t)heads * groups;
-  const int64_t total = tokens * per_token;
+  const int64_t total = tokens * groups;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += stride) {
-    const int64_t tok = w / per_token;
-    const int rem = (int)(w % per_token);
-    const int hd = rem / groups, gi = rem % groups;
+    const int64_t tok = w / groups;
+    const int gi = (int)(w - tok * groups);
     const double p = (double)pos[tok];
-    const T* src = x + (tok * heads + hd) * dk + gi * 8;
-    float a[8], r[8];
-    load_vec<T, 8>(src, a);
+    float c[4], s[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const double ang = p * inv_freq[gi * 4 + q];
-      const float c = rnd64<T>(cos(ang)), s = rnd64<T>(sin(ang));
-      const float x1 = a[2 * q], x2 = a[2 * q + 1];
-      if constexpr (!BWD) {
-        r[2 * q] = rnd<T>(mul(x1, c)) - rnd<T>(mul(x2, s));
-        r[2 * q + 1] = rnd<T>(mul(x1, s)) + rnd<T>(mul(x2, c));
-      } else {  // x1, x2 hold the output gradient pair (g1, g2)
-        r[2 * q] = rnd<T>(mul(x1, c)) + rnd<T>(mul(x2, s));
-        r[2 * q + 1] = rnd<T>(mul(x2, c)) + rnd<T>(mul(-x1, s));
-      }
+      c[q] = rnd64<T>(cos(ang));
+      s[q] = rnd64<T>(sin(ang));
     }
-    store_vec<T, 8>(y + (tok * heads + hd) * dk + gi * 8, r);
+    for (int hd = 0; hd < heads; ++hd) {
+      const int64_t off = (tok * heads + hd) * dk + gi * 8;
+      float a[8], r[8];
+      load_vec<T, 8>(x + off, a);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float x1 = a[2 * q], x2 = a[2 * q + 1];
+        if constexpr (!BWD) {
+          r[2 * q] = rnd<T>(mul(x1, c[q])) - rnd<T>(mul(x2, s[q]));
+          r[2 * q + 1] = rnd<T>(mul(x1, s[q])) + rnd<T>(mul(x2, c[q]));
+        } else {  // x1, x2 hold the output gradient pair (g1, g2)
+          r[2 * q] = rnd<T>(mul(x1, c[q])) + rnd<T>(mul(x2, s[q]));
+          r[2 * q + 1] = rnd<T>(mul(x2, c[q])) + rnd<T>(mul(-x1, s[q]));
+        }
+      }
+      store_vec<T, 8>(y + off, r);
+    }
   }
 }
 
@@ -218,7 +225,7 @@ extern "C" int vb_rotary(const void* x, const long long* pos, const double* inv_
   if (tokens == 0) return VB_OK;
   VB_REQUIRE(x && pos && inv_freq && y && aligned16(x) && aligned16(y), "rotary: null or unaligned tensor");
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16 || dtype == VB_F16, "rotary: bad dtype %d", dtype);
-  const int64_t items = tokens * heads * (dk / 8);
+  const int64_t items = tokens * (dk / 8);
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
     if (backward)
       rotary_kernel<T, true><<<grid_for(items), 256, 0, (cudaStream_t)stream>>>(
