@@ -69,19 +69,23 @@ __global__ void relu_square_bwd_kernel(const T* __restrict__ z, const T* __restr
     dz[i] = from_f32<T>(relu_square_grad<T>(to_f32<T>(z[i]), to_f32<T>(dy[i])));
 }
 
-// one thread per (token, pair group of 4 pairs = 8 elements): the group's four phases and their
-// cosines and sines (float64, the costly part) are formed once and turn that group of every head
-// of the token
+// one thread per (token, pair group of 4 pairs = 8 elements, run of `hpt` heads): the group's four
+// phases and their cosines and sines (float64, the costly part) are formed once and turn that
+// group of each head of the run (every head when there are tokens enough to fill the GPU, one
+// head per thread for the few tokens of a decode step, where latency rules)
 template <typename T, bool BWD>
 __global__ void rotary_kernel(const T* __restrict__ x, const int64_t* __restrict__ pos,
                               const double* __restrict__ inv_freq, T* __restrict__ y, int64_t tokens, int heads,
-                              int dk) {
+                              int dk, int hpt) {
   const int groups = dk / 8;  // 8 elements (4 pairs) per group
-  const int64_t total = tokens * groups;
+  const int runs = (heads + hpt - 1) / hpt;
+  const int64_t total = tokens * groups * runs;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += stride) {
-    const int64_t tok = w / groups;
-    const int gi = (int)(w - tok * groups);
+    const int64_t tr = w / groups;  // (token, run); the group varies fastest: coalesced rows
+    const int gi = (int)(w - tr * groups);
+    const int64_t tok = tr / runs;
+    const int h0 = (int)(tr - tok * runs) * hpt, h1 = min(heads, h0 + hpt);
     const double p = (double)pos[tok];
     float c[4], s[4];
 #pragma unroll
@@ -90,7 +94,7 @@ __global__ void rotary_kernel(const T* __restrict__ x, const int64_t* __restrict
       c[q] = rnd64<T>(cos(ang));
       s[q] = rnd64<T>(sin(ang));
     }
-    for (int hd = 0; hd < heads; ++hd) {
+    for (int hd = h0; hd < h1; ++hd) {
       const int64_t off = (tok * heads + hd) * dk + gi * 8;
       float a[8], r[8];
       load_vec<T, 8>(x + off, a);
@@ -225,14 +229,16 @@ extern "C" int vb_rotary(const void* x, const long long* pos, const double* inv_
   if (tokens == 0) return VB_OK;
   VB_REQUIRE(x && pos && inv_freq && y && aligned16(x) && aligned16(y), "rotary: null or unaligned tensor");
   VB_REQUIRE(dtype == VB_F32 || dtype == VB_BF16 || dtype == VB_F16, "rotary: bad dtype %d", dtype);
-  const int64_t items = tokens * (dk / 8);
+  // every head of a token per thread once there are threads enough for two waves of 256 per SM
+  const int hpt = tokens * (dk / 8) >= 148 * 256 * 2 ? heads : 1;
+  const int64_t items = tokens * (dk / 8) * ((heads + hpt - 1) / hpt);
   return VB_DISPATCH_DTYPE(dtype, T, [&]() -> int {
     if (backward)
       rotary_kernel<T, true><<<grid_for(items), 256, 0, (cudaStream_t)stream>>>(
-          (const T*)x, (const int64_t*)pos, inv_freq, (T*)y, tokens, heads, dk);
+          (const T*)x, (const int64_t*)pos, inv_freq, (T*)y, tokens, heads, dk, hpt);
     else
       rotary_kernel<T, false><<<grid_for(items), 256, 0, (cudaStream_t)stream>>>(
-          (const T*)x, (const int64_t*)pos, inv_freq, (T*)y, tokens, heads, dk);
+          (const T*)x, (const int64_t*)pos, inv_freq, (T*)y, tokens, heads, dk, hpt);
     VB_LAUNCH_CHECK("rotary");
     return VB_OK;
   });
