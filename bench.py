@@ -888,6 +888,40 @@ def profile_column(args) -> None:
     torch.cuda.synchronize(device)
 
 
+def profile_copies(args) -> None:
+    """The loop's compaction and copy-forward kernels once each, eagerly, on one pass of config 4
+    at its measured halting (B=32, T=2048, d=512; 5478 of 65536 tokens active, as after two
+    passes), after ``--warmup`` warm-ups: the flat compaction, the bucketed gather of the float32
+    residual stream, the expand of the recurrent inputs with carried fallbacks, the key select and
+    the attention-output relayout (a single process, for an ncu capture of their DRAM bytes)."""
+    import torch
+
+    from vesper_b200.kernels.compact import compact_flat, expand_rows, gather_rows, select_rows
+    from vesper_b200.kernels.slabs import SLAB_FIRST
+
+    device = torch.device("cuda", 0)
+    b, t, d, h = TRAIN_B, TRAIN_T, 512, 8
+    g = torch.Generator(device=device).manual_seed(11)
+    active = torch.zeros(b * t, dtype=torch.bool, device=device)
+    active[torch.randperm(b * t, device=device, generator=g)[:5478]] = True
+    active = active.view(b, t)
+    x = torch.randn(1, b * t, d, device=device, generator=g)
+    carried = [torch.randn(1, b * t, w, device=device, generator=g).to(torch.bfloat16) for w in (d, d, h)]
+    fresh_k = torch.randn(b, t, h, d // h, device=device, generator=g).to(torch.bfloat16)
+    carry_k = torch.randn(b, t, h, d // h, device=device, generator=g).to(torch.bfloat16)
+    oa = torch.randn(1, b * t, d, device=device, generator=g).to(torch.bfloat16)
+    with torch.no_grad():
+        for _ in range(max(args.warmup, 1) + 1):
+            rows = compact_flat(active, SLAB_FIRST)
+            (xc,) = gather_rows(rows, [x])
+            comp = [torch.randn(1, b * t, w, device=device, generator=g).to(torch.bfloat16) for w in (d, d, d, h)]
+            expand_rows(rows, comp, [None, *carried])
+            select_rows(active, [fresh_k], [carry_k])
+            assert rows.relayout is not None
+            gather_rows(rows.relayout, [oa])
+    torch.cuda.synchronize(device)
+
+
 def breakdown(args) -> None:
     """Device time per kernel of one leg under torch's profiler (CUPTI activity, no ncu):
     ``step`` one config-2 step, ``train`` one config-4 training step (a replay of the captured
@@ -981,6 +1015,8 @@ def main() -> None:
     p.add_argument("--train-steps", type=int, default=5, help="timed training-step replays")
     p.add_argument("--profile-step", action="store_true", help="warm up, run one eager step, exit")
     p.add_argument("--batch", type=int, default=B, help="batch rows per GPU (profiling only; the bench is 8)")
+    p.add_argument("--profile-copies", action="store_true",
+                   help="warm up, run the loop's compaction and copy kernels once each on config-4 sizes, exit")
     p.add_argument("--profile-column", action="store_true",
                    help="warm up, run one eager config-3 column fwd+bwd of --batch rows, exit (for ncu)")
     p.add_argument("--no-compact", action="store_true",
@@ -996,6 +1032,9 @@ def main() -> None:
         return
     if args.profile_column:
         profile_column(args)
+        return
+    if args.profile_copies:
+        profile_copies(args)
         return
     if args.impl == "reference":
         if not args.steps_ref:
