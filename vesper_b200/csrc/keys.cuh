@@ -168,6 +168,70 @@ __device__ __forceinline__ void st_f32(float* __restrict__ p, const float (&in)[
 }
 
 // sums / maxima over the G lanes of a head (G a power of two up to 32, the same on every lane)
+// Element-wise float32 arithmetic over a row of EPL values, two lanes of the row per instruction
+// where EPL is even (the packed f32x2 FMA and product of sm_100: each lane rounds exactly as
+// fmaf / a product do, so the results equal the scalar ones bit for bit).
+// d = a * b + c
+template <int N>
+__device__ __forceinline__ void fma_row(float (&d)[N], const float (&a)[N], const float (&b)[N], const float (&c)[N]) {
+  if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < N; e += 2) {
+      const float2 r = __ffma2_rn(make_float2(a[e], a[e + 1]), make_float2(b[e], b[e + 1]), make_float2(c[e], c[e + 1]));
+      d[e] = r.x;
+      d[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) d[e] = fmaf(a[e], b[e], c[e]);
+  }
+}
+// d = s * b + c (s one value for the row)
+template <int N>
+__device__ __forceinline__ void fma_row(float (&d)[N], float s, const float (&b)[N], const float (&c)[N]) {
+  if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < N; e += 2) {
+      const float2 r = __ffma2_rn(make_float2(s, s), make_float2(b[e], b[e + 1]), make_float2(c[e], c[e + 1]));
+      d[e] = r.x;
+      d[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) d[e] = fmaf(s, b[e], c[e]);
+  }
+}
+// d = a * b
+template <int N>
+__device__ __forceinline__ void mul_row(float (&d)[N], const float (&a)[N], const float (&b)[N]) {
+  if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < N; e += 2) {
+      const float2 r = __fmul2_rn(make_float2(a[e], a[e + 1]), make_float2(b[e], b[e + 1]));
+      d[e] = r.x;
+      d[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) d[e] = a[e] * b[e];
+  }
+}
+// d = s * b
+template <int N>
+__device__ __forceinline__ void mul_row(float (&d)[N], float s, const float (&b)[N]) {
+  if constexpr (N % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < N; e += 2) {
+      const float2 r = __fmul2_rn(make_float2(s, s), make_float2(b[e], b[e + 1]));
+      d[e] = r.x;
+      d[e + 1] = r.y;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) d[e] = s * b[e];
+  }
+}
+
 __device__ __forceinline__ float group_sum(float v, int G) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
@@ -523,15 +587,11 @@ __global__ void __launch_bounds__(WARPS * 32, 4) keys_bwd_kernel(
       }
       float k[EPL];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        float a = 0.f;
+      for (int e = 0; e < EPL; ++e) k[e] = 0.f;
 #pragma unroll
-        for (int r = 0; r < K; ++r) a = fmaf(tp[r][e], win[(j - r + K) % K][e], a);
-        k[e] = a;
-      }
+      for (int r = 0; r < K; ++r) fma_row<EPL>(k, tp[r], win[(j - r + K) % K], k);
       if constexpr (STATS) {
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) k[e] *= rr;
+        mul_row<EPL>(k, rr, k);
       } else {
         normalize<EPL>(k, G, floor_, rr, clamp);
       }
@@ -541,8 +601,8 @@ __global__ void __launch_bounds__(WARPS * 32, 4) keys_bwd_kernel(
       dot = group_sum(dot, G);  // every lane takes part; a head whose clamp holds drops it below
       if (!clamp) dot = 0.f;
       float du[EPL];
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) du[e] = rr * fmaf(-dot, k[e], g[e]);
+      fma_row<EPL>(du, -dot, k, g);
+      mul_row<EPL>(du, rr, du);
       // slot j held dz of tok - K, complete with token tok - 1; it restarts with tok's own term
       if constexpr (CLEAN) {
         if (w.live) st_row<T, EPL>(dq, acc[j]);
@@ -550,17 +610,12 @@ __global__ void __launch_bounds__(WARPS * 32, 4) keys_bwd_kernel(
         flush<T, EPL, K>(tok - K, acc[j], dzp, dhp, t0, t1, W, w.live);
       }
       dq += W;
+      mul_row<EPL>(acc[j], tp[0], du);
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) acc[j][e] = tp[0][e] * du[e];
-#pragma unroll
-      for (int r = 1; r < K; ++r)
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) acc[(j - r + K) % K][e] = fmaf(tp[r][e], du[e], acc[(j - r + K) % K][e]);
+      for (int r = 1; r < K; ++r) fma_row<EPL>(acc[(j - r + K) % K], tp[r], du, acc[(j - r + K) % K]);
       if (CLEAN || tok < t1) {
 #pragma unroll
-        for (int r = 0; r < K; ++r)
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) dt[r][e] = fmaf(du[e], win[(j - r + K) % K][e], dt[r][e]);
+        for (int r = 0; r < K; ++r) fma_row<EPL>(dt[r], du, win[(j - r + K) % K], dt[r]);
       }
     }
   };
