@@ -185,6 +185,14 @@ constexpr int NP = 256;
 //      thread a 1 x 4 strip of each product, the sums running over the blocks that are not zero.
 // Five barriers instead of seven, and each product's dependent chain is at most 32 terms with four
 // independent accumulators per thread. Entries above the diagonal blocks are not written.
+// acc += a * v over the four lanes of a float4, two lanes per packed f32x2 FMA (each lane rounds
+// as fmaf: the same results as four scalar FMAs)
+__device__ __forceinline__ void fma4(float4& acc, float a, const float4& v) {
+  const float2 lo = __ffma2_rn(make_float2(a, a), make_float2(v.x, v.y), make_float2(acc.x, acc.y));
+  const float2 hi = __ffma2_rn(make_float2(a, a), make_float2(v.z, v.w), make_float2(acc.z, acc.w));
+  acc = make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 constexpr int XS = 68;  // row stride of X (16-byte aligned rows)
 constexpr int AS = 68;  // row stride of A (16-byte aligned rows: written as 16-byte vectors)
 constexpr int TS = 36;  // row stride of the products' scratch
@@ -215,7 +223,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     for (int s = 0; s < 16; ++s) {
       const float a = A[(ro + r2) * AS + co + s];
       const float4 x = *reinterpret_cast<const float4*>(X + (co + s) * XS + co + q4);
-      t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
+      fma4(t, a, x);
     }
     *reinterpret_cast<float4*>(Tm + (hf * 16 + r2) * TS + q4) = t;
   }
@@ -227,7 +235,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     for (int s = 0; s < 16; ++s) {
       const float a = X[(ro + r2) * XS + ro + s];
       const float4 t = *reinterpret_cast<const float4*>(Tm + (hf * 16 + s) * TS + q4);
-      x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
+      fma4(x, a, t);
     }
     *reinterpret_cast<float4*>(X + (ro + r2) * XS + co + q4) = make_float4(-x.x, -x.y, -x.z, -x.w);
   }
@@ -241,7 +249,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     for (int k = k0; k < 32; ++k) {
       const float a = A[(32 + i3) * AS + k];
       const float4 x = *reinterpret_cast<const float4*>(X + k * XS + j4);
-      t.x = fmaf(a, x.x, t.x); t.y = fmaf(a, x.y, t.y); t.z = fmaf(a, x.z, t.z); t.w = fmaf(a, x.w, t.w);
+      fma4(t, a, x);
     }
     *reinterpret_cast<float4*>(Tm + i3 * TS + j4) = t;
   }
@@ -253,7 +261,7 @@ __device__ __forceinline__ void invert_unit_lower(const float* A, float* X, floa
     for (int k = 0; k < k1; ++k) {
       const float a = X[(32 + i3) * XS + 32 + k];
       const float4 t = *reinterpret_cast<const float4*>(Tm + k * TS + j4);
-      x.x = fmaf(a, t.x, x.x); x.y = fmaf(a, t.y, x.y); x.z = fmaf(a, t.z, x.z); x.w = fmaf(a, t.w, x.w);
+      fma4(x, a, t);
     }
     *reinterpret_cast<float4*>(X + (32 + i3) * XS + j4) = make_float4(-x.x, -x.y, -x.z, -x.w);
   }
