@@ -240,11 +240,13 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
     tmem_ld32(lane_tm + kc + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
     tmem_wait_ld();
     float mt = -INFINITY;
-    if (interior) {
+    if (interior) {  // the scaling two lanes per packed f32x2 product (each rounds as a product)
 #pragma unroll
-      for (int j = 0; j < BK / 2; ++j) {
-        sv[j] *= sl2;
-        mt = fmaxf(mt, sv[j]);
+      for (int j = 0; j < BK / 2; j += 2) {
+        const float2 v = __fmul2_rn(make_float2(sv[j], sv[j + 1]), make_float2(sl2, sl2));
+        sv[j] = v.x;
+        sv[j + 1] = v.y;
+        mt = fmaxf(mt, fmaxf(v.x, v.y));
       }
     } else {
 #pragma unroll
@@ -261,16 +263,22 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(
     const float mnew = fmaxf(m2, mt);
     const float mref = mnew == -INFINITY ? 0.f : mnew;  // all masked so far: every p is 2^-inf = 0
     const float corr = ex2(m2 - mref);
-    float ls0 = 0.f, ls1 = 0.f, ls2 = 0.f, ls3 = 0.f;
+    // the subtraction and the four running sums two lanes per packed f32x2 add (x - m is
+    // x + (-m) exactly, and each lane rounds as a scalar add: the same values as scalar code)
+    float2 l01 = make_float2(0.f, 0.f), l23 = make_float2(0.f, 0.f);
+    const float2 nm = make_float2(-mref, -mref);
 #pragma unroll
     for (int j = 0; j < BK / 2; j += 4) {
-      sv[j] = ex2(sv[j] - mref);
-      sv[j + 1] = ex2(sv[j + 1] - mref);
-      sv[j + 2] = ex2(sv[j + 2] - mref);
-      sv[j + 3] = ex2(sv[j + 3] - mref);
-      ls0 += sv[j]; ls1 += sv[j + 1]; ls2 += sv[j + 2]; ls3 += sv[j + 3];
+      const float2 d01 = __fadd2_rn(make_float2(sv[j], sv[j + 1]), nm);
+      const float2 d23 = __fadd2_rn(make_float2(sv[j + 2], sv[j + 3]), nm);
+      sv[j] = ex2(d01.x);
+      sv[j + 1] = ex2(d01.y);
+      sv[j + 2] = ex2(d23.x);
+      sv[j + 3] = ex2(d23.y);
+      l01 = __fadd2_rn(l01, make_float2(sv[j], sv[j + 1]));
+      l23 = __fadd2_rn(l23, make_float2(sv[j + 2], sv[j + 3]));
     }
-    l = l * corr + ((ls0 + ls1) + (ls2 + ls3));
+    l = l * corr + ((l01.x + l01.y) + (l23.x + l23.y));
     m2 = mnew;
     st_row32<E>(Pt, BQ, r128, kc, sv);
     st_row32<E>(Pt, BQ, r128, kc + 32, sv + 32);
