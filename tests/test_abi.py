@@ -45,3 +45,35 @@ def test_size_queries_answer_without_a_gpu() -> None:
     assert _lib.query("vb_rms_norm_bwd_workspace", 100, 512) > 0
     assert _lib.query("vb_keys_bwd_workspace", 2, 100, 128, 2, 4) > 0
     assert _lib.query("vb_delta_scan_f32_bwd_workspace", 2, 64, 4, 64) > 0
+
+
+def _refused(name: str, *args: object, match: str) -> None:
+    """The entry point returns an error status, with ``match`` in its message, before it touches
+    a pointer or launches anything (so this runs without a GPU)."""
+    try:
+        _lib.call(name, *args)
+    except _lib.KernelError as exc:
+        assert match in str(exc), str(exc)
+    else:
+        raise AssertionError(f"{name} accepted {args}")
+
+
+def test_the_compaction_entry_points_refuse_bad_arguments_without_a_gpu() -> None:
+    sizes = (ctypes.c_longlong * 1)(64)
+    ptrs = (ctypes.c_void_p * 1)(None)
+    _refused("vb_gather_rows_slabs", None, None, 1, 10, 10, 0, 1, ptrs, ptrs, sizes, None, match="bad shape")
+    _refused("vb_gather_rows_slabs", None, None, 1, 10, 10, 4, 1, ptrs, ptrs, sizes, None, match="null index")
+    _refused("vb_flatten_compaction", None, None, None, 1 << 16, 1 << 16, None, None, None, None, None, None,
+             match="exceed int32")  # fmt: skip
+    _refused("vb_flatten_compaction", None, None, None, 2, 8, None, None, None, None, None, None, match="null pointer")
+    _refused("vb_expand_rows", None, 1 << 16, 1 << 16, 1, 1, ptrs, ptrs, ptrs, sizes, None, match="exceed int32")
+
+
+def test_the_bucket_entry_points_refuse_bad_arguments_without_a_gpu() -> None:
+    bodies = (ctypes.c_void_p * 24)()
+    _refused("vb_slab_switch", None, 100, 0, None, bodies, match="buckets")
+    _refused("vb_slab_switch", None, 1 << 30, 1, None, bodies, match="buckets")  # 31 doublings: over 24
+    _refused("vb_slab_switch", None, 4096, 1024, None, bodies, match="null pointer")
+    _refused("vb_slab_begin", None, None, match="null body")
+    assert _lib.query("vb_slab_count", 0, 1024) == 0
+    assert _lib.query("vb_slab_count", 4096, 1024) == 3
